@@ -1,0 +1,125 @@
+/*
+ * uwc_b200.h -- C ABI of the B200 (sm_100a) NoisyGEMM library (libuwcb200.so).
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream (as void*, 0 = the legacy
+ * default stream), launches asynchronously on that stream and returns an int status (UWC_OK or
+ * an UWC_ERR_* code below). No entry point allocates device memory: workspaces are caller-owned
+ * and their sizes are queryable. Launch errors are reported by the return code; errors detected
+ * inside kernels (a bounded wait that ran out) are sticky bits read with uwc_device_status().
+ *
+ * Each declaration names the reference interface it replaces (paths inside
+ * srivassid/useful-work-coin). The reference launches CUDA C++ kernels through CuPy from
+ * miner/ampere/uwc_ampere/ops.py; the Python mirror of that module in this repository
+ * (useful-work-coin_b200/uwc_b200/ops.py) binds these functions with ctypes.
+ *
+ * Threading: like the reference (ops.py:62-70), callers serialize work on one stream per device;
+ * the library keeps per-device launch configuration and tensor-map caches guarded by a mutex.
+ */
+#ifndef UWC_B200_H
+#define UWC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host return values) */
+#define UWC_OK 0
+#define UWC_ERR_ARG 1     /* null pointer where one is required, bad enum value */
+#define UWC_ERR_SHAPE 2   /* shape precondition violated (the reference's asserts, ops.py:191-192) */
+#define UWC_ERR_ALIGN 3   /* pointer or row stride not 16-byte aligned */
+#define UWC_ERR_CUDA 4    /* CUDA runtime / driver error while configuring or launching */
+#define UWC_ERR_DEVICE 5  /* current device is not sm_100 (B200) */
+#define UWC_ERR_SCRATCH 6 /* caller-provided scratch too small */
+
+/* ---- device status bits (uwc_device_status) */
+#define UWC_DEV_TIMEOUT 1u /* a kernel's bounded wait ran out and the kernel unwound */
+
+/* ---- constants shared with the reference (ops.py:26-29, kernels.cu:475-480) */
+#define UWC_FLAG_HASH 1
+#define UWC_FLAG_DENOISE 2
+#define UWC_OUT_NONE 0
+#define UWC_OUT_I32 1
+#define UWC_OUT_BF16 2
+#define UWC_OUT_F32 3 /* new: detrt dequant y = fmul(fmul(float(acc), a_scale[i]), b_scale[j]) (qwen3.py:125) */
+#define UWC_WIN_WORDS 10
+
+/* Library version (major*10000 + minor*100 + patch). */
+int uwc_version(void);
+
+/* Human-readable name of a status code. */
+const char* uwc_status_string(int code);
+
+/* Sticky device status bits of the current device (UWC_DEV_*). Synchronizes the device.
+ * clear != 0 resets them to 0 afterwards. */
+int uwc_device_status(uint32_t* status_out, int clear);
+
+/* ---- BLAKE3 commitment ------------------------------------------------------------------
+ * Replaces ops.b3_root_and_seed (miner/ampere/uwc_ampere/ops.py:99-118) and the kernels
+ * b3_tree_stage1/_mid/_stage2 (kernels.cu:138-244).
+ * Keyed BLAKE3 Merkle root of `nbytes` bytes (nbytes % 1024 == 0, > 0) under the 8-word key.
+ * If seed_out != NULL also derives Pearl's cert-v3 salted seed
+ *   seed = BLAKE3(prefix || BLAKE3_keyed(salt, root || dim_le32 || 0^28))
+ * (prefix, salt: 8 words each, device). root_out may be NULL.
+ * scratch: device u32 workspace of uwc_b3_scratch_words(nbytes) words. */
+uint64_t uwc_b3_scratch_words(uint64_t nbytes);
+int uwc_b3_root_and_seed(const void* data, uint64_t nbytes, const uint32_t* key, const uint32_t* prefix,
+                         const uint32_t* salt, uint32_t dim, uint32_t* root_out, uint32_t* seed_out,
+                         uint32_t* scratch, uint64_t scratch_words, void* stream);
+
+/* ---- noise generation ------------------------------------------------------------------
+ * Replaces ops.noise_uniform (ops.py:122-125, kernels.cu:259-282): nbytes (% 32 == 0) int8 values
+ * (b & 63) - 32 from keyed BLAKE3 random_hash(block, label, key, prepend=0). If zero_me != NULL its
+ * first zero_n int32 words are set to 0 (per-call counters, no extra memset launch). */
+int uwc_noise_uniform(int8_t* out, uint64_t nbytes, const uint32_t* label, const uint32_t* key, int32_t* zero_me,
+                      int zero_n, void* stream);
+
+/* Replaces ops.noise_perm (ops.py:128-131, kernels.cu:284-301): k packed pairs
+ * first | second << 16, first = u & (r-1), second = first ^ (1 + mulhi(r-1, u)); r a power of two. */
+int uwc_noise_perm(uint32_t* out, uint32_t k, uint32_t r, const uint32_t* label, const uint32_t* key, void* stream);
+
+/* Replaces ops.noise_rows (ops.py:134-142, kernels.cu:303-372). For each of `rows` rows of src
+ * (rows x k int8): dst = src + E[first] - E[second] under Pn (if dst); projection under Pp written
+ * as lmax balanced base-128 limbs to corr[li][row][corr_off + j] (row stride 2r) and max |proj|
+ * folded into *maxabs with atomicMax (if Pp); E copied to corr[li][row][ecopy_off + j] (if
+ * ecopy_off >= 0). rows % 8 == 0, k % 16 == 0, r in {64,128,256}. */
+int uwc_noise_rows(const int8_t* src, int rows, int k, int r, const int8_t* E, const uint32_t* Pn, int8_t* dst,
+                   const uint32_t* Pp, int8_t* corr, int corr_off, int ecopy_off, int32_t* maxabs, int lmax,
+                   void* stream);
+
+/* Replaces ops.proj_matrix (ops.py:152-158, kernels.cu:397-404): S^T (r x k int8),
+ * S^T[j][l] = [P.first(l) == j] - [P.second(l) == j]. */
+int uwc_proj_matrix(const uint32_t* P, int k, int r, int8_t* St, void* stream);
+
+/* Replaces the tail of ops.project (ops.py:161-168, kernels.cu:374-395): balanced base-128
+ * limbs of an int32 projection (rows x r) into corr[li][row][corr_off + j], max |proj| into *maxabs. */
+int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_off, int32_t* maxabs, int lmax,
+                  void* stream);
+
+/* ---- the NoisyGEMM ----------------------------------------------------------------------
+ * Replaces ops.gemm (ops.py:185-198) / kernel noisy_gemm (kernels.cu:482-715), on tcgen05
+ * kind::i8 tensor cores with TMEM accumulators.
+ * C = A B^T, A: m x k, B: n x k, int8, k contiguous (row stride k bytes, 16-byte aligned).
+ *  flags & UWC_FLAG_HASH   : every r columns of k, XOR-fold each 8x16 hash tile (rows g+8i,
+ *                            cols 2t+{0,1}+8j of a 64x64 block) into msg[c % 16] (rotl 13);
+ *                            at the end hash = BLAKE3_keyed(key, msg) and, if hash <= target
+ *                            (LE U256), append {row_off, col_off, hash[8]} to wins
+ *                            (wins[0] = count, then max_wins records of UWC_WIN_WORDS words;
+ *                            the count keeps counting past max_wins). m % 64 == 0, n % 64 == 0,
+ *                            r in {64, 128, 256}, k % r == 0.
+ *  flags & UWC_FLAG_DENOISE: subtract sum_li 128^li corrA[li] corrB[li]^T (K' = 2r per limb)
+ *                            with L limbs chosen from max(maxabs[0], maxabs[1]) (<= lmax).
+ *  out_mode                : UWC_OUT_NONE / UWC_OUT_I32 (int32 m x n) / UWC_OUT_BF16
+ *                            (RNE of (float(acc) * a_scale[i]) * b_scale[j]) / UWC_OUT_F32
+ *                            (same expression in fp32, the detrt dequant).
+ * Without flags any m >= 1 works (rows past m are read as zero and not stored); k % 16 == 0. */
+int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
+             const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key, const uint32_t* target,
+             uint32_t* wins, int max_wins, const float* a_scale, const float* b_scale, void* out, int out_mode,
+             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* UWC_B200_H */

@@ -1,0 +1,171 @@
+"""The full mined path against the oracle (mirrors miner/ampere/tests/test_kernels.py:94-138,
+test_proj_gemm.py and test_gemm_cfgs.py): exact output, identical winning tiles, identical
+correction tensors across projection paths, CUDA-graph replay == eager."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops(dev):
+    from uwc_b200 import _lib, ops
+    _lib.device_status(clear=True)
+    yield ops
+    assert _lib.device_status(clear=True) == 0, "a kernel reported a device-side timeout"
+
+
+def _inputs(m, n, k, seed):
+    rng = np.random.default_rng(seed)
+    A = rng.integers(-64, 65, size=(m, k), dtype=np.int8)
+    Bt = rng.integers(-64, 65, size=(n, k), dtype=np.int8)
+    return A, Bt, rng.bytes(32)
+
+
+def _expected(A, Bt, key, r, target):
+    a_seed, b_seed, wins, msgs = O.mined_reference(A, Bt, key, r, target)
+    return a_seed, wins
+
+
+@pytest.mark.parametrize("m,n,k,r", [(256, 512, 2048, 128), (256, 512, 2048, 64), (128, 256, 1024, 64),
+                                     (384, 768, 2048, 128), (128, 320, 1024, 256), (192, 256, 1024, 64)])
+def test_mined_forward_exact_and_winners_match_oracle(ops, m, n, k, r):
+    from uwc_b200 import glue
+    A, Bt, key = _inputs(m, n, k, 7 + r)
+    target = glue.target_for(m, n, 20)
+    w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r, max_wins=4096)
+    w.setup_block(key, target)
+    out = w.forward(torch.from_numpy(A).cuda(), torch.ones(m, device="cuda"), out_mode=ops.OUT_I32)
+    assert np.array_equal(out.cpu().numpy(), O.gemm_i32(A, Bt))
+    a_seed, want = _expected(A, Bt, key, r, target)
+    assert ops.words_to_bytes(w._buf(m)["a_seed"]) == a_seed
+    got = sorted(w.winners(m))
+    assert want and got == want
+
+
+@pytest.mark.parametrize("m,n,k,r", [(256, 512, 2048, 128), (512, 512, 1024, 64), (128, 256, 2048, 64),
+                                     (384, 320, 1024, 128), (256, 256, 1024, 256)])
+def test_noise_mine_winners_match_oracle(ops, m, n, k, r):
+    from uwc_b200 import glue
+    A, Bt, key = _inputs(m, n, k, 100 + m + r)
+    target = glue.target_for(m, n, 20)
+    w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r, max_wins=4096)
+    w.setup_block(key, target)
+    w.noise_mine(torch.from_numpy(A).cuda())
+    _, want = _expected(A, Bt, key, r, target)
+    assert want and sorted(w.winners(m)) == want
+
+
+def test_golden_winners(ops, golden):
+    """Winner sets produced by the reference's own reference.py (tests/golden)."""
+    meta, _ = golden
+    for c in meta["mined"]:
+        m, n, k, r = c["m"], c["n"], c["k"], c["r"]
+        rng = np.random.default_rng(c["seed"])
+        A = rng.integers(-64, 65, size=(m, k), dtype=np.int8)
+        Bt = rng.integers(-64, 65, size=(n, k), dtype=np.int8)
+        key = rng.bytes(32)
+        target = O.bound_words(int(c["bound"], 16))
+        w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r, max_wins=4096)
+        w.setup_block(key, target)
+        out = w.forward(torch.from_numpy(A).cuda(), torch.ones(m, device="cuda"), out_mode=ops.OUT_I32)
+        got = [[a, b, h.hex()] for a, b, h in sorted(w.winners(m))]
+        assert got == c["winners"]
+        assert O.sha20(out.cpu().numpy()) == c["out_sha"][:20]
+        w.noise_mine(torch.from_numpy(A).cuda())
+        assert [[a, b, h.hex()] for a, b, h in sorted(w.winners(m))] == c["winners"]
+
+
+def test_projection_paths_identical(ops):
+    """Tensor-core projections == shared-memory-atomic noise_rows (test_proj_gemm.py:23-47)."""
+    from uwc_b200 import glue
+    for (n, k, m) in ((1024, 2048, 256), (512, 4096, 128)):
+        A, Bt, key = _inputs(m, n, k, n + k + m)
+        res = {}
+        for mode in (False, True):
+            w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=128)
+            w.setup_block(key, glue.target_for(m, n))
+            ones = torch.ones(m, dtype=torch.float32, device="cuda")
+            out = w._forward(torch.from_numpy(A).cuda(), ones, None, ops.OUT_I32, True, ops.DEFAULT_CFG, mode)
+            b = w._buf(m)
+            res[mode] = (out.clone(), b["corrA"].clone(), w.corrB.clone(), b["maxabs"].clone(), sorted(w.winners(m)))
+        for name, x, y in zip(("out", "corrA", "corrB", "maxabs"), res[False][:4], res[True][:4]):
+            assert torch.equal(x, y), name
+        assert res[False][4] == res[True][4] and 0 < len(res[True][4]) < 64
+        assert np.array_equal(res[True][0].cpu().numpy(), O.gemm_i32(A, Bt))
+
+
+def test_large_projection_needs_more_limbs(ops):
+    """An A aligned with P_B pushes |X| = |A P_B^T| past 8127, so the denoise must use 3 limbs."""
+    m, n, k, r = 128, 256, 8192, 64
+    rng = np.random.default_rng(21)
+    Bt = rng.integers(-64, 65, size=(n, k), dtype=np.int8)
+    key = bytes(range(32))
+    b_seed = O.salted_seed(O.tree_root(Bt, key), n, O.SEED_SALT_B, key)
+    PB = O.perm_matrix(O.SEED_LABEL_B, b_seed, k, r)
+    A = rng.integers(-8, 9, size=(m, k), dtype=np.int8)
+    A[:, PB[:, 0] == 0] = 64
+    A[:, PB[:, 1] == 0] = -64
+    assert O.projection(A, O.pack_perm(PB), r).max() > 8127
+    w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r)
+    w.setup_block(key, np.zeros(8, np.uint32))
+    out = w.forward(torch.from_numpy(A).cuda(), torch.ones(m, device="cuda"), out_mode=ops.OUT_I32)
+    assert int(w._buf(m)["maxabs"].max().item()) > 8127
+    assert np.array_equal(out.cpu().numpy(), O.gemm_i32(A, Bt))
+
+
+def test_bf16_forward_matches_int_path(ops):
+    """MinedWeight.forward(OUT_BF16) == RNE((float(A Bt^T) * a_scale) * b_scale) (kernels.cu:687-714)."""
+    m, n, k, r = 256, 512, 2048, 128
+    A, Bt, key = _inputs(m, n, k, 3)
+    rng = np.random.default_rng(4)
+    sa = (rng.random(m, dtype=np.float32) * 0.01).astype(np.float32)
+    sb = (rng.random(n, dtype=np.float32) * 0.01).astype(np.float32)
+    w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.from_numpy(sb).cuda(), r=r)
+    w.setup_block(key, np.zeros(8, np.uint32))
+    out = w.forward(torch.from_numpy(A).cuda(), torch.from_numpy(sa).cuda())
+    want = O.scaled_bf16(O.gemm_i32(A, Bt), sa, sb)
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), want)
+
+
+def test_graphed_forward_matches_eager(ops):
+    rng = np.random.default_rng(5)
+    m, n, k = 256, 512, 2048
+    A = torch.from_numpy(rng.integers(-64, 65, size=(m, k), dtype=np.int8)).cuda()
+    Bt = torch.from_numpy(rng.integers(-64, 65, size=(n, k), dtype=np.int8)).cuda()
+    w = ops.MinedWeight(Bt=Bt, b_scale=torch.ones(n, device="cuda"))
+    w.setup_block(rng.bytes(32), np.zeros(8, np.uint32))
+    gf = ops.GraphedForward(w, m, out_mode=ops.OUT_I32)
+    gf.A.copy_(A)
+    got = gf().clone()
+    assert np.array_equal(got.cpu().numpy(), O.gemm_i32(A.cpu().numpy(), Bt.cpu().numpy()))
+
+
+def test_win_overflow_counts_past_max(ops):
+    """Every tile wins at target = 2^256-1: the count keeps counting, records stop at max_wins."""
+    m, n, k, r = 128, 256, 1024, 128
+    A, Bt, key = _inputs(m, n, k, 9)
+    w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r, max_wins=16)
+    w.setup_block(key, O.bound_words((1 << 256) - 1))
+    w.noise_mine(torch.from_numpy(A).cuda())
+    assert w.win_count(m) == m * n // 128
+    assert len(w.winners(m)) == 16
+
+
+def test_det_linear(ops):
+    """DetLinear.int_gemm and the fused fp32 dequant (qwen3.py:106-126) at the C1 shape."""
+    from uwc_b200 import det
+    rng = np.random.default_rng(0)
+    q = rng.integers(-127, 128, (256, 2048), dtype=np.int8)
+    Wq = rng.integers(-64, 65, (6144, 2048), dtype=np.int8)
+    sx = (rng.random(256, dtype=np.float32) * 0.01).astype(np.float32)
+    sw = (rng.random(6144, dtype=np.float32) * 0.001).astype(np.float32)
+    acc = det.int_gemm(torch.from_numpy(q).cuda(), torch.from_numpy(Wq).cuda())
+    want = O.gemm_i32_blas(q, Wq)
+    assert np.array_equal(acc.cpu().numpy(), want)
+    y = det.linear_f32(torch.from_numpy(q).cuda(), torch.from_numpy(sx).cuda(), torch.from_numpy(Wq).cuda(),
+                       torch.from_numpy(sw).cuda())
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), O.det_dequant(want, sx, sw).view(np.uint32))

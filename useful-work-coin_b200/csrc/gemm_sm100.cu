@@ -1,0 +1,690 @@
+// The NoisyGEMM on Blackwell tensor cores (sm_100a): C = A B^T, int8 x int8 -> int32 with
+// tcgen05.mma kind::i8, TMEM accumulators and TMA-fed 128-byte-swizzled shared-memory stages.
+//
+// Reference semantics: noisy_gemm (miner/ampere/uwc_ampere/kernels.cu:482-715), launched by
+// ops.gemm (ops.py:185-198). Three schedules share one persistent, warp-specialized kernel:
+//
+//   MODE_MINE  FLAG_HASH, no output (MinedWeight.noise_mine, ops.py:349-364). A work unit is a
+//              256 x 256 output block held as two 128 x 256 TMEM accumulators X (rows 0-127)
+//              and Y (rows 128-255) sharing the B tile. The MMA warp alternates r-column chunks
+//              of X and Y, so the epilogue folds X's running sum while the tensor core works on Y.
+//   MODE_FWD   FLAG_DENOISE and/or FLAG_HASH with an output (MinedWeight.forward, ops.py:316-347).
+//              A unit is a 128 x 256 block held as two 128 x 128 accumulators (column halves)
+//              plus a 128 x 256 correction accumulator R = sum_li 128^li corrA[li] corrB[li]^T,
+//              built before the main loop by Horner steps (R <<= 7 done by the epilogue in TMEM).
+//              The output is acc - R, exact in int32.
+//   MODE_PLAIN no flags: a 128 x 256 block per unit, two accumulators used alternately across
+//              units so the store of one unit overlaps the main loop of the next.
+//
+// Hash tiles (pearl_glue.py:14-15): rows g + 8i (i < 8), cols 2t + {0,1} + 8j (j < 8) of a
+// 64 x 64 block. tcgen05.ld.16x256b hands thread (g = lane/4, t = lane%4) exactly rows {g, g+8}
+// and cols 8j + 2t + {0,1} of a 16-lane x 64-column slab, so a warp's two loads (lanes +0, +16 of
+// its TMEM quadrant) give every thread 64 values of ONE hash tile: the XOR-fold is register-local.
+// Rows 32-63 of a 64-row block live in the next quadrant (the next warp); XOR and rotl are linear
+// over GF(2), so each warp keeps a partial message and the two partials are XORed once per unit.
+//
+// Warp roles (640 threads, one CTA per SM, all 512 TMEM columns):
+//   0..15   epilogue: warp w reads TMEM lanes 32*(w%4).. and the 64-column block w/4
+//   16..17  hash: keyed BLAKE3 of the finished tile messages, target compare, win records
+//   18      TMA producer (one lane)
+//   19      MMA issuer (one lane); allocates and frees TMEM
+#include <algorithm>
+
+#include "uwc_device.cuh"
+#include "uwc_host.h"
+
+namespace {
+
+enum Mode { MODE_PLAIN = 0, MODE_MINE = 1, MODE_FWD = 2 };
+
+constexpr int kEpiWarps = 16;
+constexpr int kHashWarps = 2;
+constexpr int kProducerWarp = kEpiWarps + kHashWarps;   // 18
+constexpr int kMmaWarp = kProducerWarp + 1;             // 19
+constexpr int kThreads = (kMmaWarp + 1) * 32;           // 640
+constexpr int kKB = 128;                                // K bytes per stage (one 128-byte swizzle row)
+constexpr int kUN = 256;                                // output columns per unit
+constexpr int kStageBytesMine = 2 * 128 * kKB + kUN * kKB;  // A 256 rows + B 256 rows = 64 KiB
+constexpr int kStageBytesFwd = 128 * kKB + kUN * kKB;       // A 128 rows + B 256 rows = 48 KiB
+constexpr int kStagesMine = 3;
+constexpr int kStagesFwd = 4;
+constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
+constexpr int kHashBufBytes = kMaxTiles * 16 * 4;       // 32 KiB of tile messages
+constexpr int kBarBytes = 256;
+
+struct Params {
+  int m, n, k, r;
+  int hash;         // FLAG_HASH
+  int denoise;      // FLAG_DENOISE
+  int lmax;
+  int out_mode;
+  int max_wins;
+  int nm, nn, nunits;
+  const int32_t* maxabs;
+  const uint32_t* key;
+  const uint32_t* target;
+  uint32_t* wins;
+  const float* a_scale;
+  const float* b_scale;
+  void* out;
+  uint32_t* status;
+};
+
+template <int MODE>
+struct Cfg {
+  static constexpr int UM = MODE == MODE_MINE ? 256 : 128;  // output rows per unit
+  static constexpr int A_BYTES = UM * kKB;
+  static constexpr int STAGE = MODE == MODE_MINE ? kStageBytesMine : kStageBytesFwd;
+  static constexpr int NST = MODE == MODE_MINE ? kStagesMine : kStagesFwd;
+  static constexpr int HASHBUF = MODE == MODE_PLAIN ? 0 : kHashBufBytes;
+  static constexpr int SMEM = NST * STAGE + HASHBUF + kBarBytes + 1024;  // +1024: manual alignment
+  static constexpr int TILES = MODE == MODE_MINE ? 512 : 256;
+};
+
+struct Bars {
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t r_full, r_scaled, r_empty;
+  uint64_t hash_ready, hash_free;
+  uint64_t pair[8];        // odd quadrant warp -> even quadrant warp: partial messages written
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int L;
+};
+
+__device__ __forceinline__ void unit_coords(const Params& p, int u, int UM, int& m0, int& n0) {
+  constexpr int G = 16;  // group of row blocks that sweep the columns together (L2 reuse of B)
+  const int grp = G * p.nn, gid = u / grp, first = gid * G;
+  const int gsz = min(p.nm - first, G), in = u - gid * grp;
+  m0 = (first + in % gsz) * UM;
+  n0 = (in / gsz) * kUN;
+}
+
+__device__ __forceinline__ uint32_t rotl13(uint32_t x) { return __funnelshift_l(x, x, 13); }
+
+// Limb count from the projections' max |value| (kernels.cu:602-607 thresholds), capped at lmax.
+__device__ __forceinline__ int limbs_from_maxabs(const Params& p) {
+  if (!p.denoise) return 0;
+  const int mx = max(p.maxabs[0], p.maxabs[1]);
+  int L = 1;
+  if (mx > 63) L = 2;
+  if (mx > 8127) L = 3;
+  if (mx > 1040319) L = 4;
+  return min(L, p.lmax);
+}
+
+// ------------------------------------------------------------------ output stores
+__device__ __forceinline__ uint32_t bf16_rne(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+
+// Store 32 consecutive int32 accumulators of one row (columns c0..c0+31) in the chosen format.
+__device__ __forceinline__ void store_row32(const Params& p, int row, int c0, const int32_t* v) {
+  if (p.out_mode == UWC_OUT_NONE || row >= p.m || c0 >= p.n) return;
+  const bool full = c0 + 32 <= p.n;
+  if (p.out_mode == UWC_OUT_I32 || p.out_mode == UWC_OUT_F32) {
+    uint32_t w[32];
+    if (p.out_mode == UWC_OUT_I32) {
+#pragma unroll
+      for (int i = 0; i < 32; i++) w[i] = (uint32_t)v[i];
+    } else {
+      const float sx = p.a_scale[row];
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        const float sw = (c0 + i < p.n) ? __ldg(p.b_scale + c0 + i) : 0.f;
+        w[i] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn(v[i]), sx), sw));
+      }
+    }
+    uint32_t* o = reinterpret_cast<uint32_t*>(p.out) + (uint64_t)row * p.n + c0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) reinterpret_cast<uint4*>(o)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; i++)
+        if (c0 + i < p.n) o[i] = w[i];
+    }
+  } else {  // UWC_OUT_BF16: RNE((float(acc) * a_scale) * b_scale)
+    const float sx = p.a_scale[row];
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float s0 = (c0 + 2 * i < p.n) ? __ldg(p.b_scale + c0 + 2 * i) : 0.f;
+      const float s1 = (c0 + 2 * i + 1 < p.n) ? __ldg(p.b_scale + c0 + 2 * i + 1) : 0.f;
+      const float f0 = __fmul_rn(__fmul_rn(__int2float_rn(v[2 * i]), sx), s0);
+      const float f1 = __fmul_rn(__fmul_rn(__int2float_rn(v[2 * i + 1]), sx), s1);
+      w[i] = bf16_rne(f0) | (bf16_rne(f1) << 16);
+    }
+    uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + (uint64_t)row * p.n + c0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) reinterpret_cast<uint4*>(o)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; i++)
+        if (c0 + i < p.n) o[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+    }
+  }
+}
+
+// XOR of this thread's 64 values of one hash tile in a 32-lane x 64-column TMEM slab; the second
+// load is issued after the first is folded to keep register pressure at 32.
+__device__ __forceinline__ uint32_t fold_tile(uint32_t taddr) {
+  uint32_t v[32];
+  tmem_ld_16x256b_x8(taddr, v);
+  tmem_wait_ld();
+  uint32_t x = xor32(v);
+  tmem_ld_16x256b_x8(taddr + (16u << 16), v);
+  tmem_wait_ld();
+  return x ^ xor32(v);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_noisy_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmCA, const __grid_constant__ CUtensorMap tmCB, const Params p) {
+  using C = Cfg<MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint32_t* hbuf = reinterpret_cast<uint32_t*>(smem + C::NST * C::STAGE);
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE + C::HASHBUF);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NST; s++) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    const int acc_consumers = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], acc_consumers);
+    }
+    mbar_init(&bars->r_full, 1);
+    mbar_init(&bars->r_scaled, kEpiWarps);
+    mbar_init(&bars->r_empty, kEpiWarps);
+    // smem hand-offs are signalled by every writing lane (arrival counts in threads)
+    mbar_init(&bars->hash_ready, (kEpiWarps / 2) * 32);
+    mbar_init(&bars->hash_free, kHashWarps * 32);
+    for (int i = 0; i < 8; i++) mbar_init(&bars->pair[i], 32);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    bars->L = MODE == MODE_FWD ? limbs_from_maxabs(p) : 0;
+    mbar_fence_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (MODE == MODE_FWD && p.denoise) {
+      tma_prefetch_desc(&tmCA);
+      tma_prefetch_desc(&tmCB);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const int L = bars->L;
+  const int k = p.k;
+  const int kblocks = (k + kKB - 1) / kKB;
+  const int chunk = p.hash ? p.r : kKB;                // columns of k between snapshots
+  const int nch = (k + chunk - 1) / chunk;
+  const int cblocks = MODE == MODE_FWD ? (2 * p.r) / kKB : 1;  // k-blocks per correction limb
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t gk = 0;
+      for (int u = blockIdx.x; u < p.nunits && !*abort_flag; u += gridDim.x) {
+        int m0, n0;
+        unit_coords(p, u, C::UM, m0, n0);
+        const int ncorr = MODE == MODE_FWD ? L * cblocks : 0;
+        const int nblk = ncorr + kblocks;
+        for (int b = 0; b < nblk; b++, gk++) {
+          const int s = gk % C::NST;
+          const uint32_t ph = (gk / C::NST) & 1;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, abort_flag, p.status)) break;
+          uint8_t* sA = smem + s * C::STAGE;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_expect_tx(&bars->full[s], C::STAGE);
+          if (b < ncorr) {
+            const int li = L - 1 - b / cblocks, kb = b % cblocks;
+            tma_load_2d(sA, &tmCA, &bars->full[s], kb * kKB, li * p.m + m0);
+            tma_load_2d(sB, &tmCB, &bars->full[s], kb * kKB, li * p.n + n0);
+          } else {
+            const int kb = b - ncorr;
+            tma_load_2d(sA, &tmA, &bars->full[s], kb * kKB, m0);
+            tma_load_2d(sB, &tmB, &bars->full[s], kb * kKB, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t gk = 0;                 // k-blocks consumed (ring position)
+      uint32_t snaps[2] = {0, 0};      // snapshots produced per accumulator
+      uint32_t r_commits = 0, r_scaled_waits = 0;
+      int local = 0;
+      bool ok = true;
+      const uint32_t smem_base = smem_u32(smem);
+      for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
+        int m0, n0;
+        unit_coords(p, u, C::UM, m0, n0);
+        // ---- correction accumulator R (FWD): Horner over limbs, highest limb first
+        if (MODE == MODE_FWD && L > 0) {
+          const uint32_t tR = tmem + 256;
+          for (int li = L - 1; li >= 0 && ok; li--) {
+            if (li == L - 1)
+              ok = mbar_wait(&bars->r_empty, (local & 1) ^ 1, abort_flag, p.status);
+            else
+              ok = mbar_wait(&bars->r_scaled, r_scaled_waits++ & 1, abort_flag, p.status);
+            if (!ok) break;
+            tc_fence_after();
+            for (int kb = 0; kb < cblocks && ok; kb++, gk++) {
+              const int s = gk % C::NST;
+              ok = mbar_wait(&bars->full[s], (gk / C::NST) & 1, abort_flag, p.status);
+              if (!ok) break;
+              tc_fence_after();
+              const uint32_t aA = smem_base + s * C::STAGE, aB = aA + C::A_BYTES;
+#pragma unroll
+              for (int ks = 0; ks < 4; ks++)
+                mma_i8(tR, sdesc_sw128(aA + 32 * ks), sdesc_sw128(aB + 32 * ks), idesc_i8(128, 256),
+                       (li == L - 1 && kb == 0 && ks == 0) ? 0u : 1u);
+              mma_commit(&bars->empty[s]);
+            }
+            mma_commit(&bars->r_full);
+            r_commits++;
+          }
+        }
+        // ---- main loop over r-chunks of k
+        const int nacc = MODE == MODE_MINE ? (m0 + 128 < p.m ? 2 : 1) : (MODE == MODE_FWD ? 2 : 1);
+        const uint32_t acc_col[2] = {
+            MODE == MODE_PLAIN ? (uint32_t)((local & 1) * 256) : 0u,
+            MODE == MODE_MINE ? 256u : 128u};
+        const int plain_buf = local & 1;
+        uint32_t kb_released = 0;
+        const uint32_t gk0 = gk;
+        for (int c = 0; c < nch && ok; c++) {
+          const int kbeg = c * chunk, kend = min(k, kbeg + chunk);
+          for (int a = 0; a < nacc && ok; a++) {
+            const int bar_a = MODE == MODE_PLAIN ? plain_buf : a;
+            if (p.hash || c == 0) {
+              const uint32_t uses = MODE == MODE_PLAIN ? (uint32_t)(local >> 1) : snaps[a];
+              ok = mbar_wait(&bars->acc_empty[bar_a], (uses & 1) ^ 1, abort_flag, p.status);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            const uint32_t dcol = tmem + acc_col[a];
+            for (int kofs = kbeg; kofs < kend; kofs += 32) {
+              const uint32_t kb = kofs / kKB, g = gk0 + kb;
+              const int s = g % C::NST;
+              if (a == 0 && (kofs % kKB) == 0) {
+                ok = mbar_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
+                if (!ok) break;
+                tc_fence_after();
+              }
+              const uint32_t ko = kofs % kKB;
+              const uint32_t aA = smem_base + s * C::STAGE;
+              const uint32_t aB = aA + C::A_BYTES;
+              uint64_t ad, bd;
+              uint32_t id;
+              if (MODE == MODE_MINE) {
+                ad = sdesc_sw128(aA + a * (128 * kKB) + ko);
+                bd = sdesc_sw128(aB + ko);
+                id = idesc_i8(128, 256);
+              } else if (MODE == MODE_FWD) {
+                ad = sdesc_sw128(aA + ko);
+                bd = sdesc_sw128(aB + a * (128 * kKB) + ko);
+                id = idesc_i8(128, 128);
+              } else {
+                ad = sdesc_sw128(aA + ko);
+                bd = sdesc_sw128(aB + ko);
+                id = idesc_i8(128, 256);
+              }
+              mma_i8(dcol, ad, bd, id, kofs == 0 ? 0u : 1u);
+            }
+            if (!ok) break;
+            if (p.hash || c == nch - 1) {
+              mma_commit(&bars->acc_full[bar_a]);
+              if (MODE != MODE_PLAIN) snaps[a]++;
+            }
+          }
+          // release every stage whose k-range has been fully consumed by all accumulators
+          while (ok && kb_released < (uint32_t)kblocks &&
+                 ((kb_released + 1) * kKB <= (uint32_t)kend || kend == k)) {
+            mma_commit(&bars->empty[(gk0 + kb_released) % C::NST]);
+            kb_released++;
+          }
+        }
+        gk = gk0 + kblocks;
+      }
+      // drain: every MMA issued by this thread has completed before TMEM is released
+      mma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, abort_flag, p.status);
+    }
+  } else if (warp < kEpiWarps) {
+    // ------------------------------------------------------------ epilogue warps
+    const int q = warp & 3, cb = warp >> 2;
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    const int g = lane >> 2, t = lane & 3;
+    (void)g; (void)t;
+    uint32_t snaps[2] = {0, 0};
+    uint32_t r_waits = 0;
+    int local = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
+      int m0, n0;
+      unit_coords(p, u, C::UM, m0, n0);
+      if (MODE == MODE_PLAIN) {
+        const int b = local & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t col = tmem + b * 256 + cb * 64;
+#pragma unroll 1
+        for (int h = 0; h < 2; h++) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_base + col + h * 32, v);
+          tmem_wait_ld();
+          store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + h * 32, reinterpret_cast<const int32_t*>(v));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty[b]);
+        continue;
+      }
+
+      if (MODE == MODE_MINE) {
+        const bool hasY = m0 + 128 < p.m;
+        const uint32_t colX = tmem + cb * 64 + lane_base, colY = tmem + 256 + cb * 64 + lane_base;
+        uint32_t mx[16], my[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) { mx[i] = 0u; my[i] = 0u; }
+        for (int c0 = 0; c0 < nch && ok; c0 += 16) {
+#pragma unroll
+          for (int s = 0; s < 16; s++) {
+            if (c0 + s < nch && ok) {
+              ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[0], snaps[0] & 1, abort_flag, p.status));
+              if (ok) {
+                snaps[0]++;
+                tc_fence_after();
+                const uint32_t x = fold_tile(colX);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->acc_empty[0]);
+                mx[s] = rotl13(mx[s]) ^ x;
+              }
+              if (hasY && ok) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[1], snaps[1] & 1, abort_flag, p.status));
+                if (ok) {
+                  snaps[1]++;
+                  tc_fence_after();
+                  const uint32_t y = fold_tile(colY);
+                  tc_fence_before();
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive(&bars->acc_empty[1]);
+                  my[s] = rotl13(my[s]) ^ y;
+                }
+              }
+            }
+          }
+        }
+        if (!ok) break;
+        // combine the two quadrant partials of each tile and hand the messages to the hash warps
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free, (local & 1) ^ 1, abort_flag, p.status));
+        if (!ok) break;
+        const int rb = q >> 1, pair_id = cb * 2 + rb;
+        const int slotX = ((0 * 2 + rb) * 4 + cb) * 32 + lane, slotY = ((1 * 2 + rb) * 4 + cb) * 32 + lane;
+        if (q & 1) {
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            hbuf[i * kMaxTiles + slotX] = mx[i];
+            hbuf[i * kMaxTiles + slotY] = my[i];
+          }
+          mbar_arrive(&bars->pair[pair_id]);
+        } else {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->pair[pair_id], local & 1, abort_flag, p.status));
+          if (!ok) break;
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            hbuf[i * kMaxTiles + slotX] ^= mx[i];
+            hbuf[i * kMaxTiles + slotY] ^= my[i];
+          }
+          mbar_arrive(&bars->hash_ready);
+        }
+        continue;
+      }
+
+      if (MODE == MODE_FWD) {
+        // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
+        for (int step = 0; step + 1 < L && ok; step++) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int h = 0; h < 2; h++) {
+            uint32_t v[32];
+            const uint32_t ta = tmem + 256 + cb * 64 + h * 32 + lane_base;
+            tmem_ld_32x32b_x32(ta, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] <<= 7;
+            tmem_st_32x32b_x32(ta, v);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->r_scaled);
+        }
+        if (!ok) break;
+        const int a = cb >> 1;
+        const uint32_t col = tmem + a * 128 + (cb & 1) * 64 + lane_base;
+        uint32_t mm[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) mm[i] = 0u;
+        for (int c0 = 0; c0 < nch && ok; c0 += 16) {
+#pragma unroll
+          for (int s = 0; s < 16; s++) {
+            const int c = c0 + s;
+            if (c < nch && ok && (p.hash || c == nch - 1)) {
+              ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status));
+              if (!ok) break;
+              snaps[a]++;
+              tc_fence_after();
+              if (p.hash) mm[s] = rotl13(mm[s]) ^ fold_tile(col);
+              if (c == nch - 1) {
+                // output: acc - R for this warp's 32 lanes x 64 columns
+                if (L > 0) {
+                  ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
+                  if (!ok) break;
+                  tc_fence_after();
+                }
+                if (p.out_mode != UWC_OUT_NONE) {
+#pragma unroll 1
+                  for (int h = 0; h < 2; h++) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(col + h * 32, v);
+                    if (L > 0) {
+                      uint32_t rr[32];
+                      tmem_ld_32x32b_x32(tmem + 256 + cb * 64 + h * 32 + lane_base, rr);
+                      tmem_wait_ld();
+#pragma unroll
+                      for (int i = 0; i < 32; i++) v[i] = v[i] - rr[i];
+                    } else {
+                      tmem_wait_ld();
+                    }
+                    store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + h * 32, reinterpret_cast<const int32_t*>(v));
+                  }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                  mbar_arrive(&bars->acc_empty[a]);
+                  if (L > 0) mbar_arrive(&bars->r_empty);
+                }
+              } else {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
+              }
+            }
+          }
+        }
+        if (!ok) break;
+        if (p.hash) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free, (local & 1) ^ 1, abort_flag, p.status));
+          if (!ok) break;
+          const int rb = q >> 1, pair_id = cb * 2 + rb;
+          const int slot = (rb * 4 + cb) * 32 + lane;
+          if (q & 1) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slot] = mm[i];
+            mbar_arrive(&bars->pair[pair_id]);
+          } else {
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->pair[pair_id], local & 1, abort_flag, p.status));
+            if (!ok) break;
+#pragma unroll
+            for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slot] ^= mm[i];
+            mbar_arrive(&bars->hash_ready);
+          }
+        }
+      }
+    }
+  } else if (MODE != MODE_PLAIN && p.hash) {
+    // ------------------------------------------------------------ hash warps
+    const int hw = warp - kEpiWarps;
+    uint32_t key[8], tgt[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) { key[i] = p.key[i]; tgt[i] = p.target[i]; }
+    int local = 0;
+    for (int u = blockIdx.x; u < p.nunits; u += gridDim.x, local++) {
+      int m0, n0;
+      unit_coords(p, u, C::UM, m0, n0);
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->hash_ready, local & 1, abort_flag, p.status))) break;
+      for (int slot = hw * 32 + lane; slot < C::TILES; slot += kHashWarps * 32) {
+        const int ln = slot & 31, cbk = (slot >> 5) & 3, rb = (slot >> 7) & 1, a = slot >> 8;
+        const int row_off = m0 + a * 128 + rb * 64 + (ln >> 2);
+        const int col_off = n0 + cbk * 64 + 2 * (ln & 3);
+        if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) continue;
+        uint32_t msg[16], h[8];
+#pragma unroll
+        for (int i = 0; i < 16; i++) msg[i] = hbuf[i * kMaxTiles + slot];
+        b3::hash64(key, msg, h);
+        bool le = true, decided = false;
+#pragma unroll
+        for (int i = 7; i >= 0; i--) {
+          if (!decided && h[i] != tgt[i]) {
+            le = h[i] < tgt[i];
+            decided = true;
+          }
+        }
+        if (le) {
+          const uint32_t ws = atomicAdd(p.wins, 1u);
+          if (ws < (uint32_t)p.max_wins) {
+            uint32_t* rec = p.wins + 1 + (uint64_t)ws * UWC_WIN_WORDS;
+            rec[0] = (uint32_t)row_off;
+            rec[1] = (uint32_t)col_off;
+#pragma unroll
+            for (int i = 0; i < 8; i++) rec[2 + i] = h[i];
+          }
+        }
+      }
+      mbar_arrive(&bars->hash_free);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  if (*abort_flag) {
+    // let in-flight TMA copies and MMAs land before the CTA (and its shared memory) goes away
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 20000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
+}
+
+template <int MODE>
+int launch(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& ca, const CUtensorMap& cb,
+           cudaStream_t st) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(k_noisy_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<MODE>::SMEM) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return UWC_ERR_CUDA;
+    }
+    configured[dev] = 1;
+  }
+  const int grid = std::min(p.nunits, uwc_num_sms());
+  k_noisy_gemm<MODE><<<grid, kThreads, Cfg<MODE>::SMEM, st>>>(a, b, ca, cb, p);
+  return uwc_launch_status();
+}
+
+}  // namespace
+
+extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
+                        const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key,
+                        const uint32_t* target, uint32_t* wins, int max_wins, const float* a_scale,
+                        const float* b_scale, void* out, int out_mode, void* stream) {
+  const bool hash = flags & UWC_FLAG_HASH, denoise = flags & UWC_FLAG_DENOISE;
+  if (!A || !B || (flags & ~3) || out_mode < 0 || out_mode > 3) return UWC_ERR_ARG;
+  if (out_mode != UWC_OUT_NONE && !out) return UWC_ERR_ARG;
+  if ((out_mode == UWC_OUT_BF16 || out_mode == UWC_OUT_F32) && (!a_scale || !b_scale)) return UWC_ERR_ARG;
+  if (hash && (!key || !target || !wins || max_wins < 0)) return UWC_ERR_ARG;
+  if (denoise && (!corrA || !corrB || !maxabs || lmax < 1 || lmax > 4)) return UWC_ERR_ARG;
+  if (m <= 0 || n <= 0 || k <= 0 || k % 16) return UWC_ERR_SHAPE;
+  if (hash || denoise) {
+    if (m % 64 || n % 64 || k % 64) return UWC_ERR_SHAPE;
+    if (r != 64 && r != 128 && r != 256) return UWC_ERR_SHAPE;
+    if (k % r) return UWC_ERR_SHAPE;
+  }
+  if (out_mode == UWC_OUT_BF16 ? (n % 8) : (out_mode != UWC_OUT_NONE && n % 4)) return UWC_ERR_SHAPE;
+  if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)out) | ((uintptr_t)corrA) | ((uintptr_t)corrB)) & 15)
+    return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+
+  Params p{};
+  p.m = m; p.n = n; p.k = k; p.r = r;
+  p.hash = hash; p.denoise = denoise; p.lmax = lmax; p.out_mode = out_mode; p.max_wins = max_wins;
+  p.maxabs = maxabs; p.key = key; p.target = target; p.wins = wins;
+  p.a_scale = a_scale; p.b_scale = b_scale; p.out = out;
+  p.status = uwc_status_ptr();
+  const int mode = (hash && !denoise && out_mode == UWC_OUT_NONE) ? MODE_MINE : ((hash || denoise) ? MODE_FWD : MODE_PLAIN);
+  const int UM = mode == MODE_MINE ? 256 : 128;
+  p.nm = (m + UM - 1) / UM;
+  p.nn = (n + kUN - 1) / kUN;
+  p.nunits = p.nm * p.nn;
+
+  CUtensorMap ta, tb, tca, tcb;
+  int rc = uwc_make_tmap_2d(&ta, A, (uint64_t)m, (uint64_t)k, (uint64_t)k, UM, kKB);
+  if (rc == UWC_OK) rc = uwc_make_tmap_2d(&tb, B, (uint64_t)n, (uint64_t)k, (uint64_t)k, kUN, kKB);
+  if (rc != UWC_OK) return rc;
+  if (denoise) {
+    rc = uwc_make_tmap_2d(&tca, corrA, (uint64_t)lmax * m, (uint64_t)2 * r, (uint64_t)2 * r, 128, kKB);
+    if (rc == UWC_OK) rc = uwc_make_tmap_2d(&tcb, corrB, (uint64_t)lmax * n, (uint64_t)2 * r, (uint64_t)2 * r, kUN, kKB);
+    if (rc != UWC_OK) return rc;
+  } else {
+    tca = ta;
+    tcb = tb;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  if (mode == MODE_MINE) return launch<MODE_MINE>(p, ta, tb, tca, tcb, st);
+  if (mode == MODE_FWD) return launch<MODE_FWD>(p, ta, tb, tca, tcb, st);
+  return launch<MODE_PLAIN>(p, ta, tb, tca, tcb, st);
+}

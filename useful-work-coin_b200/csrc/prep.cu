@@ -1,0 +1,410 @@
+// Per-block / per-attempt preparation kernels of the NoisyGEMM path, sm_100a:
+//   BLAKE3 Merkle commitment + cert-v3 salted seed   (ops.py:99-118, kernels.cu:138-244)
+//   noise_uniform, noise_perm                        (ops.py:122-131, kernels.cu:246-301)
+//   noise_rows (noising, projection limbs, maxabs)   (ops.py:134-142, kernels.cu:303-372)
+//   proj_matrix, proj_corr (tensor-core projection)  (ops.py:145-168, kernels.cu:374-404)
+// All of them are HBM- or latency-bound SIMT kernels; the dense work is in gemm_sm100.cu.
+#include <algorithm>
+
+#include "uwc_device.cuh"
+#include "uwc_host.h"
+
+// ------------------------------------------------------------------ BLAKE3 tree
+namespace {
+constexpr int kChunksPerCta = 128;   // one thread per 1 KiB chunk
+constexpr int kReduceGroup = 1024;   // CVs reduced by one CTA of the reduce kernel
+constexpr int kPitch = 5;            // uint4 per staged 64-byte block (80 B pitch: conflict-free)
+
+// Level-wise pairwise merge of `count` chaining values in shared memory, the odd trailing node
+// carried up unchanged: this builds BLAKE3's left-balanced tree as long as the group starts at a
+// multiple of a power of two >= its size. ROOT goes on the last merge when `is_root`.
+__device__ void merge_cvs(uint32_t* cv, int count, const uint32_t* key, bool is_root) {
+  const int tid = threadIdx.x;
+  while (count > 1) {
+    const int pairs = count >> 1, odd = count & 1;
+    uint32_t res[8];
+    if (tid < pairs) {
+      uint32_t msg[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) msg[i] = cv[2 * tid * 8 + i];
+      const uint32_t fl = b3::PARENT | b3::KEYED | ((is_root && count == 2) ? b3::ROOT : 0u);
+      b3::compress(key, msg, 0, 64, fl, res);
+    }
+    __syncthreads();
+    if (tid < pairs) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) cv[tid * 8 + i] = res[i];
+    }
+    if (odd && tid == 0) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) cv[pairs * 8 + i] = cv[(count - 1) * 8 + i];
+    }
+    __syncthreads();
+    count = pairs + odd;
+  }
+}
+}  // namespace
+
+// Chaining values of 128 consecutive chunks, merged to one subtree CV per CTA.
+__global__ void __launch_bounds__(kChunksPerCta) k_b3_chunks(const uint8_t* __restrict__ data, uint64_t nchunks,
+                                                              const uint32_t* __restrict__ key,
+                                                              uint32_t* __restrict__ cvs_out) {
+  __shared__ __align__(16) uint4 stage[2][kChunksPerCta * kPitch];
+  __shared__ uint32_t cvs[kChunksPerCta * 8];
+  const int tid = threadIdx.x;
+  uint32_t k8[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) k8[i] = key[i];
+  const uint64_t base = (uint64_t)blockIdx.x * kChunksPerCta;
+  const int count = (int)min((uint64_t)kChunksPerCta, nchunks - base);
+  const uint4* g = reinterpret_cast<const uint4*>(data) + base * 64;  // 64 uint4 per chunk
+  auto fetch = [&](int buf, int blk) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int i = tid + kChunksPerCta * j, c = i >> 2, part = i & 3;
+      if (c < count) stage[buf][c * kPitch + part] = __ldg(g + (uint64_t)c * 64 + blk * 4 + part);
+    }
+  };
+  fetch(0, 0);
+  __syncthreads();
+  uint32_t cv[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) cv[i] = k8[i];
+  for (int blk = 0; blk < 16; blk++) {
+    if (blk + 1 < 16) fetch((blk + 1) & 1, blk + 1);
+    if (tid < count) {
+      uint32_t msg[16];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint4 w = stage[blk & 1][tid * kPitch + q];
+        msg[4 * q] = w.x; msg[4 * q + 1] = w.y; msg[4 * q + 2] = w.z; msg[4 * q + 3] = w.w;
+      }
+      const uint32_t fl = b3::KEYED | (blk == 0 ? b3::CHUNK_START : 0u) | (blk == 15 ? b3::CHUNK_END : 0u) |
+                          ((blk == 15 && nchunks == 1) ? b3::ROOT : 0u);
+      b3::compress(cv, msg, base + tid, 64, fl, cv);
+    }
+    __syncthreads();
+  }
+  if (tid < count) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) cvs[tid * 8 + i] = cv[i];
+  }
+  __syncthreads();
+  merge_cvs(cvs, count, k8, gridDim.x == 1 && nchunks > 1);
+  if (tid < 8) cvs_out[(uint64_t)blockIdx.x * 8 + tid] = cvs[tid];
+}
+
+// Merge aligned groups of up to 1024 CVs. With `final` (one CTA) the result is the root; the
+// salted seed seed = BLAKE3(prefix || BLAKE3_keyed(salt, root || dim || 0^28)) follows.
+__global__ void __launch_bounds__(512) k_b3_reduce(const uint32_t* __restrict__ in, uint32_t count,
+                                                   const uint32_t* __restrict__ key, uint32_t* __restrict__ out,
+                                                   int final_level, const uint32_t* __restrict__ prefix,
+                                                   const uint32_t* __restrict__ salt, uint32_t dim,
+                                                   uint32_t* __restrict__ root_out, uint32_t* __restrict__ seed_out) {
+  __shared__ uint32_t cvs[kReduceGroup * 8];
+  const uint32_t base = blockIdx.x * kReduceGroup;
+  const int cnt = (int)min((uint32_t)kReduceGroup, count - base);
+  for (int i = threadIdx.x; i < cnt * 8; i += blockDim.x) cvs[i] = in[(uint64_t)base * 8 + i];
+  uint32_t k8[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) k8[i] = key[i];
+  __syncthreads();
+  merge_cvs(cvs, cnt, k8, final_level != 0);
+  if (!final_level) {
+    if (threadIdx.x < 8) out[(uint64_t)blockIdx.x * 8 + threadIdx.x] = cvs[threadIdx.x];
+    return;
+  }
+  if (threadIdx.x == 0) {
+    uint32_t root[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) root[i] = cvs[i];
+    if (root_out) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) root_out[i] = root[i];
+    }
+    if (seed_out) {
+      uint32_t msg[16], bound[8], s8[8], seed[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) { msg[i] = root[i]; msg[8 + i] = 0u; s8[i] = salt[i]; }
+      msg[8] = dim;
+      b3::hash64(s8, msg, bound);
+#pragma unroll
+      for (int i = 0; i < 8; i++) { msg[i] = prefix[i]; msg[8 + i] = bound[i]; }
+      b3::hash64(nullptr, msg, seed);
+#pragma unroll
+      for (int i = 0; i < 8; i++) seed_out[i] = seed[i];
+    }
+  }
+}
+
+// ------------------------------------------------------------------ noise
+__device__ __forceinline__ void random_hash(uint32_t index, const uint32_t* label, const uint32_t* key, int prepend,
+                                            uint32_t* out) {
+  uint32_t msg[16], k8[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) { msg[i] = 0u; msg[8 + i] = label[i]; k8[i] = key[i]; }
+  msg[prepend] = 1u + index;
+  b3::hash64(k8, msg, out);
+}
+
+__global__ void __launch_bounds__(256) k_noise_uniform(int8_t* __restrict__ out, uint32_t nblocks,
+                                                       const uint32_t* __restrict__ label,
+                                                       const uint32_t* __restrict__ key, int32_t* __restrict__ zero_me,
+                                                       int zero_n) {
+  const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (zero_me && b < (uint32_t)zero_n) zero_me[b] = 0;
+  if (b >= nblocks) return;
+  uint32_t h[8], o[8];
+  random_hash(b, label, key, 0, h);
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    // per byte (x & 63) - 32 as int8: subtracting 32 is adding 0xE0 modulo 256 in each byte lane.
+    const uint32_t w = h[i] & 0x3F3F3F3Fu;
+    o[i] = __vadd4(w, 0xE0E0E0E0u);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + (uint64_t)b * 32);
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__global__ void __launch_bounds__(128) k_noise_perm(uint32_t* __restrict__ out, uint32_t k, uint32_t r,
+                                                    const uint32_t* __restrict__ label,
+                                                    const uint32_t* __restrict__ key) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i * 8 >= k) return;
+  uint32_t h[8];
+  random_hash(i, label, key, 1, h);
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const uint32_t l = i * 8 + j;
+    if (l < k) {
+      const uint32_t first = h[j] & (r - 1);
+      const uint32_t second = first ^ (1u + __umulhi(r - 1, h[j]));
+      out[l] = first | (second << 16);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ noise_rows
+namespace {
+constexpr int kNrRows = 8;  // rows per CTA
+}
+
+__global__ void __launch_bounds__(256) k_noise_rows(const int8_t* __restrict__ src, int rows, int k, int r,
+                                                    const int8_t* __restrict__ E, const uint32_t* __restrict__ Pn,
+                                                    int8_t* __restrict__ dst, const uint32_t* __restrict__ Pp,
+                                                    int8_t* __restrict__ corr, int corr_off, int ecopy_off,
+                                                    int32_t* __restrict__ maxabs, int lmax) {
+  extern __shared__ __align__(16) uint8_t nr_smem[];
+  int8_t* Es = reinterpret_cast<int8_t*>(nr_smem);                        // kNrRows * r
+  int32_t* proj = reinterpret_cast<int32_t*>(nr_smem + kNrRows * 256);    // kNrRows * r
+  const int tid = threadIdx.x;
+  const int row0 = blockIdx.x * kNrRows;
+  if (E)
+    for (int i = tid; i < kNrRows * r; i += 256) Es[i] = E[(uint64_t)row0 * r + i];
+  if (Pp)
+    for (int i = tid; i < kNrRows * r; i += 256) proj[i] = 0;
+  __syncthreads();
+  const int vpr = k >> 4;  // 16-byte vectors per row
+  for (int it = tid; it < kNrRows * vpr; it += 256) {
+    const int rr = it / vpr, q = it - rr * vpr;
+    const uint64_t off = (uint64_t)(row0 + rr) * k + 16 * q;
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(src + off));
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    if (dst) {
+      const uint4* pn4 = reinterpret_cast<const uint4*>(Pn + 16 * q);
+      uint32_t o[4];
+#pragma unroll
+      for (int v = 0; v < 4; v++) {
+        const uint4 p = __ldg(pn4 + v);
+        const uint32_t pv[4] = {p.x, p.y, p.z, p.w};
+        uint32_t ov = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int x = (int)(int8_t)(ws[v] >> (8 * j));
+          const int nv = x + (int)Es[rr * r + (pv[j] & 0xFFFFu)] - (int)Es[rr * r + (pv[j] >> 16)];
+          ov |= (uint32_t)(uint8_t)(int8_t)nv << (8 * j);
+        }
+        o[v] = ov;
+      }
+      *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if (Pp) {
+      const uint4* pp4 = reinterpret_cast<const uint4*>(Pp + 16 * q);
+#pragma unroll
+      for (int v = 0; v < 4; v++) {
+        const uint4 p = __ldg(pp4 + v);
+        const uint32_t pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int x = (int)(int8_t)(ws[v] >> (8 * j));
+          if (x != 0) {
+            atomicAdd(&proj[rr * r + (pv[j] & 0xFFFFu)], x);
+            atomicSub(&proj[rr * r + (pv[j] >> 16)], x);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint64_t limb_stride = (uint64_t)rows * 2 * r;
+  int local_max = 0;
+  for (int i = tid; i < kNrRows * r; i += 256) {
+    const int rr = i / r, j = i - rr * r;
+    const uint64_t rowbase = (uint64_t)(row0 + rr) * 2 * r;
+    if (Pp && corr_off >= 0) {
+      int v = proj[i];
+      local_max = max(local_max, abs(v));
+      if (corr) {
+        for (int li = 0; li < lmax; li++) {
+          const int d = ((v + 64) & 127) - 64;
+          corr[li * limb_stride + rowbase + corr_off + j] = (int8_t)d;
+          v = (v - d) >> 7;
+        }
+      }
+    }
+    if (E && corr && ecopy_off >= 0) {
+      const int8_t e = Es[i];
+      for (int li = 0; li < lmax; li++) corr[li * limb_stride + rowbase + ecopy_off + j] = e;
+    }
+  }
+  if (Pp && maxabs) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) local_max = max(local_max, __shfl_xor_sync(0xffffffffu, local_max, s));
+    if ((tid & 31) == 0) atomicMax(maxabs, local_max);
+  }
+}
+
+__global__ void __launch_bounds__(256) k_proj_matrix(const uint32_t* __restrict__ P, int k, int r,
+                                                     int8_t* __restrict__ St) {
+  const uint64_t total = (uint64_t)r * k;
+  for (uint64_t i = (uint64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (uint64_t)gridDim.x * 256) {
+    const uint32_t j = (uint32_t)(i / k), l = (uint32_t)(i - (uint64_t)j * k);
+    const uint32_t p = P[l];
+    St[i] = (int8_t)((int)((p & 0xFFFFu) == j) - (int)((p >> 16) == j));
+  }
+}
+
+__global__ void __launch_bounds__(256) k_proj_corr(const int32_t* __restrict__ proj, int rows, int r,
+                                                   int8_t* __restrict__ corr, int corr_off,
+                                                   int32_t* __restrict__ maxabs, int lmax) {
+  const uint64_t limb_stride = (uint64_t)rows * 2 * r, total = (uint64_t)rows * r;
+  int local_max = 0;
+  for (uint64_t i = (uint64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (uint64_t)gridDim.x * 256) {
+    const uint64_t rr = i / r;
+    const int j = (int)(i - rr * r);
+    int v = proj[i];
+    local_max = max(local_max, abs(v));
+    if (corr) {
+      for (int li = 0; li < lmax; li++) {
+        const int d = ((v + 64) & 127) - 64;
+        corr[li * limb_stride + rr * 2 * r + corr_off + j] = (int8_t)d;
+        v = (v - d) >> 7;
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) local_max = max(local_max, __shfl_xor_sync(0xffffffffu, local_max, s));
+  if ((threadIdx.x & 31) == 0 && maxabs) atomicMax(maxabs, local_max);
+}
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+uint64_t uwc_b3_scratch_words(uint64_t nbytes) {
+  uint64_t nch = nbytes / 1024, words = 0;
+  uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;
+  words += 8 * cnt;
+  while (cnt > (uint64_t)kReduceGroup) {
+    cnt = (cnt + kReduceGroup - 1) / kReduceGroup;
+    words += 8 * cnt;
+  }
+  return words < 8 ? 8 : words;
+}
+
+int uwc_b3_root_and_seed(const void* data, uint64_t nbytes, const uint32_t* key, const uint32_t* prefix,
+                         const uint32_t* salt, uint32_t dim, uint32_t* root_out, uint32_t* seed_out,
+                         uint32_t* scratch, uint64_t scratch_words, void* stream) {
+  if (!data || !key || !scratch || (seed_out && (!prefix || !salt))) return UWC_ERR_ARG;
+  if (nbytes == 0 || nbytes % 1024) return UWC_ERR_SHAPE;
+  if (((uintptr_t)data) & 15) return UWC_ERR_ALIGN;
+  if (scratch_words < uwc_b3_scratch_words(nbytes)) return UWC_ERR_SCRATCH;
+  UWC_CHECK_DEVICE();
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint64_t nch = nbytes / 1024;
+  uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;
+  k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch);
+  uint32_t* cur = scratch;
+  uint32_t* nxt = scratch + 8 * cnt;
+  while (cnt > (uint64_t)kReduceGroup) {
+    const uint64_t groups = (cnt + kReduceGroup - 1) / kReduceGroup;
+    k_b3_reduce<<<(unsigned)groups, 512, 0, st>>>(cur, (uint32_t)cnt, key, nxt, 0, nullptr, nullptr, 0, nullptr,
+                                                  nullptr);
+    cur = nxt;
+    nxt += 8 * groups;
+    cnt = groups;
+  }
+  k_b3_reduce<<<1, 512, 0, st>>>(cur, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out);
+  return uwc_launch_status();
+}
+
+int uwc_noise_uniform(int8_t* out, uint64_t nbytes, const uint32_t* label, const uint32_t* key, int32_t* zero_me,
+                      int zero_n, void* stream) {
+  if (!out || !label || !key || zero_n < 0 || (zero_n > 0 && !zero_me)) return UWC_ERR_ARG;
+  if (nbytes % 32) return UWC_ERR_SHAPE;
+  if (((uintptr_t)out) & 15) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  const uint64_t nblocks = nbytes / 32;
+  if (nblocks > 0xFFFFFFFFull) return UWC_ERR_SHAPE;
+  const uint64_t threads = std::max<uint64_t>(nblocks, (uint64_t)zero_n);
+  if (threads == 0) return UWC_OK;
+  k_noise_uniform<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(out, (uint32_t)nblocks, label,
+                                                                                     key, zero_me, zero_n);
+  return uwc_launch_status();
+}
+
+int uwc_noise_perm(uint32_t* out, uint32_t k, uint32_t r, const uint32_t* label, const uint32_t* key, void* stream) {
+  if (!out || !label || !key) return UWC_ERR_ARG;
+  if (r < 2 || (r & (r - 1)) || r > 65536) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  if (k == 0) return UWC_OK;
+  const uint32_t nh = (k + 7) / 8;
+  k_noise_perm<<<(nh + 127) / 128, 128, 0, (cudaStream_t)stream>>>(out, k, r, label, key);
+  return uwc_launch_status();
+}
+
+int uwc_noise_rows(const int8_t* src, int rows, int k, int r, const int8_t* E, const uint32_t* Pn, int8_t* dst,
+                   const uint32_t* Pp, int8_t* corr, int corr_off, int ecopy_off, int32_t* maxabs, int lmax,
+                   void* stream) {
+  if (!src || (dst && (!E || !Pn)) || (ecopy_off >= 0 && corr && !E) || lmax < 0) return UWC_ERR_ARG;
+  if (rows <= 0 || rows % kNrRows || k <= 0 || k % 16 || (r != 64 && r != 128 && r != 256)) return UWC_ERR_SHAPE;
+  if ((((uintptr_t)src) | ((uintptr_t)dst) | ((uintptr_t)Pn) | ((uintptr_t)Pp)) & 15) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  const int smem = kNrRows * 256 + kNrRows * r * 4;
+  k_noise_rows<<<rows / kNrRows, 256, smem, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, Pp, corr, corr_off,
+                                                                    ecopy_off, maxabs, lmax);
+  return uwc_launch_status();
+}
+
+int uwc_proj_matrix(const uint32_t* P, int k, int r, int8_t* St, void* stream) {
+  if (!P || !St) return UWC_ERR_ARG;
+  if (k <= 0 || r <= 0) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  const uint64_t n = (uint64_t)r * k;
+  const unsigned grid = (unsigned)std::min<uint64_t>(4096, (n + 255) / 256);
+  k_proj_matrix<<<grid, 256, 0, (cudaStream_t)stream>>>(P, k, r, St);
+  return uwc_launch_status();
+}
+
+int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_off, int32_t* maxabs, int lmax,
+                  void* stream) {
+  if (!proj || lmax < 0 || (corr && corr_off < 0)) return UWC_ERR_ARG;
+  if (rows <= 0 || r <= 0) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  const uint64_t n = (uint64_t)rows * r;
+  const unsigned grid = (unsigned)std::min<uint64_t>(4096, (n + 255) / 256);
+  k_proj_corr<<<grid, 256, 0, (cudaStream_t)stream>>>(proj, rows, r, corr, corr_off, maxabs, lmax);
+  return uwc_launch_status();
+}
+
+}  // extern "C"
