@@ -2,12 +2,14 @@
 // tcgen05.mma kind::i8, TMEM accumulators and TMA-fed 128-byte-swizzled shared-memory stages.
 //
 // Reference semantics: noisy_gemm (miner/ampere/uwc_ampere/kernels.cu:482-715), launched by
-// ops.gemm (ops.py:185-198). Three schedules share one persistent, warp-specialized kernel:
+// ops.gemm (ops.py:185-198). Three schedules share one persistent, warp-specialized kernel,
+// specialized at compile time on the schedule and on the hash chunk width r:
 //
 //   MODE_MINE  FLAG_HASH, no output (MinedWeight.noise_mine, ops.py:349-364). A work unit is a
-//              256 x 256 output block held as two 128 x 256 TMEM accumulators X (rows 0-127)
-//              and Y (rows 128-255) sharing the B tile. The MMA warp alternates r-column chunks
-//              of X and Y, so the epilogue folds X's running sum while the tensor core works on Y.
+//              256 x 256 output block held as four 128 x 128 TMEM accumulators: X0 X1 (rows
+//              0-127, column halves) and Y0 Y1 (rows 128-255). Per r-column chunk of k the MMA
+//              warp issues X0, X1, Y0, Y1 in turn, so each accumulator's running sum is read by
+//              the epilogue while the tensor core works on the other three.
 //   MODE_FWD   FLAG_DENOISE and/or FLAG_HASH with an output (MinedWeight.forward, ops.py:316-347).
 //              A unit is a 128 x 256 block held as two 128 x 128 accumulators (column halves)
 //              plus a 128 x 256 correction accumulator R = sum_li 128^li corrA[li] corrB[li]^T,
@@ -16,10 +18,14 @@
 //   MODE_PLAIN no flags: a 128 x 256 block per unit, two accumulators used alternately across
 //              units so the store of one unit overlaps the main loop of the next.
 //
+// The MMA issue loop is fully unrolled per 128-byte k-block stage: the tensor core only runs at
+// its rate when tcgen05.mma instructions are issued back to back.
+//
 // Hash tiles (pearl_glue.py:14-15): rows g + 8i (i < 8), cols 2t + {0,1} + 8j (j < 8) of a
-// 64 x 64 block. tcgen05.ld.16x256b hands thread (g = lane/4, t = lane%4) exactly rows {g, g+8}
-// and cols 8j + 2t + {0,1} of a 16-lane x 64-column slab, so a warp's two loads (lanes +0, +16 of
-// its TMEM quadrant) give every thread 64 values of ONE hash tile: the XOR-fold is register-local.
+// 64 x 64 block. An epilogue warp reads its TMEM quadrant (32 rows) x 64 columns with
+// tcgen05.ld.32x32b (thread = row, registers = consecutive columns), XORs each row's values
+// into four partials by t = (col / 2) % 4, then a 3-shuffle reduce-scatter over the lanes of
+// rows g, g+8, g+16, g+24 leaves lane (g + 8t) with tile (g, t)'s XOR over the quadrant.
 // Rows 32-63 of a 64-row block live in the next quadrant (the next warp); XOR and rotl are linear
 // over GF(2), so each warp keeps a partial message and the two partials are XORed once per unit.
 //
@@ -44,13 +50,9 @@ constexpr int kMmaWarp = kProducerWarp + 1;             // 19
 constexpr int kThreads = (kMmaWarp + 1) * 32;           // 640
 constexpr int kKB = 128;                                // K bytes per stage (one 128-byte swizzle row)
 constexpr int kUN = 256;                                // output columns per unit
-constexpr int kStageBytesMine = 2 * 128 * kKB + kUN * kKB;  // A 256 rows + B 256 rows = 64 KiB
-constexpr int kStageBytesFwd = 128 * kKB + kUN * kKB;       // A 128 rows + B 256 rows = 48 KiB
-constexpr int kStagesMine = 3;
-constexpr int kStagesFwd = 4;
 constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
 constexpr int kHashBufBytes = kMaxTiles * 16 * 4;       // 32 KiB of tile messages
-constexpr int kBarBytes = 256;
+constexpr int kBarBytes = 512;
 
 struct Params {
   int m, n, k, r;
@@ -70,22 +72,29 @@ struct Params {
   uint32_t* status;
 };
 
-template <int MODE>
+// R: hash chunk width in k (64, 128, 256), or 0 for no hashing.
+template <int MODE, int R>
 struct Cfg {
-  static constexpr int UM = MODE == MODE_MINE ? 256 : 128;  // output rows per unit
+  static constexpr bool HASH = R != 0;
+  static constexpr int UM = MODE == MODE_MINE ? 256 : 128;      // output rows per unit
+  static constexpr int NACC = MODE == MODE_MINE ? 4 : (MODE == MODE_FWD ? 2 : 1);
+  static constexpr int ACC_N = MODE == MODE_PLAIN ? 256 : 128;  // MMA N per accumulator
   static constexpr int A_BYTES = UM * kKB;
-  static constexpr int STAGE = MODE == MODE_MINE ? kStageBytesMine : kStageBytesFwd;
-  static constexpr int NST = MODE == MODE_MINE ? kStagesMine : kStagesFwd;
-  static constexpr int HASHBUF = MODE == MODE_PLAIN ? 0 : kHashBufBytes;
+  static constexpr int STAGE = A_BYTES + kUN * kKB;              // 64 KiB (MINE) / 48 KiB
+  static constexpr int NST = MODE == MODE_MINE ? 3 : 4;
+  static constexpr int HASHBUF = HASH ? kHashBufBytes : 0;
   static constexpr int SMEM = NST * STAGE + HASHBUF + kBarBytes + 1024;  // +1024: manual alignment
   static constexpr int TILES = MODE == MODE_MINE ? 512 : 256;
+  static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
+  static constexpr int SPAN = R == 256 ? 2 : 1;                  // stages per chunk
+  static constexpr int ACC_WARPS = MODE == MODE_PLAIN ? kEpiWarps : kEpiWarps / 2;  // readers per acc
 };
 
 struct Bars {
   uint64_t full[4];
   uint64_t empty[4];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
+  uint64_t acc_full[4];
+  uint64_t acc_empty[4];
   uint64_t r_full, r_scaled, r_empty;
   uint64_t hash_ready, hash_free;
   uint64_t pair[8];        // odd quadrant warp -> even quadrant warp: partial messages written
@@ -142,7 +151,8 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int c0, co
     uint32_t* o = reinterpret_cast<uint32_t*>(p.out) + (uint64_t)row * p.n + c0;
     if (full) {
 #pragma unroll
-      for (int i = 0; i < 8; i++) reinterpret_cast<uint4*>(o)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      for (int i = 0; i < 8; i++)
+        reinterpret_cast<uint4*>(o)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     } else {
 #pragma unroll
       for (int i = 0; i < 32; i++)
@@ -162,7 +172,8 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int c0, co
     uint16_t* o = reinterpret_cast<uint16_t*>(p.out) + (uint64_t)row * p.n + c0;
     if (full) {
 #pragma unroll
-      for (int i = 0; i < 4; i++) reinterpret_cast<uint4*>(o)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      for (int i = 0; i < 4; i++)
+        reinterpret_cast<uint4*>(o)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     } else {
 #pragma unroll
       for (int i = 0; i < 32; i++)
@@ -171,23 +182,33 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int c0, co
   }
 }
 
-// XOR of this thread's 64 values of one hash tile in a 32-lane x 64-column TMEM slab; the second
-// load is issued after the first is folded to keep register pressure at 32.
-__device__ __forceinline__ uint32_t fold_tile(uint32_t taddr) {
-  uint32_t v[32];
-  tmem_ld_16x256b_x8(taddr, v);
-  tmem_wait_ld();
-  uint32_t x = xor32(v);
-  tmem_ld_16x256b_x8(taddr + (16u << 16), v);
-  tmem_wait_ld();
-  return x ^ xor32(v);
+// ------------------------------------------------------------------ hash-tile fold
+// XOR the 32 values of one row (consecutive columns) into four partials by t = (col / 2) % 4.
+__device__ __forceinline__ void fold_row32(const uint32_t* v, uint32_t* pt) {
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const int b = 2 * t;
+    pt[t] ^= (v[b] ^ v[b + 1] ^ v[b + 8]) ^ (v[b + 9] ^ v[b + 16] ^ v[b + 17]) ^ (v[b + 24] ^ v[b + 25]);
+  }
 }
 
-template <int MODE>
+// Reduce-scatter over the lanes of rows g, g+8, g+16, g+24 (lane bits 3 and 4): lane (g + 8t)
+// ends with the XOR of partial t over those four rows.
+__device__ __forceinline__ uint32_t reduce_scatter4(const uint32_t* pt, int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8;
+  const uint32_t send_a = b4 ? pt[0] : pt[2], send_b = b4 ? pt[1] : pt[3];
+  const uint32_t keep_a = b4 ? pt[2] : pt[0], keep_b = b4 ? pt[3] : pt[1];
+  const uint32_t k0 = keep_a ^ __shfl_xor_sync(0xffffffffu, send_a, 16);
+  const uint32_t k1 = keep_b ^ __shfl_xor_sync(0xffffffffu, send_b, 16);
+  const uint32_t send = b3 ? k0 : k1, keep = b3 ? k1 : k0;
+  return keep ^ __shfl_xor_sync(0xffffffffu, send, 8);
+}
+
+template <int MODE, int R>
 __global__ void __launch_bounds__(kThreads, 1)
     k_noisy_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmCA, const __grid_constant__ CUtensorMap tmCB, const Params p) {
-  using C = Cfg<MODE>;
+  using C = Cfg<MODE, R>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint32_t* hbuf = reinterpret_cast<uint32_t*>(smem + C::NST * C::STAGE);
@@ -201,10 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
-    const int acc_consumers = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;
-    for (int a = 0; a < 2; a++) {
+    for (int a = 0; a < 4; a++) {
       mbar_init(&bars->acc_full[a], 1);
-      mbar_init(&bars->acc_empty[a], acc_consumers);
+      mbar_init(&bars->acc_empty[a], C::ACC_WARPS);
     }
     mbar_init(&bars->r_full, 1);
     mbar_init(&bars->r_scaled, kEpiWarps);
@@ -237,8 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int L = bars->L;
   const int k = p.k;
   const int kblocks = (k + kKB - 1) / kKB;
-  const int chunk = p.hash ? p.r : kKB;                // columns of k between snapshots
-  const int nch = (k + chunk - 1) / chunk;
+  const int nch = C::HASH ? k / R : 1;                         // snapshots per accumulator per unit
   const int cblocks = MODE == MODE_FWD ? (2 * p.r) / kKB : 1;  // k-blocks per correction limb
 
   if (warp == kProducerWarp) {
@@ -272,12 +291,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t gk = 0;                 // k-blocks consumed (ring position)
-      uint32_t snaps[2] = {0, 0};      // snapshots produced per accumulator
-      uint32_t r_commits = 0, r_scaled_waits = 0;
+      uint32_t gk = 0;                      // k-blocks consumed (ring position)
+      uint32_t snaps[4] = {0, 0, 0, 0};     // snapshots produced per accumulator
+      uint32_t r_scaled_waits = 0;
       int local = 0;
       bool ok = true;
       const uint32_t smem_base = smem_u32(smem);
+      constexpr uint32_t id_acc = idesc_i8(128, C::ACC_N);
       for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
         int m0, n0;
         unit_coords(p, u, C::UM, m0, n0);
@@ -297,75 +317,78 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!ok) break;
               tc_fence_after();
               const uint32_t aA = smem_base + s * C::STAGE, aB = aA + C::A_BYTES;
+              const uint64_t ad = sdesc_sw128(aA), bd = sdesc_sw128(aB);
 #pragma unroll
               for (int ks = 0; ks < 4; ks++)
-                mma_i8(tR, sdesc_sw128(aA + 32 * ks), sdesc_sw128(aB + 32 * ks), idesc_i8(128, 256),
-                       (li == L - 1 && kb == 0 && ks == 0) ? 0u : 1u);
+                mma_i8(tR, ad + 2 * ks, bd + 2 * ks, idesc_i8(128, 256), (li == L - 1 && kb == 0 && ks == 0) ? 0u : 1u);
               mma_commit(&bars->empty[s]);
             }
             mma_commit(&bars->r_full);
-            r_commits++;
           }
         }
-        // ---- main loop over r-chunks of k
-        const int nacc = MODE == MODE_MINE ? (m0 + 128 < p.m ? 2 : 1) : (MODE == MODE_FWD ? 2 : 1);
-        const uint32_t acc_col[2] = {
-            MODE == MODE_PLAIN ? (uint32_t)((local & 1) * 256) : 0u,
-            MODE == MODE_MINE ? 256u : 128u};
-        const int plain_buf = local & 1;
-        uint32_t kb_released = 0;
+        // ---- main loop, one 128-column k-block stage at a time, MMAs issued back to back
+        const int nacc = (MODE == MODE_MINE && m0 + 128 >= p.m) ? 2 : C::NACC;
+        const int pbuf = local & 1;   // PLAIN: accumulator buffer of this unit
         const uint32_t gk0 = gk;
-        for (int c = 0; c < nch && ok; c++) {
-          const int kbeg = c * chunk, kend = min(k, kbeg + chunk);
-          for (int a = 0; a < nacc && ok; a++) {
-            const int bar_a = MODE == MODE_PLAIN ? plain_buf : a;
-            if (p.hash || c == 0) {
-              const uint32_t uses = MODE == MODE_PLAIN ? (uint32_t)(local >> 1) : snaps[a];
-              ok = mbar_wait(&bars->acc_empty[bar_a], (uses & 1) ^ 1, abort_flag, p.status);
+        for (int kb = 0; kb < kblocks && ok; kb++) {
+          const uint32_t g = gk0 + kb;
+          const int s = g % C::NST;
+          ok = mbar_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t aA = smem_base + s * C::STAGE;
+          const uint64_t adesc = sdesc_sw128(aA), bdesc = sdesc_sw128(aA + C::A_BYTES);
+          if (C::HASH) {
+#pragma unroll
+            for (int part = 0; part < C::PARTS; part++) {
+              if (part == 1 && kb * kKB + 64 >= k) break;   // k % 128 == 64 with r = 64
+              const bool cstart = C::SPAN == 1 || (kb & 1) == 0;
+              const bool cend = C::SPAN == 1 || (kb & 1) == 1;
+#pragma unroll
+              for (int a = 0; a < C::NACC; a++) {
+                if (a >= nacc) break;
+                if (cstart) {
+                  ok = mbar_wait(&bars->acc_empty[a], (snaps[a] & 1) ^ 1, abort_flag, p.status);
+                  if (!ok) break;
+                  tc_fence_after();
+                }
+                // MINE: a = 2*row_half + col_half; FWD: a = col_half (descriptor offsets in 16-byte units)
+                const uint64_t ad = adesc + (MODE == MODE_MINE ? (a >> 1) * (128 * kKB / 16) : 0);
+                const uint64_t bd = bdesc + (MODE == MODE_MINE ? (a & 1) : a) * (128 * kKB / 16);
+                const uint32_t dcol = tmem + a * 128;
+#pragma unroll
+                for (int ks = part * (4 / C::PARTS); ks < (part + 1) * (4 / C::PARTS); ks++)
+                  mma_i8(dcol, ad + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
+                if (cend) {
+                  mma_commit(&bars->acc_full[a]);
+                  snaps[a]++;
+                }
+              }
               if (!ok) break;
-              tc_fence_after();
             }
-            const uint32_t dcol = tmem + acc_col[a];
-            for (int kofs = kbeg; kofs < kend; kofs += 32) {
-              const uint32_t kb = kofs / kKB, g = gk0 + kb;
-              const int s = g % C::NST;
-              if (a == 0 && (kofs % kKB) == 0) {
-                ok = mbar_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
+          } else {
+#pragma unroll
+            for (int a = 0; a < C::NACC; a++) {
+              const int ba = MODE == MODE_PLAIN ? pbuf : a;
+              if (kb == 0) {
+                const uint32_t uses = MODE == MODE_PLAIN ? (uint32_t)(local >> 1) : snaps[a];
+                ok = mbar_wait(&bars->acc_empty[ba], (uses & 1) ^ 1, abort_flag, p.status);
                 if (!ok) break;
                 tc_fence_after();
               }
-              const uint32_t ko = kofs % kKB;
-              const uint32_t aA = smem_base + s * C::STAGE;
-              const uint32_t aB = aA + C::A_BYTES;
-              uint64_t ad, bd;
-              uint32_t id;
-              if (MODE == MODE_MINE) {
-                ad = sdesc_sw128(aA + a * (128 * kKB) + ko);
-                bd = sdesc_sw128(aB + ko);
-                id = idesc_i8(128, 256);
-              } else if (MODE == MODE_FWD) {
-                ad = sdesc_sw128(aA + ko);
-                bd = sdesc_sw128(aB + a * (128 * kKB) + ko);
-                id = idesc_i8(128, 128);
-              } else {
-                ad = sdesc_sw128(aA + ko);
-                bd = sdesc_sw128(aB + ko);
-                id = idesc_i8(128, 256);
+              const uint64_t bd = bdesc + (MODE == MODE_FWD ? a * (128 * kKB / 16) : 0);
+              const uint32_t dcol = tmem + (MODE == MODE_PLAIN ? pbuf * 256 : a * 128);
+#pragma unroll
+              for (int ks = 0; ks < 4; ks++)
+                mma_i8(dcol, adesc + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
+              if (kb == kblocks - 1) {
+                mma_commit(&bars->acc_full[ba]);
+                if (MODE != MODE_PLAIN) snaps[a]++;
               }
-              mma_i8(dcol, ad, bd, id, kofs == 0 ? 0u : 1u);
-            }
-            if (!ok) break;
-            if (p.hash || c == nch - 1) {
-              mma_commit(&bars->acc_full[bar_a]);
-              if (MODE != MODE_PLAIN) snaps[a]++;
             }
           }
-          // release every stage whose k-range has been fully consumed by all accumulators
-          while (ok && kb_released < (uint32_t)kblocks &&
-                 ((kb_released + 1) * kKB <= (uint32_t)kend || kend == k)) {
-            mma_commit(&bars->empty[(gk0 + kb_released) % C::NST]);
-            kb_released++;
-          }
+          if (!ok) break;
+          mma_commit(&bars->empty[s]);
         }
         gk = gk0 + kblocks;
       }
@@ -377,9 +400,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue warps
     const int q = warp & 3, cb = warp >> 2;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    const int g = lane >> 2, t = lane & 3;
-    (void)g; (void)t;
-    uint32_t snaps[2] = {0, 0};
+    // hash slot of this thread's tile after the reduce-scatter: g = lane % 8, t = lane / 8
+    const int tslot = (lane & 7) * 4 + (lane >> 3);
+    uint32_t snaps[4] = {0, 0, 0, 0};
     uint32_t r_waits = 0;
     int local = 0;
     bool ok = true;
@@ -405,66 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
-      if (MODE == MODE_MINE) {
-        const bool hasY = m0 + 128 < p.m;
-        const uint32_t colX = tmem + cb * 64 + lane_base, colY = tmem + 256 + cb * 64 + lane_base;
-        uint32_t mx[16], my[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) { mx[i] = 0u; my[i] = 0u; }
-        for (int c0 = 0; c0 < nch && ok; c0 += 16) {
-#pragma unroll
-          for (int s = 0; s < 16; s++) {
-            if (c0 + s < nch && ok) {
-              ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[0], snaps[0] & 1, abort_flag, p.status));
-              if (ok) {
-                snaps[0]++;
-                tc_fence_after();
-                const uint32_t x = fold_tile(colX);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->acc_empty[0]);
-                mx[s] = rotl13(mx[s]) ^ x;
-              }
-              if (hasY && ok) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[1], snaps[1] & 1, abort_flag, p.status));
-                if (ok) {
-                  snaps[1]++;
-                  tc_fence_after();
-                  const uint32_t y = fold_tile(colY);
-                  tc_fence_before();
-                  __syncwarp();
-                  if (lane == 0) mbar_arrive(&bars->acc_empty[1]);
-                  my[s] = rotl13(my[s]) ^ y;
-                }
-              }
-            }
-          }
-        }
-        if (!ok) break;
-        // combine the two quadrant partials of each tile and hand the messages to the hash warps
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free, (local & 1) ^ 1, abort_flag, p.status));
-        if (!ok) break;
-        const int rb = q >> 1, pair_id = cb * 2 + rb;
-        const int slotX = ((0 * 2 + rb) * 4 + cb) * 32 + lane, slotY = ((1 * 2 + rb) * 4 + cb) * 32 + lane;
-        if (q & 1) {
-#pragma unroll
-          for (int i = 0; i < 16; i++) {
-            hbuf[i * kMaxTiles + slotX] = mx[i];
-            hbuf[i * kMaxTiles + slotY] = my[i];
-          }
-          mbar_arrive(&bars->pair[pair_id]);
-        } else {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->pair[pair_id], local & 1, abort_flag, p.status));
-          if (!ok) break;
-#pragma unroll
-          for (int i = 0; i < 16; i++) {
-            hbuf[i * kMaxTiles + slotX] ^= mx[i];
-            hbuf[i * kMaxTiles + slotY] ^= my[i];
-          }
-          mbar_arrive(&bars->hash_ready);
-        }
-        continue;
-      }
+      // MINE: accumulators X_h (a = h) and Y_h (a = 2 + h) with h = cb / 2; FWD: a = cb / 2
+      const int h = cb >> 1, cofs = (cb & 1) * 64;
+      const bool hasY = MODE == MODE_MINE && m0 + 128 < p.m;
+      const int a0 = h, a1 = 2 + h;
+      const uint32_t col0 = tmem + a0 * 128 + cofs + lane_base, col1 = tmem + a1 * 128 + cofs + lane_base;
 
       if (MODE == MODE_FWD) {
         // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
@@ -473,9 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
-          for (int h = 0; h < 2; h++) {
+          for (int hh = 0; hh < 2; hh++) {
             uint32_t v[32];
-            const uint32_t ta = tmem + 256 + cb * 64 + h * 32 + lane_base;
+            const uint32_t ta = tmem + 256 + cb * 64 + hh * 32 + lane_base;
             tmem_ld_32x32b_x32(ta, v);
             tmem_wait_ld();
 #pragma unroll
@@ -488,80 +456,119 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&bars->r_scaled);
         }
         if (!ok) break;
-        const int a = cb >> 1;
-        const uint32_t col = tmem + a * 128 + (cb & 1) * 64 + lane_base;
-        uint32_t mm[16];
+      }
+
+      constexpr int NY = MODE == MODE_MINE ? 16 : 1;
+      uint32_t m_x[16], m_y[NY];   // this thread's partial tile messages (X_h / FWD acc, Y_h)
 #pragma unroll
-        for (int i = 0; i < 16; i++) mm[i] = 0u;
+      for (int i = 0; i < 16; i++) m_x[i] = 0u;
+#pragma unroll
+      for (int i = 0; i < NY; i++) m_y[i] = 0u;
+
+      // consume one snapshot of accumulator `a` at TMEM column address `col`; returns the fold
+      auto consume = [&](int a, uint32_t col, bool last) -> uint32_t {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status));
+        if (!ok) return 0u;
+        snaps[a]++;
+        tc_fence_after();
+        uint32_t pt[4] = {0u, 0u, 0u, 0u};
+        uint32_t v[32];
+        if (C::HASH) {
+          tmem_ld_32x32b_x32(col, v);
+          tmem_wait_ld();
+          fold_row32(v, pt);
+          tmem_ld_32x32b_x32(col + 32, v);
+          tmem_wait_ld();
+        }
+        if (MODE == MODE_FWD && last) {
+          // output: acc - R for this warp's 32 rows x 64 columns, then release acc and R
+          if (L > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
+            if (!ok) return 0u;
+            tc_fence_after();
+          }
+          if (C::HASH) fold_row32(v, pt);
+          if (p.out_mode != UWC_OUT_NONE) {
+#pragma unroll 1
+            for (int hh = 0; hh < 2; hh++) {
+              uint32_t w[32];
+              tmem_ld_32x32b_x32(col + hh * 32, w);
+              tmem_wait_ld();
+              if (L > 0) {
+#pragma unroll
+                for (int qq = 0; qq < 2; qq++) {
+                  uint32_t rr[16];
+                  tmem_ld_32x32b_x16(tmem + 256 + cb * 64 + hh * 32 + qq * 16 + lane_base, rr);
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int i = 0; i < 16; i++) w[qq * 16 + i] -= rr[i];
+                }
+              }
+              store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + hh * 32, reinterpret_cast<const int32_t*>(w));
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&bars->acc_empty[a]);
+            if (L > 0) mbar_arrive(&bars->r_empty);
+          }
+        } else {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
+          if (C::HASH) fold_row32(v, pt);
+        }
+        return C::HASH ? reduce_scatter4(pt, lane) : 0u;
+      };
+
+      if (C::HASH) {
         for (int c0 = 0; c0 < nch && ok; c0 += 16) {
 #pragma unroll
           for (int s = 0; s < 16; s++) {
             const int c = c0 + s;
-            if (c < nch && ok && (p.hash || c == nch - 1)) {
-              ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status));
-              if (!ok) break;
-              snaps[a]++;
-              tc_fence_after();
-              if (p.hash) mm[s] = rotl13(mm[s]) ^ fold_tile(col);
-              if (c == nch - 1) {
-                // output: acc - R for this warp's 32 lanes x 64 columns
-                if (L > 0) {
-                  ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
-                  if (!ok) break;
-                  tc_fence_after();
-                }
-                if (p.out_mode != UWC_OUT_NONE) {
-#pragma unroll 1
-                  for (int h = 0; h < 2; h++) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(col + h * 32, v);
-                    if (L > 0) {
-                      uint32_t rr[32];
-                      tmem_ld_32x32b_x32(tmem + 256 + cb * 64 + h * 32 + lane_base, rr);
-                      tmem_wait_ld();
-#pragma unroll
-                      for (int i = 0; i < 32; i++) v[i] = v[i] - rr[i];
-                    } else {
-                      tmem_wait_ld();
-                    }
-                    store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + h * 32, reinterpret_cast<const int32_t*>(v));
-                  }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                  mbar_arrive(&bars->acc_empty[a]);
-                  if (L > 0) mbar_arrive(&bars->r_empty);
-                }
-              } else {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
+            if (c < nch && ok) {
+              const uint32_t x = consume(a0, col0, c == nch - 1);
+              m_x[s] = rotl13(m_x[s]) ^ x;
+              if (MODE == MODE_MINE && hasY && ok) {
+                const uint32_t y = consume(a1, col1, c == nch - 1);
+                m_y[s % NY] = rotl13(m_y[s % NY]) ^ y;
               }
             }
           }
         }
+      } else {
+        consume(a0, col0, true);
+      }
+      if (!ok) break;
+      if (C::HASH) {
+        // combine the two quadrant partials of each tile and hand the messages to the hash warps
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free, (local & 1) ^ 1, abort_flag, p.status));
         if (!ok) break;
-        if (p.hash) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free, (local & 1) ^ 1, abort_flag, p.status));
-          if (!ok) break;
-          const int rb = q >> 1, pair_id = cb * 2 + rb;
-          const int slot = (rb * 4 + cb) * 32 + lane;
-          if (q & 1) {
+        const int rb = q >> 1, pair_id = cb * 2 + rb;
+        const int slotX = ((0 * 2 + rb) * 4 + cb) * 32 + tslot, slotY = ((1 * 2 + rb) * 4 + cb) * 32 + tslot;
+        if (q & 1) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slot] = mm[i];
-            mbar_arrive(&bars->pair[pair_id]);
-          } else {
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars->pair[pair_id], local & 1, abort_flag, p.status));
-            if (!ok) break;
+          for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slotX] = m_x[i];
+          if (hasY) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slot] ^= mm[i];
-            mbar_arrive(&bars->hash_ready);
+            for (int i = 0; i < NY; i++) hbuf[i * kMaxTiles + slotY] = m_y[i];
           }
+          mbar_arrive(&bars->pair[pair_id]);
+        } else {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->pair[pair_id], local & 1, abort_flag, p.status));
+          if (!ok) break;
+#pragma unroll
+          for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slotX] ^= m_x[i];
+          if (hasY) {
+#pragma unroll
+            for (int i = 0; i < NY; i++) hbuf[i * kMaxTiles + slotY] ^= m_y[i];
+          }
+          mbar_arrive(&bars->hash_ready);
         }
       }
     }
-  } else if (MODE != MODE_PLAIN && p.hash) {
+  } else if (C::HASH) {
     // ------------------------------------------------------------ hash warps
     const int hw = warp - kEpiWarps;
     uint32_t key[8], tgt[8];
@@ -577,15 +584,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_off = m0 + a * 128 + rb * 64 + (ln >> 2);
         const int col_off = n0 + cbk * 64 + 2 * (ln & 3);
         if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) continue;
-        uint32_t msg[16], h[8];
+        uint32_t msg[16], hv[8];
 #pragma unroll
         for (int i = 0; i < 16; i++) msg[i] = hbuf[i * kMaxTiles + slot];
-        b3::hash64(key, msg, h);
+        b3::hash64(key, msg, hv);
         bool le = true, decided = false;
 #pragma unroll
         for (int i = 7; i >= 0; i--) {
-          if (!decided && h[i] != tgt[i]) {
-            le = h[i] < tgt[i];
+          if (!decided && hv[i] != tgt[i]) {
+            le = hv[i] < tgt[i];
             decided = true;
           }
         }
@@ -596,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             rec[0] = (uint32_t)row_off;
             rec[1] = (uint32_t)col_off;
 #pragma unroll
-            for (int i = 0; i < 8; i++) rec[2 + i] = h[i];
+            for (int i = 0; i < 8; i++) rec[2 + i] = hv[i];
           }
         }
       }
@@ -617,23 +624,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
-template <int MODE>
+template <int MODE, int R>
 int launch(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& ca, const CUtensorMap& cb,
            cudaStream_t st) {
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(k_noisy_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<MODE>::SMEM) !=
-        cudaSuccess) {
+    if (cudaFuncSetAttribute(k_noisy_gemm<MODE, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<MODE, R>::SMEM) != cudaSuccess) {
       cudaGetLastError();
       return UWC_ERR_CUDA;
     }
     configured[dev] = 1;
   }
   const int grid = std::min(p.nunits, uwc_num_sms());
-  k_noisy_gemm<MODE><<<grid, kThreads, Cfg<MODE>::SMEM, st>>>(a, b, ca, cb, p);
+  k_noisy_gemm<MODE, R><<<grid, kThreads, Cfg<MODE, R>::SMEM, st>>>(a, b, ca, cb, p);
   return uwc_launch_status();
+}
+
+template <int MODE>
+int launch_r(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& ca,
+             const CUtensorMap& cb, cudaStream_t st) {
+  if (!p.hash) return launch<MODE, 0>(p, a, b, ca, cb, st);
+  if (p.r == 64) return launch<MODE, 64>(p, a, b, ca, cb, st);
+  if (p.r == 128) return launch<MODE, 128>(p, a, b, ca, cb, st);
+  return launch<MODE, 256>(p, a, b, ca, cb, st);
 }
 
 }  // namespace
@@ -684,7 +700,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     tcb = tb;
   }
   cudaStream_t st = (cudaStream_t)stream;
-  if (mode == MODE_MINE) return launch<MODE_MINE>(p, ta, tb, tca, tcb, st);
-  if (mode == MODE_FWD) return launch<MODE_FWD>(p, ta, tb, tca, tcb, st);
-  return launch<MODE_PLAIN>(p, ta, tb, tca, tcb, st);
+  if (mode == MODE_MINE) return launch_r<MODE_MINE>(p, ta, tb, tca, tcb, st);
+  if (mode == MODE_FWD) return launch_r<MODE_FWD>(p, ta, tb, tca, tcb, st);
+  return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
 }
