@@ -113,11 +113,15 @@ int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_o
  *  out_mode                : UWC_OUT_NONE / UWC_OUT_I32 (int32 m x n) / UWC_OUT_BF16
  *                            (RNE of (float(acc) * a_scale[i]) * b_scale[j]) / UWC_OUT_F32
  *                            (same expression in fp32, the detrt dequant).
- * Without flags any m >= 1 works (rows past m are read as zero and not stored); k % 16 == 0. */
+ * Without flags any m >= 1 works (rows past m are read as zero and not stored); k % 16 == 0.
+ * workspace: device memory of at least uwc_gemm_workspace_bytes(flags) bytes, 16-byte aligned,
+ *            any contents (the kernel clears what it uses); unused (may be NULL) without FLAG_HASH.
+ *            Hashed calls that overlap on the GPU must not share a workspace. */
+uint64_t uwc_gemm_workspace_bytes(int flags);
 int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
              const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key, const uint32_t* target,
              uint32_t* wins, int max_wins, const float* a_scale, const float* b_scale, void* out, int out_mode,
-             void* stream);
+             void* workspace, uint64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -56,19 +56,19 @@ def test_shape_validation_needs_no_device():
     fake = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
     # hashed GEMM with m % 64 != 0
     rc = L.uwc_gemm(fake, fake, 100, 256, 1024, 128, 1, None, None, None, 0, fake, fake, fake, 4, None, None, None, 0,
-                    None)
+                    fake, 1 << 30, None)
     assert rc == _lib.ERR_SHAPE
     # k % r != 0
     rc = L.uwc_gemm(fake, fake, 128, 256, 1000, 128, 1, None, None, None, 0, fake, fake, fake, 4, None, None, None, 0,
-                    None)
+                    fake, 1 << 30, None)
     assert rc == _lib.ERR_SHAPE
     # bad out_mode / flags
     assert L.uwc_gemm(fake, fake, 128, 256, 1024, 128, 8, None, None, None, 0, None, None, None, 0, None, None, None, 0,
-                      None) == _lib.ERR_ARG
+                      None, 0, None) == _lib.ERR_ARG
     # unaligned operand
     bad = ctypes.c_void_p(0x1001)
     assert L.uwc_gemm(bad, fake, 128, 256, 1024, 128, 0, None, None, None, 0, None, None, None, 0, None, None, fake, 1,
-                      None) == _lib.ERR_ALIGN
+                      None, 0, None) == _lib.ERR_ALIGN
     # BLAKE3 input not a multiple of 1 KiB
     assert L.uwc_b3_root_and_seed(fake, 1000, fake, None, None, 0, None, None, fake, 64, None) == _lib.ERR_SHAPE
     # noise_rows rank must be 64/128/256

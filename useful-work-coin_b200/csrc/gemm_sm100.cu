@@ -6,10 +6,10 @@
 // specialized at compile time on the schedule and on the hash chunk width r:
 //
 //   MODE_MINE  FLAG_HASH, no output (MinedWeight.noise_mine, ops.py:349-364). A work unit is a
-//              256 x 256 output block held as four 128 x 128 TMEM accumulators: X0 X1 (rows
-//              0-127, column halves) and Y0 Y1 (rows 128-255). Per r-column chunk of k the MMA
-//              warp issues X0, X1, Y0, Y1 in turn, so each accumulator's running sum is read by
-//              the epilogue while the tensor core works on the other three.
+//              256 x 256 output block held as two 128 x 256 TMEM accumulators X (rows 0-127) and
+//              Y (rows 128-255) sharing the B tile. Per r-column chunk of k the MMA warp issues X
+//              then Y, so each accumulator's running sum is read by the epilogue while the tensor
+//              core works on the other.
 //   MODE_FWD   FLAG_DENOISE and/or FLAG_HASH with an output (MinedWeight.forward, ops.py:316-347).
 //              A unit is a 128 x 256 block held as two 128 x 128 accumulators (column halves)
 //              plus a 128 x 256 correction accumulator R = sum_li 128^li corrA[li] corrB[li]^T,
@@ -26,8 +26,12 @@
 // tcgen05.ld.32x32b (thread = row, registers = consecutive columns), XORs each row's values
 // into four partials by t = (col / 2) % 4, then a 3-shuffle reduce-scatter over the lanes of
 // rows g, g+8, g+16, g+24 leaves lane (g + 8t) with tile (g, t)'s XOR over the quadrant.
-// Rows 32-63 of a 64-row block live in the next quadrant (the next warp); XOR and rotl are linear
-// over GF(2), so each warp keeps a partial message and the two partials are XORed once per unit.
+// Rows 32-63 of a 64-row block live in the next quadrant (the next warp). XOR and rotl are linear
+// over GF(2): the reference's msg[c % 16] = rotl(msg[c % 16], 13) ^ x_c equals the XOR over the
+// chunks of slot s of rotl(x_c, 13 * (updates of slot s after c)). So every epilogue thread
+// pre-rotates its chunk contribution and red.global.xor's it into the unit's message buffer
+// (caller workspace, double-buffered per CTA): no message state in registers, and the two
+// quadrant halves of a tile combine in the same word.
 //
 // Warp roles (640 threads, one CTA per SM, all 512 TMEM columns):
 //   0..15   epilogue: warp w reads TMEM lanes 32*(w%4).. and the 64-column block w/4
@@ -51,7 +55,7 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;           // 640
 constexpr int kKB = 128;                                // K bytes per stage (one 128-byte swizzle row)
 constexpr int kUN = 256;                                // output columns per unit
 constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
-constexpr int kHashBufBytes = kMaxTiles * 16 * 4;       // 32 KiB of tile messages
+constexpr int kMsgWords = kMaxTiles * 16;               // one unit's tile messages (32 KiB)
 constexpr int kBarBytes = 512;
 
 struct Params {
@@ -66,6 +70,7 @@ struct Params {
   const uint32_t* key;
   const uint32_t* target;
   uint32_t* wins;
+  uint32_t* msgbuf;        // workspace: per CTA 2 x kMsgWords words of tile messages
   const float* a_scale;
   const float* b_scale;
   void* out;
@@ -77,17 +82,16 @@ template <int MODE, int R>
 struct Cfg {
   static constexpr bool HASH = R != 0;
   static constexpr int UM = MODE == MODE_MINE ? 256 : 128;      // output rows per unit
-  static constexpr int NACC = MODE == MODE_MINE ? 4 : (MODE == MODE_FWD ? 2 : 1);
-  static constexpr int ACC_N = MODE == MODE_PLAIN ? 256 : 128;  // MMA N per accumulator
+  static constexpr int NACC = MODE == MODE_PLAIN ? 1 : 2;
+  static constexpr int ACC_N = MODE == MODE_FWD ? 128 : 256;    // MMA N per accumulator
   static constexpr int A_BYTES = UM * kKB;
   static constexpr int STAGE = A_BYTES + kUN * kKB;              // 64 KiB (MINE) / 48 KiB
   static constexpr int NST = MODE == MODE_MINE ? 3 : 4;
-  static constexpr int HASHBUF = HASH ? kHashBufBytes : 0;
-  static constexpr int SMEM = NST * STAGE + HASHBUF + kBarBytes + 1024;  // +1024: manual alignment
+  static constexpr int SMEM = NST * STAGE + kBarBytes + 1024;  // +1024: manual alignment
   static constexpr int TILES = MODE == MODE_MINE ? 512 : 256;
   static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
   static constexpr int SPAN = R == 256 ? 2 : 1;                  // stages per chunk
-  static constexpr int ACC_WARPS = MODE == MODE_PLAIN ? kEpiWarps : kEpiWarps / 2;  // readers per acc
+  static constexpr int ACC_WARPS = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;  // readers per acc
 };
 
 struct Bars {
@@ -96,8 +100,7 @@ struct Bars {
   uint64_t acc_full[4];
   uint64_t acc_empty[4];
   uint64_t r_full, r_scaled, r_empty;
-  uint64_t hash_ready, hash_free;
-  uint64_t pair[8];        // odd quadrant warp -> even quadrant warp: partial messages written
+  uint64_t hash_ready[2], hash_free[2];   // per message buffer
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -211,8 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<MODE, R>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint32_t* hbuf = reinterpret_cast<uint32_t*>(smem + C::NST * C::STAGE);
-  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE + C::HASHBUF);
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -222,17 +224,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
-    for (int a = 0; a < 4; a++) {
+    for (int a = 0; a < 2; a++) {
       mbar_init(&bars->acc_full[a], 1);
       mbar_init(&bars->acc_empty[a], C::ACC_WARPS);
+      // message hand-offs are signalled by every lane that wrote (arrival counts in threads)
+      mbar_init(&bars->hash_ready[a], kEpiWarps * 32);
+      mbar_init(&bars->hash_free[a], kHashWarps * 32);
     }
     mbar_init(&bars->r_full, 1);
     mbar_init(&bars->r_scaled, kEpiWarps);
     mbar_init(&bars->r_empty, kEpiWarps);
-    // smem hand-offs are signalled by every writing lane (arrival counts in threads)
-    mbar_init(&bars->hash_ready, (kEpiWarps / 2) * 32);
-    mbar_init(&bars->hash_free, kHashWarps * 32);
-    for (int i = 0; i < 8; i++) mbar_init(&bars->pair[i], 32);
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
     bars->L = MODE == MODE_FWD ? limbs_from_maxabs(p) : 0;
@@ -241,6 +242,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
+  }
+  uint32_t* const msg_cta = C::HASH ? p.msgbuf + (uint64_t)blockIdx.x * (2 * kMsgWords) : nullptr;
+  if (C::HASH && warp < kEpiWarps) {
+    uint4* z = reinterpret_cast<uint4*>(msg_cta);
+    for (int i = threadIdx.x; i < 2 * kMsgWords / 4; i += kEpiWarps * 32) __stcg(z + i, make_uint4(0, 0, 0, 0));
+    __threadfence();
   }
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -292,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t gk = 0;                      // k-blocks consumed (ring position)
-      uint32_t snaps[4] = {0, 0, 0, 0};     // snapshots produced per accumulator
+      uint32_t snaps[2] = {0, 0};           // snapshots produced per accumulator
       uint32_t r_scaled_waits = 0;
       int local = 0;
       bool ok = true;
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         // ---- main loop, one 128-column k-block stage at a time, MMAs issued back to back
-        const int nacc = (MODE == MODE_MINE && m0 + 128 >= p.m) ? 2 : C::NACC;
+        const int nacc = (MODE == MODE_MINE && m0 + 128 >= p.m) ? 1 : C::NACC;
         const int pbuf = local & 1;   // PLAIN: accumulator buffer of this unit
         const uint32_t gk0 = gk;
         for (int kb = 0; kb < kblocks && ok; kb++) {
@@ -352,10 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (!ok) break;
                   tc_fence_after();
                 }
-                // MINE: a = 2*row_half + col_half; FWD: a = col_half (descriptor offsets in 16-byte units)
-                const uint64_t ad = adesc + (MODE == MODE_MINE ? (a >> 1) * (128 * kKB / 16) : 0);
-                const uint64_t bd = bdesc + (MODE == MODE_MINE ? (a & 1) : a) * (128 * kKB / 16);
-                const uint32_t dcol = tmem + a * 128;
+                // MINE: a = row half (X, Y), full 256 columns; FWD: a = column half (16-byte desc units)
+                const uint64_t ad = adesc + (MODE == MODE_MINE ? a * (128 * kKB / 16) : 0);
+                const uint64_t bd = bdesc + (MODE == MODE_MINE ? 0 : a * (128 * kKB / 16));
+                const uint32_t dcol = tmem + a * C::ACC_N;
 #pragma unroll
                 for (int ks = part * (4 / C::PARTS); ks < (part + 1) * (4 / C::PARTS); ks++)
                   mma_i8(dcol, ad + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
@@ -400,9 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue warps
     const int q = warp & 3, cb = warp >> 2;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    // hash slot of this thread's tile after the reduce-scatter: g = lane % 8, t = lane / 8
+    // message slot of this thread's tile after the reduce-scatter: g = lane % 8, t = lane / 8
     const int tslot = (lane & 7) * 4 + (lane >> 3);
-    uint32_t snaps[4] = {0, 0, 0, 0};
+    uint32_t snaps[2] = {0, 0};
     uint32_t r_waits = 0;
     int local = 0;
     bool ok = true;
@@ -428,11 +435,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
-      // MINE: accumulators X_h (a = h) and Y_h (a = 2 + h) with h = cb / 2; FWD: a = cb / 2
-      const int h = cb >> 1, cofs = (cb & 1) * 64;
+      // MINE: accumulators X (a = 0) and Y (a = 1), this warp's 64 columns cb*64 of each.
+      // FWD: accumulator a = cb / 2 (column half), its columns (cb % 2) * 64.
       const bool hasY = MODE == MODE_MINE && m0 + 128 < p.m;
-      const int a0 = h, a1 = 2 + h;
-      const uint32_t col0 = tmem + a0 * 128 + cofs + lane_base, col1 = tmem + a1 * 128 + cofs + lane_base;
+      const int a0 = MODE == MODE_MINE ? 0 : (cb >> 1);
+      const uint32_t col0 = tmem + lane_base + (MODE == MODE_MINE ? cb * 64 : a0 * 128 + (cb & 1) * 64);
+      const uint32_t col1 = tmem + lane_base + 256 + cb * 64;
+      const int buf = local & 1;
+      uint32_t* const msg = msg_cta + buf * kMsgWords;
+      // row half of the 128-row accumulator this quadrant belongs to, for the message slot
+      const int rb = q >> 1;
 
       if (MODE == MODE_FWD) {
         // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
@@ -457,15 +469,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
       }
+      if (C::HASH) {
+        // this message buffer was last used two units ago: wait until the hash warps cleared it
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free[buf], ((local >> 1) & 1) ^ 1, abort_flag, p.status));
+        if (!ok) break;
+      }
 
-      constexpr int NY = MODE == MODE_MINE ? 16 : 1;
-      uint32_t m_x[16], m_y[NY];   // this thread's partial tile messages (X_h / FWD acc, Y_h)
-#pragma unroll
-      for (int i = 0; i < 16; i++) m_x[i] = 0u;
-#pragma unroll
-      for (int i = 0; i < NY; i++) m_y[i] = 0u;
-
-      // consume one snapshot of accumulator `a` at TMEM column address `col`; returns the fold
+      // consume one snapshot of accumulator `a` at TMEM address `col`; returns this thread's fold
       auto consume = [&](int a, uint32_t col, bool last) -> uint32_t {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status));
         if (!ok) return 0u;
@@ -481,13 +491,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
         }
         if (MODE == MODE_FWD && last) {
+          if (C::HASH) fold_row32(v, pt);
           // output: acc - R for this warp's 32 rows x 64 columns, then release acc and R
           if (L > 0) {
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
             if (!ok) return 0u;
             tc_fence_after();
           }
-          if (C::HASH) fold_row32(v, pt);
           if (p.out_mode != UWC_OUT_NONE) {
 #pragma unroll 1
             for (int hh = 0; hh < 2; hh++) {
@@ -523,49 +533,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
 
       if (C::HASH) {
-        for (int c0 = 0; c0 < nch && ok; c0 += 16) {
-#pragma unroll
-          for (int s = 0; s < 16; s++) {
-            const int c = c0 + s;
-            if (c < nch && ok) {
-              const uint32_t x = consume(a0, col0, c == nch - 1);
-              m_x[s] = rotl13(m_x[s]) ^ x;
-              if (MODE == MODE_MINE && hasY && ok) {
-                const uint32_t y = consume(a1, col1, c == nch - 1);
-                m_y[s % NY] = rotl13(m_y[s % NY]) ^ y;
-              }
-            }
+        const int slot0 = ((0 * 2 + rb) * 4 + cb) * 32 + tslot, slot1 = ((1 * 2 + rb) * 4 + cb) * 32 + tslot;
+        for (int c = 0; c < nch && ok; c++) {
+          // pre-rotation: slot s = c % 16 is updated (nch - 1 - s) / 16 + 1 times; this chunk is
+          // update j = c / 16, so its contribution is rotated 13 * (remaining updates) bits
+          const int s = c & 15, j = c >> 4, upd = (nch - 1 - s) / 16 + 1;
+          const int rot = (13 * (upd - 1 - j)) & 31;
+          const uint32_t x = consume(a0, col0, c == nch - 1);
+          if (!ok) break;
+          red_xor(msg + s * kMaxTiles + slot0, __funnelshift_l(x, x, rot));
+          if (hasY) {
+            const uint32_t y = consume(1, col1, c == nch - 1);
+            if (!ok) break;
+            red_xor(msg + s * kMaxTiles + slot1, __funnelshift_l(y, y, rot));
           }
         }
+        if (!ok) break;
+        __threadfence();                       // this unit's reductions are visible before the hand-off
+        mbar_arrive(&bars->hash_ready[buf]);
       } else {
         consume(a0, col0, true);
-      }
-      if (!ok) break;
-      if (C::HASH) {
-        // combine the two quadrant partials of each tile and hand the messages to the hash warps
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free, (local & 1) ^ 1, abort_flag, p.status));
-        if (!ok) break;
-        const int rb = q >> 1, pair_id = cb * 2 + rb;
-        const int slotX = ((0 * 2 + rb) * 4 + cb) * 32 + tslot, slotY = ((1 * 2 + rb) * 4 + cb) * 32 + tslot;
-        if (q & 1) {
-#pragma unroll
-          for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slotX] = m_x[i];
-          if (hasY) {
-#pragma unroll
-            for (int i = 0; i < NY; i++) hbuf[i * kMaxTiles + slotY] = m_y[i];
-          }
-          mbar_arrive(&bars->pair[pair_id]);
-        } else {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->pair[pair_id], local & 1, abort_flag, p.status));
-          if (!ok) break;
-#pragma unroll
-          for (int i = 0; i < 16; i++) hbuf[i * kMaxTiles + slotX] ^= m_x[i];
-          if (hasY) {
-#pragma unroll
-            for (int i = 0; i < NY; i++) hbuf[i * kMaxTiles + slotY] ^= m_y[i];
-          }
-          mbar_arrive(&bars->hash_ready);
-        }
       }
     }
   } else if (C::HASH) {
@@ -578,16 +565,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < p.nunits; u += gridDim.x, local++) {
       int m0, n0;
       unit_coords(p, u, C::UM, m0, n0);
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->hash_ready, local & 1, abort_flag, p.status))) break;
+      const int buf = local & 1;
+      uint32_t* const msg = msg_cta + buf * kMsgWords;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->hash_ready[buf], (local >> 1) & 1, abort_flag, p.status))) break;
       for (int slot = hw * 32 + lane; slot < C::TILES; slot += kHashWarps * 32) {
         const int ln = slot & 31, cbk = (slot >> 5) & 3, rb = (slot >> 7) & 1, a = slot >> 8;
         const int row_off = m0 + a * 128 + rb * 64 + (ln >> 2);
         const int col_off = n0 + cbk * 64 + 2 * (ln & 3);
-        if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) continue;
-        uint32_t msg[16], hv[8];
+        uint32_t w[16], hv[8];
 #pragma unroll
-        for (int i = 0; i < 16; i++) msg[i] = hbuf[i * kMaxTiles + slot];
-        b3::hash64(key, msg, hv);
+        for (int i = 0; i < 16; i++) {
+          w[i] = __ldcg(msg + i * kMaxTiles + slot);
+          __stcg(msg + i * kMaxTiles + slot, 0u);   // clear for the unit after next
+        }
+        if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) continue;
+        b3::hash64(key, w, hv);
         bool le = true, decided = false;
 #pragma unroll
         for (int i = 7; i >= 0; i--) {
@@ -607,7 +599,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      mbar_arrive(&bars->hash_free);
+      __threadfence();
+      mbar_arrive(&bars->hash_free[buf]);
     }
   }
 
@@ -654,10 +647,16 @@ int launch_r(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const 
 
 }  // namespace
 
+extern "C" uint64_t uwc_gemm_workspace_bytes(int flags) {
+  // hashed GEMMs keep two units of tile messages per CTA (one CTA per SM)
+  return (flags & UWC_FLAG_HASH) ? (uint64_t)uwc_num_sms() * 2 * kMsgWords * 4 : 0;
+}
+
 extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
                         const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key,
                         const uint32_t* target, uint32_t* wins, int max_wins, const float* a_scale,
-                        const float* b_scale, void* out, int out_mode, void* stream) {
+                        const float* b_scale, void* out, int out_mode, void* workspace, uint64_t workspace_bytes,
+                        void* stream) {
   const bool hash = flags & UWC_FLAG_HASH, denoise = flags & UWC_FLAG_DENOISE;
   if (!A || !B || (flags & ~3) || out_mode < 0 || out_mode > 3) return UWC_ERR_ARG;
   if (out_mode != UWC_OUT_NONE && !out) return UWC_ERR_ARG;
@@ -671,15 +670,18 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     if (k % r) return UWC_ERR_SHAPE;
   }
   if (out_mode == UWC_OUT_BF16 ? (n % 8) : (out_mode != UWC_OUT_NONE && n % 4)) return UWC_ERR_SHAPE;
-  if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)out) | ((uintptr_t)corrA) | ((uintptr_t)corrB)) & 15)
+  if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)out) | ((uintptr_t)corrA) | ((uintptr_t)corrB) |
+       ((uintptr_t)workspace)) & 15)
     return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
+  if (hash && (!workspace || workspace_bytes < uwc_gemm_workspace_bytes(flags))) return UWC_ERR_SCRATCH;
 
   Params p{};
   p.m = m; p.n = n; p.k = k; p.r = r;
   p.hash = hash; p.denoise = denoise; p.lmax = lmax; p.out_mode = out_mode; p.max_wins = max_wins;
   p.maxabs = maxabs; p.key = key; p.target = target; p.wins = wins;
   p.a_scale = a_scale; p.b_scale = b_scale; p.out = out;
+  p.msgbuf = static_cast<uint32_t*>(workspace);
   p.status = uwc_status_ptr();
   const int mode = (hash && !denoise && out_mode == UWC_OUT_NONE) ? MODE_MINE : ((hash || denoise) ? MODE_FWD : MODE_PLAIN);
   const int UM = mode == MODE_MINE ? 256 : 128;

@@ -259,6 +259,11 @@ UWC_DEVI void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+// Fire-and-forget XOR into global memory (performed at L2).
+UWC_DEVI void red_xor(uint32_t* addr, uint32_t v) {
+  asm volatile("red.relaxed.gpu.global.xor.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
 // XOR of 32 words, 3-input XOR per step (LOP3).
 UWC_DEVI uint32_t xor32(const uint32_t* r) {
   uint32_t a = r[0] ^ r[1] ^ r[2], b = r[3] ^ r[4] ^ r[5], c = r[6] ^ r[7] ^ r[8], d = r[9] ^ r[10] ^ r[11];

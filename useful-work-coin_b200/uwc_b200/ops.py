@@ -165,6 +165,22 @@ def project(src: torch.Tensor, St: torch.Tensor, corr: torch.Tensor, corr_off: i
 
 
 # ------------------------------------------------------------------ GEMM
+_GEMM_WS: dict = {}
+
+
+def gemm_workspace(device, flags: int) -> torch.Tensor | None:
+    """Per-device workspace of the hashed GEMM (tile-message buffers), allocated once. Callers
+    serialize on one stream per device (like the reference's shared workspace, ops.py:258-277)."""
+    nbytes = int(lib().uwc_gemm_workspace_bytes(flags))
+    if nbytes == 0:
+        return None
+    key = str(torch.device(device))
+    ws = _GEMM_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = _GEMM_WS[key] = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws
+
+
 def gemm(A, B, *, r=128, flags=0, corrA=None, corrB=None, maxabs=None, key=None, target=None, wins=None,
          max_wins=0, a_scale=None, b_scale=None, out=None, out_mode=OUT_NONE, cfg=None):
     """C = A B^T (ops.py:185-198) with hashing / denoising / scaled output, see uwc_gemm."""
@@ -174,8 +190,10 @@ def gemm(A, B, *, r=128, flags=0, corrA=None, corrB=None, maxabs=None, key=None,
     if flags:
         assert m % 64 == 0 and n % 64 == 0 and k % 64 == 0 and r % 64 == 0 and k % r == 0, (m, n, k, r)
     lmax = corrA.shape[0] if corrA is not None else 0
+    ws = gemm_workspace(A.device, flags)
     check(lib().uwc_gemm(_p(A), _p(B), m, n, k, r, flags, _p(corrA), _p(corrB), _p(maxabs), lmax, _p(key), _p(target),
-                         _p(wins), max_wins, _p(a_scale), _p(b_scale), _p(out), out_mode, _stream()), "gemm")
+                         _p(wins), max_wins, _p(a_scale), _p(b_scale), _p(out), out_mode, _p(ws),
+                         0 if ws is None else ws.numel(), _stream()), "gemm")
     _count()
 
 
