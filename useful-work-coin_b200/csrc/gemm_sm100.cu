@@ -482,16 +482,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         snaps[a]++;
         tc_fence_after();
         uint32_t pt[4] = {0u, 0u, 0u, 0u};
-        uint32_t v[32];
+        uint32_t v[32], v2[32];
         if (C::HASH) {
+          // both halves in flight at once; the accumulator is released as soon as they landed
           tmem_ld_32x32b_x32(col, v);
-          tmem_wait_ld();
-          fold_row32(v, pt);
-          tmem_ld_32x32b_x32(col + 32, v);
+          tmem_ld_32x32b_x32(col + 32, v2);
           tmem_wait_ld();
         }
         if (MODE == MODE_FWD && last) {
-          if (C::HASH) fold_row32(v, pt);
+          if (C::HASH) {
+            fold_row32(v, pt);
+            fold_row32(v2, pt);
+          }
           // output: acc - R for this warp's 32 rows x 64 columns, then release acc and R
           if (L > 0) {
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
@@ -527,7 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
-          if (C::HASH) fold_row32(v, pt);
+          if (C::HASH) {
+            fold_row32(v, pt);
+            fold_row32(v2, pt);
+          }
         }
         return C::HASH ? reduce_scatter4(pt, lane) : 0u;
       };
