@@ -68,6 +68,19 @@ int uwc_b3_root_and_seed(const void* data, uint64_t nbytes, const uint32_t* key,
                          const uint32_t* salt, uint32_t dim, uint32_t* root_out, uint32_t* seed_out,
                          uint32_t* scratch, uint64_t scratch_words, void* stream);
 
+/* Same commitment and seed as uwc_b3_root_and_seed, for callers that cannot allocate device
+ * memory (inside CUDA graph capture, foreign-function callers without a device allocator,
+ * processes whose device memory is reserved by another framework): no counterpart in the
+ * reference. The scratch is a fixed 32 KiB array in the library's device memory, so inputs are
+ * limited to uwc_b3_noalloc_max_bytes() (128 MiB); larger ones return UWC_ERR_SCRATCH. No
+ * allocation of any kind. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and should come before any stream capture. All calls on a device share
+ * the array: calls that overlap on the GPU race and must be serialized by the caller. */
+uint64_t uwc_b3_noalloc_max_bytes(void);
+int uwc_b3_root_and_seed_noalloc(const void* data, uint64_t nbytes, const uint32_t* key, const uint32_t* prefix,
+                                 const uint32_t* salt, uint32_t dim, uint32_t* root_out, uint32_t* seed_out,
+                                 void* stream);
+
 /* ---- noise generation ------------------------------------------------------------------
  * Replaces ops.noise_uniform (ops.py:122-125, kernels.cu:259-282): nbytes (% 32 == 0) int8 values
  * (b & 63) - 32 from keyed BLAKE3 random_hash(block, label, key, prepend=0). If zero_me != NULL its

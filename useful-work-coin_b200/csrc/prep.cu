@@ -408,3 +408,71 @@ int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_o
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ commitment without allocation
+// Some callers cannot allocate device memory at the moment they commit to a matrix: code running
+// while a CUDA graph is being captured (cudaMalloc is not a capturable operation), foreign-function
+// callers (cgo, JNI, plain C) that own no device allocator and would otherwise have to manage a
+// scratch buffer per device, and processes whose device memory is fully reserved up front by
+// another framework's pool. uwc_b3_root_and_seed_noalloc serves them with a fixed scratch array
+// in the library's own device memory instead of a caller buffer.
+//
+// Limit: the scratch holds the chaining values of up to kNoAllocMaxCtas chunk groups, i.e.
+// inputs up to kNoAllocMaxBytes (128 MiB, one reduce level); larger inputs are rejected with
+// UWC_ERR_SCRATCH. The array (32 KiB) lives on every GPU that loads the library until exit.
+// All calls on a device share it and it keeps the last call's contents (every word the kernels
+// read is written first in the same call, so nothing needs clearing); calls that overlap on the
+// GPU (different streams, or concurrent host threads) race on it and must be serialized.
+namespace {
+constexpr uint64_t kNoAllocMaxCtas = kReduceGroup;                         // one final reduce level
+constexpr uint64_t kNoAllocMaxBytes = kNoAllocMaxCtas * kChunksPerCta * 1024;  // 128 MiB
+constexpr uint64_t kNoAllocWords = 8 * kNoAllocMaxCtas;
+
+static __device__ __align__(256) uint32_t g_b3_noalloc_scratch[kNoAllocWords];
+
+constexpr int kNoAllocDevices = 64;
+uint32_t* g_noalloc_ptr[kNoAllocDevices];
+
+// Device address of the static scratch on the current device. The first call on a device looks
+// it up with cudaGetSymbolAddress (with that device current); in host code the array's name is
+// only a stand-in and must never be passed to a kernel.
+int noalloc_scratch(uint32_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kNoAllocDevices) return UWC_ERR_DEVICE;
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_b3_noalloc_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return UWC_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return UWC_OK;
+}
+}  // namespace
+
+extern "C" uint64_t uwc_b3_noalloc_max_bytes(void) { return kNoAllocMaxBytes; }
+
+extern "C" int uwc_b3_root_and_seed_noalloc(const void* data, uint64_t nbytes, const uint32_t* key,
+                                            const uint32_t* prefix, const uint32_t* salt, uint32_t dim,
+                                            uint32_t* root_out, uint32_t* seed_out, void* stream) {
+  if (!data || !key || (seed_out && (!prefix || !salt))) return UWC_ERR_ARG;
+  if (nbytes == 0 || nbytes % 1024) return UWC_ERR_SHAPE;
+  if (nbytes > kNoAllocMaxBytes) return UWC_ERR_SCRATCH;
+  if (((uintptr_t)data) & 15) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  uint32_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != UWC_OK) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint64_t nch = nbytes / 1024;
+  const uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;   // <= kNoAllocMaxCtas
+  k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch);
+  k_b3_reduce<<<1, 512, 0, st>>>(scratch, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out);
+  return uwc_launch_status();
+}

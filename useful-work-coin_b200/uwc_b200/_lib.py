@@ -22,6 +22,8 @@ SIGNATURES = {
     "uwc_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint32), _I32]),
     "uwc_b3_scratch_words": (_U64, [_U64]),
     "uwc_b3_root_and_seed": (_I32, [_P, _U64, _P, _P, _P, _U32, _P, _P, _P, _U64, _P]),
+    "uwc_b3_noalloc_max_bytes": (_U64, []),
+    "uwc_b3_root_and_seed_noalloc": (_I32, [_P, _U64, _P, _P, _P, _U32, _P, _P, _P]),
     "uwc_noise_uniform": (_I32, [_P, _U64, _P, _P, _P, _I32, _P]),
     "uwc_noise_perm": (_I32, [_P, _U32, _U32, _P, _P, _P]),
     "uwc_noise_rows": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _I32, _P]),
