@@ -251,39 +251,47 @@ int orc_limbs_for(int k) {
  * msgs[(((rb * 8 + g) * (n/64) + cb) * 4 + t) * 16 + w]  (matches reference.py:138-165 shapes). */
 typedef struct {
   const int8_t *Ap, *Bp;
-  int m, n, k, r, rb0, rb1;
+  int m, n, k, r, t0, t1, ncs;
   uint32_t* msgs;
 } fold_job;
 
+/* Work item w = (row block rb, column stripe cs): 64 rows x a stripe of 64-column blocks. Items are
+ * independent (each hash tile lives in exactly one), so threads split them freely. */
 static void* fold_worker(void* arg) {
   fold_job* j = (fold_job*)arg;
-  int n = j->n, k = j->k, r = j->r, nch = k / r, ncb = n / 64;
-  int32_t* acc = (int32_t*)calloc((size_t)64 * n, sizeof(int32_t));
-  for (int rb = j->rb0; rb < j->rb1; rb++) {
-    memset(acc, 0, sizeof(int32_t) * 64 * n);
-    uint32_t* mb = j->msgs + (uint64_t)rb * 8 * ncb * 4 * 16;
-    memset(mb, 0, sizeof(uint32_t) * 8 * ncb * 4 * 16);
+  const int n = j->n, k = j->k, r = j->r, nch = k / r, ncb = n / 64, ncs = j->ncs;
+  const int cbs = (ncb + ncs - 1) / ncs;  /* 64-column blocks per stripe */
+  int32_t* acc = (int32_t*)calloc((size_t)64 * cbs * 64, sizeof(int32_t));
+  for (int w = j->t0; w < j->t1; w++) {
+    const int rb = w / ncs, cs = w % ncs, cb0 = cs * cbs, cb1 = cb0 + cbs < ncb ? cb0 + cbs : ncb;
+    if (cb0 >= cb1) continue;
+    const int wc = (cb1 - cb0) * 64, c0 = cb0 * 64;
+    memset(acc, 0, sizeof(int32_t) * 64 * wc);
+    for (int g = 0; g < 8; g++)
+      for (int cb = cb0; cb < cb1; cb++)
+        memset(j->msgs + ((((uint64_t)rb * 8 + g) * ncb + cb) * 4) * 16, 0, sizeof(uint32_t) * 4 * 16);
     for (int c = 0; c < nch; c++) {
       for (int i = 0; i < 64; i++) {
         const int8_t* a = j->Ap + (uint64_t)(rb * 64 + i) * k + (uint64_t)c * r;
-        int32_t* ar = acc + (uint64_t)i * n;
-        for (int col = 0; col < n; col++) {
-          const int8_t* b = j->Bp + (uint64_t)col * k + (uint64_t)c * r;
+        int32_t* ar = acc + (uint64_t)i * wc;
+        for (int col = 0; col < wc; col++) {
+          const int8_t* b = j->Bp + (uint64_t)(c0 + col) * k + (uint64_t)c * r;
           int32_t s = 0;
           for (int l = 0; l < r; l++) s += (int32_t)a[l] * (int32_t)b[l];
           ar[col] = (int32_t)((uint32_t)ar[col] + (uint32_t)s);
         }
       }
-      int slot = c % 16;
+      const int slot = c % 16;
       for (int g = 0; g < 8; g++)
-        for (int cb = 0; cb < ncb; cb++)
+        for (int cb = cb0; cb < cb1; cb++)
           for (int t = 0; t < 4; t++) {
             uint32_t x = 0;
             for (int i = 0; i < 8; i++)
               for (int jj = 0; jj < 8; jj++)
-                for (int e = 0; e < 2; e++) x ^= (uint32_t)acc[(uint64_t)(g + 8 * i) * n + cb * 64 + 8 * jj + 2 * t + e];
-            uint32_t* w = mb + ((uint64_t)(g * ncb + cb) * 4 + t) * 16 + slot;
-            *w = ((*w << 13) | (*w >> 19)) ^ x;
+                for (int e = 0; e < 2; e++)
+                  x ^= (uint32_t)acc[(uint64_t)(g + 8 * i) * wc + (cb - cb0) * 64 + 8 * jj + 2 * t + e];
+            uint32_t* wd = j->msgs + ((((uint64_t)rb * 8 + g) * ncb + cb) * 4 + t) * 16 + slot;
+            *wd = ((*wd << 13) | (*wd >> 19)) ^ x;
           }
     }
   }
@@ -293,14 +301,20 @@ static void* fold_worker(void* arg) {
 
 /* Ap: m x k, Bp: n x k int8 (noised operands), m % 64 == 0, n % 64 == 0, k % r == 0. */
 void orc_jackpot_msgs(const int8_t* Ap, const int8_t* Bp, int m, int n, int k, int r, uint32_t* msgs, int nthreads) {
-  int nrb = m / 64;
+  const int nrb = m / 64, ncb = n / 64;
   if (nthreads < 1) nthreads = 1;
-  if (nthreads > nrb) nthreads = nrb;
+  if (nthreads > 64) nthreads = 64;
+  /* enough column stripes that every thread has work even for a few row blocks */
+  int ncs = (nthreads * 2 + nrb - 1) / nrb;
+  if (ncs > ncb) ncs = ncb;
+  if (ncs < 1) ncs = 1;
+  const int items = nrb * ncs;
+  if (nthreads > items) nthreads = items;
   pthread_t th[64];
   fold_job jobs[64];
-  if (nthreads > 64) nthreads = 64;
   for (int t = 0; t < nthreads; t++) {
-    jobs[t] = (fold_job){Ap, Bp, m, n, k, r, nrb * t / nthreads, nrb * (t + 1) / nthreads, msgs};
+    jobs[t] = (fold_job){Ap, Bp, m, n, k, r, (int)((int64_t)items * t / nthreads),
+                         (int)((int64_t)items * (t + 1) / nthreads), ncs, msgs};
     pthread_create(&th[t], NULL, fold_worker, &jobs[t]);
   }
   for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
