@@ -207,6 +207,12 @@ __device__ __forceinline__ uint32_t reduce_scatter4(const uint32_t* pt, int lane
   return keep ^ __shfl_xor_sync(0xffffffffu, send, 8);
 }
 
+// Warp-wide bounded wait: every lane polls the barrier (measured faster to wake than one polling
+// lane plus a warp sync) and the warp agrees on the verdict.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status));
+}
+
 template <int MODE, int R>
 __global__ void __launch_bounds__(kThreads, 1)
     k_noisy_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -418,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       unit_coords(p, u, C::UM, m0, n0);
       if (MODE == MODE_PLAIN) {
         const int b = local & 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status));
+        ok = warp_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status);
         if (!ok) break;
         tc_fence_after();
         const uint32_t col = tmem + b * 256 + cb * 64;
@@ -449,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (MODE == MODE_FWD) {
         // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
         for (int step = 0; step + 1 < L && ok; step++) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
+          ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
@@ -471,13 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (C::HASH) {
         // this message buffer was last used two units ago: wait until the hash warps cleared it
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->hash_free[buf], ((local >> 1) & 1) ^ 1, abort_flag, p.status));
+        ok = warp_wait(&bars->hash_free[buf], ((local >> 1) & 1) ^ 1, abort_flag, p.status);
         if (!ok) break;
       }
 
       // consume one snapshot of accumulator `a` at TMEM address `col`; returns this thread's fold
       auto consume = [&](int a, uint32_t col, bool last) -> uint32_t {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status));
+        ok = warp_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status);
         if (!ok) return 0u;
         snaps[a]++;
         tc_fence_after();
@@ -496,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // output: acc - R for this warp's 32 rows x 64 columns, then release acc and R
           if (L > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status));
+            ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
             if (!ok) return 0u;
             tc_fence_after();
           }
@@ -542,8 +548,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < nch && ok; c++) {
           // pre-rotation: slot s = c % 16 is updated (nch - 1 - s) / 16 + 1 times; this chunk is
           // update j = c / 16, so its contribution is rotated 13 * (remaining updates) bits
-          const int s = c & 15, j = c >> 4, upd = (nch - 1 - s) / 16 + 1;
-          const int rot = (13 * (upd - 1 - j)) & 31;
+          // slot s = c % 16 is updated again by the chunks c + 16, c + 32, ... < nch: the
+          // contribution of chunk c is rotated 13 bits for each of those later updates
+          const int s = c & 15;
+          const int rot = (13 * ((nch - 1 - c) >> 4)) & 31;
           const uint32_t x = consume(a0, col0, c == nch - 1);
           if (!ok) break;
           red_xor(msg + s * kMaxTiles + slot0, __funnelshift_l(x, x, rot));
@@ -572,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       unit_coords(p, u, C::UM, m0, n0);
       const int buf = local & 1;
       uint32_t* const msg = msg_cta + buf * kMsgWords;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->hash_ready[buf], (local >> 1) & 1, abort_flag, p.status))) break;
+      if (!warp_wait(&bars->hash_ready[buf], (local >> 1) & 1, abort_flag, p.status)) break;
       for (int slot = hw * 32 + lane; slot < C::TILES; slot += kHashWarps * 32) {
         const int ln = slot & 31, cbk = (slot >> 5) & 3, rb = (slot >> 7) & 1, a = slot >> 8;
         const int row_off = m0 + a * 128 + rb * 64 + (ln >> 2);
