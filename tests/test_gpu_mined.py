@@ -169,3 +169,79 @@ def test_det_linear(ops):
     y = det.linear_f32(torch.from_numpy(q).cuda(), torch.from_numpy(sx).cuda(), torch.from_numpy(Wq).cuda(),
                        torch.from_numpy(sw).cuda())
     assert np.array_equal(y.cpu().numpy().view(np.uint32), O.det_dequant(want, sx, sw).view(np.uint32))
+
+
+@pytest.mark.parametrize("r", [64, 128])
+def test_full_size_mining_every_tile_sampled_against_oracle(ops, r):
+    """The hashed GEMM at the headline shape (8192 x 14336 x 4096): every SM processes a dozen
+    units, so message-buffer reuse and the persistent schedule are exercised. With a target that
+    every hash meets, each 64 x 64 block yields its 32 tiles exactly once; the tiles of sampled
+    blocks (corners, edges, interior) hash exactly as the oracle's fold of that block."""
+    m, n, k = 8192, 14336, 4096
+    g = torch.Generator(device="cuda").manual_seed(5 + r)
+    A = torch.randint(-64, 65, (m, k), dtype=torch.int8, device="cuda", generator=g)
+    B = torch.randint(-64, 65, (n, k), dtype=torch.int8, device="cuda", generator=g)
+    key = bytes(range(32))
+    keyw = torch.from_numpy(O.words(key).view(np.int32).copy()).cuda()
+    tgt = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+    ntiles = (m // 64) * (n // 64) * 32
+    wins = torch.zeros(1 + ntiles * 10, dtype=torch.int32, device="cuda")
+    ops.gemm(A, B, r=r, flags=1, key=keyw, target=tgt, wins=wins, max_wins=ntiles)
+    w = wins.cpu().numpy().view(np.uint32)
+    assert int(w[0]) == ntiles
+    recs = w[1:].reshape(ntiles, 10)
+    rows, cols = recs[:, 0].astype(np.int64), recs[:, 1].astype(np.int64)
+    # tile (g, t) of block (rb, cb) is reported at row 64 rb + g, col 64 cb + 2 t
+    assert np.all(rows < m) and np.all(cols < n) and np.all((rows % 64) < 8) and np.all((cols % 64) < 8)
+    assert np.all(cols % 2 == 0)
+    ids = rows * n + cols
+    assert len(np.unique(ids)) == ntiles
+    by_id = {int(i): recs[j, 2:] for j, i in enumerate(ids)}
+    An, Bn = A.cpu().numpy(), B.cpu().numpy()
+    rng = np.random.default_rng(r)
+    blocks = [(0, 0), (m // 64 - 1, n // 64 - 1), (0, n // 64 - 1), (m // 64 - 1, 0)]
+    blocks += [(int(a), int(b)) for a, b in zip(rng.integers(0, m // 64, 8), rng.integers(0, n // 64, 8))]
+    for rb, cb in blocks:
+        msgs = O.jackpot_msgs(An[rb * 64:(rb + 1) * 64], Bn[cb * 64:(cb + 1) * 64], r)
+        for gg in range(8):
+            for t in range(4):
+                want = O.jackpot_hash(msgs[0, gg, 0, t], key)
+                got = by_id[(rb * 64 + gg) * n + cb * 64 + 2 * t].astype("<u4").tobytes()
+                assert got == want, (rb, cb, gg, t)
+
+
+@pytest.mark.parametrize("mode", ["i32", "bf16", "f32"])
+def test_hashed_gemm_outputs_without_denoise(ops, mode):
+    """FLAG_HASH with an output and no denoise (the mining pass stores the product, a second pass
+    scales it): exact / RNE outputs, and the same winning tiles as the output-free mining call."""
+    rng = np.random.default_rng(77)
+    m, n, k, r = 384, 640, 1024, 64
+    A = rng.integers(-64, 65, size=(m, k), dtype=np.int8)
+    B = rng.integers(-64, 65, size=(n, k), dtype=np.int8)
+    sa = (rng.random(m, dtype=np.float32) * 0.01 + 1e-4).astype(np.float32)
+    sb = (rng.random(n, dtype=np.float32) * 0.02 + 1e-4).astype(np.float32)
+    key = rng.bytes(32)
+    keyw = torch.from_numpy(O.words(key).view(np.int32).copy()).cuda()
+    from uwc_b200 import glue
+    tgt = torch.from_numpy(glue.target_for(m, n, 20).view(np.int32).copy()).cuda()
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    w0 = torch.zeros(1 + 4096 * 10, dtype=torch.int32, device="cuda")
+    w1 = torch.zeros_like(w0)
+    ops.gemm(Ad, Bd, r=r, flags=1, key=keyw, target=tgt, wins=w0, max_wins=4096)
+    dt = {"i32": torch.int32, "bf16": torch.bfloat16, "f32": torch.float32}[mode]
+    om = {"i32": ops.OUT_I32, "bf16": ops.OUT_BF16, "f32": ops.OUT_F32}[mode]
+    out = torch.empty((m, n), dtype=dt, device="cuda")
+    ops.gemm(Ad, Bd, r=r, flags=1, key=keyw, target=tgt, wins=w1, max_wins=4096, a_scale=torch.from_numpy(sa).cuda(),
+             b_scale=torch.from_numpy(sb).cuda(), out=out, out_mode=om)
+
+    def recs(w):
+        h = w.cpu().numpy().view(np.uint32)
+        return sorted(map(tuple, h[1:1 + int(h[0]) * 10].reshape(-1, 10).tolist()))
+    assert int(w0[0]) > 0 and recs(w0) == recs(w1)
+    acc = O.gemm_i32(A, B)
+    if mode == "i32":
+        assert np.array_equal(out.cpu().numpy(), acc)
+    elif mode == "bf16":
+        assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), O.scaled_bf16(acc, sa, sb))
+    else:
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), O.det_dequant(acc, sa, sb).view(np.uint32))

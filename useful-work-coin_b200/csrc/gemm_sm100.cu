@@ -5,16 +5,20 @@
 // ops.gemm (ops.py:185-198). Three schedules share one persistent, warp-specialized kernel,
 // specialized at compile time on the schedule and on the hash chunk width r:
 //
-//   MODE_MINE  FLAG_HASH, no output (MinedWeight.noise_mine, ops.py:349-364). A work unit is a
+//   MODE_MINE  FLAG_HASH (MinedWeight.noise_mine, ops.py:349-364; MODE_MINE_OUT also stores the
+//              finished product, for MinedWeight.forward, ops.py:316-347). A work unit is a
 //              256 x 256 output block held as two 128 x 256 TMEM accumulators X (rows 0-127) and
 //              Y (rows 128-255) sharing the B tile. Per r-column chunk of k the MMA warp issues X
 //              then Y, so each accumulator's running sum is read by the epilogue while the tensor
 //              core works on the other.
-//   MODE_FWD   FLAG_DENOISE and/or FLAG_HASH with an output (MinedWeight.forward, ops.py:316-347).
+//   MODE_FWD   FLAG_DENOISE without FLAG_HASH (MinedWeight.forward with hash_tiles=False).
 //              A unit is a 128 x 256 block held as two 128 x 128 accumulators (column halves)
 //              plus a 128 x 256 correction accumulator R = sum_li 128^li corrA[li] corrB[li]^T,
 //              built before the main loop by Horner steps (R <<= 7 done by the epilogue in TMEM).
 //              The output is acc - R, exact in int32.
+//   MODE_CORR  second pass of a hashed, denoised call: only the correction accumulator R (same
+//              Horner build), then out = acc - R with acc read back from the int32 product that
+//              MODE_MINE_OUT stored. Hashing thus always runs on the mining schedule.
 //   MODE_PLAIN no flags: a 128 x 256 block per unit, two accumulators used alternately across
 //              units so the store of one unit overlaps the main loop of the next.
 //
@@ -45,7 +49,7 @@
 
 namespace {
 
-enum Mode { MODE_PLAIN = 0, MODE_MINE = 1, MODE_FWD = 2 };
+enum Mode { MODE_PLAIN = 0, MODE_MINE = 1, MODE_FWD = 2, MODE_CORR = 3, MODE_MINE_OUT = 4 };
 
 constexpr int kEpiWarps = 16;
 constexpr int kHashWarps = 2;
@@ -71,6 +75,7 @@ struct Params {
   const uint32_t* target;
   uint32_t* wins;
   uint32_t* msgbuf;        // workspace: per CTA 2 x kMsgWords words of tile messages
+  const int32_t* acc_in;   // MODE_CORR: the uncorrected int32 product, m x n
   const float* a_scale;
   const float* b_scale;
   void* out;
@@ -81,14 +86,16 @@ struct Params {
 template <int MODE, int R>
 struct Cfg {
   static constexpr bool HASH = R != 0;
-  static constexpr int UM = MODE == MODE_MINE ? 256 : 128;      // output rows per unit
+  static constexpr bool MINE = MODE == MODE_MINE || MODE == MODE_MINE_OUT;   // the mining schedule
+  static constexpr int UM = MINE ? 256 : 128;                    // output rows per unit
   static constexpr int NACC = MODE == MODE_PLAIN ? 1 : 2;
   static constexpr int ACC_N = MODE == MODE_FWD ? 128 : 256;    // MMA N per accumulator
+  static constexpr bool CORR = MODE == MODE_FWD || MODE == MODE_CORR;  // builds the correction R
   static constexpr int A_BYTES = UM * kKB;
   static constexpr int STAGE = A_BYTES + kUN * kKB;              // 64 KiB (MINE) / 48 KiB
-  static constexpr int NST = MODE == MODE_MINE ? 3 : 4;
+  static constexpr int NST = MINE ? 3 : 4;
   static constexpr int SMEM = NST * STAGE + kBarBytes + 1024;  // +1024: manual alignment
-  static constexpr int TILES = MODE == MODE_MINE ? 512 : 256;
+  static constexpr int TILES = MINE ? 512 : 256;
   static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
   static constexpr int SPAN = R == 256 ? 2 : 1;                  // stages per chunk
   static constexpr int ACC_WARPS = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;  // readers per acc
@@ -114,8 +121,6 @@ __device__ __forceinline__ void unit_coords(const Params& p, int u, int UM, int&
   m0 = (first + in % gsz) * UM;
   n0 = (in / gsz) * kUN;
 }
-
-__device__ __forceinline__ uint32_t rotl13(uint32_t x) { return __funnelshift_l(x, x, 13); }
 
 // Limb count from the projections' max |value| (kernels.cu:602-607 thresholds), capped at lmax.
 __device__ __forceinline__ int limbs_from_maxabs(const Params& p) {
@@ -195,16 +200,25 @@ __device__ __forceinline__ void fold_row32(const uint32_t* v, uint32_t* pt) {
   }
 }
 
+// f ? if1 : if0 for f in {0, 1}, as two multiply-adds: the selects of the reduce-scatter run on
+// the FMA pipe, next to the XOR fold that saturates the integer ALU pipe.
+__device__ __forceinline__ uint32_t imad_sel(uint32_t if1, uint32_t if0, uint32_t f) {
+  uint32_t d, r;
+  asm("mad.lo.u32 %0, %1, 0xFFFFFFFF, %2;" : "=r"(d) : "r"(if0), "r"(if1));
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(d), "r"(f), "r"(if0));
+  return r;
+}
+
 // Reduce-scatter over the lanes of rows g, g+8, g+16, g+24 (lane bits 3 and 4): lane (g + 8t)
-// ends with the XOR of partial t over those four rows.
+// ends with the XOR of partial t over those four rows. Each step sends the half the partner keeps
+// and recovers its own half as (both halves) ^ (sent half).
 __device__ __forceinline__ uint32_t reduce_scatter4(const uint32_t* pt, int lane) {
-  const bool b4 = lane & 16, b3 = lane & 8;
-  const uint32_t send_a = b4 ? pt[0] : pt[2], send_b = b4 ? pt[1] : pt[3];
-  const uint32_t keep_a = b4 ? pt[2] : pt[0], keep_b = b4 ? pt[3] : pt[1];
-  const uint32_t k0 = keep_a ^ __shfl_xor_sync(0xffffffffu, send_a, 16);
-  const uint32_t k1 = keep_b ^ __shfl_xor_sync(0xffffffffu, send_b, 16);
-  const uint32_t send = b3 ? k0 : k1, keep = b3 ? k1 : k0;
-  return keep ^ __shfl_xor_sync(0xffffffffu, send, 8);
+  const uint32_t f4 = (lane >> 4) & 1, f3 = (lane >> 3) & 1;
+  const uint32_t send_a = imad_sel(pt[0], pt[2], f4), send_b = imad_sel(pt[1], pt[3], f4);
+  const uint32_t k0 = pt[0] ^ pt[2] ^ send_a ^ __shfl_xor_sync(0xffffffffu, send_a, 16);
+  const uint32_t k1 = pt[1] ^ pt[3] ^ send_b ^ __shfl_xor_sync(0xffffffffu, send_b, 16);
+  const uint32_t send = imad_sel(k0, k1, f3);
+  return k0 ^ k1 ^ send ^ __shfl_xor_sync(0xffffffffu, send, 8);
 }
 
 // Warp-wide bounded wait: every lane polls the barrier (measured faster to wake than one polling
@@ -242,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->r_empty, kEpiWarps);
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
-    bars->L = MODE == MODE_FWD ? limbs_from_maxabs(p) : 0;
+    bars->L = C::CORR ? limbs_from_maxabs(p) : 0;
     mbar_fence_init();
   }
   if (warp == kMmaWarp) {
@@ -258,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (MODE == MODE_FWD && p.denoise) {
+    if (C::CORR && p.denoise) {
       tma_prefetch_desc(&tmCA);
       tma_prefetch_desc(&tmCB);
     }
@@ -269,9 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   const int L = bars->L;
   const int k = p.k;
-  const int kblocks = (k + kKB - 1) / kKB;
+  const int kblocks = MODE == MODE_CORR ? 0 : (k + kKB - 1) / kKB;
   const int nch = C::HASH ? k / R : 1;                         // snapshots per accumulator per unit
-  const int cblocks = MODE == MODE_FWD ? (2 * p.r) / kKB : 1;  // k-blocks per correction limb
+  const int cblocks = C::CORR ? (2 * p.r) / kKB : 1;  // k-blocks per correction limb
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
@@ -280,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < p.nunits && !*abort_flag; u += gridDim.x) {
         int m0, n0;
         unit_coords(p, u, C::UM, m0, n0);
-        const int ncorr = MODE == MODE_FWD ? L * cblocks : 0;
+        const int ncorr = C::CORR ? L * cblocks : 0;
         const int nblk = ncorr + kblocks;
         for (int b = 0; b < nblk; b++, gk++) {
           const int s = gk % C::NST;
@@ -315,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int m0, n0;
         unit_coords(p, u, C::UM, m0, n0);
         // ---- correction accumulator R (FWD): Horner over limbs, highest limb first
-        if (MODE == MODE_FWD && L > 0) {
+        if (C::CORR && L > 0) {
           const uint32_t tR = tmem + 256;
           for (int li = L - 1; li >= 0 && ok; li--) {
             if (li == L - 1)
@@ -340,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         // ---- main loop, one 128-column k-block stage at a time, MMAs issued back to back
-        const int nacc = (MODE == MODE_MINE && m0 + 128 >= p.m) ? 1 : C::NACC;
+        const int nacc = (C::MINE && m0 + 128 >= p.m) ? 1 : C::NACC;
         const int pbuf = local & 1;   // PLAIN: accumulator buffer of this unit
         const uint32_t gk0 = gk;
         for (int kb = 0; kb < kblocks && ok; kb++) {
@@ -366,8 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                   tc_fence_after();
                 }
                 // MINE: a = row half (X, Y), full 256 columns; FWD: a = column half (16-byte desc units)
-                const uint64_t ad = adesc + (MODE == MODE_MINE ? a * (128 * kKB / 16) : 0);
-                const uint64_t bd = bdesc + (MODE == MODE_MINE ? 0 : a * (128 * kKB / 16));
+                const uint64_t ad = adesc + (C::MINE ? a * (128 * kKB / 16) : 0);
+                const uint64_t bd = bdesc + (C::MINE ? 0 : a * (128 * kKB / 16));
                 const uint32_t dcol = tmem + a * C::ACC_N;
 #pragma unroll
                 for (int ks = part * (4 / C::PARTS); ks < (part + 1) * (4 / C::PARTS); ks++)
@@ -443,16 +457,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // MINE: accumulators X (a = 0) and Y (a = 1), this warp's 64 columns cb*64 of each.
       // FWD: accumulator a = cb / 2 (column half), its columns (cb % 2) * 64.
-      const bool hasY = MODE == MODE_MINE && m0 + 128 < p.m;
-      const int a0 = MODE == MODE_MINE ? 0 : (cb >> 1);
-      const uint32_t col0 = tmem + lane_base + (MODE == MODE_MINE ? cb * 64 : a0 * 128 + (cb & 1) * 64);
+      const bool hasY = C::MINE && m0 + 128 < p.m;
+      const int a0 = C::MINE ? 0 : (cb >> 1);
+      const uint32_t col0 = tmem + lane_base + (C::MINE ? cb * 64 : a0 * 128 + (cb & 1) * 64);
       const uint32_t col1 = tmem + lane_base + 256 + cb * 64;
       const int buf = local & 1;
       uint32_t* const msg = msg_cta + buf * kMsgWords;
       // row half of the 128-row accumulator this quadrant belongs to, for the message slot
       const int rb = q >> 1;
 
-      if (MODE == MODE_FWD) {
+      if (C::CORR) {
         // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
         for (int step = 0; step + 1 < L && ok; step++) {
           ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
@@ -474,6 +488,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&bars->r_scaled);
         }
         if (!ok) break;
+      }
+      if (MODE == MODE_CORR) {
+        // out = acc - R (R = 0 without denoising), acc read back from the int32 matrix the
+        // mining pass stored, then scaled / converted to the output format
+        if (L > 0) {
+          ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        const int row = m0 + 32 * q + lane;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; hh++) {
+          const int c0 = n0 + cb * 64 + hh * 32;
+          int32_t w[32];
+          if (row < p.m && c0 + 32 <= p.n) {
+            const int4* src = reinterpret_cast<const int4*>(p.acc_in + (uint64_t)row * p.n + c0);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const int4 x = __ldcs(src + i);
+              w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) w[i] = (row < p.m && c0 + i < p.n) ? p.acc_in[(uint64_t)row * p.n + c0 + i] : 0;
+          }
+          if (L > 0) {
+#pragma unroll
+            for (int qq = 0; qq < 2; qq++) {
+              uint32_t rr[16];
+              tmem_ld_32x32b_x16(tmem + 256 + cb * 64 + hh * 32 + qq * 16 + lane_base, rr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; i++) w[qq * 16 + i] -= (int32_t)rr[i];
+            }
+          }
+          store_row32(p, row, c0, w);
+        }
+        if (L > 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->r_empty);
+        }
+        continue;
       }
       if (C::HASH) {
         // this message buffer was last used two units ago: wait until the hash warps cleared it
@@ -539,28 +596,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             fold_row32(v, pt);
             fold_row32(v2, pt);
           }
+          if (MODE == MODE_MINE_OUT && last) {
+            // the finished product, raw int32: this thread's row, 64 consecutive columns
+            const int row = m0 + a * 128 + 32 * q + lane, c0 = n0 + cb * 64;
+            if (row < p.m && c0 < p.n) {
+              uint4* o = reinterpret_cast<uint4*>(static_cast<int32_t*>(p.out) + (uint64_t)row * p.n + c0);
+#pragma unroll
+              for (int i = 0; i < 8; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+#pragma unroll
+              for (int i = 0; i < 8; i++) o[8 + i] = make_uint4(v2[4 * i], v2[4 * i + 1], v2[4 * i + 2], v2[4 * i + 3]);
+            }
+          }
         }
         return C::HASH ? reduce_scatter4(pt, lane) : 0u;
       };
 
       if (C::HASH) {
         const int slot0 = ((0 * 2 + rb) * 4 + cb) * 32 + tslot, slot1 = ((1 * 2 + rb) * 4 + cb) * 32 + tslot;
-        for (int c = 0; c < nch && ok; c++) {
-          // pre-rotation: slot s = c % 16 is updated (nch - 1 - s) / 16 + 1 times; this chunk is
-          // update j = c / 16, so its contribution is rotated 13 * (remaining updates) bits
-          // slot s = c % 16 is updated again by the chunks c + 16, c + 32, ... < nch: the
-          // contribution of chunk c is rotated 13 bits for each of those later updates
+        // slot s = c % 16 is updated again by the chunks c + 16, c + 32, ... < nch: the
+        // contribution of chunk c is rotated 13 bits for each of those later updates
+        auto chunk = [&](int c, bool last) {
           const int s = c & 15;
           const int rot = (13 * ((nch - 1 - c) >> 4)) & 31;
-          const uint32_t x = consume(a0, col0, c == nch - 1);
-          if (!ok) break;
+          const uint32_t x = consume(a0, col0, last);
+          if (!ok) return;
           red_xor(msg + s * kMaxTiles + slot0, __funnelshift_l(x, x, rot));
           if (hasY) {
-            const uint32_t y = consume(1, col1, c == nch - 1);
-            if (!ok) break;
+            const uint32_t y = consume(1, col1, last);
+            if (!ok) return;
             red_xor(msg + s * kMaxTiles + slot1, __funnelshift_l(y, y, rot));
           }
-        }
+        };
+        // the last chunk of MINE_OUT (which also stores the product) is peeled off the loop
+        const int nloop = MODE == MODE_MINE_OUT ? nch - 1 : nch;
+        for (int c = 0; c < nloop && ok; c++) chunk(c, false);
+        if (MODE == MODE_MINE_OUT && ok) chunk(nch - 1, true);
         if (!ok) break;
         __threadfence();                       // this unit's reductions are visible before the hand-off
         mbar_arrive(&bars->hash_ready[buf]);
@@ -652,7 +722,6 @@ int launch(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CU
 template <int MODE>
 int launch_r(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& ca,
              const CUtensorMap& cb, cudaStream_t st) {
-  if (!p.hash) return launch<MODE, 0>(p, a, b, ca, cb, st);
   if (p.r == 64) return launch<MODE, 64>(p, a, b, ca, cb, st);
   if (p.r == 128) return launch<MODE, 128>(p, a, b, ca, cb, st);
   return launch<MODE, 256>(p, a, b, ca, cb, st);
@@ -660,9 +729,21 @@ int launch_r(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const 
 
 }  // namespace
 
-extern "C" uint64_t uwc_gemm_workspace_bytes(int flags) {
-  // hashed GEMMs keep two units of tile messages per CTA (one CTA per SM)
+namespace {
+// Workspace layout: tile messages (hashed calls), then the int32 product when a hashed call writes
+// bf16 (the second pass reads it back; I32 / F32 outputs hold it in place).
+uint64_t msg_bytes(int flags) {
   return (flags & UWC_FLAG_HASH) ? (uint64_t)uwc_num_sms() * 2 * kMsgWords * 4 : 0;
+}
+bool needs_acc_buffer(int flags, int out_mode) {
+  return (flags & UWC_FLAG_HASH) && out_mode == UWC_OUT_BF16;
+}
+}  // namespace
+
+extern "C" uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mode) {
+  uint64_t bytes = msg_bytes(flags);
+  if (needs_acc_buffer(flags, out_mode) && m > 0 && n > 0) bytes += (uint64_t)m * n * 4;
+  return bytes;
 }
 
 extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
@@ -687,7 +768,8 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
        ((uintptr_t)workspace)) & 15)
     return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
-  if (hash && (!workspace || workspace_bytes < uwc_gemm_workspace_bytes(flags))) return UWC_ERR_SCRATCH;
+  const uint64_t need = uwc_gemm_workspace_bytes(m, n, flags, out_mode);
+  if (need && (!workspace || workspace_bytes < need)) return UWC_ERR_SCRATCH;
 
   Params p{};
   p.m = m; p.n = n; p.k = k; p.r = r;
@@ -696,13 +778,12 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   p.a_scale = a_scale; p.b_scale = b_scale; p.out = out;
   p.msgbuf = static_cast<uint32_t*>(workspace);
   p.status = uwc_status_ptr();
-  const int mode = (hash && !denoise && out_mode == UWC_OUT_NONE) ? MODE_MINE : ((hash || denoise) ? MODE_FWD : MODE_PLAIN);
-  const int UM = mode == MODE_MINE ? 256 : 128;
-  p.nm = (m + UM - 1) / UM;
   p.nn = (n + kUN - 1) / kUN;
-  p.nunits = p.nm * p.nn;
+  cudaStream_t st = (cudaStream_t)stream;
 
   CUtensorMap ta, tb, tca, tcb;
+  // A-side boxes: 256 rows for the mining schedule, 128 otherwise
+  const int UM = hash ? 256 : 128;
   int rc = uwc_make_tmap_2d(&ta, A, (uint64_t)m, (uint64_t)k, (uint64_t)k, UM, kKB);
   if (rc == UWC_OK) rc = uwc_make_tmap_2d(&tb, B, (uint64_t)n, (uint64_t)k, (uint64_t)k, kUN, kKB);
   if (rc != UWC_OK) return rc;
@@ -714,8 +795,38 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     tca = ta;
     tcb = tb;
   }
-  cudaStream_t st = (cudaStream_t)stream;
-  if (mode == MODE_MINE) return launch_r<MODE_MINE>(p, ta, tb, tca, tcb, st);
-  if (mode == MODE_FWD) return launch_r<MODE_FWD>(p, ta, tb, tca, tcb, st);
-  return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
+
+  if (!hash) {
+    p.nm = (m + 127) / 128;
+    p.nunits = p.nm * p.nn;
+    if (denoise) return launch<MODE_FWD, 0>(p, ta, tb, tca, tcb, st);
+    return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
+  }
+
+  // Hashed: the mining schedule hashes every tile. With an output it also stores the finished
+  // product as raw int32, into `out` (I32 / F32 outputs, rewritten in place) or into the workspace
+  // (BF16); a second pass then writes out = acc - R (R = 0 without denoising), scaled.
+  int32_t* acc = nullptr;
+  if (out_mode != UWC_OUT_NONE) {
+    acc = needs_acc_buffer(flags, out_mode)
+              ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + msg_bytes(flags))
+              : static_cast<int32_t*>(out);
+    p.out = acc;
+    p.out_mode = UWC_OUT_I32;
+  }
+  p.nm = (m + 255) / 256;
+  p.nunits = p.nm * p.nn;
+  rc = out_mode == UWC_OUT_NONE ? launch_r<MODE_MINE>(p, ta, tb, tca, tcb, st)
+                                : launch_r<MODE_MINE_OUT>(p, ta, tb, tca, tcb, st);
+  const bool second_pass = out_mode != UWC_OUT_NONE && (denoise || out_mode != UWC_OUT_I32);
+  if (rc != UWC_OK || !second_pass) return rc;
+
+  Params q = p;
+  q.hash = 0;
+  q.out = out;
+  q.out_mode = out_mode;
+  q.acc_in = acc;
+  q.nm = (m + 127) / 128;
+  q.nunits = q.nm * q.nn;
+  return launch<MODE_CORR, 0>(q, ta, tb, tca, tcb, st);
 }

@@ -29,7 +29,7 @@ SIGNATURES = {
     "uwc_noise_rows": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _I32, _P, _I32, _P]),
     "uwc_proj_matrix": (_I32, [_P, _I32, _I32, _P, _P]),
     "uwc_proj_corr": (_I32, [_P, _I32, _I32, _P, _I32, _P, _I32, _P]),
-    "uwc_gemm_workspace_bytes": (_U64, [_I32]),
+    "uwc_gemm_workspace_bytes": (_U64, [_I32, _I32, _I32, _I32]),
     "uwc_gemm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32,
                         _P, _U64, _P]),
 }

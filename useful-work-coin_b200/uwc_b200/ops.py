@@ -168,10 +168,11 @@ def project(src: torch.Tensor, St: torch.Tensor, corr: torch.Tensor, corr_off: i
 _GEMM_WS: dict = {}
 
 
-def gemm_workspace(device, flags: int) -> torch.Tensor | None:
-    """Per-device workspace of the hashed GEMM (tile-message buffers), allocated once. Callers
-    serialize on one stream per device (like the reference's shared workspace, ops.py:258-277)."""
-    nbytes = int(lib().uwc_gemm_workspace_bytes(flags))
+def gemm_workspace(device, m: int, n: int, flags: int, out_mode: int) -> torch.Tensor | None:
+    """Per-device workspace of the hashed GEMM (tile messages; the int32 product of a denoised bf16
+    forward), grown on demand. Callers serialize on one stream per device (like the reference's
+    shared workspace, ops.py:258-277)."""
+    nbytes = int(lib().uwc_gemm_workspace_bytes(m, n, flags, out_mode))
     if nbytes == 0:
         return None
     key = str(torch.device(device))
@@ -190,7 +191,7 @@ def gemm(A, B, *, r=128, flags=0, corrA=None, corrB=None, maxabs=None, key=None,
     if flags:
         assert m % 64 == 0 and n % 64 == 0 and k % 64 == 0 and r % 64 == 0 and k % r == 0, (m, n, k, r)
     lmax = corrA.shape[0] if corrA is not None else 0
-    ws = gemm_workspace(A.device, flags)
+    ws = gemm_workspace(A.device, m, n, flags, out_mode)
     check(lib().uwc_gemm(_p(A), _p(B), m, n, k, r, flags, _p(corrA), _p(corrB), _p(maxabs), lmax, _p(key), _p(target),
                          _p(wins), max_wins, _p(a_scale), _p(b_scale), _p(out), out_mode, _p(ws),
                          0 if ws is None else ws.numel(), _stream()), "gemm")
