@@ -139,6 +139,43 @@ int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int f
              uint32_t* wins, int max_wins, const float* a_scale, const float* b_scale, void* out, int out_mode,
              void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- deterministic linear: producers
+ * and consumers of the int8 GEMM, bit-identical to runtime/detrt's emulated-fp32 ops (every + - * /
+ * sqrt rounded once, detrt's order; exact maxima; int64 fixed-point sums). One CTA per row; rows of
+ * up to 51200 values. bs: Hadamard block size, 0/1 = none, else a power of two dividing k.
+ * Pointers to device memory; x rows 16-byte aligned, q rows 4-byte aligned, k % 4 == 0. */
+
+/* detrt.core.quant_act (runtime/detrt/core.py:188-196; GPU form runtime/detgpu/kernels.py:75-115):
+ * y = fwht(x, bs), s = max(max|y|, 1e-8) / 64, q = clamp(rint(y / s), -64, 64) (int8 m x k),
+ * scale = s * (1 / sqrt(bs)) when bs > 1 else s (float32 m). */
+int uwc_quant_act(const float* x, int m, int k, int bs, int8_t* q, float* scale, void* stream);
+/* The same from bf16 rows: ops.quant_rows_had (miner/ampere/uwc_ampere/ops.py:172-181, kernels.cu:723-778). */
+int uwc_quant_rows_had(const uint16_t* x_bf16, int m, int k, int bs, int8_t* q, float* scale, void* stream);
+/* quant_act split for a row-parallel (column-sharded) linear; no counterpart in the reference,
+ * which has no tensor parallelism. fwht_absmax: amax[i] = max|fwht(x_i, bs)| of this shard.
+ * quant_act_global: quant_act of this shard with the row absmax amax[i] given (the max over all
+ * shards, e.g. after an all-reduce MAX): identical q and scale to quant_act on the full row. */
+int uwc_fwht_absmax(const float* x, int m, int k, int bs, float* amax, void* stream);
+int uwc_quant_act_global(const float* x, int m, int k, int bs, const float* amax, int8_t* q, float* scale,
+                         void* stream);
+/* quant_act(det_rmsnorm(x, w, eps), bs) (runtime/detgpu/kernels.py:117-191, 712-728): the
+ * normalized row stays on chip. eps is rounded to float32 as detrt does. */
+int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, int bs, double eps, int8_t* q, float* scale,
+                      void* stream);
+/* quant_act(det_silu(g) * u, bs) with [g | u] = fmul(fmul(float(acc), s3[i]), sw[j]) of the gate/up
+ * GEMM output acc (int32 m x 2I) (runtime/detgpu/kernels.py:356-396, 816-826); q: int8 m x I. */
+int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float* sw, int m, int I, int bs, int8_t* q,
+                     float* scale, void* stream);
+/* out = x + fmul(fmul(float(acc), s[i]), sw[j]) (runtime/detgpu/kernels.py:346-354, 805-813). */
+int uwc_dequant_residual(const int32_t* acc, const float* s, const float* sw, const float* x, int m, int k,
+                         float* out, void* stream);
+/* The qkv GEMM output (int32 N x (H + 2 Hkv) * 128) -> int8 q (N,H,128), k, v (N,Hkv,128) with
+ * per-head float32 scales (runtime/detgpu/kernels.py:303-344, 788-802): dequant, q/k head RMSNorm
+ * when qknorm (Qwen3), rope with cos_t / sin_t rows (row r uses position r % T), quant_sym(127). */
+int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
+                 const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps, int qknorm,
+                 int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,205 @@
+"""CPU oracle for the deterministic int8 linear's producers and consumers -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU legs may import this module.
+
+A numpy restatement of runtime/detrt's emulated-fp32 primitives (paths inside
+srivassid/useful-work-coin) and of the fused detgpu row kernels built from them:
+
+  fadd / fsub / fmul / fdiv / fsqrt (one rounding per op)   runtime/detrt/core.py:53-70
+  pow2_f32, pow2_f64                                         runtime/detrt/core.py:74-82
+  exact_rowsum (int64 fixed point, row-max scale)            runtime/detrt/core.py:85-108
+  det_exp (degree-7 2^f polynomial), det_silu                runtime/detrt/core.py:103-127,146-148
+  det_rmsnorm                                                runtime/detrt/core.py:151-159
+  quant_sym, fwht, quant_act                                 runtime/detrt/core.py:162-196
+  deq = fmul(fmul(float(acc), s), sw)                        runtime/detgpu/kernels.py:35
+  rmsnorm_quant (norm fused into the quantizer)              runtime/detgpu/kernels.py:117-191
+  qkv_post (dequant, q/k head RMSNorm, rope, quant_sym 127)  runtime/detgpu/kernels.py:303-344,
+                                                             runtime/detrt/fast.py:108-120
+  dequant_residual (x + deq(acc))                            runtime/detgpu/kernels.py:346-354
+  swiglu_quant (quant_act(silu(gate) * up))                  runtime/detgpu/kernels.py:356-396
+
+numpy float32 arithmetic on x86-64 is IEEE single precision with one rounding per operation,
+which is exactly detrt's float64-then-round emulation for + - * / sqrt; the helpers below still
+spell the float64 round trip out. Pinned by tests/test_det_oracle.py against vectors that
+tests/golden/make_golden_det.py produced with detrt itself.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+F32, F64 = np.float32, np.float64
+
+# detrt.core._EXP2 / _LOG2E (core.py:100-102): the project's own exp polynomial
+EXP2 = [1.0, 0.6931471824645996, 0.2402263879776001, 0.055505119264125824, 0.00961404386907816,
+        0.001342222560197115, 0.0001435537706129253, 2.1489791834028438e-05]
+LOG2E = 1.4426950408889634
+
+
+def c32(v: float) -> np.float32:
+    return F32(F64(v))
+
+
+def fadd(a, b):
+    return (np.asarray(a, F32).astype(F64) + np.asarray(b, F32).astype(F64)).astype(F32)
+
+
+def fsub(a, b):
+    return (np.asarray(a, F32).astype(F64) - np.asarray(b, F32).astype(F64)).astype(F32)
+
+
+def fmul(a, b):
+    return (np.asarray(a, F32).astype(F64) * np.asarray(b, F32).astype(F64)).astype(F32)
+
+
+def fdiv(a, b):
+    return (np.asarray(a, F32).astype(F64) / np.asarray(b, F32).astype(F64)).astype(F32)
+
+
+def fsqrt(a):
+    return np.sqrt(np.asarray(a, F32).astype(F64)).astype(F32)
+
+
+def pow2_f32(n):
+    return ((np.asarray(n).astype(np.int32) + 127) << 23).astype(np.int32).view(F32)
+
+
+def pow2_f64(n):
+    return ((np.asarray(n).astype(np.int64) + 1023) << 52).astype(np.int64).view(F64)
+
+
+def exact_rowsum(x: np.ndarray, max_terms: int) -> np.ndarray:
+    """Order-independent row sum: each term rounded once to int64 at 2^shift (core.py:85-108)."""
+    x = np.asarray(x, F32)
+    L = max(1, math.ceil(math.log2(max_terms)))
+    amax = np.abs(x).max(axis=-1, keepdims=True)
+    _, e = np.frexp(amax)
+    shift = np.clip((62 - L) - e.astype(np.int64), -1000, 1000)
+    q = np.rint(x.astype(F64) * pow2_f64(shift)).astype(np.int64)
+    s = q.sum(axis=-1, keepdims=True)
+    return (s.astype(F64) * pow2_f64(-shift)).astype(F32)[..., 0]
+
+
+def det_exp(z: np.ndarray) -> np.ndarray:
+    z = np.asarray(z, F32)
+    t = fmul(z, c32(LOG2E))
+    under = t < c32(-126.0)
+    over = t >= c32(128.0)
+    t = np.where(under | over | np.isnan(t), F32(0), t).astype(F32)
+    n = np.floor(t).astype(F32)
+    f = fsub(t, n)
+    p = np.full_like(f, c32(EXP2[7]))
+    for cf in reversed(EXP2[:7]):
+        p = fadd(fmul(p, f), c32(cf))
+    r = fmul(p, pow2_f32(n))
+    r = np.where(under, F32(0), r)
+    r = np.where(over, F32(np.inf), r)
+    return np.where(np.isnan(z), z, r).astype(F32)
+
+
+def det_silu(x: np.ndarray) -> np.ndarray:
+    x = np.asarray(x, F32)
+    return fdiv(x, fadd(c32(1.0), det_exp(-x)))
+
+
+def det_rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.asarray(x, F32)
+    d = x.shape[-1]
+    ss = exact_rowsum(fmul(x, x), d)
+    mean = fmul(ss, c32(1.0 / d))
+    r = fdiv(c32(1.0), fsqrt(fadd(mean, c32(eps))))
+    return fmul(fmul(x, r[..., None]), np.asarray(w, F32))
+
+
+def quant_sym(x: np.ndarray, qmax: int):
+    x = np.asarray(x, F32)
+    amax = np.abs(x).max(axis=-1, keepdims=True)
+    s = fdiv(np.maximum(amax, c32(1e-8)), c32(float(qmax)))
+    q = np.clip(np.rint(fdiv(x, s)), -qmax, qmax)
+    return q, s
+
+
+def fwht(x: np.ndarray, bs: int) -> np.ndarray:
+    """Unnormalized block Walsh-Hadamard transform, stages h = 1, 2, 4, ...: (a, b) -> (a+b, a-b)."""
+    v = np.asarray(x, F32)
+    if bs <= 1:
+        return v.copy()
+    shp = v.shape
+    k = shp[-1]
+    v = v.reshape(-1, k)
+    h = 1
+    while h < bs:
+        v = v.reshape(v.shape[0], k // (2 * h), 2, h)
+        a, b = v[:, :, 0, :], v[:, :, 1, :]
+        v = np.stack([fadd(a, b), fsub(a, b)], axis=2).reshape(-1, k)
+        h *= 2
+    return v.reshape(shp)
+
+
+def quant_act(x: np.ndarray, bs: int, qmax: int = 64):
+    """(int8 q, float32 scale) with the 1/sqrt(bs) normalization folded into the scale."""
+    y = fwht(x, bs)
+    q, s = quant_sym(y, qmax)
+    if bs > 1:
+        s = fmul(s, fdiv(c32(1.0), fsqrt(c32(float(bs)))))
+    return q.astype(np.int8), s[..., 0]
+
+
+def quant_act_global(x: np.ndarray, bs: int, amax: np.ndarray, qmax: int = 64):
+    """quant_act of a column shard whose row absmax (of the transformed row) is `amax`, the max
+    over all shards: the row-parallel tensor-parallel form. Same q and scale as the full row."""
+    y = fwht(x, bs)
+    s = fdiv(np.maximum(np.asarray(amax, F32)[:, None], c32(1e-8)), c32(float(qmax)))
+    q = np.clip(np.rint(fdiv(y, s)), -qmax, qmax)
+    if bs > 1:
+        s = fmul(s, fdiv(c32(1.0), fsqrt(c32(float(bs)))))
+    return q.astype(np.int8), s[..., 0]
+
+
+def fwht_absmax(x: np.ndarray, bs: int) -> np.ndarray:
+    return np.abs(fwht(x, bs)).max(axis=-1)
+
+
+def deq(acc: np.ndarray, s: np.ndarray, sw: np.ndarray) -> np.ndarray:
+    return fmul(fmul(np.asarray(acc, np.int32).astype(F32), np.asarray(s, F32)[:, None]), np.asarray(sw, F32)[None, :])
+
+
+def rmsnorm_quant(x: np.ndarray, w: np.ndarray, eps: float, bs: int):
+    return quant_act(det_rmsnorm(x, w, eps), bs)
+
+
+def dequant_residual(acc: np.ndarray, s: np.ndarray, sw: np.ndarray, x: np.ndarray) -> np.ndarray:
+    return fadd(np.asarray(x, F32), deq(acc, s, sw))
+
+
+def swiglu_quant(acc: np.ndarray, s3: np.ndarray, sw: np.ndarray, bs: int):
+    I = acc.shape[1] // 2
+    gu = deq(acc, s3, sw)
+    return quant_act(fmul(det_silu(gu[:, :I]), gu[:, I:]), bs)
+
+
+def qkv_post(acc, s1, sw, qnw, knw, cos, sin, T: int, H: int, Hkv: int, eps: float, qknorm: bool = True):
+    """(qq (N,H,128) int8, qs (N,H,1) f32, kq, ks, vq, vs) from the qkv GEMM's int32 output.
+    Row r of acc is token position r % T; cos / sin are (T or more, 128) float32 tables."""
+    hd = 128
+    N = acc.shape[0]
+    qkv = deq(acc, s1, sw)
+    q = qkv[:, :H * hd].reshape(N, H, hd)
+    k = qkv[:, H * hd:(H + Hkv) * hd].reshape(N, Hkv, hd)
+    v = qkv[:, (H + Hkv) * hd:].reshape(N, Hkv, hd)
+    if qknorm:
+        q = det_rmsnorm(q, qnw, eps)
+        k = det_rmsnorm(k, knw, eps)
+    pos = np.arange(N) % T
+    c = np.asarray(cos, F32)[pos][:, None, :]
+    sn = np.asarray(sin, F32)[pos][:, None, :]
+    half = hd // 2
+
+    def rope(z):
+        return fadd(fmul(z, c), fmul(np.concatenate([-z[..., half:], z[..., :half]], -1), sn))
+    qq, qs = quant_sym(rope(q), 127)
+    kq, ks = quant_sym(rope(k), 127)
+    vq, vs = quant_sym(v, 127)
+    i8 = lambda z: z.astype(np.int8)
+    return i8(qq), qs, i8(kq), ks, i8(vq), vs

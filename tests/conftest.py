@@ -34,3 +34,10 @@ def dev():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="session")
+def det_golden():
+    """Vectors from the reference's detrt (tests/golden/make_golden_det.py)."""
+    import numpy as np
+    return dict(np.load(os.path.join(GOLDEN, "det_golden.npz")))

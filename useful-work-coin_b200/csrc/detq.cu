@@ -1,0 +1,413 @@
+// Producers and consumers of the deterministic int8 linear (runtime/detrt, runtime/detgpu), sm_100a.
+//
+// Each kernel reproduces detrt's emulated-fp32 arithmetic bit for bit: every + - * / sqrt is an
+// explicitly rounded IEEE intrinsic (__fadd_rn, __fmul_rn, __fdiv_rn, __fsqrt_rn), which the
+// compiler never contracts, applied in detrt's order; maxima are exact and sums are detrt's int64
+// fixed point, so neither depends on how threads split a row.
+//
+//   quant_act         fwht(bs) + quant_sym(64) + 1/sqrt(bs) scale fold   runtime/detrt/core.py:171-196
+//   quant_rows_had    the same from bf16 rows (the mined bf16 linear)      miner/ampere/uwc_ampere/kernels.cu:717-778
+//   fwht_absmax /     the row-parallel split of quant_act: per-shard max,  (tensor-parallel form, new)
+//   quant_act_global  then quantize with the max over shards
+//   rmsnorm_quant     det_rmsnorm then quant_act                           runtime/detgpu/kernels.py:117-191
+//   swiglu_quant      quant_act(det_silu(gate) * up) of the dequantized    runtime/detgpu/kernels.py:356-396
+//                     gate/up GEMM output
+//   dequant_residual  x + fmul(fmul(float(acc), s), sw)                    runtime/detgpu/kernels.py:346-354
+//   qkv_post          dequant, q/k head RMSNorm, rope, quant_sym(127)      runtime/detgpu/kernels.py:303-344
+//
+// Row kernels keep one row in shared memory (one CTA of 256 threads per row) and read / write HBM
+// once; they are bandwidth-bound by design.
+#include <algorithm>
+
+#include "uwc_device.cuh"
+#include "uwc_host.h"
+
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr int kMaxRowSmem = 200 * 1024;   // k <= 51200 floats per row
+
+// detrt.core._EXP2 and _LOG2E (core.py:100-102), rounded to float32 as detrt's c32 does.
+__constant__ const float kExp2[8] = {(float)1.0, (float)0.6931471824645996, (float)0.2402263879776001,
+                            (float)0.055505119264125824, (float)0.00961404386907816, (float)0.001342222560197115,
+                            (float)0.0001435537706129253, (float)2.1489791834028438e-05};
+constexpr float kLog2e = (float)1.4426950408889634;
+constexpr float kTiny = (float)1e-8;
+
+__device__ __forceinline__ float pow2f(int n) { return __int_as_float((n + 127) << 23); }
+__device__ __forceinline__ double pow2d(int n) { return __longlong_as_double((long long)(n + 1023) << 52); }
+
+// detrt.core.det_exp (core.py:111-127): 2^(z log2 e) as 2^n * poly(f), one rounding per op.
+__device__ __forceinline__ float det_exp(float z) {
+  float t = __fmul_rn(z, kLog2e);
+  const bool under = t < -126.0f, over = t >= 128.0f;
+  if (under || over || isnan(t)) t = 0.0f;
+  const float n = floorf(t);
+  const float f = __fsub_rn(t, n);
+  float p = kExp2[7];
+#pragma unroll
+  for (int i = 6; i >= 0; i--) p = __fadd_rn(__fmul_rn(p, f), kExp2[i]);
+  float r = __fmul_rn(p, pow2f((int)n));
+  if (under) r = 0.0f;
+  if (over) r = __int_as_float(0x7f800000);
+  if (isnan(z)) r = z;
+  return r;
+}
+
+__device__ __forceinline__ float deq(int acc, float s, float sw) { return __fmul_rn(__fmul_rn(__int2float_rn(acc), s), sw); }
+
+__device__ __forceinline__ float warp_maxf(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ long long warp_sumll(long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide max / int64 sum over kRowThreads threads (exact, any order).
+__device__ float block_maxf(float v, float* red) {
+  v = warp_maxf(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int i = 1; i < kRowThreads / 32; i++) m = fmaxf(m, red[i]);
+  return m;
+}
+__device__ long long block_sumll(long long v, long long* red) {
+  v = warp_sumll(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  long long s = 0;
+#pragma unroll
+  for (int i = 0; i < kRowThreads / 32; i++) s += red[i];
+  return s;
+}
+
+// In-place unnormalized block Walsh-Hadamard transform of a shared-memory row (core.py:171-185):
+// stages h = 1, 2, 4, ... < bs, pairs (i, i + h) of each 2h-block -> (a + b, a - b).
+__device__ void fwht_row(float* row, int k, int bs) {
+  for (int lh = 0; (1 << lh) < bs; lh++) {
+    const int h = 1 << lh;
+    for (int p = threadIdx.x; p < (k >> 1); p += kRowThreads) {
+      const int i = ((p >> lh) << (lh + 1)) | (p & (h - 1)), j = i + h;
+      const float a = row[i], b = row[j];
+      row[i] = __fadd_rn(a, b);
+      row[j] = __fsub_rn(a, b);
+    }
+    __syncthreads();
+  }
+}
+
+// quant_sym of the staged row with row absmax `amax` and qmax = 64 (core.py:162-168), then the
+// quant_act scale fold (core.py:188-196).
+__device__ void quant_row64(const float* row, int k, int bs, float amax, int8_t* q, float* scale_out) {
+  const float s = __fdiv_rn(fmaxf(amax, kTiny), 64.0f);
+  for (int i = threadIdx.x * 4; i < k; i += kRowThreads * 4) {
+    uint32_t o = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float v = fminf(fmaxf(rintf(__fdiv_rn(row[i + j], s)), -64.f), 64.f);
+      o |= ((uint32_t)(uint8_t)(int8_t)(int)v) << (8 * j);
+    }
+    *reinterpret_cast<uint32_t*>(q + i) = o;
+  }
+  if (threadIdx.x == 0) *scale_out = bs > 1 ? __fmul_rn(s, __fdiv_rn(1.0f, __fsqrt_rn((float)bs))) : s;
+}
+
+__device__ float row_absmax(const float* row, int k, float* red) {
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < k; i += kRowThreads) mx = fmaxf(mx, fabsf(row[i]));
+  return block_maxf(mx, red);
+}
+
+// Stage row r of x (fp32 or bf16, k % 4 == 0) into shared memory.
+template <bool BF16>
+__device__ void load_row(const void* x, int r, int k, float* row) {
+  if (BF16) {
+    const uint2* src = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + (uint64_t)r * k);
+    for (int i = threadIdx.x; i < k / 4; i += kRowThreads) {
+      const uint2 v = src[i];
+      row[4 * i] = __uint_as_float(v.x << 16);
+      row[4 * i + 1] = __uint_as_float(v.x & 0xFFFF0000u);
+      row[4 * i + 2] = __uint_as_float(v.y << 16);
+      row[4 * i + 3] = __uint_as_float(v.y & 0xFFFF0000u);
+    }
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + (uint64_t)r * k);
+    for (int i = threadIdx.x; i < k / 4; i += kRowThreads) reinterpret_cast<float4*>(row)[i] = src[i];
+  }
+  __syncthreads();
+}
+
+// MODE 0: quant_act (local absmax). MODE 1: only the transformed row's absmax -> amax[r].
+// MODE 2: quantize with amax[r] given (the max over the row's column shards).
+template <int MODE, bool BF16>
+__global__ void __launch_bounds__(kRowThreads) k_quant_act(const void* __restrict__ x, int k, int bs,
+                                                           float* __restrict__ amax, int8_t* __restrict__ q,
+                                                           float* __restrict__ scale) {
+  extern __shared__ float row[];
+  __shared__ float red[kRowThreads / 32];
+  const int r = blockIdx.x;
+  load_row<BF16>(x, r, k, row);
+  if (bs > 1) fwht_row(row, k, bs);
+  if (MODE == 2) {
+    quant_row64(row, k, bs, amax[r], q + (uint64_t)r * k, scale + r);
+    return;
+  }
+  const float mx = row_absmax(row, k, red);
+  if (MODE == 1) {
+    if (threadIdx.x == 0) amax[r] = mx;
+    return;
+  }
+  quant_row64(row, k, bs, mx, q + (uint64_t)r * k, scale + r);
+}
+
+// det_rmsnorm (core.py:151-159, exact_rowsum core.py:85-108) then quant_act.
+__global__ void __launch_bounds__(kRowThreads) k_rmsnorm_quant(const float* __restrict__ x, const float* __restrict__ w,
+                                                               int k, int bs, float inv_d, float eps, int L,
+                                                               int8_t* __restrict__ q, float* __restrict__ scale) {
+  extern __shared__ float row[];
+  __shared__ float red[kRowThreads / 32];
+  __shared__ long long redl[kRowThreads / 32];
+  const int r = blockIdx.x;
+  load_row<false>(x, r, k, row);
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < k; i += kRowThreads) mx = fmaxf(mx, __fmul_rn(row[i], row[i]));
+  mx = block_maxf(mx, red);
+  int e;
+  frexpf(mx, &e);
+  const int sh = min(max((62 - L) - e, -1000), 1000);
+  const double up = pow2d(sh);
+  long long acc = 0;
+  for (int i = threadIdx.x; i < k; i += kRowThreads) acc += __double2ll_rn((double)__fmul_rn(row[i], row[i]) * up);
+  acc = block_sumll(acc, redl);
+  const float ss = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+  const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_d), eps)));
+  for (int i = threadIdx.x; i < k; i += kRowThreads) row[i] = __fmul_rn(__fmul_rn(row[i], rr), w[i]);
+  __syncthreads();
+  if (bs > 1) fwht_row(row, k, bs);
+  const float am = row_absmax(row, k, red);
+  quant_row64(row, k, bs, am, q + (uint64_t)r * k, scale + r);
+}
+
+// quant_act(fmul(det_silu(gate), up)) of the dequantized gate/up GEMM output (N x 2I int32).
+__global__ void __launch_bounds__(kRowThreads) k_swiglu_quant(const int32_t* __restrict__ acc,
+                                                              const float* __restrict__ s3, const float* __restrict__ sw,
+                                                              int I, int bs, int8_t* __restrict__ q,
+                                                              float* __restrict__ scale) {
+  extern __shared__ float row[];
+  __shared__ float red[kRowThreads / 32];
+  const int r = blockIdx.x;
+  const float s = s3[r];
+  const int32_t* ar = acc + (uint64_t)r * 2 * I;
+  for (int i = threadIdx.x; i < I; i += kRowThreads) {
+    const float g = deq(ar[i], s, sw[i]), u = deq(ar[I + i], s, sw[I + i]);
+    row[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, det_exp(-g))), u);
+  }
+  __syncthreads();
+  if (bs > 1) fwht_row(row, I, bs);
+  const float am = row_absmax(row, I, red);
+  quant_row64(row, I, bs, am, q + (uint64_t)r * I, scale + r);
+}
+
+// out = fadd(x, deq(acc)), 4 elements per thread (k % 4 == 0).
+__global__ void k_dequant_residual(const int32_t* __restrict__ acc, const float* __restrict__ s,
+                                   const float* __restrict__ sw, const float* __restrict__ x, int k, uint64_t n4,
+                                   float* __restrict__ out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t e = 4 * i, r = e / k;
+    const int c = (int)(e - r * k);
+    const int4 a = reinterpret_cast<const int4*>(acc)[i];
+    const float4 xv = reinterpret_cast<const float4*>(x)[i];
+    const float4 w = *reinterpret_cast<const float4*>(sw + c);
+    const float sr = s[r];
+    float4 o;
+    o.x = __fadd_rn(xv.x, deq(a.x, sr, w.x));
+    o.y = __fadd_rn(xv.y, deq(a.y, sr, w.y));
+    o.z = __fadd_rn(xv.z, deq(a.z, sr, w.z));
+    o.w = __fadd_rn(xv.w, deq(a.w, sr, w.w));
+    reinterpret_cast<float4*>(out)[i] = o;
+  }
+}
+
+// quant_sym(qmax = 127) of one 128-wide head held as element lane + 32 j in v[j].
+__device__ __forceinline__ void head_quant127(const float* v, int lane, int8_t* q, float* scale) {
+  float mx = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; j++) mx = fmaxf(mx, fabsf(v[j]));
+  mx = warp_maxf(mx);
+  const float s = __fdiv_rn(fmaxf(mx, kTiny), 127.0f);
+#pragma unroll
+  for (int j = 0; j < 4; j++) q[lane + 32 * j] = (int8_t)(int)fminf(fmaxf(rintf(__fdiv_rn(v[j], s)), -127.f), 127.f);
+  if (lane == 0) *scale = s;
+}
+
+// The qkv GEMM's int32 row -> quantized q, k, v heads (detrt/fast.py:108-120). One CTA per row
+// (token), one warp per head; element i of a head is v[j] of lane i % 32 with j = i / 32, so the
+// rope partner i +- 64 is v[j +- 2] of the same lane.
+__global__ void __launch_bounds__(kRowThreads) k_qkv_post(
+    const int32_t* __restrict__ acc, const float* __restrict__ s1, const float* __restrict__ sw,
+    const float* __restrict__ qnw, const float* __restrict__ knw, const float* __restrict__ cosT,
+    const float* __restrict__ sinT, int T, int H, int Hkv, float inv_hd, float eps, int qknorm,
+    int8_t* __restrict__ qq, float* __restrict__ qs, int8_t* __restrict__ kq, float* __restrict__ ks,
+    int8_t* __restrict__ vq, float* __restrict__ vs) {
+  const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nh = H + 2 * Hkv, width = nh * 128, t = row % T;
+  const float s = s1[row];
+  for (int hh = warp; hh < nh; hh += kRowThreads / 32) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int c = hh * 128 + lane + 32 * j;
+      v[j] = deq(acc[(uint64_t)row * width + c], s, sw[c]);
+    }
+    if (hh >= H + Hkv) {
+      const int hv = hh - H - Hkv;
+      head_quant127(v, lane, vq + ((uint64_t)row * Hkv + hv) * 128, vs + (uint64_t)row * Hkv + hv);
+      continue;
+    }
+    if (qknorm) {
+      // det_rmsnorm over the head (exact_rowsum with max_terms = 128, so L = 7)
+      float mx = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; j++) mx = fmaxf(mx, __fmul_rn(v[j], v[j]));
+      mx = warp_maxf(mx);
+      int e;
+      frexpf(mx, &e);
+      const int sh = min(max((62 - 7) - e, -1000), 1000);
+      long long a = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) a += __double2ll_rn((double)__fmul_rn(v[j], v[j]) * pow2d(sh));
+      a = warp_sumll(a);
+      const float ss = __double2float_rn(__ll2double_rn(a) * pow2d(-sh));
+      const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_hd), eps)));
+      const float* w = hh < H ? qnw : knw;
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] = __fmul_rn(__fmul_rn(v[j], rr), w[lane + 32 * j]);
+    }
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int i = lane + 32 * j;
+      const float rot = j < 2 ? -v[j + 2] : v[j - 2];
+      o[j] = __fadd_rn(__fmul_rn(v[j], cosT[t * 128 + i]), __fmul_rn(rot, sinT[t * 128 + i]));
+    }
+    if (hh < H)
+      head_quant127(o, lane, qq + ((uint64_t)row * H + hh) * 128, qs + (uint64_t)row * H + hh);
+    else
+      head_quant127(o, lane, kq + ((uint64_t)row * Hkv + hh - H) * 128, ks + (uint64_t)row * Hkv + hh - H);
+  }
+}
+
+// smallest L >= 1 with 2^L >= n (detrt's ceil(log2(max_terms)))
+int ceil_log2(int n) {
+  int L = 1;
+  while ((1 << L) < n) L++;
+  return L;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+int row_smem_ok(int k, const void* kernel) {
+  if (4 * k > kMaxRowSmem) return UWC_ERR_SHAPE;
+  if (4 * k > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxRowSmem) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  return UWC_OK;
+}
+
+bool bs_ok(int k, int bs) { return bs <= 1 || ((bs & (bs - 1)) == 0 && k % bs == 0); }
+
+template <int MODE, bool BF16>
+int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, float* scale, void* stream) {
+  if (!x || m < 0 || k <= 0 || k % 4 || !bs_ok(k, bs)) return UWC_ERR_ARG;
+  if (MODE != 1 && (!q || !scale)) return UWC_ERR_ARG;
+  if (MODE != 0 && !amax) return UWC_ERR_ARG;
+  if (!aligned16(x) || (q && ((uintptr_t)q & 3))) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  const int rc = row_smem_ok(k, (const void*)k_quant_act<MODE, BF16>);
+  if (rc != UWC_OK) return rc;
+  k_quant_act<MODE, BF16><<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
+  return uwc_launch_status();
+}
+
+}  // namespace
+
+extern "C" int uwc_quant_act(const float* x, int m, int k, int bs, int8_t* q, float* scale, void* stream) {
+  return launch_quant<0, false>(x, m, k, bs, nullptr, q, scale, stream);
+}
+
+extern "C" int uwc_quant_rows_had(const uint16_t* x_bf16, int m, int k, int bs, int8_t* q, float* scale, void* stream) {
+  return launch_quant<0, true>(x_bf16, m, k, bs, nullptr, q, scale, stream);
+}
+
+extern "C" int uwc_fwht_absmax(const float* x, int m, int k, int bs, float* amax, void* stream) {
+  return launch_quant<1, false>(x, m, k, bs, amax, nullptr, nullptr, stream);
+}
+
+extern "C" int uwc_quant_act_global(const float* x, int m, int k, int bs, const float* amax, int8_t* q, float* scale,
+                                    void* stream) {
+  return launch_quant<2, false>(x, m, k, bs, const_cast<float*>(amax), q, scale, stream);
+}
+
+extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, int bs, double eps, int8_t* q,
+                                 float* scale, void* stream) {
+  if (!x || !w || !q || !scale || m < 0 || k <= 0 || k % 4 || !bs_ok(k, bs)) return UWC_ERR_ARG;
+  if (!aligned16(x) || ((uintptr_t)q & 3)) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant);
+  if (rc != UWC_OK) return rc;
+  // detrt rounds 1/d and eps from float64 to float32 (core.c32)
+  k_rmsnorm_quant<<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, (float)(1.0 / k), (float)eps,
+                                                                  ceil_log2(k), q, scale);
+  return uwc_launch_status();
+}
+
+extern "C" int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float* sw, int m, int I, int bs, int8_t* q,
+                                float* scale, void* stream) {
+  if (!acc || !s3 || !sw || !q || !scale || m < 0 || I <= 0 || I % 4 || !bs_ok(I, bs)) return UWC_ERR_ARG;
+  if ((uintptr_t)q & 3) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  const int rc = row_smem_ok(I, (const void*)k_swiglu_quant);
+  if (rc != UWC_OK) return rc;
+  k_swiglu_quant<<<m, kRowThreads, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
+  return uwc_launch_status();
+}
+
+extern "C" int uwc_dequant_residual(const int32_t* acc, const float* s, const float* sw, const float* x, int m, int k,
+                                    float* out, void* stream) {
+  if (!acc || !s || !sw || !x || !out || m < 0 || k <= 0 || k % 4) return UWC_ERR_ARG;
+  if (!aligned16(acc) || !aligned16(sw) || !aligned16(x) || !aligned16(out)) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  const uint64_t n4 = (uint64_t)m * k / 4;
+  if (n4 == 0) return UWC_OK;
+  const int grid = (int)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)uwc_num_sms() * 16);
+  k_dequant_residual<<<grid, 256, 0, (cudaStream_t)stream>>>(acc, s, sw, x, k, n4, out);
+  return uwc_launch_status();
+}
+
+extern "C" int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
+                            const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps,
+                            int qknorm, int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs,
+                            void* stream) {
+  if (!acc || !s1 || !sw || !cos_t || !sin_t || !qq || !qs || !kq || !ks || !vq || !vs) return UWC_ERR_ARG;
+  if (qknorm && (!qnw || !knw)) return UWC_ERR_ARG;
+  if (N < 0 || T <= 0 || H <= 0 || Hkv <= 0) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  if (N == 0) return UWC_OK;
+  k_qkv_post<<<N, kRowThreads, 0, (cudaStream_t)stream>>>(acc, s1, sw, qnw, knw, cos_t, sin_t, T, H, Hkv,
+                                                          (float)(1.0 / 128), (float)eps, qknorm, qq, qs, kq, ks, vq,
+                                                          vs);
+  return uwc_launch_status();
+}

@@ -15,7 +15,7 @@ OK, ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_CUDA, ERR_DEVICE, ERR_SCRATCH = range(7)
 DEV_TIMEOUT = 1
 
 # (name, restype, argtypes) for every function declared in include/uwc_b200.h
-_P, _U32, _U64, _I32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
+_P, _U32, _U64, _I32, _F64 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_double
 SIGNATURES = {
     "uwc_version": (_I32, []),
     "uwc_status_string": (ctypes.c_char_p, [_I32]),
@@ -32,6 +32,15 @@ SIGNATURES = {
     "uwc_gemm_workspace_bytes": (_U64, [_I32, _I32, _I32, _I32]),
     "uwc_gemm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32,
                         _P, _U64, _P]),
+    "uwc_quant_act": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P]),
+    "uwc_quant_rows_had": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P]),
+    "uwc_fwht_absmax": (_I32, [_P, _I32, _I32, _I32, _P, _P]),
+    "uwc_quant_act_global": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "uwc_rmsnorm_quant": (_I32, [_P, _P, _I32, _I32, _I32, _F64, _P, _P, _P]),
+    "uwc_swiglu_quant": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _P, _P]),
+    "uwc_dequant_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _P, _P]),
+    "uwc_qkv_post": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F64, _I32, _P, _P, _P, _P, _P, _P,
+                            _P]),
 }
 
 _LIB = None

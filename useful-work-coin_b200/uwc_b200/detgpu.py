@@ -1,0 +1,148 @@
+"""The deterministic int8 linear's fused producers and consumers on B200, with the names and
+semantics of runtime/detgpu/kernels.py (quant_act, rmsnorm_quant, qkv_post, dequant_residual,
+swiglu_quant) and runtime/detgpu/stages.py (linear, norm_linear), plus quant_rows_had of
+miner/ampere/uwc_ampere/ops.py:172-181. Every output is bit-identical to runtime/detrt.
+
+A linear layer `lin` is anything with `.Wq` (n x k int8, on the GPU), `.sw` (n float32) and `.bs`
+(Hadamard block), e.g. detrt.qwen3.DetLinear. Its GEMM runs on this library's tcgen05 kernel with
+the dequant fused into the epilogue (det.linear_f32), so no int32 matrix round-trips HBM.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import det
+from ._lib import check, lib
+from .ops import _count, _p, _stream
+
+
+def _f32(x: torch.Tensor) -> torch.Tensor:
+    assert x.dtype == torch.float32 and x.is_cuda, (x.dtype, x.device)
+    return x.contiguous()
+
+
+def quant_act(x: torch.Tensor, bs: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """detrt.core.quant_act(x, bs) for float32 x (rows, k): (int8 q, float32 scale)."""
+    x = _f32(x)
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty(m, dtype=torch.float32, device=x.device)
+    check(lib().uwc_quant_act(_p(x), m, k, bs, _p(q), _p(s), _stream()), "quant_act")
+    _count()
+    return q, s
+
+
+def quant_rows_had(x: torch.Tensor, bs: int, q: torch.Tensor | None = None, scale: torch.Tensor | None = None):
+    """x: m x k bf16 -> (int8 q in [-64, 64], float32 per-row scale), block Hadamard of size bs."""
+    assert x.dtype == torch.bfloat16 and x.is_contiguous()
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device) if q is None else q
+    scale = torch.empty(m, dtype=torch.float32, device=x.device) if scale is None else scale
+    check(lib().uwc_quant_rows_had(_p(x), m, k, bs, _p(q), _p(scale), _stream()), "quant_rows_had")
+    _count()
+    return q, scale
+
+
+def fwht_absmax(x: torch.Tensor, bs: int) -> torch.Tensor:
+    """Per-row max |fwht(x, bs)| of a column shard (the row-parallel quantizer's first half)."""
+    x = _f32(x)
+    m, k = x.shape
+    amax = torch.empty(m, dtype=torch.float32, device=x.device)
+    check(lib().uwc_fwht_absmax(_p(x), m, k, bs, _p(amax), _stream()), "fwht_absmax")
+    _count()
+    return amax
+
+
+def quant_act_global(x: torch.Tensor, bs: int, amax: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant_act of a column shard given the full row's transformed absmax (max over shards)."""
+    x = _f32(x)
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty(m, dtype=torch.float32, device=x.device)
+    check(lib().uwc_quant_act_global(_p(x), m, k, bs, _p(amax.contiguous()), _p(q), _p(s), _stream()),
+          "quant_act_global")
+    _count()
+    return q, s
+
+
+def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, bs: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """detrt.core.quant_act(detrt.core.det_rmsnorm(x, w, eps), bs) for float32 x (rows, k)."""
+    x, w = _f32(x), _f32(w)
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty(m, dtype=torch.float32, device=x.device)
+    check(lib().uwc_rmsnorm_quant(_p(x), _p(w), m, k, bs, float(eps), _p(q), _p(s), _stream()), "rmsnorm_quant")
+    _count()
+    return q, s
+
+
+def swiglu_quant(acc: torch.Tensor, s3: torch.Tensor, sw: torch.Tensor, bs: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant_act(det_silu(gate) * up, bs) of the gate/up GEMM's int32 output (N x 2I)."""
+    acc = acc.contiguous()
+    assert acc.dtype == torch.int32
+    N, two_i = acc.shape
+    I = two_i // 2
+    q = torch.empty((N, I), dtype=torch.int8, device=acc.device)
+    sc = torch.empty(N, dtype=torch.float32, device=acc.device)
+    check(lib().uwc_swiglu_quant(_p(acc), _p(_f32(s3)), _p(_f32(sw)), N, I, bs, _p(q), _p(sc), _stream()),
+          "swiglu_quant")
+    _count()
+    return q, sc
+
+
+def dequant_residual(acc: torch.Tensor, s: torch.Tensor, sw: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """x + fmul(fmul(float(acc), s[:, None]), sw[None, :]): the residual add after o / down."""
+    acc, x = acc.contiguous(), _f32(x)
+    assert acc.dtype == torch.int32
+    N, k = acc.shape
+    out = torch.empty((N, k), dtype=torch.float32, device=acc.device)
+    check(lib().uwc_dequant_residual(_p(acc), _p(_f32(s)), _p(_f32(sw)), _p(x), N, k, _p(out), _stream()),
+          "dequant_residual")
+    _count()
+    return out
+
+
+def qkv_post(acc, s1, sw, qnw, knw, cos, sin, T: int, H: int, Hkv: int, eps: float, qknorm: bool = True):
+    """Quantized q, k, v from the qkv GEMM's int32 output: (qq (N,H,128) int8, qs (N,H,1), kq, ks, vq, vs).
+    qknorm False (Llama, Mistral): no per-head RMSNorm before rope."""
+    acc = acc.contiguous()
+    assert acc.dtype == torch.int32
+    N = acc.shape[0]
+    dev = acc.device
+    e = lambda *shape, dt=torch.int8: torch.empty(shape, dtype=dt, device=dev)
+    qq, qs = e(N, H, 128), e(N, H, 1, dt=torch.float32)
+    kq, ks = e(N, Hkv, 128), e(N, Hkv, 1, dt=torch.float32)
+    vq, vs = e(N, Hkv, 128), e(N, Hkv, 1, dt=torch.float32)
+    qn = _f32(qnw) if qknorm else None
+    kn = _f32(knw) if qknorm else None
+    check(lib().uwc_qkv_post(_p(acc), _p(_f32(s1)), _p(_f32(sw)), _p(qn), _p(kn), _p(_f32(cos)), _p(_f32(sin)),
+                             N, T, H, Hkv, float(eps), int(bool(qknorm)), _p(qq), _p(qs), _p(kq), _p(ks), _p(vq),
+                             _p(vs), _stream()), "qkv_post")
+    _count()
+    return qq, qs, kq, ks, vq, vs
+
+
+def linear_q(lin, q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """fmul(fmul(float(q @ Wq^T), s), sw): the dequantized GEMM of already-quantized rows."""
+    return det.linear_f32(q, s, lin.Wq, lin.sw)
+
+
+def linear(lin, x: torch.Tensor) -> torch.Tensor:
+    """runtime/detgpu/stages.py:85-93: quant_act, int8 GEMM, dequant (fused in the GEMM epilogue)."""
+    q, s = quant_act(x, lin.bs)
+    return linear_q(lin, q, s)
+
+
+def norm_linear(lin, w_norm: torch.Tensor, x: torch.Tensor, eps: float) -> torch.Tensor:
+    """runtime/detgpu/stages.py:96-104: linear(det_rmsnorm(x, w_norm, eps)) with the norm fused
+    into the quantizer."""
+    q, s = rmsnorm_quant(x, w_norm, eps, lin.bs)
+    return linear_q(lin, q, s)
+
+
+def mlp_residual(gu, down, w_norm: torch.Tensor, r1: torch.Tensor, eps: float) -> torch.Tensor:
+    """The MLP half of runtime/detgpu/stages.py layer_fused (:148-153): rmsnorm_quant, gate/up GEMM,
+    swiglu_quant, down GEMM, dequant_residual -- bit-identical to detrt.fast (:182-189)."""
+    q3, s3 = rmsnorm_quant(r1, w_norm, eps, gu.bs)
+    q4, s4 = swiglu_quant(det.int_gemm(q3, gu.Wq), s3, gu.sw, down.bs)
+    return dequant_residual(det.int_gemm(q4, down.Wq), s4, down.sw, r1)
