@@ -179,3 +179,28 @@ def test_scaled_epilogues(ops, mode):
         ops.gemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), a_scale=torch.from_numpy(sa).cuda(),
                  b_scale=torch.from_numpy(sb).cuda(), out=out, out_mode=ops.OUT_F32)
         assert np.array_equal(out.cpu().numpy().view(np.uint32), O.det_dequant(acc, sa, sb).view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n,k", [(32, 768, 4096), (1, 512, 1024), (7, 4096, 14336 // 2), (32, 14336, 4096),
+                                   (96, 256, 128 * 3 + 16)])
+@pytest.mark.parametrize("mode", ["i32", "f32", "bf16"])
+def test_skinny_split_k_gemm(ops, m, n, k, mode):
+    """Decode-sized GEMMs take the split-K schedule (int32 partials added into the product):
+    exact int32, and the fp32 / bf16 epilogues applied once to the summed product."""
+    rng = np.random.default_rng(m * 7 + n + k)
+    A = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    B = rng.integers(-64, 65, size=(n, k), dtype=np.int8)
+    acc = O.gemm_i32(A, B)
+    sa = (rng.random(m, dtype=np.float32) * 0.01 + 1e-4).astype(np.float32)
+    sb = (rng.random(n, dtype=np.float32) * 0.02 + 1e-4).astype(np.float32)
+    dt = {"i32": torch.int32, "f32": torch.float32, "bf16": torch.bfloat16}[mode]
+    om = {"i32": ops.OUT_I32, "f32": ops.OUT_F32, "bf16": ops.OUT_BF16}[mode]
+    out = torch.full((m, n), 7, dtype=dt, device="cuda")
+    ops.gemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), a_scale=torch.from_numpy(sa).cuda(),
+             b_scale=torch.from_numpy(sb).cuda(), out=out, out_mode=om)
+    if mode == "i32":
+        assert np.array_equal(out.cpu().numpy(), acc)
+    elif mode == "f32":
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), O.det_dequant(acc, sa, sb).view(np.uint32))
+    else:
+        assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), O.scaled_bf16(acc, sa, sb))

@@ -70,6 +70,7 @@ struct Params {
   int out_mode;
   int max_wins;
   int nm, nn, nunits;
+  int nsplit, kps;         // PLAIN split-K: k-block ranges per unit (nsplit 1 = whole k)
   const int32_t* maxabs;
   const uint32_t* key;
   const uint32_t* target;
@@ -120,6 +121,22 @@ __device__ __forceinline__ void unit_coords(const Params& p, int u, int UM, int&
   const int gsz = min(p.nm - first, G), in = u - gid * grp;
   m0 = (first + in % gsz) * UM;
   n0 = (in / gsz) * kUN;
+}
+
+// Unit u of a split-K PLAIN launch: output block (unit_coords of u % (nm * nn)) and the k-block
+// range [kb0, kb0 + nkb) of split u / (nm * nn). Without splitting, the whole k.
+__device__ __forceinline__ void unit_span(const Params& p, int u, int UM, int kblocks, int& m0, int& n0, int& kb0,
+                                          int& nkb) {
+  if (p.nsplit > 1) {
+    const int nmn = p.nm * p.nn, ks = u / nmn;
+    unit_coords(p, u - ks * nmn, UM, m0, n0);
+    kb0 = ks * p.kps;
+    nkb = min(kblocks - kb0, p.kps);
+  } else {
+    unit_coords(p, u, UM, m0, n0);
+    kb0 = 0;
+    nkb = kblocks;
+  }
 }
 
 // Limb count from the projections' max |value| (kernels.cu:602-607 thresholds), capped at lmax.
@@ -292,10 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t gk = 0;
       for (int u = blockIdx.x; u < p.nunits && !*abort_flag; u += gridDim.x) {
-        int m0, n0;
-        unit_coords(p, u, C::UM, m0, n0);
+        int m0, n0, kb0, nkb;
+        unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
         const int ncorr = C::CORR ? L * cblocks : 0;
-        const int nblk = ncorr + kblocks;
+        const int nblk = ncorr + nkb;
         for (int b = 0; b < nblk; b++, gk++) {
           const int s = gk % C::NST;
           const uint32_t ph = (gk / C::NST) & 1;
@@ -308,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sA, &tmCA, &bars->full[s], kb * kKB, li * p.m + m0);
             tma_load_2d(sB, &tmCB, &bars->full[s], kb * kKB, li * p.n + n0);
           } else {
-            const int kb = b - ncorr;
+            const int kb = kb0 + b - ncorr;
             tma_load_2d(sA, &tmA, &bars->full[s], kb * kKB, m0);
             tma_load_2d(sB, &tmB, &bars->full[s], kb * kKB, n0);
           }
@@ -326,8 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t smem_base = smem_u32(smem);
       constexpr uint32_t id_acc = idesc_i8(128, C::ACC_N);
       for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
-        int m0, n0;
-        unit_coords(p, u, C::UM, m0, n0);
+        int m0, n0, kb0, nkb;
+        unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
         // ---- correction accumulator R (FWD): Horner over limbs, highest limb first
         if (C::CORR && L > 0) {
           const uint32_t tR = tmem + 256;
@@ -357,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nacc = (C::MINE && m0 + 128 >= p.m) ? 1 : C::NACC;
         const int pbuf = local & 1;   // PLAIN: accumulator buffer of this unit
         const uint32_t gk0 = gk;
-        for (int kb = 0; kb < kblocks && ok; kb++) {
+        for (int kb = 0; kb < nkb && ok; kb++) {   // kb counts from this unit's first k-block
           const uint32_t g = gk0 + kb;
           const int s = g % C::NST;
           ok = mbar_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
@@ -408,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int ks = 0; ks < 4; ks++)
                 mma_i8(dcol, adesc + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
-              if (kb == kblocks - 1) {
+              if (kb == nkb - 1) {
                 mma_commit(&bars->acc_full[ba]);
                 if (MODE != MODE_PLAIN) snaps[a]++;
               }
@@ -417,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           mma_commit(&bars->empty[s]);
         }
-        gk = gk0 + kblocks;
+        gk = gk0 + nkb;
       }
       // drain: every MMA issued by this thread has completed before TMEM is released
       mma_commit(&bars->drain);
@@ -434,8 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
-      int m0, n0;
-      unit_coords(p, u, C::UM, m0, n0);
+      int m0, n0, kb0, nkb;
+      unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
       if (MODE == MODE_PLAIN) {
         const int b = local & 1;
         ok = warp_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status);
@@ -447,7 +464,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tmem_ld_32x32b_x32(lane_base + col + h * 32, v);
           tmem_wait_ld();
-          store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + h * 32, reinterpret_cast<const int32_t*>(v));
+          const int row = m0 + 32 * q + lane, c0 = n0 + cb * 64 + h * 32;
+          if (p.nsplit > 1) {
+            // split-K partial: integer adds into the zeroed int32 product commute, so the sum is
+            // exact whatever order the splits land in
+            if (row < p.m && c0 < p.n) {
+              int32_t* o = static_cast<int32_t*>(p.out) + (uint64_t)row * p.n + c0;
+#pragma unroll
+              for (int i = 0; i < 32; i++)
+                if (c0 + i < p.n) atomicAdd(o + i, (int32_t)v[i]);
+            }
+          } else {
+            store_row32(p, row, c0, reinterpret_cast<const int32_t*>(v));
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -738,11 +767,20 @@ uint64_t msg_bytes(int flags) {
 bool needs_acc_buffer(int flags, int out_mode) {
   return (flags & UWC_FLAG_HASH) && out_mode == UWC_OUT_BF16;
 }
+// Skinny plain GEMMs (decode-sized m, tensor-parallel shards of n) have fewer 128 x 256 output
+// blocks than half the SMs: they split k across units and add int32 partials.
+bool split_k(int m, int n) {
+  const int blocks = ((m + 127) / 128) * ((n + kUN - 1) / kUN);
+  return 2 * blocks <= uwc_num_sms();
+}
 }  // namespace
 
 extern "C" uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mode) {
   uint64_t bytes = msg_bytes(flags);
   if (needs_acc_buffer(flags, out_mode) && m > 0 && n > 0) bytes += (uint64_t)m * n * 4;
+  // split-K with a scaled output: the int32 product is summed here, then scaled by a second pass
+  if (!flags && (out_mode == UWC_OUT_F32 || out_mode == UWC_OUT_BF16) && m > 0 && n > 0 && split_k(m, n))
+    bytes += (uint64_t)m * n * 4;
   return bytes;
 }
 
@@ -796,11 +834,39 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     tcb = tb;
   }
 
+  const int kblocks = (k + kKB - 1) / kKB;
+  p.nsplit = 1;
+  p.kps = kblocks;
   if (!hash) {
     p.nm = (m + 127) / 128;
     p.nunits = p.nm * p.nn;
     if (denoise) return launch<MODE_FWD, 0>(p, ta, tb, tca, tcb, st);
-    return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
+    if (out_mode == UWC_OUT_NONE || !split_k(m, n) || kblocks < 2)
+      return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
+    // split-K: each unit owns a k-block range of one output block and adds its int32 partial into
+    // the zeroed product (`out` itself for I32, else the workspace, scaled by a second pass)
+    const int splits = std::min(kblocks, std::max(1, uwc_num_sms() / p.nunits));
+    p.kps = (kblocks + splits - 1) / splits;
+    p.nsplit = (kblocks + p.kps - 1) / p.kps;
+    int32_t* acc = out_mode == UWC_OUT_I32 ? static_cast<int32_t*>(out)
+                                           : reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + msg_bytes(flags));
+    if (cudaMemsetAsync(acc, 0, (size_t)m * n * 4, st) != cudaSuccess) {
+      cudaGetLastError();
+      return UWC_ERR_CUDA;
+    }
+    p.out = acc;
+    p.out_mode = UWC_OUT_I32;
+    p.nunits *= p.nsplit;
+    rc = launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
+    if (rc != UWC_OK || out_mode == UWC_OUT_I32) return rc;
+    Params q = p;
+    q.nsplit = 1;
+    q.kps = kblocks;
+    q.nunits = q.nm * q.nn;
+    q.out = out;
+    q.out_mode = out_mode;
+    q.acc_in = acc;
+    return launch<MODE_CORR, 0>(q, ta, tb, tca, tcb, st);
   }
 
   // Hashed: the mining schedule hashes every tile. With an output it also stores the finished
@@ -823,6 +889,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
 
   Params q = p;
   q.hash = 0;
+  q.nsplit = 1;
   q.out = out;
   q.out_mode = out_mode;
   q.acc_in = acc;
