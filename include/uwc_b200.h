@@ -166,7 +166,12 @@ int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, int bs, doub
  * GEMM output acc (int32 m x 2I) (runtime/detgpu/kernels.py:356-396, 816-826); q: int8 m x I. */
 int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float* sw, int m, int I, int bs, int8_t* q,
                      float* scale, void* stream);
-/* out = x + fmul(fmul(float(acc), s[i]), sw[j]) (runtime/detgpu/kernels.py:346-354, 805-813). */
+/* h = fmul(det_silu(g), u) as fp32 (m x I): the input of a row-parallel down projection, which
+ * quantizes its own column shard (uwc_fwht_absmax / uwc_quant_act_global). No counterpart in the
+ * reference (it has no tensor parallelism); same per-element ops as uwc_swiglu_quant. m <= 65535. */
+int uwc_swiglu(const int32_t* acc, const float* s3, const float* sw, int m, int I, float* h, void* stream);
+/* out = x + fmul(fmul(float(acc), s[i]), sw[j]) (runtime/detgpu/kernels.py:346-354, 805-813);
+ * x may be NULL: out = fmul(fmul(float(acc), s[i]), sw[j]), the plain dequant. */
 int uwc_dequant_residual(const int32_t* acc, const float* s, const float* sw, const float* x, int m, int k,
                          float* out, void* stream);
 /* The qkv GEMM output (int32 N x (H + 2 Hkv) * 128) -> int8 q (N,H,128), k, v (N,Hkv,128) with

@@ -1,0 +1,73 @@
+"""Tensor-parallel linears on 2+ GPUs over NCCL with this library's CUDA kernels: the MLP block and
+a row-parallel projection at Llama-3.1-8B widths (hidden 4096, MLP 14336), at decode (M = 32) and
+prefill-like M, bit-identical to the same layer on one GPU. Skipped with fewer than 2 GPUs."""
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _weights(Dm, I):
+    g = torch.Generator().manual_seed(8)
+    gq = torch.randint(-64, 65, (2 * I, Dm), dtype=torch.int8, generator=g)
+    dq = torch.randint(-64, 65, (Dm, I), dtype=torch.int8, generator=g)
+    gs = torch.rand(2 * I, generator=g) * 1e-3 + 1e-5
+    ds = torch.rand(Dm, generator=g) * 1e-3 + 1e-5
+    wn = 1 + 0.1 * torch.randn(Dm, generator=g)
+    return gq, gs, dq, ds, wn
+
+
+def _worker(rank, world, port, outdir, Dm, I, ms):
+    for p in (os.path.join(HERE, ".."), os.path.join(HERE, "..", "useful-work-coin_b200")):
+        sys.path.insert(0, os.path.abspath(p))
+    import torch.distributed as dist
+    from uwc_b200 import tp
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        gq, gs, dq, ds, wn = _weights(Dm, I)
+        mlp = tp.TPMLP(gq, gs, 512, dq, ds, 512, rank, world, dev)
+        res = {}
+        for m in ms:
+            r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
+            res[f"y{m}"] = mlp.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
+        torch.cuda.synchronize()
+        np.savez(os.path.join(outdir, f"rank{rank}.npz"), **res)
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_mlp_nccl_matches_one_gpu(tmp_path):
+    world = min(torch.cuda.device_count(), 8)
+    Dm, I, ms = 4096, 14336, (32, 300)
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), Dm, I, ms), nprocs=world, join=True)
+    from uwc_b200 import detgpu
+
+    class Lin:
+        def __init__(self, Wq, sw, bs):
+            self.Wq, self.sw, self.bs = Wq.cuda(), sw.cuda(), bs
+    gq, gs, dq, ds, wn = _weights(Dm, I)
+    gu, down = Lin(gq, gs, 512), Lin(dq, ds, 512)
+    for m in ms:
+        r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).cuda()
+        ref = detgpu.mlp_residual(gu, down, wn.cuda(), r1, 1e-5).cpu().numpy()
+        for r in range(world):
+            y = np.load(os.path.join(tmp_path, f"rank{r}.npz"))[f"y{m}"]
+            assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), (m, r)

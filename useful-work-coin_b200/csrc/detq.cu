@@ -12,6 +12,7 @@
 //   rmsnorm_quant     det_rmsnorm then quant_act                           runtime/detgpu/kernels.py:117-191
 //   swiglu_quant      quant_act(det_silu(gate) * up) of the dequantized    runtime/detgpu/kernels.py:356-396
 //                     gate/up GEMM output
+//   swiglu            the fp32 fmul(det_silu(gate), up) row (tensor-parallel form, new)
 //   dequant_residual  x + fmul(fmul(float(acc), s), sw)                    runtime/detgpu/kernels.py:346-354
 //   qkv_post          dequant, q/k head RMSNorm, rope, quant_sym(127)      runtime/detgpu/kernels.py:303-344
 //
@@ -196,7 +197,13 @@ __global__ void __launch_bounds__(kRowThreads) k_rmsnorm_quant(const float* __re
   quant_row64(row, k, bs, am, q + (uint64_t)r * k, scale + r);
 }
 
-// quant_act(fmul(det_silu(gate), up)) of the dequantized gate/up GEMM output (N x 2I int32).
+// fmul(det_silu(gate), up) of the dequantized gate/up GEMM output (N x 2I int32)
+__device__ __forceinline__ float swiglu_at(const int32_t* ar, float s, const float* sw, int I, int i) {
+  const float g = deq(ar[i], s, sw[i]), u = deq(ar[I + i], s, sw[I + i]);
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, det_exp(-g))), u);
+}
+
+// quant_act(fmul(det_silu(gate), up)) of the gate/up GEMM output, one row per CTA.
 __global__ void __launch_bounds__(kRowThreads) k_swiglu_quant(const int32_t* __restrict__ acc,
                                                               const float* __restrict__ s3, const float* __restrict__ sw,
                                                               int I, int bs, int8_t* __restrict__ q,
@@ -206,17 +213,23 @@ __global__ void __launch_bounds__(kRowThreads) k_swiglu_quant(const int32_t* __r
   const int r = blockIdx.x;
   const float s = s3[r];
   const int32_t* ar = acc + (uint64_t)r * 2 * I;
-  for (int i = threadIdx.x; i < I; i += kRowThreads) {
-    const float g = deq(ar[i], s, sw[i]), u = deq(ar[I + i], s, sw[I + i]);
-    row[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, det_exp(-g))), u);
-  }
+  for (int i = threadIdx.x; i < I; i += kRowThreads) row[i] = swiglu_at(ar, s, sw, I, i);
   __syncthreads();
   if (bs > 1) fwht_row(row, I, bs);
   const float am = row_absmax(row, I, red);
   quant_row64(row, I, bs, am, q + (uint64_t)r * I, scale + r);
 }
 
-// out = fadd(x, deq(acc)), 4 elements per thread (k % 4 == 0).
+// The fp32 SwiGLU row alone (the input of a row-parallel down projection, quantized per shard).
+__global__ void k_swiglu(const int32_t* __restrict__ acc, const float* __restrict__ s3, const float* __restrict__ sw,
+                         int I, float* __restrict__ h) {
+  const int r = blockIdx.y;
+  const int32_t* ar = acc + (uint64_t)r * 2 * I;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < I; i += gridDim.x * blockDim.x)
+    h[(uint64_t)r * I + i] = swiglu_at(ar, s3[r], sw, I, i);
+}
+
+// out = fadd(x, deq(acc)) (x == nullptr: out = deq(acc)), 4 elements per thread (k % 4 == 0).
 __global__ void k_dequant_residual(const int32_t* __restrict__ acc, const float* __restrict__ s,
                                    const float* __restrict__ sw, const float* __restrict__ x, int k, uint64_t n4,
                                    float* __restrict__ out) {
@@ -224,14 +237,13 @@ __global__ void k_dequant_residual(const int32_t* __restrict__ acc, const float*
     const uint64_t e = 4 * i, r = e / k;
     const int c = (int)(e - r * k);
     const int4 a = reinterpret_cast<const int4*>(acc)[i];
-    const float4 xv = reinterpret_cast<const float4*>(x)[i];
     const float4 w = *reinterpret_cast<const float4*>(sw + c);
     const float sr = s[r];
-    float4 o;
-    o.x = __fadd_rn(xv.x, deq(a.x, sr, w.x));
-    o.y = __fadd_rn(xv.y, deq(a.y, sr, w.y));
-    o.z = __fadd_rn(xv.z, deq(a.z, sr, w.z));
-    o.w = __fadd_rn(xv.w, deq(a.w, sr, w.w));
+    float4 o = make_float4(deq(a.x, sr, w.x), deq(a.y, sr, w.y), deq(a.z, sr, w.z), deq(a.w, sr, w.w));
+    if (x) {
+      const float4 xv = reinterpret_cast<const float4*>(x)[i];
+      o = make_float4(__fadd_rn(xv.x, o.x), __fadd_rn(xv.y, o.y), __fadd_rn(xv.z, o.z), __fadd_rn(xv.w, o.w));
+    }
     reinterpret_cast<float4*>(out)[i] = o;
   }
 }
@@ -385,10 +397,19 @@ extern "C" int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float
   return uwc_launch_status();
 }
 
+extern "C" int uwc_swiglu(const int32_t* acc, const float* s3, const float* sw, int m, int I, float* h, void* stream) {
+  if (!acc || !s3 || !sw || !h || m < 0 || I <= 0) return UWC_ERR_ARG;
+  if (m > 65535) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  k_swiglu<<<dim3((I + 255) / 256, m), 256, 0, (cudaStream_t)stream>>>(acc, s3, sw, I, h);
+  return uwc_launch_status();
+}
+
 extern "C" int uwc_dequant_residual(const int32_t* acc, const float* s, const float* sw, const float* x, int m, int k,
                                     float* out, void* stream) {
-  if (!acc || !s || !sw || !x || !out || m < 0 || k <= 0 || k % 4) return UWC_ERR_ARG;
-  if (!aligned16(acc) || !aligned16(sw) || !aligned16(x) || !aligned16(out)) return UWC_ERR_ALIGN;
+  if (!acc || !s || !sw || !out || m < 0 || k <= 0 || k % 4) return UWC_ERR_ARG;
+  if (!aligned16(acc) || !aligned16(sw) || (x && !aligned16(x)) || !aligned16(out)) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   const uint64_t n4 = (uint64_t)m * k / 4;
   if (n4 == 0) return UWC_OK;

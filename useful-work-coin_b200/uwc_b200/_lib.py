@@ -38,6 +38,7 @@ SIGNATURES = {
     "uwc_quant_act_global": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
     "uwc_rmsnorm_quant": (_I32, [_P, _P, _I32, _I32, _I32, _F64, _P, _P, _P]),
     "uwc_swiglu_quant": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _P, _P]),
+    "uwc_swiglu": (_I32, [_P, _P, _P, _I32, _I32, _P, _P]),
     "uwc_dequant_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _P, _P]),
     "uwc_qkv_post": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F64, _I32, _P, _P, _P, _P, _P, _P,
                             _P]),

@@ -90,9 +90,11 @@ def swiglu_quant(acc: torch.Tensor, s3: torch.Tensor, sw: torch.Tensor, bs: int)
     return q, sc
 
 
-def dequant_residual(acc: torch.Tensor, s: torch.Tensor, sw: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
-    """x + fmul(fmul(float(acc), s[:, None]), sw[None, :]): the residual add after o / down."""
-    acc, x = acc.contiguous(), _f32(x)
+def dequant_residual(acc: torch.Tensor, s: torch.Tensor, sw: torch.Tensor, x: torch.Tensor | None) -> torch.Tensor:
+    """x + fmul(fmul(float(acc), s[:, None]), sw[None, :]): the residual add after o / down
+    (x None: the dequantized product alone)."""
+    acc = acc.contiguous()
+    x = None if x is None else _f32(x)
     assert acc.dtype == torch.int32
     N, k = acc.shape
     out = torch.empty((N, k), dtype=torch.float32, device=acc.device)
@@ -100,6 +102,21 @@ def dequant_residual(acc: torch.Tensor, s: torch.Tensor, sw: torch.Tensor, x: to
           "dequant_residual")
     _count()
     return out
+
+
+def dequant(acc: torch.Tensor, s: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    return dequant_residual(acc, s, sw, None)
+
+
+def swiglu(acc: torch.Tensor, s3: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
+    """fp32 fmul(det_silu(gate), up) of the gate/up GEMM's int32 output (N x 2I) -> N x I."""
+    acc = acc.contiguous()
+    assert acc.dtype == torch.int32
+    N, two_i = acc.shape
+    h = torch.empty((N, two_i // 2), dtype=torch.float32, device=acc.device)
+    check(lib().uwc_swiglu(_p(acc), _p(_f32(s3)), _p(_f32(sw)), N, two_i // 2, _p(h), _stream()), "swiglu")
+    _count()
+    return h
 
 
 def qkv_post(acc, s1, sw, qnw, knw, cos, sin, T: int, H: int, Hkv: int, eps: float, qknorm: bool = True):

@@ -1,0 +1,139 @@
+"""Tensor-parallel deterministic int8 linears over torch.distributed (NCCL over NVLink on B200s).
+
+New: the reference splits a model only into pipeline stages of whole layers
+(runtime/detrt/qwen3.py:151-158); these layers split single linears across GPUs and stay
+bit-identical to one device:
+
+  ColumnParallelLinear  rows of W (output features) split across ranks; each rank computes its
+                        output columns with the dequant fused into the GEMM; `gather` concatenates.
+  RowParallelLinear     columns of W (input features) split on Hadamard-block boundaries. Each rank
+                        transforms its activation shard, the row absmax is all-reduced with MAX
+                        (exact), every rank quantizes with the full row's scale (so q is the full
+                        row's q, sliced), multiplies its shard, and the int32 partial products are
+                        all-reduced with SUM -- exact, since integer addition is associative --
+                        before the dequant (+ residual).
+  TPMLP                 the MLP block of runtime/detrt/fast.py:182-189: rmsnorm_quant on the
+                        replicated input, gate/up column-parallel on the down projection's k shards,
+                        fp32 SwiGLU, row-parallel down projection with the residual add.
+
+`kernels` is the device backend: by default this library's CUDA kernels (GPUKernels); tests pass
+a CPU stand-in built from the oracle to check the sharding and collectives with gloo ranks.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def even_bounds(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
+    """[lo, hi) of `rank`'s share of n items cut on multiples of `align` (n % align == 0), as even
+    as the alignment allows; earlier ranks take the remainder."""
+    assert n % align == 0, (n, align)
+    units = n // align
+    base, extra = divmod(units, world)
+    lo = rank * base + min(rank, extra)
+    hi = lo + base + (1 if rank < extra else 0)
+    return lo * align, hi * align
+
+
+class GPUKernels:
+    """The CUDA backend (uwc_b200.detgpu / uwc_b200.det)."""
+
+    @staticmethod
+    def _mods():
+        from . import det, detgpu
+        return det, detgpu
+
+    def linear_f32(self, q, s, Wq, sw):
+        return self._mods()[0].linear_f32(q, s, Wq, sw)
+
+    def int_gemm(self, q, Wq):
+        return self._mods()[0].int_gemm(q, Wq)
+
+    def fwht_absmax(self, x, bs):
+        return self._mods()[1].fwht_absmax(x, bs)
+
+    def quant_act_global(self, x, bs, amax):
+        return self._mods()[1].quant_act_global(x, bs, amax)
+
+    def rmsnorm_quant(self, x, w, eps, bs):
+        return self._mods()[1].rmsnorm_quant(x, w, eps, bs)
+
+    def swiglu(self, acc, s3, sw):
+        return self._mods()[1].swiglu(acc, s3, sw)
+
+    def dequant_residual(self, acc, s, sw, x):
+        return self._mods()[1].dequant_residual(acc, s, sw, x)
+
+
+def _default(kernels):
+    return GPUKernels() if kernels is None else kernels
+
+
+class ColumnParallelLinear:
+    """W (n x k int8, per-row scales sw) split by output rows; forward(q, s) -> this rank's columns."""
+
+    def __init__(self, Wq: torch.Tensor, sw: torch.Tensor, bs: int, rank: int, world: int, device, kernels=None,
+                 group=None):
+        n = Wq.shape[0]
+        self.n, self.bs, self.group, self.world = n, bs, group, world
+        self.lo, self.hi = even_bounds(n, world, rank, 4 if n % 4 == 0 else 1)
+        self.Wq = Wq[self.lo:self.hi].contiguous().to(device)
+        self.sw = sw[self.lo:self.hi].contiguous().to(device)
+        self.K = _default(kernels)
+
+    def forward(self, q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+        return self.K.linear_f32(q, s, self.Wq, self.sw)
+
+    def gather(self, y_local: torch.Tensor) -> torch.Tensor:
+        """The full output (m x n) on every rank: all_gather of the column shards (exact copies)."""
+        parts = [torch.empty((y_local.shape[0], hi - lo), dtype=y_local.dtype, device=y_local.device)
+                 for lo, hi in (even_bounds(self.n, self.world, r, 4 if self.n % 4 == 0 else 1)
+                                for r in range(self.world))]
+        dist.all_gather(parts, y_local.contiguous(), group=self.group)
+        return torch.cat(parts, dim=1)
+
+
+class RowParallelLinear:
+    """W (n x k) split by input columns on Hadamard-block boundaries; forward(x_shard) -> full output."""
+
+    def __init__(self, Wq: torch.Tensor, sw: torch.Tensor, bs: int, rank: int, world: int, device, kernels=None,
+                 group=None, bounds: tuple[int, int] | None = None):
+        n, k = Wq.shape
+        self.n, self.k, self.bs, self.group = n, k, bs, group
+        align = max(bs, 16)
+        self.lo, self.hi = bounds if bounds is not None else even_bounds(k, world, rank, align)
+        assert self.lo % align == 0 and self.hi % align == 0, "shards must hold whole Hadamard blocks"
+        self.Wq = Wq[:, self.lo:self.hi].contiguous().to(device)
+        self.sw = sw.contiguous().to(device)
+        self.K = _default(kernels)
+
+    def forward(self, x_shard: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        K = self.K
+        amax = K.fwht_absmax(x_shard, self.bs)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        q, s = K.quant_act_global(x_shard, self.bs, amax)
+        acc = K.int_gemm(q, self.Wq)
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
+        return K.dequant_residual(acc, s, self.sw, residual)
+
+
+class TPMLP:
+    """gate/up (2I x D, gate rows then up rows) and down (D x I) split over the ranks of `group`."""
+
+    def __init__(self, gu_Wq, gu_sw, gu_bs: int, down_Wq, down_sw, down_bs: int, rank: int, world: int, device,
+                 kernels=None, group=None):
+        I = down_Wq.shape[1]
+        assert gu_Wq.shape[0] == 2 * I
+        lo, hi = even_bounds(I, world, rank, max(down_bs, 16))
+        self.gu_bs = gu_bs
+        self.gu_Wq = torch.cat([gu_Wq[lo:hi], gu_Wq[I + lo:I + hi]]).contiguous().to(device)
+        self.gu_sw = torch.cat([gu_sw[lo:hi], gu_sw[I + lo:I + hi]]).contiguous().to(device)
+        self.down = RowParallelLinear(down_Wq, down_sw, down_bs, rank, world, device, kernels, group, (lo, hi))
+        self.K = _default(kernels)
+
+    def forward(self, r1: torch.Tensor, w_norm: torch.Tensor, eps: float) -> torch.Tensor:
+        K = self.K
+        q3, s3 = K.rmsnorm_quant(r1, w_norm, eps, self.gu_bs)
+        h = K.swiglu(K.int_gemm(q3, self.gu_Wq), s3, self.gu_sw)
+        return self.down.forward(h, residual=r1)
