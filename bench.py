@@ -36,7 +36,13 @@ WORKLOADS = {
     "c3-mine": (8192, 14336, 4096, 64, "NoisyGEMM noise mining, Llama-3.1-8B MLP shape (configs[2])"),
     "c3-mine-r128": (8192, 14336, 4096, 128, "configs[2] shape at the consensus rank 128"),
     "c2-forward": (4096, 4096, 4096, 64, "NoisyGEMM mining block with denoise + int32 output (configs[1])"),
+    # one Llama-3.1-8B layer's deterministic int8 linears, tensor-parallel over the ranks
+    "c5-decode": (32, 4096, 14336, 0, "Llama-3.1-8B layer linears, TP over ranks, batch-32 decode (configs[4])"),
+    "c5-prefill": (16384, 4096, 14336, 0, "Llama-3.1-8B layer linears, TP over ranks, M=16384 prefill (configs[4])"),
 }
+# Llama-3.1-8B linears of one layer: (name, n, k, kind); qkv n = (32 + 2 * 8) * 128
+C5_LINEARS = [("qkv", 6144, 4096, "col"), ("o", 4096, 4096, "row"), ("gate_up", 28672, 4096, "col"),
+              ("down", 4096, 14336, "row")]
 
 
 def parse():
@@ -198,9 +204,45 @@ def cpu_baseline(m, n, k, r, budget_s=15.0):
                       f"{dt:.1f} s on {th} threads (oracle/uwc_oracle.c)"}
 
 
+def c5_cpu_sample(m, seed=0):
+    """The layer's four linears on the host as runtime/detrt's CPU DetLinear.int_gemm computes them
+    (float64 matmul of int8-valued operands, qwen3.py:111-113) for `m` rows. (seconds, ops, bytes, threads)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    t, ops, nbytes = 0.0, 0.0, 0.0
+    for _, n, k, _ in C5_LINEARS:
+        W = torch.randint(-64, 65, (n, k), dtype=torch.int8, generator=g).to(torch.float64)
+        q = torch.randint(-127, 128, (m, k), dtype=torch.int8, generator=g).to(torch.float64)
+        t0 = time.perf_counter()
+        (q @ W.t()).to(torch.int32)
+        t += time.perf_counter() - t0
+        ops += 2.0 * m * n * k
+        nbytes += n * k
+    return t, ops, nbytes, torch.get_num_threads()
+
+
 def run_reference(a, world, rank):
     m, n, k, r, desc = WORKLOADS[a.workload]
     if rank != 0:
+        return
+    if a.workload.startswith("c5"):
+        decode = a.workload == "c5-decode"
+        rows = m if decode else 256
+        tot_t = tot_ops = tot_b = 0.0
+        for i in range(a.warmup + a.steps):
+            dt, ops_, nb, th = c5_cpu_sample(rows, seed=i)
+            if i >= a.warmup:
+                tot_t, tot_ops, tot_b = tot_t + dt, tot_ops + ops_, tot_b + nb
+        value = tot_b / tot_t / 1e9 if decode else tot_ops / tot_t / 1e12
+        unit = "GB/s (int8 weights streamed)" if decode else "int8 TOPS"
+        sample = f"{rows} rows through the 4 linears per step (float64 host matmul, DetLinear CPU path), {th} threads"
+        line = {"impl": "reference", "metric": C5_METRIC, "value": value, "unit": unit, "n_gpus": a.gpus,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot_t / a.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)",
+                "config": {"workload": a.workload, "m": m, "desc": desc},
+                "cpu_baseline": {"value": value, "unit": unit, "cores": th, "kind": "port", "sample": sample},
+                "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     vals = []
     sample = None
@@ -221,7 +263,114 @@ def run_reference(a, world, rank):
     print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------------ GPU arm
+# ------------------------------------------------------------------ GPU arm, configs[4]
+C5_METRIC = "Deterministic int8 linear, Llama-3.1-8B layer, tensor-parallel (int8 TOPS prefill / weight GB/s decode)"
+
+
+def run_c5(a, world, rank, local):
+    """One step = the layer's four linears on this library, TP over the ranks: rmsnorm_quant +
+    qkv (column-parallel), o (row-parallel, + residual), then the MLP block (gate/up column-parallel,
+    SwiGLU, down row-parallel, + residual). Attention is not part of the path: o_proj reads a seeded
+    activation shard. Every int32 partial product is summed by NCCL all-reduce (exact)."""
+    import torch
+
+    from uwc_b200 import _lib, detgpu, ops, tp
+    m = WORKLOADS[a.workload][0]
+    decode = a.workload == "c5-decode"
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _lib.device_status(clear=True)
+    g = torch.Generator(device=dev).manual_seed(77)
+    W = {nm: torch.randint(-64, 65, (n, k), dtype=torch.int8, device=dev, generator=g) for nm, n, k, _ in C5_LINEARS}
+    S = {nm: torch.rand(n, device=dev, generator=g) * 1e-3 + 1e-5 for nm, n, _, _ in C5_LINEARS}
+    D, bs = 4096, 512
+    qkv = tp.ColumnParallelLinear(W["qkv"], S["qkv"], bs, rank, world, dev)
+    o = tp.RowParallelLinear(W["o"], S["o"], bs, rank, world, dev)
+    mlp = tp.TPMLP(W["gate_up"], S["gate_up"], bs, W["down"], S["down"], bs, rank, world, dev)
+    del W
+    wn = 1 + 0.1 * torch.randn(D, device=dev, generator=g)
+    x = torch.randn(m, D, device=dev, generator=g)
+    oc = torch.randn(m, o.hi - o.lo, device=dev, generator=g)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step(xin):
+        q1, s1 = detgpu.rmsnorm_quant(xin, wn, 1e-5, bs)
+        qkv.forward(q1, s1)
+        r1 = o.forward(oc, residual=xin)
+        return mlp.forward(r1, wn, 1e-5)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(a.warmup):
+        step(x)
+    barrier(world)
+    l0 = ops.LAUNCHES
+    sampler = ClockSampler(local)
+    sampler.start()
+    evs = []
+    for i in range(a.steps):
+        flush.fill_(i & 0xFF)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step(x)
+        e1.record(stream)
+        evs.append((e0, e1))
+    barrier(world)
+    clocks = sampler.stop()
+    launches = ops.LAUNCHES - l0
+    t_ms = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs), world)
+    ops_step = sum(2.0 * m * n * k for _, n, k, _ in C5_LINEARS)
+    wbytes = sum(n * k for _, n, k, _ in C5_LINEARS)               # int8 weights, all ranks together
+    value = (wbytes if decode else ops_step) * a.steps / (t_ms / 1e3) / (1e9 if decode else 1e12)
+    unit = "GB/s (int8 weights streamed)" if decode else "int8 TOPS"
+    # e2e: activations in from pinned host memory, the layer output back, every step
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((m, D), dtype=torch.float32).pin_memory()
+    xd = torch.empty_like(x)
+    ev2 = []
+    barrier(world)
+    for i in range(a.steps):
+        flush.fill_(i & 0xFF)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        xd.copy_(x_host, non_blocking=True)
+        y_host.copy_(step(xd), non_blocking=True)
+        e1.record(stream)
+        ev2.append((e0, e1))
+    barrier(world)
+    t2 = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev2), world)
+    e2e = (wbytes if decode else ops_step) * a.steps / (t2 / 1e3) / (1e9 if decode else 1e12)
+    pk = peaks()
+    per_rank = value / world
+    status = _lib.device_status(clear=True)
+    if rank != 0:
+        return
+    if decode:
+        roof = {"bound": "hbm", "achieved": per_rank, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": per_rank / pk["hbm_gbs"], "traffic": None, "kernel": "whole step (weight stream)",
+                "peak_source": pk["src"]}
+    else:
+        peak_tops = int8_peak(8192, 8192, 4096, flush)
+        roof = {"bound": "tensor", "achieved": per_rank, "peak": peak_tops, "unit": "TOP/s",
+                "frac": per_rank / peak_tops, "traffic": None, "kernel": "whole step",
+                "peak_source": "cuBLASLt int8 8192^2 x 4096 burst, measured in this run"}
+    line = {"metric": C5_METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (seeded int8 weights and fp32 activations)",
+            "config": {"workload": a.workload, "m": m, "desc": WORKLOADS[a.workload][4],
+                       "linears": [f"{nm} {n}x{k} {kind}" for nm, n, k, kind in C5_LINEARS],
+                       "parallelism": f"tp{world}", "l2": "flushed (256 MiB write) before each step"},
+            "roofline": roof,
+            "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": m * D * 4, "d2h_bytes_per_step": m * D * 4},
+            "gpu_launches": launches, "clocks": clocks, "device_status": status}
+    if not a.no_cpu_baseline:
+        rows = m if decode else 128
+        dt, ops_, nb, th = c5_cpu_sample(rows)
+        v = nb / dt / 1e9 if decode else ops_ / dt / 1e12
+        line["cpu_baseline"] = {"value": v, "unit": unit, "cores": th, "kind": "port",
+                                "sample": f"{rows} rows through the 4 linears (float64 host matmul), {dt:.1f} s"}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm, NoisyGEMM
 def run_b200(a, world, rank, local):
     import numpy as np
     import torch
@@ -350,6 +499,8 @@ def main():
     try:
         if a.impl == "reference":
             run_reference(a, world, rank)
+        elif a.workload.startswith("c5"):
+            run_c5(a, world, rank, local)
         else:
             run_b200(a, world, rank, local)
     finally:

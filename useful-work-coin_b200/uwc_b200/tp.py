@@ -25,6 +25,12 @@ import torch
 import torch.distributed as dist
 
 
+def _all_reduce(t: torch.Tensor, op, group) -> None:
+    """all_reduce over `group`; a no-op for a single rank (no process group needed)."""
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(t, op=op, group=group)
+
+
 def even_bounds(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
     """[lo, hi) of `rank`'s share of n items cut on multiples of `align` (n % align == 0), as even
     as the alignment allows; earlier ranks take the remainder."""
@@ -90,6 +96,8 @@ class ColumnParallelLinear:
         parts = [torch.empty((y_local.shape[0], hi - lo), dtype=y_local.dtype, device=y_local.device)
                  for lo, hi in (even_bounds(self.n, self.world, r, 4 if self.n % 4 == 0 else 1)
                                 for r in range(self.world))]
+        if self.world == 1:
+            return y_local
         dist.all_gather(parts, y_local.contiguous(), group=self.group)
         return torch.cat(parts, dim=1)
 
@@ -111,10 +119,10 @@ class RowParallelLinear:
     def forward(self, x_shard: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         K = self.K
         amax = K.fwht_absmax(x_shard, self.bs)
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        _all_reduce(amax, dist.ReduceOp.MAX, self.group)
         q, s = K.quant_act_global(x_shard, self.bs, amax)
         acc = K.int_gemm(q, self.Wq)
-        dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
+        _all_reduce(acc, dist.ReduceOp.SUM, self.group)
         return K.dequant_residual(acc, s, self.sw, residual)
 
 
