@@ -40,6 +40,8 @@ WORKLOADS = {
     "c5-decode": (32, 4096, 14336, 0, "Llama-3.1-8B layer linears, TP over ranks, batch-32 decode (configs[4])"),
     "c5-prefill": (16384, 4096, 14336, 0, "Llama-3.1-8B layer linears, TP over ranks, M=16384 prefill (configs[4])"),
 }
+# DRAM bytes per launch of the dominant kernel from one ncu capture (committed summary under profiles/)
+TRAFFIC = {"c3-mine": 149.4e6 + 3.9e6}
 # Llama-3.1-8B linears of one layer: (name, n, k, kind); qkv n = (32 + 2 * 8) * 128
 C5_LINEARS = [("qkv", 6144, 4096, "col"), ("o", 4096, 4096, "row"), ("gate_up", 28672, 4096, "col"),
               ("down", 4096, 14336, "row")]
@@ -480,7 +482,10 @@ def run_b200(a, world, rank, local):
             "tiles_hashed_per_s": tiles_per_s,
             "pct_int8_peak": 100.0 * value / world / peak_tops,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOP/s",
-                         "frac": achieved / peak_tops, "traffic": None, "kernel": "k_noisy_gemm",
+                         "frac": achieved / peak_tops, "traffic": TRAFFIC.get(a.workload),
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch, "
+                                           "profiles/k_noisy_gemm_mine_r64_c3_ncu_full.md" if a.workload in TRAFFIC
+                                           else None, "kernel": "k_noisy_gemm",
                          "peak_source": "cuBLASLt int8 (torch._int_mm) on the same shape, burst, measured in "
                                         "this run (MEASURED_PEAKS.json has no int8 entry; its bf16 figure "
                                         f"{pk['bf16_tflops']} TF/s, {pk['src']})",
