@@ -192,3 +192,25 @@ def test_norm_linear_matches_oracle(dg):
     got = dg.norm_linear(lin, cu(wn), cu(x), 1e-6)
     q, s = D.rmsnorm_quant(x, wn, 1e-6, 128)
     same(got, O.det_dequant(O.gemm_i32(q, lin.Wq_np), s, lin.sw_np))
+
+
+def test_many_rows_path_matches_oracle(dg):
+    """At least as many rows as SMs take the 256-thread row CTAs (fewer rows use 1024 threads)."""
+    rng = np.random.default_rng(300)
+    x = _rows(rng, 300, 2048)
+    w = (1.0 + 0.2 * rng.standard_normal(2048)).astype(np.float32)
+    q, s = dg.quant_act(cu(x), 512)
+    wq, ws = D.quant_act(x, 512)
+    same(q, wq)
+    same(s, ws)
+    q, s = dg.rmsnorm_quant(cu(x), cu(w), 1e-6, 128)
+    wq, ws = D.rmsnorm_quant(x, w, 1e-6, 128)
+    same(q, wq)
+    same(s, ws)
+    acc = rng.integers(-(1 << 22), 1 << 22, size=(300, 2 * 1024), dtype=np.int32)
+    s3 = (rng.random(300) * 1e-4 + 1e-7).astype(np.float32)
+    sw = (rng.random(2048) * 1e-2 + 1e-5).astype(np.float32)
+    q, s = dg.swiglu_quant(cu(acc), cu(s3), cu(sw), 256)
+    wq, ws = D.swiglu_quant(acc, s3, sw, 256)
+    same(q, wq)
+    same(s, ws)

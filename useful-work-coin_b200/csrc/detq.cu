@@ -19,13 +19,16 @@
 // Row kernels keep one row in shared memory (one CTA of 256 threads per row) and read / write HBM
 // once; they are bandwidth-bound by design.
 #include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "uwc_device.cuh"
 #include "uwc_host.h"
 
 namespace {
 
-constexpr int kRowThreads = 256;
+constexpr int kRowThreads = 256;      // threads per row CTA (1024 for few-row calls)
 constexpr int kMaxRowSmem = 200 * 1024;   // k <= 51200 floats per row
 
 // detrt.core._EXP2 and _LOG2E (core.py:100-102), rounded to float32 as detrt's c32 does.
@@ -68,7 +71,8 @@ __device__ __forceinline__ long long warp_sumll(long long v) {
   return v;
 }
 
-// Block-wide max / int64 sum over kRowThreads threads (exact, any order).
+// Block-wide max / int64 sum over the CTA's NT threads (exact, any order).
+template <int NT>
 __device__ float block_maxf(float v, float* red) {
   v = warp_maxf(v);
   __syncthreads();
@@ -76,9 +80,10 @@ __device__ float block_maxf(float v, float* red) {
   __syncthreads();
   float m = red[0];
 #pragma unroll
-  for (int i = 1; i < kRowThreads / 32; i++) m = fmaxf(m, red[i]);
+  for (int i = 1; i < NT / 32; i++) m = fmaxf(m, red[i]);
   return m;
 }
+template <int NT>
 __device__ long long block_sumll(long long v, long long* red) {
   v = warp_sumll(v);
   __syncthreads();
@@ -86,16 +91,17 @@ __device__ long long block_sumll(long long v, long long* red) {
   __syncthreads();
   long long s = 0;
 #pragma unroll
-  for (int i = 0; i < kRowThreads / 32; i++) s += red[i];
+  for (int i = 0; i < NT / 32; i++) s += red[i];
   return s;
 }
 
 // In-place unnormalized block Walsh-Hadamard transform of a shared-memory row (core.py:171-185):
 // stages h = 1, 2, 4, ... < bs, pairs (i, i + h) of each 2h-block -> (a + b, a - b).
+template <int NT>
 __device__ void fwht_row(float* row, int k, int bs) {
   for (int lh = 0; (1 << lh) < bs; lh++) {
     const int h = 1 << lh;
-    for (int p = threadIdx.x; p < (k >> 1); p += kRowThreads) {
+    for (int p = threadIdx.x; p < (k >> 1); p += NT) {
       const int i = ((p >> lh) << (lh + 1)) | (p & (h - 1)), j = i + h;
       const float a = row[i], b = row[j];
       row[i] = __fadd_rn(a, b);
@@ -107,9 +113,10 @@ __device__ void fwht_row(float* row, int k, int bs) {
 
 // quant_sym of the staged row with row absmax `amax` and qmax = 64 (core.py:162-168), then the
 // quant_act scale fold (core.py:188-196).
+template <int NT>
 __device__ void quant_row64(const float* row, int k, int bs, float amax, int8_t* q, float* scale_out) {
   const float s = __fdiv_rn(fmaxf(amax, kTiny), 64.0f);
-  for (int i = threadIdx.x * 4; i < k; i += kRowThreads * 4) {
+  for (int i = threadIdx.x * 4; i < k; i += NT * 4) {
     uint32_t o = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -121,18 +128,19 @@ __device__ void quant_row64(const float* row, int k, int bs, float amax, int8_t*
   if (threadIdx.x == 0) *scale_out = bs > 1 ? __fmul_rn(s, __fdiv_rn(1.0f, __fsqrt_rn((float)bs))) : s;
 }
 
+template <int NT>
 __device__ float row_absmax(const float* row, int k, float* red) {
   float mx = 0.f;
-  for (int i = threadIdx.x; i < k; i += kRowThreads) mx = fmaxf(mx, fabsf(row[i]));
-  return block_maxf(mx, red);
+  for (int i = threadIdx.x; i < k; i += NT) mx = fmaxf(mx, fabsf(row[i]));
+  return block_maxf<NT>(mx, red);
 }
 
 // Stage row r of x (fp32 or bf16, k % 4 == 0) into shared memory.
-template <bool BF16>
+template <int NT, bool BF16>
 __device__ void load_row(const void* x, int r, int k, float* row) {
   if (BF16) {
     const uint2* src = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + (uint64_t)r * k);
-    for (int i = threadIdx.x; i < k / 4; i += kRowThreads) {
+    for (int i = threadIdx.x; i < k / 4; i += NT) {
       const uint2 v = src[i];
       row[4 * i] = __uint_as_float(v.x << 16);
       row[4 * i + 1] = __uint_as_float(v.x & 0xFFFF0000u);
@@ -141,60 +149,61 @@ __device__ void load_row(const void* x, int r, int k, float* row) {
     }
   } else {
     const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + (uint64_t)r * k);
-    for (int i = threadIdx.x; i < k / 4; i += kRowThreads) reinterpret_cast<float4*>(row)[i] = src[i];
+    for (int i = threadIdx.x; i < k / 4; i += NT) reinterpret_cast<float4*>(row)[i] = src[i];
   }
   __syncthreads();
 }
 
 // MODE 0: quant_act (local absmax). MODE 1: only the transformed row's absmax -> amax[r].
 // MODE 2: quantize with amax[r] given (the max over the row's column shards).
-template <int MODE, bool BF16>
-__global__ void __launch_bounds__(kRowThreads) k_quant_act(const void* __restrict__ x, int k, int bs,
+template <int NT, int MODE, bool BF16>
+__global__ void __launch_bounds__(NT) k_quant_act(const void* __restrict__ x, int k, int bs,
                                                            float* __restrict__ amax, int8_t* __restrict__ q,
                                                            float* __restrict__ scale) {
   extern __shared__ float row[];
-  __shared__ float red[kRowThreads / 32];
+  __shared__ float red[NT / 32];
   const int r = blockIdx.x;
-  load_row<BF16>(x, r, k, row);
-  if (bs > 1) fwht_row(row, k, bs);
+  load_row<NT, BF16>(x, r, k, row);
+  if (bs > 1) fwht_row<NT>(row, k, bs);
   if (MODE == 2) {
-    quant_row64(row, k, bs, amax[r], q + (uint64_t)r * k, scale + r);
+    quant_row64<NT>(row, k, bs, amax[r], q + (uint64_t)r * k, scale + r);
     return;
   }
-  const float mx = row_absmax(row, k, red);
+  const float mx = row_absmax<NT>(row, k, red);
   if (MODE == 1) {
     if (threadIdx.x == 0) amax[r] = mx;
     return;
   }
-  quant_row64(row, k, bs, mx, q + (uint64_t)r * k, scale + r);
+  quant_row64<NT>(row, k, bs, mx, q + (uint64_t)r * k, scale + r);
 }
 
 // det_rmsnorm (core.py:151-159, exact_rowsum core.py:85-108) then quant_act.
-__global__ void __launch_bounds__(kRowThreads) k_rmsnorm_quant(const float* __restrict__ x, const float* __restrict__ w,
+template <int NT>
+__global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ x, const float* __restrict__ w,
                                                                int k, int bs, float inv_d, float eps, int L,
                                                                int8_t* __restrict__ q, float* __restrict__ scale) {
   extern __shared__ float row[];
-  __shared__ float red[kRowThreads / 32];
-  __shared__ long long redl[kRowThreads / 32];
+  __shared__ float red[NT / 32];
+  __shared__ long long redl[NT / 32];
   const int r = blockIdx.x;
-  load_row<false>(x, r, k, row);
+  load_row<NT, false>(x, r, k, row);
   float mx = 0.f;
-  for (int i = threadIdx.x; i < k; i += kRowThreads) mx = fmaxf(mx, __fmul_rn(row[i], row[i]));
-  mx = block_maxf(mx, red);
+  for (int i = threadIdx.x; i < k; i += NT) mx = fmaxf(mx, __fmul_rn(row[i], row[i]));
+  mx = block_maxf<NT>(mx, red);
   int e;
   frexpf(mx, &e);
   const int sh = min(max((62 - L) - e, -1000), 1000);
   const double up = pow2d(sh);
   long long acc = 0;
-  for (int i = threadIdx.x; i < k; i += kRowThreads) acc += __double2ll_rn((double)__fmul_rn(row[i], row[i]) * up);
-  acc = block_sumll(acc, redl);
+  for (int i = threadIdx.x; i < k; i += NT) acc += __double2ll_rn((double)__fmul_rn(row[i], row[i]) * up);
+  acc = block_sumll<NT>(acc, redl);
   const float ss = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
   const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_d), eps)));
-  for (int i = threadIdx.x; i < k; i += kRowThreads) row[i] = __fmul_rn(__fmul_rn(row[i], rr), w[i]);
+  for (int i = threadIdx.x; i < k; i += NT) row[i] = __fmul_rn(__fmul_rn(row[i], rr), w[i]);
   __syncthreads();
-  if (bs > 1) fwht_row(row, k, bs);
-  const float am = row_absmax(row, k, red);
-  quant_row64(row, k, bs, am, q + (uint64_t)r * k, scale + r);
+  if (bs > 1) fwht_row<NT>(row, k, bs);
+  const float am = row_absmax<NT>(row, k, red);
+  quant_row64<NT>(row, k, bs, am, q + (uint64_t)r * k, scale + r);
 }
 
 // fmul(det_silu(gate), up) of the dequantized gate/up GEMM output (N x 2I int32)
@@ -204,20 +213,21 @@ __device__ __forceinline__ float swiglu_at(const int32_t* ar, float s, const flo
 }
 
 // quant_act(fmul(det_silu(gate), up)) of the gate/up GEMM output, one row per CTA.
-__global__ void __launch_bounds__(kRowThreads) k_swiglu_quant(const int32_t* __restrict__ acc,
+template <int NT>
+__global__ void __launch_bounds__(NT) k_swiglu_quant(const int32_t* __restrict__ acc,
                                                               const float* __restrict__ s3, const float* __restrict__ sw,
                                                               int I, int bs, int8_t* __restrict__ q,
                                                               float* __restrict__ scale) {
   extern __shared__ float row[];
-  __shared__ float red[kRowThreads / 32];
+  __shared__ float red[NT / 32];
   const int r = blockIdx.x;
   const float s = s3[r];
   const int32_t* ar = acc + (uint64_t)r * 2 * I;
-  for (int i = threadIdx.x; i < I; i += kRowThreads) row[i] = swiglu_at(ar, s, sw, I, i);
+  for (int i = threadIdx.x; i < I; i += NT) row[i] = swiglu_at(ar, s, sw, I, i);
   __syncthreads();
-  if (bs > 1) fwht_row(row, I, bs);
-  const float am = row_absmax(row, I, red);
-  quant_row64(row, I, bs, am, q + (uint64_t)r * I, scale + r);
+  if (bs > 1) fwht_row<NT>(row, I, bs);
+  const float am = row_absmax<NT>(row, I, red);
+  quant_row64<NT>(row, I, bs, am, q + (uint64_t)r * I, scale + r);
 }
 
 // The fp32 SwiGLU row alone (the input of a row-parallel down projection, quantized per shard).
@@ -326,15 +336,27 @@ int ceil_log2(int n) {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+// Row kernels stage a row in dynamic shared memory; rows over 48 KiB need the opt-in, set once per
+// kernel and device (never during a stream capture after the first call).
 int row_smem_ok(int k, const void* kernel) {
   if (4 * k > kMaxRowSmem) return UWC_ERR_SHAPE;
-  if (4 * k > 48 * 1024 &&
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxRowSmem) != cudaSuccess) {
+  if (4 * k <= 48 * 1024) return UWC_OK;
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({dev, kernel})) return UWC_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxRowSmem) != cudaSuccess) {
     cudaGetLastError();
     return UWC_ERR_CUDA;
   }
+  done.insert({dev, kernel});
   return UWC_OK;
 }
+
+// Fewer rows than SMs (decode): 1024 threads per row shorten each row's latency.
+bool few_rows(int m) { return m < uwc_num_sms(); }
 
 bool bs_ok(int k, int bs) { return bs <= 1 || ((bs & (bs - 1)) == 0 && k % bs == 0); }
 
@@ -346,9 +368,15 @@ int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, fl
   if (!aligned16(x) || (q && ((uintptr_t)q & 3))) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
-  const int rc = row_smem_ok(k, (const void*)k_quant_act<MODE, BF16>);
-  if (rc != UWC_OK) return rc;
-  k_quant_act<MODE, BF16><<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
+  if (few_rows(m)) {
+    const int rc = row_smem_ok(k, (const void*)k_quant_act<1024, MODE, BF16>);
+    if (rc != UWC_OK) return rc;
+    k_quant_act<1024, MODE, BF16><<<m, 1024, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
+  } else {
+    const int rc = row_smem_ok(k, (const void*)k_quant_act<kRowThreads, MODE, BF16>);
+    if (rc != UWC_OK) return rc;
+    k_quant_act<kRowThreads, MODE, BF16><<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
+  }
   return uwc_launch_status();
 }
 
@@ -377,11 +405,18 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
   if (!aligned16(x) || ((uintptr_t)q & 3)) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
-  const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant);
-  if (rc != UWC_OK) return rc;
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
-  k_rmsnorm_quant<<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, (float)(1.0 / k), (float)eps,
-                                                                  ceil_log2(k), q, scale);
+  const float inv_d = (float)(1.0 / k), eps32 = (float)eps;
+  if (few_rows(m)) {
+    const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<1024>);
+    if (rc != UWC_OK) return rc;
+    k_rmsnorm_quant<1024><<<m, 1024, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, inv_d, eps32, ceil_log2(k), q, scale);
+  } else {
+    const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<kRowThreads>);
+    if (rc != UWC_OK) return rc;
+    k_rmsnorm_quant<kRowThreads><<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, inv_d, eps32,
+                                                                                 ceil_log2(k), q, scale);
+  }
   return uwc_launch_status();
 }
 
@@ -391,9 +426,15 @@ extern "C" int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float
   if ((uintptr_t)q & 3) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
-  const int rc = row_smem_ok(I, (const void*)k_swiglu_quant);
-  if (rc != UWC_OK) return rc;
-  k_swiglu_quant<<<m, kRowThreads, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
+  if (few_rows(m)) {
+    const int rc = row_smem_ok(I, (const void*)k_swiglu_quant<1024>);
+    if (rc != UWC_OK) return rc;
+    k_swiglu_quant<1024><<<m, 1024, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
+  } else {
+    const int rc = row_smem_ok(I, (const void*)k_swiglu_quant<kRowThreads>);
+    if (rc != UWC_OK) return rc;
+    k_swiglu_quant<kRowThreads><<<m, kRowThreads, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
+  }
   return uwc_launch_status();
 }
 
