@@ -60,7 +60,7 @@ constexpr int kKB = 128;                                // K bytes per stage (on
 constexpr int kUN = 256;                                // output columns per unit
 constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
 constexpr int kMsgWords = kMaxTiles * 16;               // one unit's tile messages (32 KiB)
-constexpr int kBarBytes = 512;
+constexpr int kBarBytes = 256;
 
 struct Params {
   int m, n, k, r;
@@ -94,14 +94,20 @@ struct Cfg {
   static constexpr bool CORR = MODE == MODE_FWD || MODE == MODE_CORR;  // builds the correction R
   static constexpr int A_BYTES = UM * kKB;
   static constexpr int STAGE = A_BYTES + kUN * kKB;              // 64 KiB (MINE) / 48 KiB
-  static constexpr int NST = MINE ? 3 : 4;
-  static constexpr int SMEM = NST * STAGE + kBarBytes + 1024;  // +1024: manual alignment
+  // MODE_MINE_OUT and MODE_CORR trade stages for the epilogue's tiles (below)
+  static constexpr int NST = MODE == MODE_MINE ? 3 : (MODE == MODE_MINE_OUT || MODE == MODE_CORR ? 2 : 4);
+  // Per epilogue warp a padded 32 x 33-word shared-memory tile that turns thread-per-row data into
+  // row-contiguous global accesses (MODE_CORR's read-back and stores, MODE_MINE_OUT's store).
+  static constexpr int TILE_WORDS = 32 * 33;
+  static constexpr int TILE_BYTES = (MODE == MODE_CORR || MODE == MODE_MINE_OUT) ? kEpiWarps * TILE_WORDS * 4 : 0;
+  static constexpr int SMEM = NST * STAGE + TILE_BYTES + kBarBytes + 1024;  // +1024: manual alignment
   static constexpr int TILES = MINE ? 512 : 256;
   static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
   static constexpr int SPAN = R == 256 ? 2 : 1;                  // stages per chunk
   static constexpr int ACC_WARPS = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;  // readers per acc
 };
 
+struct Bars;
 struct Bars {
   uint64_t full[4];
   uint64_t empty[4];
@@ -114,6 +120,7 @@ struct Bars {
   int abort_flag;
   int L;
 };
+static_assert(sizeof(Bars) <= kBarBytes, "barrier block");
 
 __device__ __forceinline__ void unit_coords(const Params& p, int u, int UM, int& m0, int& n0) {
   constexpr int G = 16;  // group of row blocks that sweep the columns together (L2 reuse of B)
@@ -207,6 +214,25 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int c0, co
   }
 }
 
+// Four consecutive outputs of one row (c % 4 == 0, n % 4 == 0) in the chosen format.
+__device__ __forceinline__ void store4(const Params& p, int row, int c, int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
+  if (p.out_mode == UWC_OUT_I32) {
+    *reinterpret_cast<int4*>(static_cast<int32_t*>(p.out) + (uint64_t)row * p.n + c) = make_int4(v0, v1, v2, v3);
+    return;
+  }
+  const float sx = p.a_scale[row];
+  const float f0 = __fmul_rn(__fmul_rn(__int2float_rn(v0), sx), __ldg(p.b_scale + c));
+  const float f1 = __fmul_rn(__fmul_rn(__int2float_rn(v1), sx), __ldg(p.b_scale + c + 1));
+  const float f2 = __fmul_rn(__fmul_rn(__int2float_rn(v2), sx), __ldg(p.b_scale + c + 2));
+  const float f3 = __fmul_rn(__fmul_rn(__int2float_rn(v3), sx), __ldg(p.b_scale + c + 3));
+  if (p.out_mode == UWC_OUT_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + (uint64_t)row * p.n + c) = make_float4(f0, f1, f2, f3);
+  } else {
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + (uint64_t)row * p.n + c) =
+        make_uint2(bf16_rne(f0) | (bf16_rne(f1) << 16), bf16_rne(f2) | (bf16_rne(f3) << 16));
+  }
+}
+
 // ------------------------------------------------------------------ hash-tile fold
 // XOR the 32 values of one row (consecutive columns) into four partials by t = (col / 2) % 4.
 __device__ __forceinline__ void fold_row32(const uint32_t* v, uint32_t* pt) {
@@ -251,7 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<MODE, R>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE);
+  uint32_t* const tiles = reinterpret_cast<uint32_t*>(smem + C::NST * C::STAGE);
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE + C::TILE_BYTES);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -347,11 +374,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
         // ---- correction accumulator R (FWD): Horner over limbs, highest limb first
         if (C::CORR && L > 0) {
-          const uint32_t tR = tmem + 256;
+          // MODE_CORR with up to two limbs keeps each limb's product in its own 256 columns (the
+          // epilogue adds them as P0 + (P1 << 7)); otherwise Horner steps in columns 256..511
+          const bool direct = MODE == MODE_CORR && L <= 2;
           for (int li = L - 1; li >= 0 && ok; li--) {
+            const uint32_t tR = tmem + (direct ? 256 * li : 256);
             if (li == L - 1)
               ok = mbar_wait(&bars->r_empty, (local & 1) ^ 1, abort_flag, p.status);
-            else
+            else if (!direct)
               ok = mbar_wait(&bars->r_scaled, r_scaled_waits++ & 1, abort_flag, p.status);
             if (!ok) break;
             tc_fence_after();
@@ -364,10 +394,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t ad = sdesc_sw128(aA), bd = sdesc_sw128(aB);
 #pragma unroll
               for (int ks = 0; ks < 4; ks++)
-                mma_i8(tR, ad + 2 * ks, bd + 2 * ks, idesc_i8(128, 256), (li == L - 1 && kb == 0 && ks == 0) ? 0u : 1u);
+                mma_i8(tR, ad + 2 * ks, bd + 2 * ks, idesc_i8(128, 256),
+                       ((direct || li == L - 1) && kb == 0 && ks == 0) ? 0u : 1u);
               mma_commit(&bars->empty[s]);
             }
-            mma_commit(&bars->r_full);
+            if (!direct || li == 0) mma_commit(&bars->r_full);
           }
         }
         // ---- main loop, one 128-column k-block stage at a time, MMAs issued back to back
@@ -495,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // row half of the 128-row accumulator this quadrant belongs to, for the message slot
       const int rb = q >> 1;
 
-      if (C::CORR) {
+      if (C::CORR && !(MODE == MODE_CORR && L <= 2)) {
         // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
         for (int step = 0; step + 1 < L && ok; step++) {
           ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
@@ -526,33 +557,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
         }
-        const int row = m0 + 32 * q + lane;
+        uint32_t* const tile = tiles + warp * C::TILE_WORDS;
 #pragma unroll 1
         for (int hh = 0; hh < 2; hh++) {
           const int c0 = n0 + cb * 64 + hh * 32;
-          int32_t w[32];
-          if (row < p.m && c0 + 32 <= p.n) {
-            const int4* src = reinterpret_cast<const int4*>(p.acc_in + (uint64_t)row * p.n + c0);
+          // R for this warp's 32 rows x 32 columns (thread = row), staged transposed in shared memory
+          uint32_t rr[32];
+          if (L > 2) {
+            tmem_ld_32x32b_x32(tmem + 256 + cb * 64 + hh * 32 + lane_base, rr);
+            tmem_wait_ld();
+          } else if (L > 0) {
+            // R = P0 + (P1 << 7): the same int32 value as the Horner form
+            const uint32_t ta = tmem + cb * 64 + hh * 32 + lane_base;
+            tmem_ld_32x32b_x32(ta, rr);
+            if (L == 2) {
+              uint32_t r1[32];
+              tmem_ld_32x32b_x32(ta + 256, r1);
+              tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-              const int4 x = __ldcs(src + i);
-              w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+              for (int i = 0; i < 32; i++) rr[i] += r1[i] << 7;
+            } else {
+              tmem_wait_ld();
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; i++) w[i] = (row < p.m && c0 + i < p.n) ? p.acc_in[(uint64_t)row * p.n + c0 + i] : 0;
+            for (int i = 0; i < 32; i++) rr[i] = 0u;
           }
-          if (L > 0) {
 #pragma unroll
-            for (int qq = 0; qq < 2; qq++) {
-              uint32_t rr[16];
-              tmem_ld_32x32b_x16(tmem + 256 + cb * 64 + hh * 32 + qq * 16 + lane_base, rr);
-              tmem_wait_ld();
+          for (int j = 0; j < 32; j++) tile[lane * 33 + j] = rr[j];
+          __syncwarp();
+          // 4 rows x 32 columns per pass: 8 lanes per row, 4 consecutive columns per lane; all eight
+          // passes' loads are issued before the first use (4 KiB in flight per warp)
+          const int cl = 4 * (lane & 7), c = c0 + cl;
+          int4 a[8];
 #pragma unroll
-              for (int i = 0; i < 16; i++) w[qq * 16 + i] -= (int32_t)rr[i];
+          for (int pass = 0; pass < 8; pass++) {
+            const int row = m0 + 32 * q + pass * 4 + (lane >> 3);
+            a[pass] = (row < p.m && c < p.n) ? __ldcs(reinterpret_cast<const int4*>(p.acc_in + (uint64_t)row * p.n + c))
+                                             : make_int4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int pass = 0; pass < 8; pass++) {
+            const int rl = pass * 4 + (lane >> 3), row = m0 + 32 * q + rl;
+            if (row < p.m && c < p.n) {
+              const uint32_t* t = tile + rl * 33 + cl;
+              store4(p, row, c, a[pass].x - (int32_t)t[0], a[pass].y - (int32_t)t[1], a[pass].z - (int32_t)t[2],
+                     a[pass].w - (int32_t)t[3]);
             }
           }
-          store_row32(p, row, c0, w);
+          __syncwarp();
         }
         if (L > 0) {
           tc_fence_before();
@@ -626,14 +679,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             fold_row32(v2, pt);
           }
           if (MODE == MODE_MINE_OUT && last) {
-            // the finished product, raw int32: this thread's row, 64 consecutive columns
-            const int row = m0 + a * 128 + 32 * q + lane, c0 = n0 + cb * 64;
-            if (row < p.m && c0 < p.n) {
-              uint4* o = reinterpret_cast<uint4*>(static_cast<int32_t*>(p.out) + (uint64_t)row * p.n + c0);
+            // the finished product, raw int32, staged through this warp's shared-memory tile so the
+            // stores are row-contiguous (4 rows x 128 bytes per instruction)
+            uint32_t* const tile = tiles + warp * C::TILE_WORDS;
+            const int r0 = m0 + a * 128 + 32 * q, cl = 4 * (lane & 7);
 #pragma unroll
-              for (int i = 0; i < 8; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            for (int hh = 0; hh < 2; hh++) {
+              const uint32_t* src = hh ? v2 : v;
 #pragma unroll
-              for (int i = 0; i < 8; i++) o[8 + i] = make_uint4(v2[4 * i], v2[4 * i + 1], v2[4 * i + 2], v2[4 * i + 3]);
+              for (int j = 0; j < 32; j++) tile[lane * 33 + j] = src[j];
+              __syncwarp();
+              const int c = n0 + cb * 64 + hh * 32 + cl;
+#pragma unroll
+              for (int pass = 0; pass < 8; pass++) {
+                const int rl = pass * 4 + (lane >> 3), row = r0 + rl;
+                const uint32_t* t = tile + rl * 33 + cl;
+                if (row < p.m && c < p.n)
+                  *reinterpret_cast<uint4*>(static_cast<int32_t*>(p.out) + (uint64_t)row * p.n + c) =
+                      make_uint4(t[0], t[1], t[2], t[3]);
+              }
+              __syncwarp();
             }
           }
         }
