@@ -95,11 +95,12 @@ struct Cfg {
   static constexpr int A_BYTES = UM * kKB;
   static constexpr int STAGE = A_BYTES + kUN * kKB;              // 64 KiB (MINE) / 48 KiB
   // MODE_MINE_OUT and MODE_CORR trade stages for the epilogue's tiles (below)
-  static constexpr int NST = MODE == MODE_MINE ? 3 : (MODE == MODE_MINE_OUT || MODE == MODE_CORR ? 2 : 4);
+  static constexpr int NST = MODE == MODE_MINE || MODE == MODE_PLAIN ? 3 : (MODE == MODE_MINE_OUT || MODE == MODE_CORR ? 2 : 4);
   // Per epilogue warp a padded 32 x 33-word shared-memory tile that turns thread-per-row data into
-  // row-contiguous global accesses (MODE_CORR's read-back and stores, MODE_MINE_OUT's store).
+  // row-contiguous global accesses (MODE_CORR's read-back and stores, MODE_MINE_OUT's and
+  // MODE_PLAIN's stores).
   static constexpr int TILE_WORDS = 32 * 33;
-  static constexpr int TILE_BYTES = (MODE == MODE_CORR || MODE == MODE_MINE_OUT) ? kEpiWarps * TILE_WORDS * 4 : 0;
+  static constexpr int TILE_BYTES = MODE == MODE_FWD || MODE == MODE_MINE ? 0 : kEpiWarps * TILE_WORDS * 4;
   static constexpr int SMEM = NST * STAGE + TILE_BYTES + kBarBytes + 1024;  // +1024: manual alignment
   static constexpr int TILES = MINE ? 512 : 256;
   static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
@@ -505,6 +506,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 32; i++)
                 if (c0 + i < p.n) atomicAdd(o + i, (int32_t)v[i]);
             }
+          } else if (p.out_mode != UWC_OUT_NONE && (p.n & 3) == 0) {
+            // through this warp's tile: 4 rows x 32 columns per store instruction
+            uint32_t* const tile = tiles + warp * C::TILE_WORDS;
+#pragma unroll
+            for (int j = 0; j < 32; j++) tile[lane * 33 + j] = v[j];
+            __syncwarp();
+            const int cl = 4 * (lane & 7), c = c0 + cl;
+#pragma unroll
+            for (int pass = 0; pass < 8; pass++) {
+              const int rl = pass * 4 + (lane >> 3), r = m0 + 32 * q + rl;
+              const uint32_t* t = tile + rl * 33 + cl;
+              if (r < p.m && c < p.n) store4(p, r, c, (int32_t)t[0], (int32_t)t[1], (int32_t)t[2], (int32_t)t[3]);
+            }
+            __syncwarp();
           } else {
             store_row32(p, row, c0, reinterpret_cast<const int32_t*>(v));
           }
