@@ -81,6 +81,7 @@ struct Params {
   const float* b_scale;
   void* out;
   uint32_t* status;
+  uint32_t one;      // 1, opaque to the compiler (multiply-add additions in the tile hash)
 };
 
 // R: hash chunk width in k (64, 128, 256), or 0 for no hashing.
@@ -334,9 +335,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // The whole warp runs the schedule (loop state stays warp-uniform, off the vector ALU that
+    // the epilogue saturates); one elected lane issues the copies.
+    {
+      const bool leader = elect_one();
       uint32_t gk = 0;
-      for (int u = blockIdx.x; u < p.nunits && !*abort_flag; u += gridDim.x) {
+      for (int u = blockIdx.x; u < p.nunits && !__any_sync(0xffffffffu, *abort_flag); u += gridDim.x) {
         int m0, n0, kb0, nkb;
         unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
         const int ncorr = C::CORR ? L * cblocks : 0;
@@ -344,9 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int b = 0; b < nblk; b++, gk++) {
           const int s = gk % C::NST;
           const uint32_t ph = (gk / C::NST) & 1;
-          if (!mbar_wait(&bars->empty[s], ph ^ 1, abort_flag, p.status)) break;
+          if (!warp_wait(&bars->empty[s], ph ^ 1, abort_flag, p.status)) break;
           uint8_t* sA = smem + s * C::STAGE;
           uint8_t* sB = sA + C::A_BYTES;
+          if (!leader) continue;
           mbar_expect_tx(&bars->full[s], C::STAGE);
           if (b < ncorr) {
             const int li = L - 1 - b / cblocks, kb = b % cblocks;
@@ -362,7 +367,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // As for the producer: the whole warp waits and keeps the schedule, one elected lane issues
+    // the MMAs and commits.
+    {
+      const bool leader = elect_one();
       uint32_t gk = 0;                      // k-blocks consumed (ring position)
       uint32_t snaps[2] = {0, 0};           // snapshots produced per accumulator
       uint32_t r_scaled_waits = 0;
@@ -381,25 +389,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int li = L - 1; li >= 0 && ok; li--) {
             const uint32_t tR = tmem + (direct ? 256 * li : 256);
             if (li == L - 1)
-              ok = mbar_wait(&bars->r_empty, (local & 1) ^ 1, abort_flag, p.status);
+              ok = warp_wait(&bars->r_empty, (local & 1) ^ 1, abort_flag, p.status);
             else if (!direct)
-              ok = mbar_wait(&bars->r_scaled, r_scaled_waits++ & 1, abort_flag, p.status);
+              ok = warp_wait(&bars->r_scaled, r_scaled_waits++ & 1, abort_flag, p.status);
             if (!ok) break;
             tc_fence_after();
             for (int kb = 0; kb < cblocks && ok; kb++, gk++) {
               const int s = gk % C::NST;
-              ok = mbar_wait(&bars->full[s], (gk / C::NST) & 1, abort_flag, p.status);
+              ok = warp_wait(&bars->full[s], (gk / C::NST) & 1, abort_flag, p.status);
               if (!ok) break;
               tc_fence_after();
               const uint32_t aA = smem_base + s * C::STAGE, aB = aA + C::A_BYTES;
               const uint64_t ad = sdesc_sw128(aA), bd = sdesc_sw128(aB);
+              if (leader) {
 #pragma unroll
-              for (int ks = 0; ks < 4; ks++)
-                mma_i8(tR, ad + 2 * ks, bd + 2 * ks, idesc_i8(128, 256),
-                       ((direct || li == L - 1) && kb == 0 && ks == 0) ? 0u : 1u);
-              mma_commit(&bars->empty[s]);
+                for (int ks = 0; ks < 4; ks++)
+                  mma_i8(tR, ad + 2 * ks, bd + 2 * ks, idesc_i8(128, 256),
+                         ((direct || li == L - 1) && kb == 0 && ks == 0) ? 0u : 1u);
+              }
+              if (leader) mma_commit(&bars->empty[s]);
             }
-            if (!direct || li == 0) mma_commit(&bars->r_full);
+            if (leader && (!direct || li == 0)) mma_commit(&bars->r_full);
           }
         }
         // ---- main loop, one 128-column k-block stage at a time, MMAs issued back to back
@@ -409,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < nkb && ok; kb++) {   // kb counts from this unit's first k-block
           const uint32_t g = gk0 + kb;
           const int s = g % C::NST;
-          ok = mbar_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
+          ok = warp_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
           if (!ok) break;
           tc_fence_after();
           const uint32_t aA = smem_base + s * C::STAGE;
@@ -424,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int a = 0; a < C::NACC; a++) {
                 if (a >= nacc) break;
                 if (cstart) {
-                  ok = mbar_wait(&bars->acc_empty[a], (snaps[a] & 1) ^ 1, abort_flag, p.status);
+                  ok = warp_wait(&bars->acc_empty[a], (snaps[a] & 1) ^ 1, abort_flag, p.status);
                   if (!ok) break;
                   tc_fence_after();
                 }
@@ -432,11 +442,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t ad = adesc + (C::MINE ? a * (128 * kKB / 16) : 0);
                 const uint64_t bd = bdesc + (C::MINE ? 0 : a * (128 * kKB / 16));
                 const uint32_t dcol = tmem + a * C::ACC_N;
+                if (leader) {
 #pragma unroll
-                for (int ks = part * (4 / C::PARTS); ks < (part + 1) * (4 / C::PARTS); ks++)
-                  mma_i8(dcol, ad + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
+                  for (int ks = part * (4 / C::PARTS); ks < (part + 1) * (4 / C::PARTS); ks++)
+                    mma_i8(dcol, ad + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
+                }
                 if (cend) {
-                  mma_commit(&bars->acc_full[a]);
+                  if (leader) mma_commit(&bars->acc_full[a]);
                   snaps[a]++;
                 }
               }
@@ -448,29 +460,31 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int ba = MODE == MODE_PLAIN ? pbuf : a;
               if (kb == 0) {
                 const uint32_t uses = MODE == MODE_PLAIN ? (uint32_t)(local >> 1) : snaps[a];
-                ok = mbar_wait(&bars->acc_empty[ba], (uses & 1) ^ 1, abort_flag, p.status);
+                ok = warp_wait(&bars->acc_empty[ba], (uses & 1) ^ 1, abort_flag, p.status);
                 if (!ok) break;
                 tc_fence_after();
               }
               const uint64_t bd = bdesc + (MODE == MODE_FWD ? a * (128 * kKB / 16) : 0);
               const uint32_t dcol = tmem + (MODE == MODE_PLAIN ? pbuf * 256 : a * 128);
+              if (leader) {
 #pragma unroll
-              for (int ks = 0; ks < 4; ks++)
-                mma_i8(dcol, adesc + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
+                for (int ks = 0; ks < 4; ks++)
+                  mma_i8(dcol, adesc + 2 * ks, bd + 2 * ks, id_acc, (kb == 0 && ks == 0) ? 0u : 1u);
+              }
               if (kb == nkb - 1) {
-                mma_commit(&bars->acc_full[ba]);
+                if (leader) mma_commit(&bars->acc_full[ba]);
                 if (MODE != MODE_PLAIN) snaps[a]++;
               }
             }
           }
           if (!ok) break;
-          mma_commit(&bars->empty[s]);
+          if (leader) mma_commit(&bars->empty[s]);
         }
         gk = gk0 + nkb;
       }
-      // drain: every MMA issued by this thread has completed before TMEM is released
-      mma_commit(&bars->drain);
-      mbar_wait(&bars->drain, 0, abort_flag, p.status);
+      // drain: every MMA issued by the leader has completed before TMEM is released
+      if (leader) mma_commit(&bars->drain);
+      warp_wait(&bars->drain, 0, abort_flag, p.status);
     }
   } else if (warp < kEpiWarps) {
     // ------------------------------------------------------------ epilogue warps
@@ -771,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __stcg(msg + i * kMaxTiles + slot, 0u);   // clear for the unit after next
         }
         if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) continue;
-        b3::hash64(key, w, hv);
+        b3::hash64<true>(key, w, hv, p.one);
         bool le = true, decided = false;
 #pragma unroll
         for (int i = 7; i >= 0; i--) {
@@ -896,6 +910,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   p.a_scale = a_scale; p.b_scale = b_scale; p.out = out;
   p.msgbuf = static_cast<uint32_t*>(workspace);
   p.status = uwc_status_ptr();
+  p.one = 1u;
   p.nn = (n + kUN - 1) / kUN;
   cudaStream_t st = (cudaStream_t)stream;
 

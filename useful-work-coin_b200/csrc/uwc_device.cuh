@@ -37,17 +37,49 @@ UWC_DEVI uint32_t ror(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
   c = c + d;                           \
   b = ror(b ^ c, 7);
 
+// a + b as an integer multiply-add by `one` (a run-time 1 the compiler cannot fold): the sum
+// runs on the FMA pipe instead of the integer ALU pipe.
+UWC_DEVI uint32_t add_fma(uint32_t a, uint32_t b, uint32_t one) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(one), "r"(b));
+  return d;
+}
+
+// G with its additions on the FMA pipe (same values as UWC_B3_G).
+#define UWC_B3_G_FMA(a, b, c, d, x, y)          \
+  a = add_fma(add_fma(a, b, one), (x), one);    \
+  d = ror(d ^ a, 16);                           \
+  c = add_fma(c, d, one);                       \
+  b = ror(b ^ c, 12);                           \
+  a = add_fma(add_fma(a, b, one), (y), one);    \
+  d = ror(d ^ a, 8);                            \
+  c = add_fma(c, d, one);                       \
+  b = ror(b ^ c, 7);
+
 // One round on the 16-word state with message words in the current (permuted) order, then
 // the spec's message permutation [2,6,3,10,7,0,4,13,1,11,12,5,9,14,15,8] applied in place.
-UWC_DEVI void round_and_permute(uint32_t* v, uint32_t* m) {
-  UWC_B3_G(v[0], v[4], v[8], v[12], m[0], m[1]);
-  UWC_B3_G(v[1], v[5], v[9], v[13], m[2], m[3]);
-  UWC_B3_G(v[2], v[6], v[10], v[14], m[4], m[5]);
-  UWC_B3_G(v[3], v[7], v[11], v[15], m[6], m[7]);
-  UWC_B3_G(v[0], v[5], v[10], v[15], m[8], m[9]);
-  UWC_B3_G(v[1], v[6], v[11], v[12], m[10], m[11]);
-  UWC_B3_G(v[2], v[7], v[8], v[13], m[12], m[13]);
-  UWC_B3_G(v[3], v[4], v[9], v[14], m[14], m[15]);
+// FMA_ADDS: additions on the FMA pipe (`one` must be 1), for kernels whose ALU pipe is busy.
+template <bool FMA_ADDS = false>
+UWC_DEVI void round_and_permute(uint32_t* v, uint32_t* m, uint32_t one = 1u) {
+  if (FMA_ADDS) {
+    UWC_B3_G_FMA(v[0], v[4], v[8], v[12], m[0], m[1]);
+    UWC_B3_G_FMA(v[1], v[5], v[9], v[13], m[2], m[3]);
+    UWC_B3_G_FMA(v[2], v[6], v[10], v[14], m[4], m[5]);
+    UWC_B3_G_FMA(v[3], v[7], v[11], v[15], m[6], m[7]);
+    UWC_B3_G_FMA(v[0], v[5], v[10], v[15], m[8], m[9]);
+    UWC_B3_G_FMA(v[1], v[6], v[11], v[12], m[10], m[11]);
+    UWC_B3_G_FMA(v[2], v[7], v[8], v[13], m[12], m[13]);
+    UWC_B3_G_FMA(v[3], v[4], v[9], v[14], m[14], m[15]);
+  } else {
+    UWC_B3_G(v[0], v[4], v[8], v[12], m[0], m[1]);
+    UWC_B3_G(v[1], v[5], v[9], v[13], m[2], m[3]);
+    UWC_B3_G(v[2], v[6], v[10], v[14], m[4], m[5]);
+    UWC_B3_G(v[3], v[7], v[11], v[15], m[6], m[7]);
+    UWC_B3_G(v[0], v[5], v[10], v[15], m[8], m[9]);
+    UWC_B3_G(v[1], v[6], v[11], v[12], m[10], m[11]);
+    UWC_B3_G(v[2], v[7], v[8], v[13], m[12], m[13]);
+    UWC_B3_G(v[3], v[4], v[9], v[14], m[14], m[15]);
+  }
   uint32_t t0 = m[0], t1 = m[1], t3 = m[3], t4 = m[4], t5 = m[5], t8 = m[8], t9 = m[9], t10 = m[10], t11 = m[11],
            t12 = m[12], t13 = m[13], t14 = m[14], t15 = m[15], t6 = m[6], t7 = m[7], t2 = m[2];
   m[0] = t2; m[1] = t6; m[2] = t3; m[3] = t10; m[4] = t7; m[5] = t0; m[6] = t4; m[7] = t13;
@@ -55,21 +87,23 @@ UWC_DEVI void round_and_permute(uint32_t* v, uint32_t* m) {
 }
 
 // out = first 8 words of compress(cv, msg, counter, blen, flags). `msg` is clobbered.
+template <bool FMA_ADDS = false>
 UWC_DEVI void compress(const uint32_t* cv, uint32_t* msg, uint64_t counter, uint32_t blen, uint32_t flags,
-                       uint32_t* out) {
+                       uint32_t* out, uint32_t one = 1u) {
   uint32_t v[16];
 #pragma unroll
   for (int i = 0; i < 8; i++) v[i] = cv[i];
   v[8] = IV[0]; v[9] = IV[1]; v[10] = IV[2]; v[11] = IV[3];
   v[12] = (uint32_t)counter; v[13] = (uint32_t)(counter >> 32); v[14] = blen; v[15] = flags;
 #pragma unroll
-  for (int r = 0; r < 7; r++) round_and_permute(v, msg);
+  for (int r = 0; r < 7; r++) round_and_permute<FMA_ADDS>(v, msg, one);
 #pragma unroll
   for (int i = 0; i < 8; i++) out[i] = v[i] ^ v[i + 8];
 }
 
 // Single-block (64-byte) hash, keyed when key != nullptr. `msg` is clobbered.
-UWC_DEVI void hash64(const uint32_t* key, uint32_t* msg, uint32_t* out) {
+template <bool FMA_ADDS = false>
+UWC_DEVI void hash64(const uint32_t* key, uint32_t* msg, uint32_t* out, uint32_t one = 1u) {
   uint32_t cv[8];
   uint32_t fl = CHUNK_START | CHUNK_END | ROOT;
   if (key) {
@@ -80,7 +114,7 @@ UWC_DEVI void hash64(const uint32_t* key, uint32_t* msg, uint32_t* out) {
 #pragma unroll
     for (int i = 0; i < 8; i++) cv[i] = IV[i];
   }
-  compress(cv, msg, 0, 64, fl, out);
+  compress<FMA_ADDS>(cv, msg, 0, 64, fl, out, one);
 }
 }  // namespace b3
 
@@ -138,6 +172,18 @@ UWC_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag
       }
     }
   }
+}
+
+// True in exactly one lane of the converged warp (elect.sync): the warp keeps running a role's
+// schedule together, so its loop state stays warp-uniform, and only the elected lane issues.
+UWC_DEVI bool elect_one() {
+  uint32_t is_leader;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(is_leader));
+  return is_leader != 0;
 }
 
 UWC_DEVI void named_bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
