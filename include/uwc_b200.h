@@ -181,6 +181,30 @@ int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw, const flo
                  const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps, int qknorm,
                  int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs, void* stream);
 
+/* Deterministic attention from quantized q, k, v (runtime/detrt/qwen3.py:254-283 _attention;
+ * GPU form runtime/detgpu/kernels.py:731-771 attention): exact int32 Q K^T, scores
+ * fmul(fmul(fmul(float(dot), qs), ks), inv_sqrt_hd), causal mask, det_exp, exact int64 row sum,
+ * P * sv quantized to 14 bits, P V as two 7-bit limbs summed exactly, times the row scale.
+ * Queries qq (B * Tq, H, 128) int8 and qs (B * Tq, H) are the Tq new tokens of each of B sequences
+ * at absolute positions start .. start + Tq - 1; query t sees keys 0 .. start + t. Keys / values
+ * (int8, 128 per head) are read at kc + b * kv_seq + j * kv_tok + g * kv_head (element strides,
+ * multiples of 16), their scales at ks + b * s_seq + j * s_tok + g * s_head; g = h / (H / Hkv).
+ * Token-major prefill (the detgpu call): kv_seq = Tq * Hkv * 128, kv_tok = Hkv * 128,
+ * kv_head = 128; a KV cache (B, Hkv, maxlen, 128): kv_seq = Hkv * maxlen * 128, kv_head =
+ * maxlen * 128, kv_tok = 128. out (B * Tq, H * 128) float32. UWC_ERR_SHAPE when one query row's
+ * start + Tq scores do not fit in shared memory (about 51 000 keys). */
+int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                  const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq, long long kv_tok,
+                  long long kv_head, long long s_seq, long long s_tok, long long s_head, float inv_sqrt_hd,
+                  float* out, void* stream);
+/* det_rmsnorm (runtime/detrt/core.py:151-159) of m rows of k floats: the final norm of
+ * DetQwen3.forward (runtime/detrt/qwen3.py:299), float32 out. */
+int uwc_rmsnorm(const float* x, const float* w, int m, int k, double eps, float* out, void* stream);
+/* DetQwen3.logprobs (runtime/detrt/qwen3.py:302-312) of m rows of V logits: z = lg - max,
+ * lp = z - det_log(exact_rowsum(det_exp(z), 2^18)) into lp (may be NULL), and the greedy token
+ * of generate_greedy (qwen3.py:323, the first index of the maximal lp) into tok (may be NULL). */
+int uwc_logprobs(const float* logits, int m, int V, float* lp, long long* tok, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

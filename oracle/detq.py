@@ -203,3 +203,62 @@ def qkv_post(acc, s1, sw, qnw, knw, cos, sin, T: int, H: int, Hkv: int, eps: flo
     vq, vs = quant_sym(v, 127)
     i8 = lambda z: z.astype(np.int8)
     return i8(qq), qs, i8(kq), ks, i8(vq), vs
+
+
+# ------------------------------------------------------------------ attention and log-softmax
+P_LEVELS = 16383       # runtime/detrt/qwen3.py:34, 14-bit attention probabilities
+MAX_KEYS = 1 << 20     # runtime/detrt/qwen3.py:33
+
+
+def attention(qq, qs, K, SK, V, SV, start: int, inv_sqrt_hd: float):
+    """runtime/detrt/qwen3.py:253-283 for one batch of queries over a key / value cache.
+
+    qq (B, Tq, H, 128) int8 and qs (B, Tq, H) are the queries at positions start .. start+Tq-1;
+    K, V (B, S, Hkv, 128) int8 and SK, SV (B, S, Hkv) with S = start + Tq. Returns o (B, Tq, H, 128)
+    float32: exact Q K^T, scale chain, causal mask, det_exp, exact row sum, 14-bit P, exact P V."""
+    B, Tq, H, _ = qq.shape
+    S, Hkv = K.shape[1], K.shape[2]
+    rep = H // Hkv
+    Kh = np.repeat(K.astype(np.int64), rep, axis=2)               # (B, S, H, 128)
+    Vh = np.repeat(V.astype(np.int64), rep, axis=2)
+    SKh = np.repeat(np.asarray(SK, F32), rep, axis=2)             # (B, S, H)
+    SVh = np.repeat(np.asarray(SV, F32), rep, axis=2)
+    dot = np.einsum("bthd,bshd->bhts", qq.astype(np.int64), Kh)   # exact
+    qs_ = np.asarray(qs, F32).transpose(0, 2, 1)[..., None]        # (B, H, Tq, 1)
+    sk_ = SKh.transpose(0, 2, 1)[:, :, None, :]                    # (B, H, 1, S)
+    sc = fmul(fmul(fmul(dot.astype(F32), qs_), sk_), c32(inv_sqrt_hd))
+    qpos = start + np.arange(Tq)[:, None]
+    sc = np.where(np.arange(S)[None, :] <= qpos, sc, F32(-np.inf)).astype(F32)
+    mx = sc.max(axis=-1, keepdims=True)
+    e = det_exp(fsub(sc, mx))
+    den = exact_rowsum(e, MAX_KEYS)
+    Pv = fmul(fdiv(e, den[..., None]), SVh.transpose(0, 2, 1)[:, :, None, :])
+    pmax = Pv.max(axis=-1, keepdims=True)
+    sp = fdiv(np.maximum(pmax, c32(1e-30)), c32(float(P_LEVELS)))
+    pi = np.clip(np.rint(fdiv(Pv, sp)), 0, P_LEVELS).astype(np.int64)
+    acc = np.einsum("bhts,bshd->bhtd", pi, Vh)                     # exact in int64
+    o = fmul(acc.astype(F32), sp)
+    return o.transpose(0, 2, 1, 3)
+
+
+def det_log(x):
+    """runtime/detrt/core.py:130-143: log m as 2 atanh((m-1)/(m+1)) (odd series to s^15), + e ln 2."""
+    x = np.asarray(x, F32)
+    m, e = np.frexp(x)
+    m = fmul(m, c32(2.0))
+    ef = (e - 1).astype(F32)
+    s = fdiv(fsub(m, c32(1.0)), fadd(m, c32(1.0)))
+    s2 = fmul(s, s)
+    acc = np.full_like(s, c32(1.0 / 15))
+    for k in range(13, 0, -2):
+        acc = fadd(fmul(acc, s2), c32(1.0 / k))
+    lm = fmul(fmul(acc, s), c32(2.0))
+    return fadd(fmul(ef, c32(0.6931471805599453)), lm)
+
+
+def logprobs(lg):
+    """runtime/detrt/qwen3.py:302-312 rows: z = lg - max, z - det_log(exact_rowsum(det_exp(z), 2^18))."""
+    lg = np.asarray(lg, F32)
+    z = fsub(lg, lg.max(axis=-1, keepdims=True))
+    den = exact_rowsum(det_exp(z), 1 << 18)
+    return fsub(z, det_log(den)[..., None])

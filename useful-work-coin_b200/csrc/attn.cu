@@ -1,0 +1,389 @@
+// The rest of runtime/detrt's forward on sm_100a: exact integer attention, the final RMSNorm and
+// the deterministic log-softmax + greedy argmax. Bit-identical to runtime/detrt/qwen3.py.
+//
+//   k_attention   _attention's core (qwen3.py:254-283, GPU form runtime/detgpu/kernels.py attention)
+//                 from quantized q, k, v: exact int32 Q K^T, the fp32 scale chain, causal mask,
+//                 det_exp, exact int64 row sum, P = e / den, P * sv quantized to 14 bits, P V
+//                 as two 7-bit limbs, each an exact int32 dot, summed in int64, times the scale.
+//   k_rmsnorm     det_rmsnorm (core.py:151-159) to fp32 (the final norm).
+//   k_logprobs    logprobs (qwen3.py:302-312): max, det_exp, exact row sum (2^18 terms), det_log;
+//                 the greedy token is the first index of the row's maximal log-probability
+//                 (generate_greedy, qwen3.py:315-329).
+//
+// Attention layout: one CTA per (sequence, query head, block of QT query rows). The CTA keeps its
+// rows' scores in shared memory (QT x S floats), overwritten in place by e, P * sv and finally the
+// 14-bit integer probabilities; V is staged per 64-key tile transposed (dims x keys) so the P V
+// dot products run four keys per dp4a. Keys and values are read with strides, so the same kernel
+// serves the prefill layout (token-major, the detgpu call) and a KV cache (head-major, decode).
+#include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "det_math.cuh"
+#include "uwc_device.cuh"
+#include "uwc_host.h"
+
+namespace {
+
+constexpr int kAttnThreads = 256;
+constexpr int kHd = 128;               // head dim (the detgpu attention kernels' fixed width)
+constexpr int kTileKeys = 64;          // keys per staged V tile
+constexpr int kVtPitch = kTileKeys + 4;  // bytes per transposed V row (padding against bank conflicts)
+constexpr int kPLevels = 16383;        // qwen3.py P_LEVELS: 14-bit probabilities
+constexpr int kMaxKeysLog2 = 20;       // qwen3.py MAX_KEYS = 2^20 (exact_rowsum's length bound)
+
+// detrt.core.det_log (core.py:130-143): x = m 2^e, log m = 2 atanh((m - 1) / (m + 1)) as the odd
+// series to s^15 in Horner form; one rounding per op.
+__device__ __forceinline__ float det_log(float x) {
+  int e;
+  float m = frexpf(x, &e);  // m in [0.5, 1)
+  m = __fmul_rn(m, 2.0f);
+  const float ef = (float)(e - 1);
+  const float s = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+  const float s2 = __fmul_rn(s, s);
+  float acc = (float)(1.0 / 15);
+  acc = __fadd_rn(__fmul_rn(acc, s2), (float)(1.0 / 13));
+  acc = __fadd_rn(__fmul_rn(acc, s2), (float)(1.0 / 11));
+  acc = __fadd_rn(__fmul_rn(acc, s2), (float)(1.0 / 9));
+  acc = __fadd_rn(__fmul_rn(acc, s2), (float)(1.0 / 7));
+  acc = __fadd_rn(__fmul_rn(acc, s2), (float)(1.0 / 5));
+  acc = __fadd_rn(__fmul_rn(acc, s2), (float)(1.0 / 3));
+  acc = __fadd_rn(__fmul_rn(acc, s2), 1.0f);
+  const float lm = __fmul_rn(__fmul_rn(acc, s), 2.0f);
+  return __fadd_rn(__fmul_rn(ef, (float)0.6931471805599453), lm);
+}
+
+// Exact fixed-point row sum term (core.py:85-108): the int64 image of v at scale 2^sh.
+__device__ __forceinline__ long long fixed_term(float v, double up) { return __double2ll_rn((double)v * up); }
+
+__device__ __forceinline__ int fixed_shift(float amax, int L) {
+  int e;
+  frexpf(amax, &e);
+  return min(max((62 - L) - e, -1000), 1000);
+}
+
+struct AttnArgs {
+  const int8_t* qq;   // (N_q, H, 128), row n = b * Tq + t
+  const float* qs;    // (N_q, H)
+  const int8_t* kc;   // keys: element (b, j, g, d) at b * kv_seq + j * kv_tok + g * kv_head + d
+  const float* ks;    // key scales: (b, j, g) at b * s_seq + j * s_tok + g * s_head
+  const int8_t* vc;   // values, same strides as the keys
+  const float* vs;    // value scales, same strides as the key scales
+  long long kv_seq, kv_tok, kv_head, s_seq, s_tok, s_head;
+  int Tq, start, H, Hkv;
+  float inv_sqrt_hd;
+  float* out;         // (N_q, H * 128)
+};
+
+// Row r of this CTA is query t = t0 + r at absolute position start + t; it sees keys 0..start + t.
+template <int QT>
+__global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, int spitch) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  float* sc = reinterpret_cast<float*>(sm);                              // QT x spitch
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(sm + (size_t)QT * spitch * 4);  // QT x 32 words
+  uint8_t* vt = reinterpret_cast<uint8_t*>(qrow + QT * 32);             // 128 x kVtPitch
+  __shared__ float s_qs[QT], s_sp[QT];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.x / a.H, h = blockIdx.x % a.H, g = h / (a.H / a.Hkv);
+  const int t0 = blockIdx.y * QT;
+  const int nrows = min(QT, a.Tq - t0);
+  const int S = a.start + t0 + nrows;                      // keys this CTA needs
+  const int Sp = (S + kTileKeys - 1) / kTileKeys * kTileKeys;
+  const int8_t* kb = a.kc + b * a.kv_seq + g * a.kv_head;
+  const int8_t* vb = a.vc + b * a.kv_seq + g * a.kv_head;
+  const float* ksb = a.ks + b * a.s_seq + g * a.s_head;
+  const float* vsb = a.vs + b * a.s_seq + g * a.s_head;
+
+  // ---- queries (int8 rows) and their scales
+  for (int i = tid; i < QT * 32; i += kAttnThreads) {
+    const int r = i >> 5;
+    qrow[i] = r < nrows ? reinterpret_cast<const uint32_t*>(a.qq + ((size_t)(b * a.Tq + t0 + r) * a.H + h) * kHd)[i & 31]
+                        : 0u;
+  }
+  if (tid < QT) s_qs[tid] = tid < nrows ? a.qs[(size_t)(b * a.Tq + t0 + tid) * a.H + h] : 0.f;
+  __syncthreads();
+
+  // ---- scores: fmul(fmul(fmul(float(q . k), qs), ks), 1/sqrt(hd)), -inf past the query's position
+  for (int j = tid; j < S; j += kAttnThreads) {
+    uint32_t kw[32];
+    const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)j * a.kv_tok);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint4 v = __ldg(kp + i);
+      kw[4 * i] = v.x; kw[4 * i + 1] = v.y; kw[4 * i + 2] = v.z; kw[4 * i + 3] = v.w;
+    }
+    const float ksj = __ldg(ksb + (size_t)j * a.s_tok);
+#pragma unroll 1
+    for (int r = 0; r < nrows; r++) {
+      int dot = 0;
+#pragma unroll
+      for (int i = 0; i < 32; i++) dot = __dp4a((int)kw[i], (int)qrow[r * 32 + i], dot);
+      const float v = __fmul_rn(__fmul_rn(__fmul_rn((float)dot, s_qs[r]), ksj), a.inv_sqrt_hd);
+      sc[r * spitch + j] = j <= a.start + t0 + r ? v : __int_as_float(0xff800000);
+    }
+  }
+  __syncthreads();
+
+  // ---- per row (one warp per row): max, det_exp, exact sum, P * sv, 14-bit quantization
+  for (int r = warp; r < nrows; r += kAttnThreads / 32) {
+    float* row = sc + r * spitch;
+    float mx = __int_as_float(0xff800000);
+    for (int j = lane; j < S; j += 32) mx = fmaxf(mx, row[j]);
+    mx = warp_maxf(mx);
+    float emax = 0.f;
+    for (int j = lane; j < S; j += 32) {
+      const float e = det_exp(__fsub_rn(row[j], mx));
+      row[j] = e;
+      emax = fmaxf(emax, e);
+    }
+    emax = warp_maxf(emax);
+    const int sh = fixed_shift(emax, kMaxKeysLog2);
+    const double up = pow2d(sh);
+    long long acc = 0;
+    for (int j = lane; j < S; j += 32) acc += fixed_term(row[j], up);
+    acc = warp_sumll(acc);
+    const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+    float pmax = 0.f;
+    for (int j = lane; j < S; j += 32) {
+      const float pv = __fmul_rn(__fdiv_rn(row[j], den), __ldg(vsb + (size_t)j * a.s_tok));
+      row[j] = pv;
+      pmax = fmaxf(pmax, pv);
+    }
+    pmax = warp_maxf(pmax);
+    const float sp = __fdiv_rn(fmaxf(pmax, 1e-30f), (float)kPLevels);
+    for (int j = lane; j < Sp; j += 32) {
+      int pi = 0;
+      if (j < S) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels);
+      reinterpret_cast<int*>(row)[j] = pi;
+    }
+    if (lane == 0) s_sp[r] = sp;
+  }
+  __syncthreads();
+
+  // ---- P V: warp w owns rows w, w + 8, ...; lane l owns dims l, l + 32, l + 64, l + 96. Per
+  // 64-key tile, V is staged transposed (vt[dim][key], 4 keys per word) and each dp4a adds four
+  // keys' hi (resp. lo) limbs times their values: every sum is an exact int32 (|sum| <
+  // 127 * 127 * S), and (hi << 7) + lo is summed in int64 as detrt does per 1024-key chunk.
+  constexpr int RPW = (QT + 7) / 8;   // rows per warp
+  int acc_hi[RPW][4], acc_lo[RPW][4];
+#pragma unroll
+  for (int i = 0; i < RPW; i++)
+#pragma unroll
+    for (int y = 0; y < 4; y++) acc_hi[i][y] = acc_lo[i][y] = 0;
+  const uint32_t* vtw = reinterpret_cast<const uint32_t*>(vt);
+  for (int j0 = 0; j0 < S; j0 += kTileKeys) {
+    // transposed load: 4 keys x 4 dims per block, 16 x 32 blocks per tile
+    for (int bi = tid; bi < (kTileKeys / 4) * (kHd / 4); bi += kAttnThreads) {
+      const int kg = bi >> 5, dg = bi & 31;
+      uint32_t w[4];
+#pragma unroll
+      for (int x = 0; x < 4; x++) {
+        const int j = j0 + 4 * kg + x;
+        w[x] = j < S ? __ldg(reinterpret_cast<const uint32_t*>(vb + (size_t)j * a.kv_tok) + dg) : 0u;
+      }
+      const uint32_t lo01 = __byte_perm(w[0], w[1], 0x5140), hi01 = __byte_perm(w[0], w[1], 0x7362);
+      const uint32_t lo23 = __byte_perm(w[2], w[3], 0x5140), hi23 = __byte_perm(w[2], w[3], 0x7362);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(vt + (size_t)(4 * dg) * kVtPitch) + kg;
+      dst[0] = __byte_perm(lo01, lo23, 0x5410);
+      dst[kVtPitch / 4] = __byte_perm(lo01, lo23, 0x7632);
+      dst[2 * kVtPitch / 4] = __byte_perm(hi01, hi23, 0x5410);
+      dst[3 * kVtPitch / 4] = __byte_perm(hi01, hi23, 0x7632);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < RPW; i++) {
+      const int r = warp + 8 * i;
+      if (r < nrows) {
+        const int4* prow = reinterpret_cast<const int4*>(sc + r * spitch + j0);
+#pragma unroll 4
+        for (int kg = 0; kg < kTileKeys / 4; kg++) {
+          const int4 p4 = prow[kg];
+          // 14-bit probabilities -> four 7-bit hi limbs and four 7-bit lo limbs, one byte each
+          const uint32_t lo4 = __byte_perm(__byte_perm(p4.x, p4.y, 0x0040), __byte_perm(p4.z, p4.w, 0x0040), 0x5410) &
+                               0x7F7F7F7Fu;
+          const uint32_t hi4 = __byte_perm(__byte_perm(p4.x << 1, p4.y << 1, 0x0051),
+                                           __byte_perm(p4.z << 1, p4.w << 1, 0x0051), 0x5410);
+#pragma unroll
+          for (int y = 0; y < 4; y++) {
+            const int vv = (int)vtw[(lane + 32 * y) * (kVtPitch / 4) + kg];
+            acc_hi[i][y] = __dp4a((int)hi4, vv, acc_hi[i][y]);
+            acc_lo[i][y] = __dp4a((int)lo4, vv, acc_lo[i][y]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // o = fmul(float(acc), sp) with acc = (hi << 7) + lo exact in int64 (qwen3.py:276-282)
+#pragma unroll
+  for (int i = 0; i < RPW; i++) {
+    const int r = warp + 8 * i;
+    if (r < nrows) {
+      float* o = a.out + (size_t)(b * a.Tq + t0 + r) * a.H * kHd + h * kHd;
+#pragma unroll
+      for (int y = 0; y < 4; y++)
+        o[lane + 32 * y] = __fmul_rn(__ll2float_rn(((long long)acc_hi[i][y] << 7) + acc_lo[i][y]), s_sp[r]);
+    }
+  }
+}
+
+// det_rmsnorm (core.py:151-159) of one row per CTA, float32 out.
+template <int NT>
+__global__ void __launch_bounds__(NT) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, int k,
+                                                float inv_d, float eps, int L, float* __restrict__ out) {
+  __shared__ float red[NT / 32];
+  __shared__ long long redl[NT / 32];
+  const float* xr = x + (size_t)blockIdx.x * k;
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < k; i += NT) mx = fmaxf(mx, __fmul_rn(xr[i], xr[i]));
+  mx = block_maxf<NT>(mx, red);
+  const int sh = fixed_shift(mx, L);
+  const double up = pow2d(sh);
+  long long acc = 0;
+  for (int i = threadIdx.x; i < k; i += NT) acc += fixed_term(__fmul_rn(xr[i], xr[i]), up);
+  acc = block_sumll<NT>(acc, redl);
+  const float ss = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+  const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_d), eps)));
+  float* o = out + (size_t)blockIdx.x * k;
+  for (int i = threadIdx.x; i < k; i += NT) o[i] = __fmul_rn(__fmul_rn(xr[i], rr), w[i]);
+}
+
+// Larger log-probability wins; equal values keep the lower index (torch.argmax's first maximum).
+__device__ __forceinline__ void better(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+// logprobs of one row of logits per CTA (qwen3.py:302-312): z = lg - max, lp = z - det_log(den),
+// den = exact_rowsum(det_exp(z), 2^18); optionally the first index of the maximal lp.
+template <int NT>
+__global__ void __launch_bounds__(NT) k_logprobs(const float* __restrict__ lg, int V, float* __restrict__ lp,
+                                                 long long* __restrict__ tok) {
+  __shared__ float red[NT / 32];
+  __shared__ long long redl[NT / 32];
+  __shared__ float rv[NT / 32];
+  __shared__ int ri[NT / 32];
+  const float* x = lg + (size_t)blockIdx.x * V;
+  float mx = __int_as_float(0xff800000);
+  for (int i = threadIdx.x; i < V; i += NT) mx = fmaxf(mx, x[i]);
+  mx = block_maxf<NT>(mx, red);
+  float emax = 0.f;
+  for (int i = threadIdx.x; i < V; i += NT) emax = fmaxf(emax, det_exp(__fsub_rn(x[i], mx)));
+  emax = block_maxf<NT>(emax, red);
+  const int sh = fixed_shift(emax, 18);
+  const double up = pow2d(sh);
+  long long acc = 0;
+  for (int i = threadIdx.x; i < V; i += NT) acc += fixed_term(det_exp(__fsub_rn(x[i], mx)), up);
+  acc = block_sumll<NT>(acc, redl);
+  const float lden = det_log(__double2float_rn(__ll2double_rn(acc) * pow2d(-sh)));
+  float bv = __int_as_float(0xff800000);
+  int bi = 0x7fffffff;
+  float* o = lp ? lp + (size_t)blockIdx.x * V : nullptr;
+  for (int i = threadIdx.x; i < V; i += NT) {
+    const float v = __fsub_rn(__fsub_rn(x[i], mx), lden);
+    if (o) o[i] = v;
+    better(bv, bi, v, i);
+  }
+  if (!tok) return;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, off);
+    better(bv, bi, v2, i2);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    rv[threadIdx.x >> 5] = bv;
+    ri[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int wdx = 1; wdx < NT / 32; wdx++) better(bv, bi, rv[wdx], ri[wdx]);
+    tok[blockIdx.x] = bi;
+  }
+}
+
+constexpr int kAttnSmemMax = 200 * 1024;
+
+size_t attn_smem(int QT, int spitch) { return (size_t)QT * spitch * 4 + (size_t)QT * 128 + (size_t)kHd * kVtPitch; }
+
+// Opt in to more than 48 KiB of dynamic shared memory, once per kernel and device.
+int smem_optin(const void* kernel, int bytes) {
+  if (bytes <= 48 * 1024) return UWC_OK;
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({dev, kernel})) return UWC_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmemMax) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  done.insert({dev, kernel});
+  return UWC_OK;
+}
+
+template <int QT>
+int launch_attn(const AttnArgs& a, int B, int spitch, cudaStream_t st) {
+  const int smem = (int)attn_smem(QT, spitch);
+  const int rc = smem_optin((const void*)k_attention<QT>, smem);
+  if (rc != UWC_OK) return rc;
+  k_attention<QT><<<dim3(B * a.H, (a.Tq + QT - 1) / QT), kAttnThreads, smem, st>>>(a, spitch);
+  return uwc_launch_status();
+}
+
+}  // namespace
+
+extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                             const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq,
+                             long long kv_tok, long long kv_head, long long s_seq, long long s_tok, long long s_head,
+                             float inv_sqrt_hd, float* out, void* stream) {
+  if (!qq || !qs || !kc || !ks || !vc || !vs || !out) return UWC_ERR_ARG;
+  if (B < 0 || Tq < 0 || start < 0 || H <= 0 || Hkv <= 0 || H % Hkv) return UWC_ERR_SHAPE;
+  if ((((uintptr_t)qq) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15) return UWC_ERR_ALIGN;
+  if (kv_tok % 16 || kv_head % 16 || kv_seq % 16) return UWC_ERR_ALIGN;   // 16-byte key / value rows
+  UWC_CHECK_DEVICE();
+  if (B == 0 || Tq == 0) return UWC_OK;
+  if ((long long)B * H > 0x7fffffffLL) return UWC_ERR_SHAPE;
+  const int S = start + Tq;
+  const int spitch = (S + kTileKeys - 1) / kTileKeys * kTileKeys;
+  AttnArgs a{qq, qs, kc, ks, vc, vs, kv_seq, kv_tok, kv_head, s_seq, s_tok, s_head, Tq, start, H, Hkv, inv_sqrt_hd,
+             out};
+  cudaStream_t st = (cudaStream_t)stream;
+  // the widest query block whose score rows fit in shared memory (and not wider than Tq needs)
+  const int want = Tq >= 16 ? 16 : Tq >= 8 ? 8 : Tq >= 4 ? 4 : Tq >= 2 ? 2 : 1;
+  for (int QT = want; QT >= 1; QT >>= 1) {
+    if (attn_smem(QT, spitch) > (size_t)kAttnSmemMax) continue;
+    switch (QT) {
+      case 16: return launch_attn<16>(a, B, spitch, st);
+      case 8: return launch_attn<8>(a, B, spitch, st);
+      case 4: return launch_attn<4>(a, B, spitch, st);
+      case 2: return launch_attn<2>(a, B, spitch, st);
+      default: return launch_attn<1>(a, B, spitch, st);
+    }
+  }
+  return UWC_ERR_SHAPE;   // more keys than one score row of shared memory holds
+}
+
+extern "C" int uwc_rmsnorm(const float* x, const float* w, int m, int k, double eps, float* out, void* stream) {
+  if (!x || !w || !out || m < 0 || k <= 0) return UWC_ERR_ARG;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  int L = 1;
+  while ((1 << L) < k) L++;
+  // detrt rounds 1/d and eps from float64 to float32 (core.c32)
+  k_rmsnorm<256><<<m, 256, 0, (cudaStream_t)stream>>>(x, w, k, (float)(1.0 / k), (float)eps, L, out);
+  return uwc_launch_status();
+}
+
+extern "C" int uwc_logprobs(const float* logits, int m, int V, float* lp, long long* tok, void* stream) {
+  if (!logits || m < 0 || V <= 0 || (!lp && !tok)) return UWC_ERR_ARG;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  k_logprobs<1024><<<m, 1024, 0, (cudaStream_t)stream>>>(logits, V, lp, tok);
+  return uwc_launch_status();
+}

@@ -16,6 +16,7 @@ DEV_TIMEOUT = 1
 
 # (name, restype, argtypes) for every function declared in include/uwc_b200.h
 _P, _U32, _U64, _I32, _F64 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_double
+_I64, _F32 = ctypes.c_longlong, ctypes.c_float
 SIGNATURES = {
     "uwc_version": (_I32, []),
     "uwc_status_string": (ctypes.c_char_p, [_I32]),
@@ -42,6 +43,10 @@ SIGNATURES = {
     "uwc_dequant_residual": (_I32, [_P, _P, _P, _P, _I32, _I32, _P, _P]),
     "uwc_qkv_post": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F64, _I32, _P, _P, _P, _P, _P, _P,
                             _P]),
+    "uwc_attention": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64,
+                             _F32, _P, _P]),
+    "uwc_rmsnorm": (_I32, [_P, _P, _I32, _I32, _F64, _P, _P]),
+    "uwc_logprobs": (_I32, [_P, _I32, _I32, _P, _P, _P]),
 }
 
 _LIB = None

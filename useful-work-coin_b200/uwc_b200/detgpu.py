@@ -163,3 +163,58 @@ def mlp_residual(gu, down, w_norm: torch.Tensor, r1: torch.Tensor, eps: float) -
     q3, s3 = rmsnorm_quant(r1, w_norm, eps, gu.bs)
     q4, s4 = swiglu_quant(det.int_gemm(q3, gu.Wq), s3, gu.sw, down.bs)
     return dequant_residual(det.int_gemm(q4, down.Wq), s4, down.sw, r1)
+
+
+def _attn(qq, qs, kc, ks, vc, vs, B, Tq, start, H, Hkv, strides, inv_sqrt_hd) -> torch.Tensor:
+    assert qq.dtype == torch.int8 and qq.shape[-1] == 128 and qq.is_contiguous(), (qq.dtype, qq.shape)
+    out = torch.empty((B * Tq, H * 128), dtype=torch.float32, device=qq.device)
+    check(lib().uwc_attention(_p(qq), _p(_f32(qs)), _p(kc), _p(ks), _p(vc), _p(vs), B, Tq, start, H, Hkv, *strides,
+                              float(inv_sqrt_hd), _p(out), _stream()), "attention")
+    _count()
+    return out
+
+
+def attention(qq, qs, kq, ks, vq, vs, B: int, T: int, H: int, Hkv: int, inv_sqrt_hd_f32: float) -> torch.Tensor:
+    """runtime/detgpu/kernels.py attention: detrt's attention of B sequences of T tokens from
+    quantized q, k, v -- qq (N, H, 128), kq and vq (N, Hkv, 128) int8, qs (N, H, 1), ks and vs
+    (N, Hkv, 1) float32, N = B * T. Returns o as (N, H * 128) float32."""
+    i8 = lambda z: z.to(torch.int8).contiguous()
+    kq, vq = i8(kq), i8(vq)
+    ks, vs = _f32(ks), _f32(vs)
+    strides = (T * Hkv * 128, Hkv * 128, 128, T * Hkv, Hkv, 1)
+    return _attn(i8(qq), qs, kq, ks, vq, vs, B, T, 0, H, Hkv, strides, inv_sqrt_hd_f32)
+
+
+def attention_cache(qq, qs, cache: dict, B: int, Tq: int, start: int, H: int, Hkv: int,
+                    inv_sqrt_hd_f32: float) -> torch.Tensor:
+    """Attention of Tq new tokens per sequence (positions start .. start + Tq - 1) over a KV cache
+    laid out as runtime/detrt/qwen3.py new_cache: k, v (B, Hkv, maxlen, 128) int8, sk, sv
+    (B, Hkv, maxlen, 1) float32, already holding keys 0 .. start + Tq - 1 (qwen3.py:254-283)."""
+    k, v, sk, sv = cache["k"], cache["v"], cache["sk"], cache["sv"]
+    assert k.is_contiguous() and v.is_contiguous() and sk.is_contiguous() and sv.is_contiguous()
+    maxlen = k.shape[2]
+    assert start + Tq <= maxlen
+    strides = (Hkv * maxlen * 128, 128, maxlen * 128, Hkv * maxlen, 1, maxlen)
+    return _attn(qq.contiguous(), qs, k, sk, v, sv, B, Tq, start, H, Hkv, strides, inv_sqrt_hd_f32)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """detrt.core.det_rmsnorm(x, w, eps) for float32 rows."""
+    x, w = _f32(x), _f32(w)
+    m, k = x.shape
+    out = torch.empty_like(x)
+    check(lib().uwc_rmsnorm(_p(x), _p(w), m, k, float(eps), _p(out), _stream()), "rmsnorm")
+    _count()
+    return out
+
+
+def logprobs(logits: torch.Tensor, want_lp: bool = True):
+    """DetQwen3.logprobs rows (runtime/detrt/qwen3.py:302-312) and the greedy tokens (the first
+    index of each row's maximal log-probability): (lp or None, tokens int64)."""
+    lg = _f32(logits)
+    m, V = lg.shape
+    lp = torch.empty_like(lg) if want_lp else None
+    tok = torch.empty(m, dtype=torch.int64, device=lg.device)
+    check(lib().uwc_logprobs(_p(lg), m, V, _p(lp), _p(tok), _stream()), "logprobs")
+    _count()
+    return lp, tok

@@ -1,0 +1,242 @@
+"""runtime/detrt/qwen3.py's deterministic Qwen3 / Llama forward on B200, bit-identical to detrt.
+
+`DetQwen3` keeps the reference class's name, constructor arguments and methods (new_cache,
+forward, logprobs, generate_greedy; qwen3.py:137-329), so provider code and the reference's own
+determinism tests can switch by import. Every op runs on this library's kernels:
+
+  embedding row gather                       torch indexing (a copy)
+  det_rmsnorm + quant_act                    rmsnorm_quant            qwen3.py:294 + DetLinear
+  q / k / v linear                           tcgen05 int8 GEMM        DetLinear.int_gemm
+  dequant, q/k head norm, rope, quant127     qkv_post                 qwen3.py:240-252
+  attention (cache, causal, exact P V)       attention_cache          qwen3.py:253-283
+  o linear + residual                        quant_act, GEMM, dequant_residual
+  MLP + residual                             detgpu.mlp_residual      qwen3.py:295-297
+  final norm                                 rmsnorm                  qwen3.py:299
+  lm_head, log-softmax, greedy argmax        GEMM (dequant fused), logprobs   qwen3.py:302-329
+
+Weights are quantized on the GPU with quant_act, which is DetLinear's own quantization
+(fwht(bs), quant_sym(64), the 1/sqrt(bs) fold; qwen3.py:73-88) evaluated bit for bit.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import torch
+
+from . import det, detgpu
+
+MAX_KEYS = 1 << 20          # qwen3.py:33, the attention row sum's length bound (kernel constant)
+ARCH_QWEN3, ARCH_LLAMA = 0, 1
+ARCHS = {"qwen3": ARCH_QWEN3, "llama": ARCH_LLAMA, "mistral": ARCH_LLAMA}
+
+
+def llama3_inv_freq(inv: np.ndarray, factor: float, low: float, high: float, orig: int) -> np.ndarray:
+    """Llama 3.1+ rotary frequency scaling, in float64 (qwen3.py:38-47): long wavelengths divided
+    by `factor`, short ones kept, a linear blend in between."""
+    low_wl, high_wl = orig / low, orig / high
+    wl = 2 * np.pi / inv
+    scaled = np.where(wl > low_wl, inv / factor, inv)
+    blend = (orig / wl - low) / (high - low)
+    mid = (1 - blend) * scaled / factor + blend * scaled
+    in_mid = (wl >= high_wl) & (wl <= low_wl)
+    return np.where(in_mid, mid, scaled)
+
+
+def rope_table(theta: float, head_dim: int, max_pos: int = 8192, scaling: dict | None = None):
+    """float32 cos / sin rows for positions 0..max_pos-1 (qwen3.py:50-68): angles in float64,
+    emb = [ang, ang], rounded once to float32. Returns (cos, sin, sha256 of cos||sin)."""
+    inv = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float64) / head_dim))
+    if scaling:
+        inv = llama3_inv_freq(inv, float(scaling["factor"]), float(scaling["low_freq_factor"]),
+                              float(scaling["high_freq_factor"]), int(scaling["original_max_position_embeddings"]))
+    ang = np.arange(max_pos, dtype=np.float64)[:, None] * inv[None, :]
+    emb = np.concatenate([ang, ang], axis=1)
+    cos, sin = np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
+    return cos, sin, hashlib.sha256(cos.tobytes() + sin.tobytes()).hexdigest()
+
+
+def rope_config(cfg) -> tuple[float, dict | None]:
+    """(theta, Llama 3 scaling or None) of a transformers config (qwen3.py:133-148)."""
+    rp = dict(getattr(cfg, "rope_parameters", None) or {})
+    rs = dict(getattr(cfg, "rope_scaling", None) or {})
+    theta = getattr(cfg, "rope_theta", None) or rp.get("rope_theta") or 1e6
+    kind = rp.get("rope_type") or rs.get("rope_type") or rs.get("type") or "default"
+    if kind == "default":
+        return float(theta), None
+    if kind != "llama3":
+        raise ValueError(f"rope scaling {kind!r} is not supported by the deterministic runtime")
+    src = rp if rp.get("rope_type") == "llama3" else rs
+    return float(theta), {k: src[k] for k in ("factor", "low_freq_factor", "high_freq_factor",
+                                              "original_max_position_embeddings")}
+
+
+class Linear:
+    """A deterministic int8 linear (DetLinear, qwen3.py:71-126): Wq (n x k int8), sw (n float32),
+    bs (Hadamard block). `int_gemm(q)` is the exact int32 q @ Wq^T; calling it on float32 rows
+    quantizes them (quant_act) and returns the dequantized product."""
+
+    def __init__(self, W: torch.Tensor, device, hadamard_block: int):
+        n, k = W.shape
+        self.n, self.k = n, k
+        self.bs = min(hadamard_block, k & -k) if hadamard_block else 0
+        Wq, sw = [], []
+        for r0 in range(0, n, 16384):                      # bound the float32 staging copy
+            q, s = detgpu.quant_act(W[r0:r0 + 16384].to(device=device, dtype=torch.float32), self.bs)
+            Wq.append(q)
+            sw.append(s)
+        self.Wq = torch.cat(Wq).contiguous()
+        self.sw = torch.cat(sw).contiguous()
+
+    def int_gemm(self, q: torch.Tensor) -> torch.Tensor:
+        return det.int_gemm(q, self.Wq)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        q, s = detgpu.quant_act(x, self.bs)
+        return det.linear_f32(q, s, self.Wq, self.sw)
+
+
+class DetQwen3:
+    """Qwen3, Llama and Mistral checkpoints on one B200 (qwen3.py:151-329): the same outputs, bit
+    for bit, as the reference's DetQwen3 on any device. hf_model: a transformers causal LM (its
+    weights are read once and quantized on the GPU)."""
+
+    def __init__(self, hf_model, device="cuda", hadamard_block: int = 512, mine: bool = False, max_pos: int = 8192):
+        cfg = hf_model.config
+        if mine:
+            raise ValueError("the mined GEMM path of DetQwen3 is MinedWeight (ops.py); this runtime is the plain one")
+        if cfg.model_type not in ARCHS:
+            raise ValueError(f"model type {cfg.model_type!r} is not supported (supported: {sorted(ARCHS)})")
+        if getattr(cfg, "attention_bias", False) or getattr(cfg, "mlp_bias", False):
+            raise ValueError("biased attention or MLP projections are not supported")
+        if getattr(cfg, "hidden_act", "silu") != "silu":
+            raise ValueError(f"activation {cfg.hidden_act!r} is not supported")
+        sw_ = getattr(cfg, "sliding_window", None)
+        if ARCHS[cfg.model_type] == ARCH_LLAMA and sw_ is not None and sw_ < max_pos:
+            raise ValueError(f"sliding-window attention ({sw_} < MaxPos {max_pos}) is not supported")
+        self.device = torch.device(device)
+        base = hf_model.model
+        W = lambda mod: mod.weight.detach()
+        hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        layers = []
+        for lay in base.layers:
+            at, mlp = lay.self_attn, lay.mlp
+            layers.append(dict(
+                in_norm=W(lay.input_layernorm), post_norm=W(lay.post_attention_layernorm),
+                q_norm=W(at.q_norm) if hasattr(at, "q_norm") else None,
+                k_norm=W(at.k_norm) if hasattr(at, "k_norm") else None,
+                qkv=torch.cat([W(at.q_proj), W(at.k_proj), W(at.v_proj)]), o=W(at.o_proj),
+                gu=torch.cat([W(mlp.gate_proj), W(mlp.up_proj)]), down=W(mlp.down_proj)))
+        self._build(cfg.model_type, cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, hd,
+                    cfg.rms_norm_eps, rope_config(cfg), W(base.embed_tokens), layers, W(base.norm),
+                    W(hf_model.lm_head), hadamard_block, max_pos)
+
+    @classmethod
+    def from_weights(cls, model_type: str, D: int, H: int, Hkv: int, hd: int, eps: float, rope, embed, layers,
+                     norm, lm_head, device="cuda", hadamard_block: int = 512, max_pos: int = 8192) -> "DetQwen3":
+        """The same model from raw float weights (layers: dicts with in_norm, post_norm, q_norm,
+        k_norm, qkv = [q; k; v], o, gu = [gate; up], down), e.g. random-initialized on the GPU."""
+        self = cls.__new__(cls)
+        self.device = torch.device(device)
+        self._build(model_type, D, H, Hkv, hd, eps, rope, embed, layers, norm, lm_head, hadamard_block, max_pos)
+        return self
+
+    def _build(self, model_type, D, H, Hkv, hd, eps, rope, embed, layers, norm, lm_head, hb, max_pos):
+        if hd != 128:
+            raise ValueError(f"head_dim {hd}: the attention kernel is built for head_dim 128")
+        dev = self.device
+        f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
+        self.arch = ARCHS[model_type]
+        self.qk_norm = self.arch == ARCH_QWEN3
+        self.D, self.H, self.Hkv, self.hd, self.eps = D, H, Hkv, hd, eps
+        self.hadamard_block = hb
+        cos, sin, self.rope_sha = rope_table(rope[0], hd, max_pos, rope[1])
+        self.cos, self.sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+        self.embed = f32(embed)
+        ones = torch.ones(hd, dtype=torch.float32, device=dev)   # Llama / Mistral: q/k norms never read
+        self.layers = []
+        for L in layers:
+            self.layers.append(dict(
+                in_norm=f32(L["in_norm"]), post_norm=f32(L["post_norm"]),
+                q_norm=f32(L["q_norm"]) if self.qk_norm else ones, k_norm=f32(L["k_norm"]) if self.qk_norm else ones,
+                qkv=Linear(L["qkv"], dev, hb), o=Linear(L["o"], dev, hb), gu=Linear(L["gu"], dev, hb),
+                down=Linear(L["down"], dev, hb)))
+        self.norm = f32(norm)
+        self.lm_head = Linear(lm_head, dev, hb)
+        # float(torch.tensor(1 / sqrt(hd)).to(F32)): the float64 value rounded once to float32
+        self.inv_sqrt_hd = float(np.float32(1.0 / np.sqrt(hd)))
+
+    def linears(self):
+        for L in self.layers:
+            yield from (L["qkv"], L["o"], L["gu"], L["down"])
+        yield self.lm_head
+
+    # ---------------------------------------------------------------- cache (qwen3.py:216-221)
+    def new_cache(self, B: int, max_len: int):
+        dev = self.device
+        z = lambda *s, dt=torch.int8: torch.zeros(*s, dtype=dt, device=dev)
+        return [dict(k=z(B, self.Hkv, max_len, self.hd), sk=z(B, self.Hkv, max_len, 1, dt=torch.float32),
+                     v=z(B, self.Hkv, max_len, self.hd), sv=z(B, self.Hkv, max_len, 1, dt=torch.float32))
+                for _ in self.layers]
+
+    # ---------------------------------------------------------------- forward (qwen3.py:286-299)
+    def _layer(self, L, x, cache, B: int, T: int, start: int, cos_t, sin_t) -> torch.Tensor:
+        H, Hkv, hd = self.H, self.Hkv, self.hd
+        q1, s1 = detgpu.rmsnorm_quant(x, L["in_norm"], self.eps, L["qkv"].bs)
+        qq, qs, kq, ks, vq, vs = detgpu.qkv_post(L["qkv"].int_gemm(q1), s1, L["qkv"].sw, L["q_norm"], L["k_norm"],
+                                                 cos_t, sin_t, T, H, Hkv, self.eps, self.qk_norm)
+        end = start + T
+        cache["k"][:, :, start:end] = kq.view(B, T, Hkv, hd).transpose(1, 2)
+        cache["v"][:, :, start:end] = vq.view(B, T, Hkv, hd).transpose(1, 2)
+        cache["sk"][:, :, start:end] = ks.view(B, T, Hkv, 1).transpose(1, 2)
+        cache["sv"][:, :, start:end] = vs.view(B, T, Hkv, 1).transpose(1, 2)
+        o = detgpu.attention_cache(qq, qs, cache, B, T, start, H, Hkv, self.inv_sqrt_hd)
+        q2, s2 = detgpu.quant_act(o, L["o"].bs)
+        r1 = detgpu.dequant_residual(L["o"].int_gemm(q2), s2, L["o"].sw, x)
+        return detgpu.mlp_residual(L["gu"], L["down"], L["post_norm"], r1, self.eps)
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor, cache, start: int = 0, layer_hashes: list | None = None) -> torch.Tensor:
+        """ids: (B, T) tokens at positions start..start+T-1. Returns the final-norm hidden (B, T, D) fp32."""
+        B, T = ids.shape
+        x = self.embed[ids.to(self.device).reshape(-1)]
+        cos_t = self.cos[start:start + T].contiguous()
+        sin_t = self.sin[start:start + T].contiguous()
+        for L, c in zip(self.layers, cache):
+            x = self._layer(L, x, c, B, T, start, cos_t, sin_t)
+            if layer_hashes is not None:
+                layer_hashes.append(sha(x.reshape(B, T, self.D)))
+        return detgpu.rmsnorm(x, self.norm, self.eps).reshape(B, T, self.D)
+
+    @torch.no_grad()
+    def logprobs(self, hidden: torch.Tensor, chunk: int = 256) -> torch.Tensor:
+        """log_softmax(lm_head(hidden)) rows, deterministic (qwen3.py:302-312)."""
+        flat = hidden.reshape(-1, self.D).to(self.device)
+        out = [detgpu.logprobs(self.lm_head(flat[s0:s0 + chunk]))[0] for s0 in range(0, flat.shape[0], chunk)]
+        return torch.cat(out).reshape(*hidden.shape[:-1], -1)
+
+    @torch.no_grad()
+    def next_tokens(self, last: torch.Tensor) -> torch.Tensor:
+        """Greedy tokens of hidden rows (B, D): argmax of logprobs, first maximum (qwen3.py:322-323)."""
+        return detgpu.logprobs(self.lm_head(last.reshape(-1, self.D)), want_lp=False)[1]
+
+    @torch.no_grad()
+    def generate_greedy(self, prompt: torch.Tensor, n_new: int):
+        """Prefill the prompt, then decode n_new tokens one at a time (qwen3.py:315-329).
+        Returns (tokens (B, n_new), step hiddens (B, n_new, D))."""
+        B, T0 = prompt.shape
+        cache = self.new_cache(B, T0 + n_new)
+        last = self.forward(prompt, cache, 0)[:, -1]
+        toks, hs = [], []
+        for i in range(n_new):
+            nxt = self.next_tokens(last)
+            toks.append(nxt)
+            hs.append(last)
+            if i + 1 < n_new:
+                last = self.forward(nxt[:, None], cache, T0 + i)[:, 0]
+        return torch.stack(toks, 1), torch.stack(hs, 1)
+
+
+def sha(t: torch.Tensor) -> str:
+    """sha256[:20] of a tensor's bytes (qwen3.py:332-334)."""
+    return hashlib.sha256(t.detach().contiguous().cpu().numpy().tobytes()).hexdigest()[:20]
