@@ -39,6 +39,9 @@ WORKLOADS = {
     # one Llama-3.1-8B layer's deterministic int8 linears, tensor-parallel over the ranks
     "c5-decode": (32, 4096, 14336, 0, "Llama-3.1-8B layer linears, TP over ranks, batch-32 decode (configs[4])"),
     "c5-prefill": (16384, 4096, 14336, 0, "Llama-3.1-8B layer linears, TP over ranks, M=16384 prefill (configs[4])"),
+    # (batch, prompt tokens, generated tokens)
+    "c4-generate": (8, 2048, 128, 0, "Qwen3-1.7B deterministic int8 forward, random-init: batch 8 x 2048 prefill + "
+                                     "128-token greedy decode (configs[3])"),
 }
 # DRAM bytes per launch of the dominant kernel from one ncu capture (committed summary under profiles/)
 TRAFFIC = {"c3-mine": 149.4e6 + 3.9e6}
@@ -227,6 +230,19 @@ def run_reference(a, world, rank):
     m, n, k, r, desc = WORKLOADS[a.workload]
     if rank != 0:
         return
+    if a.workload.startswith("c4"):
+        vals = [c4_cpu_sample(seed=i) for i in range(a.warmup + a.steps)][a.warmup:]
+        t, th = sum(v[0] for v in vals), vals[0][1]
+        value = 16 * a.steps / t
+        sample = "oracle layer forward, 1 x 16 prompt tokens per step through 2 full-width layers, scaled to 28 layers"
+        line = {"impl": "reference", "metric": C4_METRIC, "value": value, "unit": "tokens/s", "n_gpus": a.gpus,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * t / a.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)",
+                "config": {"workload": a.workload, "desc": desc},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": th, "kind": "port", "sample": sample},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if a.workload.startswith("c5"):
         decode = a.workload == "c5-decode"
         rows = m if decode else 256
@@ -382,6 +398,142 @@ def run_c5(a, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ GPU arm, configs[3]
+C4_METRIC = "Deterministic Qwen3-1.7B int8 forward: tokens/s (batch 8 x 2048 prefill + 128-token greedy decode)"
+
+
+def c4_cpu_sample(tokens=16, layers=2, seed=0):
+    """The oracle's layer forward (oracle/detq.py, float64 host GEMMs as detrt's CPU DetLinear) for
+    one sequence of `tokens` tokens through `layers` Qwen3-1.7B-wide layers with random quantized
+    weights. Returns (seconds per 28-layer forward, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import detq as D
+    from uwc_b200.detmodel import QWEN3_1P7B as S
+    from uwc_b200.detmodel import rope_table
+    rng = np.random.default_rng(seed)
+    D_, H, Hkv, I = S["D"], S["H"], S["Hkv"], S["I"]
+    lin = lambda n, k: (rng.integers(-64, 65, (n, k)).astype(np.int8), (rng.random(n) * 1e-3 + 1e-5).astype(np.float32),
+                        512)
+    nrm = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    Ls = [dict(in_norm=nrm(D_), post_norm=nrm(D_), q_norm=nrm(128), k_norm=nrm(128), qkv=lin((H + 2 * Hkv) * 128, D_),
+               o=lin(D_, H * 128), gu=lin(2 * I, D_), down=lin(D_, I)) for _ in range(layers)]
+    cos, sin, _ = rope_table(S["theta"], 128, tokens)
+    x = (rng.standard_normal((tokens, D_)) * 0.05).astype(np.float32)
+    inv = float(np.float32(1 / np.sqrt(128)))
+    t0 = time.perf_counter()
+    for L in Ls:
+        x = D.layer_forward(L, x, 1, tokens, H, Hkv, S["eps"], cos, sin, inv)
+    dt = (time.perf_counter() - t0) * S["layers"] / layers
+    import torch
+    return dt, torch.get_num_threads()
+
+
+def run_c4(a, world, rank, local):
+    """One step = one provider job of configs[3] through this library's DetQwen3: prefill of
+    B x T0 prompt tokens (28 layers), then n_new greedy tokens decoded one at a time with the KV
+    cache (lm_head, log-softmax and argmax on the GPU). With N GPUs every rank runs its own batch
+    (replicas: the forward does not shard)."""
+    import torch
+
+    from uwc_b200 import _lib, ops
+    from uwc_b200.detmodel import QWEN3_1P7B, random_model
+    B, T0, n_new, _, desc = WORKLOADS[a.workload]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _lib.device_status(clear=True)
+    model = random_model(QWEN3_1P7B, dev, seed=7)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    prompt = torch.randint(0, QWEN3_1P7B["vocab"], (B, T0), device=dev, generator=g)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def job(ids, evs=None):
+        cache = model.new_cache(B, T0 + n_new)
+        if evs:
+            evs[0].record(stream)
+        last = model.forward(ids, cache, 0)[:, -1]
+        if evs:
+            evs[1].record(stream)
+        toks = []
+        for i in range(n_new):
+            nxt = model.next_tokens(last)
+            toks.append(nxt)
+            if i + 1 < n_new:
+                last = model.forward(nxt[:, None], cache, T0 + i)[:, 0]
+        if evs:
+            evs[2].record(stream)
+        return torch.stack(toks, 1)
+
+    for _ in range(a.warmup):
+        job(prompt)
+    barrier(world)
+    l0 = ops.LAUNCHES
+    sampler = ClockSampler(local)
+    sampler.start()
+    evs = []
+    for i in range(a.steps):
+        flush.fill_(i & 0xFF)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        job(prompt, e)
+        evs.append(e)
+    barrier(world)
+    clocks = sampler.stop()
+    launches = ops.LAUNCHES - l0
+    t_pre = max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs), world)
+    t_dec = max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in evs), world)
+    t_ms = max_over_ranks(sum(e[0].elapsed_time(e[2]) for e in evs), world)
+    toks_step = B * (T0 + n_new)
+    value = world * toks_step * a.steps / (t_ms / 1e3)
+    # e2e: prompt ids from pinned host memory in, the generated tokens back, every step
+    p_host = prompt.cpu().pin_memory()
+    out_host = torch.empty((B, n_new), dtype=torch.int64).pin_memory()
+    p_dev = torch.empty_like(prompt)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(a.steps):
+        p_dev.copy_(p_host, non_blocking=True)
+        out_host.copy_(job(p_dev), non_blocking=True)
+    e1.record(stream)
+    barrier(world)
+    t2 = max_over_ranks(e0.elapsed_time(e1), world)
+    status = _lib.device_status(clear=True)
+    if rank != 0:
+        return
+    S = QWEN3_1P7B
+    lin_params = S["layers"] * ((S["H"] + 2 * S["Hkv"]) * 128 * S["D"] + S["D"] * S["H"] * 128 + 3 * S["I"] * S["D"])
+    pre_ops = 2.0 * lin_params * B * T0
+    dec_bytes = (lin_params + S["vocab"] * S["D"]) * (n_new - 1) + S["vocab"] * S["D"]   # int8 weights streamed
+    peak_tops = int8_peak(8192, 8192, 4096, flush)
+    pk = peaks()
+    line = {"metric": C4_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (random-init weights N(0, 0.02), seeded prompts)",
+            "config": {"workload": a.workload, "batch": B, "prompt": T0, "new_tokens": n_new, "desc": desc,
+                       "model": "Qwen3-1.7B shape: 28 layers, hidden 2048, 16/8 heads, head_dim 128, MLP 6144, "
+                                "vocab 151936, Hadamard block 512", "parallelism": f"replicas x{world}",
+                       "l2": "flushed (256 MiB write) before each step"},
+            "prefill_tokens_per_s": world * B * T0 * a.steps / (t_pre / 1e3),
+            "decode_tokens_per_s": world * B * n_new * a.steps / (t_dec / 1e3),
+            "prefill_ms": t_pre / a.steps, "decode_ms": t_dec / a.steps,
+            "roofline": {"bound": "tensor", "achieved": pre_ops * a.steps / (t_pre / 1e3) / 1e12, "peak": peak_tops,
+                         "unit": "TOP/s", "frac": pre_ops * a.steps / (t_pre / 1e3) / 1e12 / peak_tops,
+                         "traffic": None, "kernel": "prefill (linear int8 ops / prefill time)",
+                         "peak_source": "cuBLASLt int8 8192^2 x 4096 burst, measured in this run",
+                         "decode_weight_gbs": dec_bytes * a.steps / (t_dec / 1e3) / 1e9,
+                         "decode_peak_gbs": pk["hbm_gbs"]},
+            "e2e": {"value": world * toks_step * a.steps / (t2 / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": B * T0 * 8, "d2h_bytes_per_step": B * n_new * 8},
+            "gpu_launches": launches, "clocks": clocks, "device_status": status}
+    if not a.no_cpu_baseline:
+        dt, th = c4_cpu_sample()
+        line["cpu_baseline"] = {"value": 16 / dt, "unit": "tokens/s", "cores": th, "kind": "port",
+                                "sample": f"oracle layer forward, 1 x 16 prompt tokens through 2 full-width layers, "
+                                          f"scaled to 28 layers ({dt:.1f} s per 28-layer forward)"}
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ GPU arm, NoisyGEMM
 def run_b200(a, world, rank, local):
     import numpy as np
@@ -516,6 +668,8 @@ def main():
             run_reference(a, world, rank)
         elif a.workload.startswith("c5"):
             run_c5(a, world, rank, local)
+        elif a.workload.startswith("c4"):
+            run_c4(a, world, rank, local)
         else:
             run_b200(a, world, rank, local)
     finally:

@@ -17,11 +17,16 @@ srivassid/useful-work-coin) and of the fused detgpu row kernels built from them:
                                                              runtime/detrt/fast.py:108-120
   dequant_residual (x + deq(acc))                            runtime/detgpu/kernels.py:346-354
   swiglu_quant (quant_act(silu(gate) * up))                  runtime/detgpu/kernels.py:356-396
+  attention (exact Q K^T, det_exp softmax, 14-bit P, exact PV) runtime/detrt/qwen3.py:253-283
+  det_log, logprobs                                          runtime/detrt/core.py:130-143,
+                                                             runtime/detrt/qwen3.py:302-312
+  int_gemm, quantize_linear, layer_forward                   runtime/detrt/qwen3.py:71-126,239-297
 
 numpy float32 arithmetic on x86-64 is IEEE single precision with one rounding per operation,
 which is exactly detrt's float64-then-round emulation for + - * / sqrt; the helpers below still
-spell the float64 round trip out. Pinned by tests/test_det_oracle.py against vectors that
-tests/golden/make_golden_det.py produced with detrt itself.
+spell the float64 round trip out. Pinned by tests/test_det_oracle.py and tests/test_model_oracle.py
+against vectors that tests/golden/make_golden_det.py and make_golden_model.py produced with detrt
+itself (the layer composition reproduces detrt's whole prefill forward of a tiny Qwen3).
 """
 from __future__ import annotations
 
@@ -262,3 +267,39 @@ def logprobs(lg):
     z = fsub(lg, lg.max(axis=-1, keepdims=True))
     den = exact_rowsum(det_exp(z), 1 << 18)
     return fsub(z, det_log(den)[..., None])
+
+
+# ------------------------------------------------------------------ the whole forward
+def int_gemm(q, Wq):
+    """DetLinear.int_gemm on CPU (runtime/detrt/qwen3.py:110-111): q @ Wq^T in float64, exact for
+    int8 operands (every partial sum is an integer below 2^53), returned as int64."""
+    return (np.asarray(q, np.float64) @ np.asarray(Wq, np.float64).T).astype(np.int64)
+
+
+def quantize_linear(W, hadamard_block: int):
+    """DetLinear's weight quantization (qwen3.py:73-88): (Wq int8, sw float32, bs)."""
+    W = np.asarray(W, F32)
+    bs = min(hadamard_block, W.shape[1] & -W.shape[1]) if hadamard_block else 0
+    Wq, sw = quant_act(W, bs)
+    return Wq, sw, bs
+
+
+def layer_forward(L: dict, x, B: int, T: int, H: int, Hkv: int, eps: float, cos, sin, inv_sqrt_hd: float,
+                  qk_norm: bool = True):
+    """One decoder layer of DetQwen3.forward for B sequences of T tokens from position 0
+    (qwen3.py:239-297): x (B*T, D) float32 -> (B*T, D). L holds float32 norms and quantized
+    linears (Wq, sw, bs) under qkv, o, gu, down."""
+    Wq, sw, bs = L["qkv"]
+    q1, s1 = rmsnorm_quant(x, L["in_norm"], eps, bs)
+    qq, qs, kq, ks, vq, vs = qkv_post(int_gemm(q1, Wq), s1, sw, L["q_norm"], L["k_norm"], cos, sin, T, H, Hkv, eps,
+                                      qk_norm)
+    o = attention(qq.reshape(B, T, H, 128), qs.reshape(B, T, H), kq.reshape(B, T, Hkv, 128), ks.reshape(B, T, Hkv),
+                  vq.reshape(B, T, Hkv, 128), vs.reshape(B, T, Hkv), 0, inv_sqrt_hd).reshape(B * T, H * 128)
+    Wq, sw, bs = L["o"]
+    q2, s2 = quant_act(o, bs)
+    r1 = dequant_residual(int_gemm(q2, Wq), s2, sw, x)
+    Wq, sw, bs = L["gu"]
+    q3, s3 = rmsnorm_quant(r1, L["post_norm"], eps, bs)
+    Wq2, sw2, bs2 = L["down"]
+    q4, s4 = swiglu_quant(int_gemm(q3, Wq), s3, sw, bs2)
+    return dequant_residual(int_gemm(q4, Wq2), s4, sw2, r1)

@@ -57,3 +57,34 @@ def test_oracle_logprobs_of_the_tiny_model(mg):
     acc = q.astype(np.int64) @ Wq.astype(np.int64).T
     lg = D.fmul(D.fmul(acc.astype(np.float32), sx[:, None]), sw[None, :])
     assert np.array_equal(D.logprobs(lg).view(np.int32), g["lp_last"].view(np.int32))
+
+
+def test_oracle_forward_of_the_tiny_model(mg):
+    """The oracle's layer composition (quantized linears, qkv_post, attention, MLP, final norm)
+    reproduces detrt's prefill hidden of the tiny model bit for bit."""
+    pytest.importorskip("transformers")
+    import detq as D
+    import model_fixture as mf
+    from uwc_b200.detmodel import rope_table
+    meta, g = mg
+    hf = mf.tiny_model()
+    cfg, hb = mf.CFG, mf.HADAMARD_BLOCK
+    f = lambda t: t.detach().float().numpy()
+    cos, sin, sha = rope_table(cfg["rope_parameters"]["rope_theta"], cfg["head_dim"], 8192)
+    assert sha == meta["rope_sha"]
+    B, T = g["prompt"].shape
+    x = f(hf.model.embed_tokens.weight)[g["prompt"].reshape(-1)]
+    inv = float(np.float32(1.0 / np.sqrt(cfg["head_dim"])))
+    import torch
+    for lay in hf.model.layers:
+        at, mlp = lay.self_attn, lay.mlp
+        L = dict(in_norm=f(lay.input_layernorm.weight), post_norm=f(lay.post_attention_layernorm.weight),
+                 q_norm=f(at.q_norm.weight), k_norm=f(at.k_norm.weight),
+                 qkv=D.quantize_linear(f(torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight])), hb),
+                 o=D.quantize_linear(f(at.o_proj.weight), hb),
+                 gu=D.quantize_linear(f(torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight])), hb),
+                 down=D.quantize_linear(f(mlp.down_proj.weight), hb))
+        x = D.layer_forward(L, x, B, T, cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["rms_norm_eps"],
+                            cos, sin, inv)
+    h = D.det_rmsnorm(x, f(hf.model.norm.weight), cfg["rms_norm_eps"]).reshape(B, T, -1)
+    assert np.array_equal(h.view(np.int32), g["hidden"].view(np.int32))

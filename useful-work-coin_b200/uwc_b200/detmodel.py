@@ -159,8 +159,8 @@ class DetQwen3:
             self.layers.append(dict(
                 in_norm=f32(L["in_norm"]), post_norm=f32(L["post_norm"]),
                 q_norm=f32(L["q_norm"]) if self.qk_norm else ones, k_norm=f32(L["k_norm"]) if self.qk_norm else ones,
-                qkv=Linear(L["qkv"], dev, hb), o=Linear(L["o"], dev, hb), gu=Linear(L["gu"], dev, hb),
-                down=Linear(L["down"], dev, hb)))
+                **{nm: L[nm] if isinstance(L[nm], Linear) else Linear(L[nm], dev, hb)
+                   for nm in ("qkv", "o", "gu", "down")}))
         self.norm = f32(norm)
         self.lm_head = Linear(lm_head, dev, hb)
         # float(torch.tensor(1 / sqrt(hd)).to(F32)): the float64 value rounded once to float32
@@ -240,3 +240,39 @@ class DetQwen3:
 def sha(t: torch.Tensor) -> str:
     """sha256[:20] of a tensor's bytes (qwen3.py:332-334)."""
     return hashlib.sha256(t.detach().contiguous().cpu().numpy().tobytes()).hexdigest()[:20]
+
+
+QWEN3_1P7B = dict(model_type="qwen3", D=2048, H=16, Hkv=8, hd=128, I=6144, layers=28, vocab=151936, eps=1e-6,
+                  theta=1e6, tied=True)
+
+
+def random_model(shape: dict = QWEN3_1P7B, device="cuda", seed: int = 0, std: float = 0.02,
+                 hadamard_block: int = 512, max_pos: int = 8192) -> DetQwen3:
+    """A random-initialized model of the given shape, generated and quantized on the GPU one layer
+    at a time (linear weights and the embedding N(0, std), norm weights 1 + N(0, 0.1))."""
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    D, H, Hkv, hd, I = shape["D"], shape["H"], shape["Hkv"], shape["hd"], shape["I"]
+    rnd = lambda *s: torch.randn(*s, device=dev, generator=g) * std
+    nrm = lambda n: 1 + 0.1 * torch.randn(n, device=dev, generator=g)
+    self = DetQwen3.__new__(DetQwen3)
+    self.device = dev
+    embed = rnd(shape["vocab"], D)
+    lm_head = embed if shape.get("tied") else rnd(shape["vocab"], D)
+    layers = []
+    for _ in range(shape["layers"]):
+        # one layer's float weights at a time: quantized right away, then freed
+        L = dict(in_norm=nrm(D), post_norm=nrm(D), q_norm=nrm(hd), k_norm=nrm(hd),
+                 qkv=rnd((H + 2 * Hkv) * hd, D), o=rnd(D, H * hd), gu=rnd(2 * I, D), down=rnd(D, I))
+        layers.append(_QuantizedLayer(L, dev, hadamard_block))
+    self._build(shape["model_type"], D, H, Hkv, hd, shape["eps"], (shape["theta"], None), embed, layers,
+                nrm(D), lm_head, hadamard_block, max_pos)
+    return self
+
+
+class _QuantizedLayer(dict):
+    """A layer's weights with its linears already quantized (so random_model never holds more
+    than one layer of float weights)."""
+
+    def __init__(self, L: dict, dev, hb: int):
+        super().__init__({k: (Linear(v, dev, hb) if k in ("qkv", "o", "gu", "down") else v) for k, v in L.items()})
