@@ -77,20 +77,28 @@ struct AttnArgs {
 };
 
 // Row r of this CTA is query t = t0 + r at absolute position start + t; it sees keys 0..start + t.
+// QT <= 8 rows; each row is owned by WPR = 8 / QT warps, which split its keys (a single decode row
+// uses the whole CTA). Partial maxima and integer sums combine exactly, in any order.
 template <int QT>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, int spitch) {
+  constexpr int NW = kAttnThreads / 32, WPR = NW / QT;
+  static_assert(QT >= 1 && QT <= NW && NW % QT == 0, "rows per CTA");
   extern __shared__ __align__(16) uint8_t sm[];
   float* sc = reinterpret_cast<float*>(sm);                              // QT x spitch
   uint32_t* qrow = reinterpret_cast<uint32_t*>(sm + (size_t)QT * spitch * 4);  // QT x 32 words
   uint8_t* vt = reinterpret_cast<uint8_t*>(qrow + QT * 32);             // 128 x kVtPitch
-  __shared__ float s_qs[QT], s_sp[QT];
+  __shared__ float s_qs[QT], s_sp[QT], s_red[QT][WPR];
+  __shared__ long long s_redl[QT][WPR];
+  // rows split over several warps combine their P V partials here (after the V tile)
+  long long* s_out = reinterpret_cast<long long*>(vt + kHd * kVtPitch);   // QT x WPR x 128
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = warp / WPR, part = warp % WPR;              // this warp's row and key split
   const int b = blockIdx.x / a.H, h = blockIdx.x % a.H, g = h / (a.H / a.Hkv);
   const int t0 = blockIdx.y * QT;
   const int nrows = min(QT, a.Tq - t0);
+  const bool live = r < nrows;
   const int S = a.start + t0 + nrows;                      // keys this CTA needs
-  const int Sp = (S + kTileKeys - 1) / kTileKeys * kTileKeys;
   const int8_t* kb = a.kc + b * a.kv_seq + g * a.kv_head;
   const int8_t* vb = a.vc + b * a.kv_seq + g * a.kv_head;
   const float* ksb = a.ks + b * a.s_seq + g * a.s_head;
@@ -98,9 +106,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
 
   // ---- queries (int8 rows) and their scales
   for (int i = tid; i < QT * 32; i += kAttnThreads) {
-    const int r = i >> 5;
-    qrow[i] = r < nrows ? reinterpret_cast<const uint32_t*>(a.qq + ((size_t)(b * a.Tq + t0 + r) * a.H + h) * kHd)[i & 31]
-                        : 0u;
+    const int rr = i >> 5;
+    qrow[i] = rr < nrows ? reinterpret_cast<const uint32_t*>(a.qq + ((size_t)(b * a.Tq + t0 + rr) * a.H + h) * kHd)[i & 31]
+                         : 0u;
   }
   if (tid < QT) s_qs[tid] = tid < nrows ? a.qs[(size_t)(b * a.Tq + t0 + tid) * a.H + h] : 0.f;
   __syncthreads();
@@ -116,71 +124,99 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
     }
     const float ksj = __ldg(ksb + (size_t)j * a.s_tok);
 #pragma unroll 1
-    for (int r = 0; r < nrows; r++) {
+    for (int rr = 0; rr < nrows; rr++) {
+      const uint4* qv = reinterpret_cast<const uint4*>(qrow + rr * 32);
       int dot = 0;
 #pragma unroll
-      for (int i = 0; i < 32; i++) dot = __dp4a((int)kw[i], (int)qrow[r * 32 + i], dot);
-      const float v = __fmul_rn(__fmul_rn(__fmul_rn((float)dot, s_qs[r]), ksj), a.inv_sqrt_hd);
-      sc[r * spitch + j] = j <= a.start + t0 + r ? v : __int_as_float(0xff800000);
+      for (int i = 0; i < 8; i++) {
+        const uint4 qw = qv[i];
+        dot = __dp4a((int)kw[4 * i], (int)qw.x, dot);
+        dot = __dp4a((int)kw[4 * i + 1], (int)qw.y, dot);
+        dot = __dp4a((int)kw[4 * i + 2], (int)qw.z, dot);
+        dot = __dp4a((int)kw[4 * i + 3], (int)qw.w, dot);
+      }
+      const float v = __fmul_rn(__fmul_rn(__fmul_rn((float)dot, s_qs[rr]), ksj), a.inv_sqrt_hd);
+      sc[rr * spitch + j] = j <= a.start + t0 + rr ? v : __int_as_float(0xff800000);
     }
   }
   __syncthreads();
 
-  // ---- per row (one warp per row): max, det_exp, exact sum, P * sv, 14-bit quantization
-  for (int r = warp; r < nrows; r += kAttnThreads / 32) {
-    float* row = sc + r * spitch;
-    float mx = __int_as_float(0xff800000);
-    for (int j = lane; j < S; j += 32) mx = fmaxf(mx, row[j]);
-    mx = warp_maxf(mx);
-    float emax = 0.f;
-    for (int j = lane; j < S; j += 32) {
+  // ---- per row: max, det_exp, exact sum, P * sv, 14-bit quantization. The row's WPR warps take
+  // keys j = 32 * part + lane (mod 32 * WPR) and combine their partials through shared memory.
+  float* row = sc + r * spitch;
+  const int j0 = 32 * part + lane, js = 32 * WPR;
+  auto row_max = [&](float v) -> float {
+    v = warp_maxf(v);
+    if (lane == 0) s_red[r][part] = v;
+    __syncthreads();
+    float m = s_red[r][0];
+#pragma unroll
+    for (int i = 1; i < WPR; i++) m = fmaxf(m, s_red[r][i]);
+    __syncthreads();
+    return m;
+  };
+  float mx = __int_as_float(0xff800000);
+  if (live)
+    for (int j = j0; j < S; j += js) mx = fmaxf(mx, row[j]);
+  mx = row_max(mx);
+  float emax = 0.f;
+  if (live)
+    for (int j = j0; j < S; j += js) {
       const float e = det_exp(__fsub_rn(row[j], mx));
       row[j] = e;
       emax = fmaxf(emax, e);
     }
-    emax = warp_maxf(emax);
-    const int sh = fixed_shift(emax, kMaxKeysLog2);
-    const double up = pow2d(sh);
-    long long acc = 0;
-    for (int j = lane; j < S; j += 32) acc += fixed_term(row[j], up);
-    acc = warp_sumll(acc);
-    const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
-    float pmax = 0.f;
-    for (int j = lane; j < S; j += 32) {
+  emax = row_max(emax);
+  const int sh = fixed_shift(emax, kMaxKeysLog2);
+  long long acc = 0;
+  if (live) {
+    if (sh <= 100) {                 // |e| 2^sh stays a normal float below 2^62: exact in fp32
+      const float up = pow2f(sh);
+      for (int j = j0; j < S; j += js) acc += __float2ll_rn(__fmul_rn(row[j], up));
+    } else {
+      const double up = pow2d(sh);
+      for (int j = j0; j < S; j += js) acc += fixed_term(row[j], up);
+    }
+  }
+  acc = warp_sumll(acc);
+  if (lane == 0) s_redl[r][part] = acc;
+  __syncthreads();
+  acc = 0;
+#pragma unroll
+  for (int i = 0; i < WPR; i++) acc += s_redl[r][i];
+  const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+  float pmax = 0.f;
+  if (live)
+    for (int j = j0; j < S; j += js) {
       const float pv = __fmul_rn(__fdiv_rn(row[j], den), __ldg(vsb + (size_t)j * a.s_tok));
       row[j] = pv;
       pmax = fmaxf(pmax, pv);
     }
-    pmax = warp_maxf(pmax);
-    const float sp = __fdiv_rn(fmaxf(pmax, 1e-30f), (float)kPLevels);
-    for (int j = lane; j < Sp; j += 32) {
+  pmax = row_max(pmax);
+  const float sp = __fdiv_rn(fmaxf(pmax, 1e-30f), (float)kPLevels);
+  const int Sp = (S + kTileKeys - 1) / kTileKeys * kTileKeys;
+  if (live)
+    for (int j = j0; j < Sp; j += js) {
       int pi = 0;
       if (j < S) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels);
       reinterpret_cast<int*>(row)[j] = pi;
     }
-    if (lane == 0) s_sp[r] = sp;
-  }
+  if (lane == 0 && part == 0) s_sp[r] = sp;
   __syncthreads();
 
-  // ---- P V: warp w owns rows w, w + 8, ...; lane l owns dims l, l + 32, l + 64, l + 96. Per
-  // 64-key tile, V is staged transposed (vt[dim][key], 4 keys per word) and each dp4a adds four
-  // keys' hi (resp. lo) limbs times their values: every sum is an exact int32 (|sum| <
-  // 127 * 127 * S), and (hi << 7) + lo is summed in int64 as detrt does per 1024-key chunk.
-  constexpr int RPW = (QT + 7) / 8;   // rows per warp
-  int acc_hi[RPW][4], acc_lo[RPW][4];
-#pragma unroll
-  for (int i = 0; i < RPW; i++)
-#pragma unroll
-    for (int y = 0; y < 4; y++) acc_hi[i][y] = acc_lo[i][y] = 0;
+  // ---- P V: lane l owns dims l, l + 32, l + 64, l + 96 of its row; the row's warps split each
+  // 64-key tile's 4-key groups. V is staged per tile transposed (vt[dim][key], 4 keys a word), so
+  // each dp4a adds four keys' hi (resp. lo) limbs times their values: exact int32 partial sums
+  // (|sum| < 127 * 127 * S), combined as (hi << 7) + lo in int64 (detrt sums per 1024-key chunk).
+  int acc_hi[4] = {0, 0, 0, 0}, acc_lo[4] = {0, 0, 0, 0};
   const uint32_t* vtw = reinterpret_cast<const uint32_t*>(vt);
-  for (int j0 = 0; j0 < S; j0 += kTileKeys) {
-    // transposed load: 4 keys x 4 dims per block, 16 x 32 blocks per tile
+  for (int jt = 0; jt < S; jt += kTileKeys) {
     for (int bi = tid; bi < (kTileKeys / 4) * (kHd / 4); bi += kAttnThreads) {
       const int kg = bi >> 5, dg = bi & 31;
       uint32_t w[4];
 #pragma unroll
       for (int x = 0; x < 4; x++) {
-        const int j = j0 + 4 * kg + x;
+        const int j = jt + 4 * kg + x;
         w[x] = j < S ? __ldg(reinterpret_cast<const uint32_t*>(vb + (size_t)j * a.kv_tok) + dg) : 0u;
       }
       const uint32_t lo01 = __byte_perm(w[0], w[1], 0x5140), hi01 = __byte_perm(w[0], w[1], 0x7362);
@@ -192,39 +228,44 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
       dst[3 * kVtPitch / 4] = __byte_perm(hi01, hi23, 0x7632);
     }
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < RPW; i++) {
-      const int r = warp + 8 * i;
-      if (r < nrows) {
-        const int4* prow = reinterpret_cast<const int4*>(sc + r * spitch + j0);
+    if (live) {
+      const int4* prow = reinterpret_cast<const int4*>(sc + r * spitch + jt);
 #pragma unroll 4
-        for (int kg = 0; kg < kTileKeys / 4; kg++) {
-          const int4 p4 = prow[kg];
-          // 14-bit probabilities -> four 7-bit hi limbs and four 7-bit lo limbs, one byte each
-          const uint32_t lo4 = __byte_perm(__byte_perm(p4.x, p4.y, 0x0040), __byte_perm(p4.z, p4.w, 0x0040), 0x5410) &
-                               0x7F7F7F7Fu;
-          const uint32_t hi4 = __byte_perm(__byte_perm(p4.x << 1, p4.y << 1, 0x0051),
-                                           __byte_perm(p4.z << 1, p4.w << 1, 0x0051), 0x5410);
+      for (int kg = part; kg < kTileKeys / 4; kg += WPR) {
+        const int4 p4 = prow[kg];
+        // 14-bit probabilities -> four 7-bit hi limbs and four 7-bit lo limbs, one byte each
+        const uint32_t lo4 =
+            __byte_perm(__byte_perm(p4.x, p4.y, 0x0040), __byte_perm(p4.z, p4.w, 0x0040), 0x5410) & 0x7F7F7F7Fu;
+        const uint32_t hi4 = __byte_perm(__byte_perm(p4.x << 1, p4.y << 1, 0x0051),
+                                         __byte_perm(p4.z << 1, p4.w << 1, 0x0051), 0x5410);
 #pragma unroll
-          for (int y = 0; y < 4; y++) {
-            const int vv = (int)vtw[(lane + 32 * y) * (kVtPitch / 4) + kg];
-            acc_hi[i][y] = __dp4a((int)hi4, vv, acc_hi[i][y]);
-            acc_lo[i][y] = __dp4a((int)lo4, vv, acc_lo[i][y]);
-          }
+        for (int y = 0; y < 4; y++) {
+          const int vv = (int)vtw[(lane + 32 * y) * (kVtPitch / 4) + kg];
+          acc_hi[y] = __dp4a((int)hi4, vv, acc_hi[y]);
+          acc_lo[y] = __dp4a((int)lo4, vv, acc_lo[y]);
         }
       }
     }
     __syncthreads();
   }
-  // o = fmul(float(acc), sp) with acc = (hi << 7) + lo exact in int64 (qwen3.py:276-282)
+  // o = fmul(float(acc), sp), acc the exact int64 sum over the row's warps (qwen3.py:276-282)
+  float* o = a.out + (size_t)(b * a.Tq + t0 + r) * a.H * kHd + h * kHd;
+  if constexpr (WPR == 1) {
+    if (live)
 #pragma unroll
-  for (int i = 0; i < RPW; i++) {
-    const int r = warp + 8 * i;
-    if (r < nrows) {
-      float* o = a.out + (size_t)(b * a.Tq + t0 + r) * a.H * kHd + h * kHd;
-#pragma unroll
-      for (int y = 0; y < 4; y++)
-        o[lane + 32 * y] = __fmul_rn(__ll2float_rn(((long long)acc_hi[i][y] << 7) + acc_lo[i][y]), s_sp[r]);
+      for (int y = 0; y < 4; y++) o[lane + 32 * y] = __fmul_rn(__ll2float_rn(((long long)acc_hi[y] << 7) + acc_lo[y]), s_sp[r]);
+  } else {
+  #pragma unroll
+    for (int y = 0; y < 4; y++) s_out[(r * WPR + part) * kHd + lane + 32 * y] = ((long long)acc_hi[y] << 7) + acc_lo[y];
+    __syncthreads();
+    if (live && part == 0) {
+  #pragma unroll
+      for (int y = 0; y < 4; y++) {
+        long long t = 0;
+  #pragma unroll
+        for (int i = 0; i < WPR; i++) t += s_out[(r * WPR + i) * kHd + lane + 32 * y];
+        o[lane + 32 * y] = __fmul_rn(__ll2float_rn(t), s_sp[r]);
+      }
     }
   }
 }
@@ -308,7 +349,11 @@ __global__ void __launch_bounds__(NT) k_logprobs(const float* __restrict__ lg, i
 
 constexpr int kAttnSmemMax = 200 * 1024;
 
-size_t attn_smem(int QT, int spitch) { return (size_t)QT * spitch * 4 + (size_t)QT * 128 + (size_t)kHd * kVtPitch; }
+// scores (QT x spitch floats), query rows, the transposed V tile, and for rows split over several
+// warps (QT < 8) their int64 P V partials (8 warps x 128 dims)
+size_t attn_smem(int QT, int spitch) {
+  return (size_t)QT * spitch * 4 + (size_t)QT * 128 + (size_t)kHd * kVtPitch + (QT < 8 ? (size_t)8 * kHd * 8 : 0);
+}
 
 // Opt in to more than 48 KiB of dynamic shared memory, once per kernel and device.
 int smem_optin(const void* kernel, int bytes) {
@@ -355,11 +400,10 @@ extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc
              out};
   cudaStream_t st = (cudaStream_t)stream;
   // the widest query block whose score rows fit in shared memory (and not wider than Tq needs)
-  const int want = Tq >= 16 ? 16 : Tq >= 8 ? 8 : Tq >= 4 ? 4 : Tq >= 2 ? 2 : 1;
+  const int want = Tq >= 8 ? 8 : Tq >= 4 ? 4 : Tq >= 2 ? 2 : 1;
   for (int QT = want; QT >= 1; QT >>= 1) {
     if (attn_smem(QT, spitch) > (size_t)kAttnSmemMax) continue;
     switch (QT) {
-      case 16: return launch_attn<16>(a, B, spitch, st);
       case 8: return launch_attn<8>(a, B, spitch, st);
       case 4: return launch_attn<4>(a, B, spitch, st);
       case 2: return launch_attn<2>(a, B, spitch, st);
