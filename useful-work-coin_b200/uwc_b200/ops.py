@@ -168,6 +168,18 @@ def project(src: torch.Tensor, St: torch.Tensor, corr: torch.Tensor, corr_off: i
 _GEMM_WS: dict = {}
 
 
+def quant_rows_had(x: torch.Tensor, bs: int, q: torch.Tensor | None = None, scale: torch.Tensor | None = None):
+    """ops.py:172-181: bf16 rows (m x k) -> block Walsh-Hadamard (size bs, 0 = none), then per-row
+    int8 in [-64, 64] with float32 scale max|x'| / 64 folded with 1/sqrt(bs)."""
+    assert x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 2
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device) if q is None else q
+    scale = torch.empty(m, dtype=torch.float32, device=x.device) if scale is None else scale
+    check(lib().uwc_quant_rows_had(_p(x), m, k, bs, _p(q), _p(scale), _stream()), "quant_rows_had")
+    _count()
+    return q, scale
+
+
 def gemm_workspace(device, m: int, n: int, flags: int, out_mode: int) -> torch.Tensor | None:
     """Per-device workspace of the hashed GEMM (tile messages; the int32 product of a denoised bf16
     forward), grown on demand. Callers serialize on one stream per device (like the reference's
