@@ -205,6 +205,22 @@ int uwc_rmsnorm(const float* x, const float* w, int m, int k, double eps, float*
  * of generate_greedy (qwen3.py:323, the first index of the maximal lp) into tok (may be NULL). */
 int uwc_logprobs(const float* logits, int m, int V, float* lp, long long* tok, void* stream);
 
+/* Stage-output commitments (runtime/detgpu/sha.py; formats runtime/detrt/stage.py:26-72 and
+ * runtime/agent/proto.py:24-35): for float32 rows of D values, row_root = RFC 6962 Merkle root of
+ * sha256(0x00 || block) over 1 KiB blocks of the row's little-endian bytes, the token leaf
+ * sha256(0x00 || "sout" || u32le t || row_root) with t = row % T, and a stage's root = the Merkle
+ * root of its T leaves. Digests are written as 8 big-endian SHA-256 state words. D <= 8192.
+ * Scratch: uwc_stage_scratch_words(nrows, D) u32 words of caller device memory. */
+uint64_t uwc_stage_scratch_words(long long nrows, int D);
+/* The token leaves of nrows rows (nrows a multiple of T) into leaves (nrows x 8 words):
+ * sout_leaves (runtime/detgpu/sha.py:103-135). */
+int uwc_stage_out_leaves(const float* rows, long long nrows, int D, int T, uint32_t* scratch,
+                         uint64_t scratch_words, uint32_t* leaves, void* stream);
+/* The roots of B stages of T rows each (rows B*T x D) into roots (B x 8 words): stage_roots_gpu
+ * (runtime/detgpu/sha.py:138-163), agent.proto.stage_output_root per stage. */
+int uwc_stage_roots(const float* rows, int B, int T, int D, uint32_t* scratch, uint64_t scratch_words,
+                    uint32_t* roots, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,9 @@ SIGNATURES = {
                              _F32, _P, _P]),
     "uwc_rmsnorm": (_I32, [_P, _P, _I32, _I32, _F64, _P, _P]),
     "uwc_logprobs": (_I32, [_P, _I32, _I32, _P, _P, _P]),
+    "uwc_stage_scratch_words": (_U64, [_I64, _I32]),
+    "uwc_stage_out_leaves": (_I32, [_P, _I64, _I32, _I32, _P, _U64, _P, _P]),
+    "uwc_stage_roots": (_I32, [_P, _I32, _I32, _I32, _P, _U64, _P, _P]),
 }
 
 _LIB = None
