@@ -455,14 +455,34 @@ def run_c4(a, world, rank, local):
         last = model.forward(ids, cache, 0)[:, -1]
         if evs:
             evs[1].record(stream)
-        toks = []
-        for i in range(n_new):
-            nxt = model.next_tokens(last)
-            toks.append(nxt)
-            if i + 1 < n_new:
-                last = model.forward(nxt[:, None], cache, T0 + i)[:, 0]
+        toks = decode(last, cache)
         if evs:
             evs[2].record(stream)
+        return toks
+
+    def decode(last, cache):
+        """model.generate_greedy's decode half: the first step eager, the rest one CUDA graph
+        replayed per token (the position lives in device memory)."""
+        nxt = model.next_tokens(last)
+        toks = [nxt]
+        pos = torch.full((1,), T0, dtype=torch.int32, device=dev)
+        tok_in = nxt.clone()
+        h, nxt = model._decode_step(tok_in, cache, pos, T0 + n_new - 2)
+        toks.append(nxt.clone())
+        tok_in.copy_(nxt)
+        pos += 1
+        g = torch.cuda.CUDAGraph()
+        c0 = ops.LAUNCHES
+        with torch.cuda.graph(g):
+            _, nxt_s = model._decode_step(tok_in, cache, pos, T0 + n_new - 2)
+            tok_in.copy_(nxt_s)
+            pos.add_(1)
+        per_step = ops.LAUNCHES - c0          # this library's kernels in one captured step
+        for _ in range(2, n_new):
+            g.replay()
+            toks.append(nxt_s.clone())
+        ops._count(per_step * (n_new - 3))    # replays run the captured kernels n_new - 2 times
+        del g
         return torch.stack(toks, 1)
 
     for _ in range(a.warmup):

@@ -180,6 +180,12 @@ int uwc_dequant_residual(const int32_t* acc, const float* s, const float* sw, co
 int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
                  const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps, int qknorm,
                  int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs, void* stream);
+/* uwc_qkv_post with full cos / sin tables and the start position in device memory: row r uses
+ * rope position *pos + r % T (a decode step's graph reads the position instead of baking it in). */
+int uwc_qkv_post_at(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
+                    const float* cos_table, const float* sin_table, const int* pos, int N, int T, int H, int Hkv,
+                    double eps, int qknorm, int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs,
+                    void* stream);
 
 /* Deterministic attention from quantized q, k, v (runtime/detrt/qwen3.py:254-283 _attention;
  * GPU form runtime/detgpu/kernels.py:731-771 attention): exact int32 Q K^T, scores
@@ -197,6 +203,18 @@ int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const flo
                   const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq, long long kv_tok,
                   long long kv_head, long long s_seq, long long s_tok, long long s_head, float inv_sqrt_hd,
                   float* out, void* stream);
+/* uwc_attention with the start position read from device memory (*start <= max_start), so one
+ * CUDA graph serves every decode step; shared memory is sized for max_start + Tq keys. No
+ * counterpart in the reference (its decode runs eagerly, runtime/detrt/qwen3.py:315-329). */
+int uwc_attention_at(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                     const float* vs, int B, int Tq, const int* start, int max_start, int H, int Hkv,
+                     long long kv_seq, long long kv_tok, long long kv_head, long long s_seq, long long s_tok,
+                     long long s_head, float inv_sqrt_hd, float* out, void* stream);
+/* The KV cache write of runtime/detrt/qwen3.py:249-252: token t of sequence b (kq / vq (B*T, Hkv,
+ * 128) int8, ks / vs (B*T, Hkv) float32) into a cache k, v (B, Hkv, maxlen, 128), sk, sv
+ * (B, Hkv, maxlen) at position *pos + t (device memory; positions past maxlen are skipped). */
+int uwc_kv_append(const int8_t* kq, const float* ks, const int8_t* vq, const float* vs, int B, int T, int Hkv,
+                  int maxlen, const int* pos, int8_t* kc, float* skc, int8_t* vc, float* svc, void* stream);
 /* det_rmsnorm (runtime/detrt/core.py:151-159) of m rows of k floats: the final norm of
  * DetQwen3.forward (runtime/detrt/qwen3.py:299), float32 out. */
 int uwc_rmsnorm(const float* x, const float* w, int m, int k, double eps, float* out, void* stream);

@@ -107,9 +107,10 @@ def test_forward_logprobs_greedy_equal_detrt(dev, mg, model):
     assert np.array_equal(bits(h), g["hidden"].view(np.int32)), "prefill hidden differs from detrt"
     lp = model.logprobs(h[:, -1:])
     assert np.array_equal(bits(lp[:, 0]), g["lp_last"].view(np.int32)), "log-probabilities differ"
-    toks, step_h = model.generate_greedy(prompt, 12)
-    assert toks.cpu().numpy().tolist() == g["toks"].tolist(), "greedy tokens differ"
-    assert np.array_equal(bits(step_h), g["step_h"].view(np.int32)), "decode hiddens differ"
+    for graph in (False, True):
+        toks, step_h = model.generate_greedy(prompt, 12, graph=graph)
+        assert toks.cpu().numpy().tolist() == g["toks"].tolist(), f"greedy tokens differ (graph={graph})"
+        assert np.array_equal(bits(step_h), g["step_h"].view(np.int32)), f"decode hiddens differ (graph={graph})"
 
 
 def test_prefill_equals_decode_equals_teacher_forcing(dev, model):

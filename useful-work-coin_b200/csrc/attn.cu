@@ -74,6 +74,7 @@ struct AttnArgs {
   int Tq, start, H, Hkv;
   float inv_sqrt_hd;
   float* out;         // (N_q, H * 128)
+  const int* start_dev;   // when set, the start position is read here (one graph for every decode step)
 };
 
 // Row r of this CTA is query t = t0 + r at absolute position start + t; it sees keys 0..start + t.
@@ -98,7 +99,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
   const int t0 = blockIdx.y * QT;
   const int nrows = min(QT, a.Tq - t0);
   const bool live = r < nrows;
-  const int S = a.start + t0 + nrows;                      // keys this CTA needs
+  const int start = a.start_dev ? __ldg(a.start_dev) : a.start;
+  const int S = start + t0 + nrows;                        // keys this CTA needs
   const int8_t* kb = a.kc + b * a.kv_seq + g * a.kv_head;
   const int8_t* vb = a.vc + b * a.kv_seq + g * a.kv_head;
   const float* ksb = a.ks + b * a.s_seq + g * a.s_head;
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
         dot = __dp4a((int)kw[4 * i + 3], (int)qw.w, dot);
       }
       const float v = __fmul_rn(__fmul_rn(__fmul_rn((float)dot, s_qs[rr]), ksj), a.inv_sqrt_hd);
-      sc[rr * spitch + j] = j <= a.start + t0 + rr ? v : __int_as_float(0xff800000);
+      sc[rr * spitch + j] = j <= start + t0 + rr ? v : __int_as_float(0xff800000);
     }
   }
   __syncthreads();
@@ -383,10 +385,11 @@ int launch_attn(const AttnArgs& a, int B, int spitch, cudaStream_t st) {
 
 }  // namespace
 
-extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
-                             const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq,
-                             long long kv_tok, long long kv_head, long long s_seq, long long s_tok, long long s_head,
-                             float inv_sqrt_hd, float* out, void* stream) {
+namespace {
+int attention_impl(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                   const float* vs, int B, int Tq, int start, const int* start_dev, int H, int Hkv, long long kv_seq,
+                   long long kv_tok, long long kv_head, long long s_seq, long long s_tok, long long s_head,
+                   float inv_sqrt_hd, float* out, void* stream) {
   if (!qq || !qs || !kc || !ks || !vc || !vs || !out) return UWC_ERR_ARG;
   if (B < 0 || Tq < 0 || start < 0 || H <= 0 || Hkv <= 0 || H % Hkv) return UWC_ERR_SHAPE;
   if ((((uintptr_t)qq) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15) return UWC_ERR_ALIGN;
@@ -397,7 +400,7 @@ extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc
   const int S = start + Tq;
   const int spitch = (S + kTileKeys - 1) / kTileKeys * kTileKeys;
   AttnArgs a{qq, qs, kc, ks, vc, vs, kv_seq, kv_tok, kv_head, s_seq, s_tok, s_head, Tq, start, H, Hkv, inv_sqrt_hd,
-             out};
+             out, start_dev};
   cudaStream_t st = (cudaStream_t)stream;
   // the widest query block whose score rows fit in shared memory (and not wider than Tq needs)
   const int want = Tq >= 8 ? 8 : Tq >= 4 ? 4 : Tq >= 2 ? 2 : 1;
@@ -412,6 +415,64 @@ extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc
   }
   return UWC_ERR_SHAPE;   // more keys than one score row of shared memory holds
 }
+
+// KV cache append: token t of sequence b (token-major kq / vq rows, N = B * T) -> cache position
+// pos + t, pos read from device memory. One warp per (b, t, kv head).
+__global__ void __launch_bounds__(256) k_kv_append(const int8_t* __restrict__ kq, const float* __restrict__ ks,
+                                                   const int8_t* __restrict__ vq, const float* __restrict__ vs, int B,
+                                                   int T, int Hkv, int maxlen, const int* __restrict__ pos,
+                                                   int8_t* __restrict__ kc, float* __restrict__ skc,
+                                                   int8_t* __restrict__ vc, float* __restrict__ svc) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)B * T * Hkv) return;
+  const int g = (int)(w % Hkv), n = (int)(w / Hkv), b = n / T, t = n % T;
+  const int p = __ldg(pos) + t;
+  if (p >= maxlen) return;
+  const long long dst = ((long long)b * Hkv + g) * maxlen + p;      // (b, g, p) of the cache
+  if (lane < 8)
+    reinterpret_cast<uint4*>(kc + dst * kHd)[lane] = reinterpret_cast<const uint4*>(kq + w * kHd)[lane];
+  else if (lane < 16)
+    reinterpret_cast<uint4*>(vc + dst * kHd)[lane - 8] = reinterpret_cast<const uint4*>(vq + w * kHd)[lane - 8];
+  else if (lane == 16)
+    skc[dst] = ks[w];
+  else if (lane == 17)
+    svc[dst] = vs[w];
+}
+}  // namespace
+
+extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                             const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq,
+                             long long kv_tok, long long kv_head, long long s_seq, long long s_tok, long long s_head,
+                             float inv_sqrt_hd, float* out, void* stream) {
+  return attention_impl(qq, qs, kc, ks, vc, vs, B, Tq, start, nullptr, H, Hkv, kv_seq, kv_tok, kv_head, s_seq, s_tok,
+                        s_head, inv_sqrt_hd, out, stream);
+}
+
+extern "C" int uwc_attention_at(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                                const float* vs, int B, int Tq, const int* start, int max_start, int H, int Hkv,
+                                long long kv_seq, long long kv_tok, long long kv_head, long long s_seq,
+                                long long s_tok, long long s_head, float inv_sqrt_hd, float* out, void* stream) {
+  if (!start || max_start < 0) return UWC_ERR_ARG;
+  // shared memory and the query-block width are sized for the largest start the caller allows
+  return attention_impl(qq, qs, kc, ks, vc, vs, B, Tq, max_start, start, H, Hkv, kv_seq, kv_tok, kv_head, s_seq,
+                        s_tok, s_head, inv_sqrt_hd, out, stream);
+}
+
+extern "C" int uwc_kv_append(const int8_t* kq, const float* ks, const int8_t* vq, const float* vs, int B, int T,
+                             int Hkv, int maxlen, const int* pos, int8_t* kc, float* skc, int8_t* vc, float* svc,
+                             void* stream) {
+  if (!kq || !ks || !vq || !vs || !pos || !kc || !skc || !vc || !svc) return UWC_ERR_ARG;
+  if (B < 0 || T < 0 || Hkv <= 0 || maxlen <= 0) return UWC_ERR_SHAPE;
+  if ((((uintptr_t)kq) | ((uintptr_t)vq) | ((uintptr_t)kc) | ((uintptr_t)vc)) & 15) return UWC_ERR_ALIGN;
+  UWC_CHECK_DEVICE();
+  const long long warps = (long long)B * T * Hkv;
+  if (warps == 0) return UWC_OK;
+  k_kv_append<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(kq, ks, vq, vs, B, T, Hkv,
+                                                                                       maxlen, pos, kc, skc, vc, svc);
+  return uwc_launch_status();
+}
+
 
 extern "C" int uwc_rmsnorm(const float* x, const float* w, int m, int k, double eps, float* out, void* stream) {
   if (!x || !w || !out || m < 0 || k <= 0) return UWC_ERR_ARG;

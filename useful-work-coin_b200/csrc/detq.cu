@@ -215,9 +215,10 @@ __global__ void __launch_bounds__(kRowThreads) k_qkv_post(
     const float* __restrict__ qnw, const float* __restrict__ knw, const float* __restrict__ cosT,
     const float* __restrict__ sinT, int T, int H, int Hkv, float inv_hd, float eps, int qknorm,
     int8_t* __restrict__ qq, float* __restrict__ qs, int8_t* __restrict__ kq, float* __restrict__ ks,
-    int8_t* __restrict__ vq, float* __restrict__ vs) {
+    int8_t* __restrict__ vq, float* __restrict__ vs, const int* __restrict__ pos0) {
   const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nh = H + 2 * Hkv, width = nh * 128, t = row % T;
+  // rope table row: position r % T, offset by a device-side start position when given
+  const int nh = H + 2 * Hkv, width = nh * 128, t = row % T + (pos0 ? __ldg(pos0) : 0);
   const float s = s1[row];
   for (int hh = warp; hh < nh; hh += kRowThreads / 32) {
     float v[4];
@@ -396,10 +397,11 @@ extern "C" int uwc_dequant_residual(const int32_t* acc, const float* s, const fl
   return uwc_launch_status();
 }
 
-extern "C" int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
-                            const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps,
-                            int qknorm, int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs,
-                            void* stream) {
+namespace {
+int qkv_post_launch(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
+                    const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps, int qknorm,
+                    int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs, const int* pos0,
+                    void* stream) {
   if (!acc || !s1 || !sw || !cos_t || !sin_t || !qq || !qs || !kq || !ks || !vq || !vs) return UWC_ERR_ARG;
   if (qknorm && (!qnw || !knw)) return UWC_ERR_ARG;
   if (N < 0 || T <= 0 || H <= 0 || Hkv <= 0) return UWC_ERR_SHAPE;
@@ -407,6 +409,24 @@ extern "C" int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw
   if (N == 0) return UWC_OK;
   k_qkv_post<<<N, kRowThreads, 0, (cudaStream_t)stream>>>(acc, s1, sw, qnw, knw, cos_t, sin_t, T, H, Hkv,
                                                           (float)(1.0 / 128), (float)eps, qknorm, qq, qs, kq, ks, vq,
-                                                          vs);
+                                                          vs, pos0);
   return uwc_launch_status();
+}
+}  // namespace
+
+extern "C" int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
+                            const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps,
+                            int qknorm, int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs,
+                            void* stream) {
+  return qkv_post_launch(acc, s1, sw, qnw, knw, cos_t, sin_t, N, T, H, Hkv, eps, qknorm, qq, qs, kq, ks, vq, vs,
+                         nullptr, stream);
+}
+
+extern "C" int uwc_qkv_post_at(const int32_t* acc, const float* s1, const float* sw, const float* qnw,
+                               const float* knw, const float* cos_table, const float* sin_table, const int* pos,
+                               int N, int T, int H, int Hkv, double eps, int qknorm, int8_t* qq, float* qs,
+                               int8_t* kq, float* ks, int8_t* vq, float* vs, void* stream) {
+  if (!pos) return UWC_ERR_ARG;
+  return qkv_post_launch(acc, s1, sw, qnw, knw, cos_table, sin_table, N, T, H, Hkv, eps, qknorm, qq, qs, kq, ks, vq,
+                         vs, pos, stream);
 }

@@ -218,3 +218,47 @@ def logprobs(logits: torch.Tensor, want_lp: bool = True):
     check(lib().uwc_logprobs(_p(lg), m, V, _p(lp), _p(tok), _stream()), "logprobs")
     _count()
     return lp, tok
+
+
+def qkv_post_at(acc, s1, sw, qnw, knw, cos_table, sin_table, pos: torch.Tensor, T: int, H: int, Hkv: int, eps: float,
+                qknorm: bool = True):
+    """qkv_post with the rope rows at the device-side position pos (int32, one element) + r % T."""
+    acc = acc.contiguous()
+    assert acc.dtype == torch.int32 and pos.dtype == torch.int32
+    N = acc.shape[0]
+    dev = acc.device
+    e = lambda *shape, dt=torch.int8: torch.empty(shape, dtype=dt, device=dev)
+    qq, qs = e(N, H, 128), e(N, H, 1, dt=torch.float32)
+    kq, ks = e(N, Hkv, 128), e(N, Hkv, 1, dt=torch.float32)
+    vq, vs = e(N, Hkv, 128), e(N, Hkv, 1, dt=torch.float32)
+    qn = _f32(qnw) if qknorm else None
+    kn = _f32(knw) if qknorm else None
+    check(lib().uwc_qkv_post_at(_p(acc), _p(_f32(s1)), _p(_f32(sw)), _p(qn), _p(kn), _p(_f32(cos_table)),
+                                _p(_f32(sin_table)), _p(pos), N, T, H, Hkv, float(eps), int(bool(qknorm)), _p(qq),
+                                _p(qs), _p(kq), _p(ks), _p(vq), _p(vs), _stream()), "qkv_post_at")
+    _count()
+    return qq, qs, kq, ks, vq, vs
+
+
+def kv_append(kq, ks, vq, vs, cache: dict, B: int, T: int, pos: torch.Tensor) -> None:
+    """Write the new tokens' keys / values into the cache at the device-side position pos."""
+    k, v, sk, sv = cache["k"], cache["v"], cache["sk"], cache["sv"]
+    Hkv, maxlen = k.shape[1], k.shape[2]
+    check(lib().uwc_kv_append(_p(kq.contiguous()), _p(_f32(ks)), _p(vq.contiguous()), _p(_f32(vs)), B, T, Hkv, maxlen,
+                              _p(pos), _p(k), _p(sk), _p(v), _p(sv), _stream()), "kv_append")
+    _count()
+
+
+def attention_cache_at(qq, qs, cache: dict, B: int, Tq: int, pos: torch.Tensor, max_start: int, H: int, Hkv: int,
+                       inv_sqrt_hd_f32: float) -> torch.Tensor:
+    """attention_cache with the start position read from device memory (pos <= max_start)."""
+    k, v, sk, sv = cache["k"], cache["v"], cache["sk"], cache["sv"]
+    maxlen = k.shape[2]
+    assert max_start + Tq <= maxlen and pos.dtype == torch.int32
+    qq = qq.contiguous()
+    out = torch.empty((B * Tq, H * 128), dtype=torch.float32, device=qq.device)
+    strides = (Hkv * maxlen * 128, 128, maxlen * 128, Hkv * maxlen, 1, maxlen)
+    check(lib().uwc_attention_at(_p(qq), _p(_f32(qs)), _p(k), _p(sk), _p(v), _p(sv), B, Tq, _p(pos), max_start, H,
+                                 Hkv, *strides, float(inv_sqrt_hd_f32), _p(out), _stream()), "attention_at")
+    _count()
+    return out

@@ -220,20 +220,66 @@ class DetQwen3:
         """Greedy tokens of hidden rows (B, D): argmax of logprobs, first maximum (qwen3.py:322-323)."""
         return detgpu.logprobs(self.lm_head(last.reshape(-1, self.D)), want_lp=False)[1]
 
+    def _decode_step(self, tok: torch.Tensor, cache, pos: torch.Tensor, max_start: int):
+        """One decode step for B sequences with the position in device memory (int32 `pos`): the
+        token embedding, every layer, the final norm and the greedy next token. The same
+        arithmetic as forward(tok[:, None], cache, pos) + next_tokens; capturable as one graph."""
+        B = tok.shape[0]
+        H, Hkv, hd = self.H, self.Hkv, self.hd
+        x = self.embed[tok]
+        for L, c in zip(self.layers, cache):
+            q1, s1 = detgpu.rmsnorm_quant(x, L["in_norm"], self.eps, L["qkv"].bs)
+            qq, qs, kq, ks, vq, vs = detgpu.qkv_post_at(L["qkv"].int_gemm(q1), s1, L["qkv"].sw, L["q_norm"],
+                                                        L["k_norm"], self.cos, self.sin, pos, 1, H, Hkv, self.eps,
+                                                        self.qk_norm)
+            detgpu.kv_append(kq, ks, vq, vs, c, B, 1, pos)
+            o = detgpu.attention_cache_at(qq, qs, c, B, 1, pos, max_start, H, Hkv, self.inv_sqrt_hd)
+            q2, s2 = detgpu.quant_act(o, L["o"].bs)
+            r1 = detgpu.dequant_residual(L["o"].int_gemm(q2), s2, L["o"].sw, x)
+            x = detgpu.mlp_residual(L["gu"], L["down"], L["post_norm"], r1, self.eps)
+        h = detgpu.rmsnorm(x, self.norm, self.eps)
+        return h, self.next_tokens(h)
+
     @torch.no_grad()
-    def generate_greedy(self, prompt: torch.Tensor, n_new: int):
+    def generate_greedy(self, prompt: torch.Tensor, n_new: int, graph: bool = True):
         """Prefill the prompt, then decode n_new tokens one at a time (qwen3.py:315-329).
-        Returns (tokens (B, n_new), step hiddens (B, n_new, D))."""
+        Returns (tokens (B, n_new), step hiddens (B, n_new, D)).
+
+        graph=True replays the decode step as one CUDA graph: the step reads its position from
+        device memory (qkv_post_at, kv_append, attention_cache_at), so a single capture serves
+        every step. The outputs are the same bits as the eager loop."""
         B, T0 = prompt.shape
         cache = self.new_cache(B, T0 + n_new)
         last = self.forward(prompt, cache, 0)[:, -1]
-        toks, hs = [], []
-        for i in range(n_new):
-            nxt = self.next_tokens(last)
-            toks.append(nxt)
-            hs.append(last)
-            if i + 1 < n_new:
-                last = self.forward(nxt[:, None], cache, T0 + i)[:, 0]
+        if n_new == 0:
+            return torch.empty((B, 0), dtype=torch.int64, device=self.device), last[:, None][:, :0]
+        nxt = self.next_tokens(last)
+        toks, hs = [nxt], [last]
+        if not graph or n_new < 3:
+            for i in range(1, n_new):
+                last = self.forward(toks[-1][:, None], cache, T0 + i - 1)[:, 0]
+                toks.append(self.next_tokens(last))
+                hs.append(last)
+            return torch.stack(toks, 1), torch.stack(hs, 1)
+        max_start = T0 + n_new - 2
+        pos = torch.full((1,), T0, dtype=torch.int32, device=self.device)
+        tok_in = nxt.clone()
+        # the first step runs eagerly (kernel attributes, workspaces), then the step is captured
+        h, nxt = self._decode_step(tok_in, cache, pos, max_start)
+        toks.append(nxt.clone())
+        hs.append(h.clone())
+        tok_in.copy_(nxt)
+        pos += 1
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            h_s, nxt_s = self._decode_step(tok_in, cache, pos, max_start)
+            tok_in.copy_(nxt_s)
+            pos.add_(1)
+        for _ in range(2, n_new):
+            g.replay()
+            toks.append(nxt_s.clone())
+            hs.append(h_s.clone())
+        del g
         return torch.stack(toks, 1), torch.stack(hs, 1)
 
 
