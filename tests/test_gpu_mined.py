@@ -245,3 +245,34 @@ def test_hashed_gemm_outputs_without_denoise(ops, mode):
         assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), O.scaled_bf16(acc, sa, sb))
     else:
         assert np.array_equal(out.cpu().numpy().view(np.uint32), O.det_dequant(acc, sa, sb).view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_host_miner_matches_noise_mine(dev):
+    """HostMiner (overlapped uploads from pinned memory) reports the same winners per attempt as
+    noise_mine on device-resident inputs."""
+    import torch
+
+    from uwc_b200 import glue, ops
+    m, n, k, r = 256, 512, 2048, 64
+    rng = np.random.default_rng(5)
+    Bt = torch.from_numpy(rng.integers(-64, 65, (n, k), dtype=np.int8)).to(dev)
+    w = ops.MinedWeight(Bt=Bt, b_scale=torch.ones(n, device=dev), r=r, max_wins=4096)
+    w.setup_block(rng.bytes(32), glue.target_for(m, n, 20))
+    As = [rng.integers(-64, 65, (m, k), dtype=np.int8) for _ in range(4)]
+    want = []
+    for A in As:
+        w.noise_mine(torch.from_numpy(A).to(dev))
+        want.append(sorted(w.winners(m)))
+    hm = ops.HostMiner(w, m, k, dev)
+    hosts = [torch.from_numpy(A).pin_memory() for A in As]
+    outs = [torch.empty(w._buf(m)["wins"].numel(), dtype=torch.int32).pin_memory() for _ in As]
+    for A_h, o in zip(hosts, outs):
+        hm.mine(A_h, o)
+    torch.cuda.synchronize()
+    for o, ww in zip(outs, want):
+        words = o.numpy().view(np.uint32)
+        cnt = min(int(words[0]), w.max_wins)
+        recs = words[1:1 + cnt * ops.WIN_WORDS].reshape(cnt, ops.WIN_WORDS)
+        got = sorted((int(x[0]), int(x[1]), x[2:].astype("<u4").tobytes()) for x in recs)
+        assert got == ww and ww

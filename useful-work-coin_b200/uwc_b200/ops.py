@@ -369,6 +369,40 @@ class MinedWeight:
         return [(int(x[0]), int(x[1]), x[2:].astype("<u4").tobytes()) for x in recs]
 
 
+class HostMiner:
+    """Noise mining from nonce matrices in pinned host memory, the way a miner fed by another
+    process or machine runs miner_loop.py:109-111: the upload of attempt i + 1 (a copy stream, two
+    device buffers) overlaps the commit, noise and hashed GEMM of attempt i, and every attempt's
+    win records come back to pinned host memory. Results equal noise_mine + winners per attempt."""
+
+    def __init__(self, w: "MinedWeight", m: int, k: int, device):
+        self.w, self.m, self.k = w, m, k
+        dev = torch.device(device)
+        self.A = [torch.empty((m, k), dtype=torch.int8, device=dev) for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream(dev)
+        self.uploaded = [torch.cuda.Event() for _ in range(2)]
+        self.consumed = [torch.cuda.Event() for _ in range(2)]
+        self.wins_dev = w._buf(m)["wins"]
+        self.i = 0
+
+    def mine(self, A_host: torch.Tensor, wins_host: torch.Tensor) -> None:
+        """Enqueue one attempt: A_host (m x k int8, pinned), its win records (the device wins
+        buffer's words) copied into wins_host (pinned int32) when the attempt is done. Asynchronous."""
+        assert A_host.is_pinned() and A_host.shape == (self.m, self.k) and wins_host.is_pinned()
+        s = self.i & 1
+        main = torch.cuda.current_stream()
+        with torch.cuda.stream(self.copy_stream):
+            if self.i >= 2:
+                self.copy_stream.wait_event(self.consumed[s])     # the attempt two back read this buffer
+            self.A[s].copy_(A_host, non_blocking=True)
+            self.uploaded[s].record(self.copy_stream)
+        main.wait_event(self.uploaded[s])
+        self.w.noise_mine(self.A[s])
+        self.consumed[s].record(main)
+        wins_host.copy_(self.wins_dev, non_blocking=True)
+        self.i += 1
+
+
 class GraphedForward:
     """MinedWeight.forward captured as one CUDA graph for a fixed m (static input/output buffers)."""
 
