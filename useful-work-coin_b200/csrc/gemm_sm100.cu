@@ -37,11 +37,12 @@
 // (caller workspace, double-buffered per CTA): no message state in registers, and the two
 // quadrant halves of a tile combine in the same word.
 //
-// Warp roles (640 threads, one CTA per SM, all 512 TMEM columns):
-//   0..15   epilogue: warp w reads TMEM lanes 32*(w%4).. and the 64-column block w/4
-//   16..17  hash: keyed BLAKE3 of the finished tile messages, target compare, win records
-//   18      TMA producer (one lane)
-//   19      MMA issuer (one lane); allocates and frees TMEM
+// Warp roles (576 threads, one CTA per SM, all 512 TMEM columns):
+//   0..15   epilogue: warp w reads TMEM lanes 32*(w%4).. and the 64-column block w/4; at the end
+//           of a hashed unit each of the 512 threads hashes one tile (keyed BLAKE3 of its message,
+//           target compare, win record), so the hash work is spread over all four SM sub-partitions
+//   16      TMA producer (one elected lane issues)
+//   17      MMA issuer (one lane issues); allocates and frees TMEM
 #include <algorithm>
 
 #include "uwc_device.cuh"
@@ -52,10 +53,9 @@ namespace {
 enum Mode { MODE_PLAIN = 0, MODE_MINE = 1, MODE_FWD = 2, MODE_CORR = 3, MODE_MINE_OUT = 4 };
 
 constexpr int kEpiWarps = 16;
-constexpr int kHashWarps = 2;
-constexpr int kProducerWarp = kEpiWarps + kHashWarps;   // 18
-constexpr int kMmaWarp = kProducerWarp + 1;             // 19
-constexpr int kThreads = (kMmaWarp + 1) * 32;           // 640
+constexpr int kProducerWarp = kEpiWarps;               // 16
+constexpr int kMmaWarp = kProducerWarp + 1;             // 17
+constexpr int kThreads = (kMmaWarp + 1) * 32;           // 576
 constexpr int kKB = 128;                                // K bytes per stage (one 128-byte swizzle row)
 constexpr int kUN = 256;                                // output columns per unit
 constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
@@ -103,7 +103,6 @@ struct Cfg {
   static constexpr int TILE_WORDS = 32 * 33;
   static constexpr int TILE_BYTES = MODE == MODE_FWD || MODE == MODE_MINE ? 0 : kEpiWarps * TILE_WORDS * 4;
   static constexpr int SMEM = NST * STAGE + TILE_BYTES + kBarBytes + 1024;  // +1024: manual alignment
-  static constexpr int TILES = MINE ? 512 : 256;
   static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
   static constexpr int SPAN = R == 256 ? 2 : 1;                  // stages per chunk
   static constexpr int ACC_WARPS = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;  // readers per acc
@@ -116,7 +115,7 @@ struct Bars {
   uint64_t acc_full[4];
   uint64_t acc_empty[4];
   uint64_t r_full, r_scaled, r_empty;
-  uint64_t hash_ready[2], hash_free[2];   // per message buffer
+  uint64_t hash_ready[2];   // per message buffer: every epilogue thread's XOR reductions landed
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -266,6 +265,42 @@ __device__ __forceinline__ uint32_t reduce_scatter4(const uint32_t* pt, int lane
   return k0 ^ k1 ^ send ^ __shfl_xor_sync(0xffffffffu, send, 8);
 }
 
+// Keyed BLAKE3 of hash tile `slot` of a finished unit's message buffer, target compare and win
+// record (kernels.cu:574-596). Slot bits: lane-in-group (5), 64-column block (2), 64-row half (1),
+// 128-row accumulator (1); the message words of a slot are kMaxTiles apart. Clears the words.
+__device__ __forceinline__ void hash_tile(const Params& p, uint32_t* msg, int m0, int n0, int slot) {
+  const int ln = slot & 31, cbk = (slot >> 5) & 3, rb = (slot >> 7) & 1, a = slot >> 8;
+  uint32_t w[16], hv[8], key[8];
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    w[i] = __ldcg(msg + i * kMaxTiles + slot);
+    __stcg(msg + i * kMaxTiles + slot, 0u);   // clear for the unit after next
+  }
+  if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) return;
+#pragma unroll
+  for (int i = 0; i < 8; i++) key[i] = __ldg(p.key + i);
+  b3::hash64<true>(key, w, hv, p.one);
+  bool le = true, decided = false;
+#pragma unroll
+  for (int i = 7; i >= 0; i--) {
+    const uint32_t t = __ldg(p.target + i);
+    if (!decided && hv[i] != t) {
+      le = hv[i] < t;
+      decided = true;
+    }
+  }
+  if (le) {
+    const uint32_t ws = atomicAdd(p.wins, 1u);
+    if (ws < (uint32_t)p.max_wins) {
+      uint32_t* rec = p.wins + 1 + (uint64_t)ws * UWC_WIN_WORDS;
+      rec[0] = (uint32_t)(m0 + a * 128 + rb * 64 + (ln >> 2));
+      rec[1] = (uint32_t)(n0 + cbk * 64 + 2 * (ln & 3));
+#pragma unroll
+      for (int i = 0; i < 8; i++) rec[2 + i] = hv[i];
+    }
+  }
+}
+
 // Warp-wide bounded wait: every lane polls the barrier (measured faster to wake than one polling
 // lane plus a warp sync) and the warp agrees on the verdict.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
@@ -295,7 +330,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->acc_empty[a], C::ACC_WARPS);
       // message hand-offs are signalled by every lane that wrote (arrival counts in threads)
       mbar_init(&bars->hash_ready[a], kEpiWarps * 32);
-      mbar_init(&bars->hash_free[a], kHashWarps * 32);
     }
     mbar_init(&bars->r_full, 1);
     mbar_init(&bars->r_scaled, kEpiWarps);
@@ -643,11 +677,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
-      if (C::HASH) {
-        // this message buffer was last used two units ago: wait until the hash warps cleared it
-        ok = warp_wait(&bars->hash_free[buf], ((local >> 1) & 1) ^ 1, abort_flag, p.status);
-        if (!ok) break;
-      }
 
       // consume one snapshot of accumulator `a` at TMEM address `col`; returns this thread's fold
       auto consume = [&](int a, uint32_t col, bool last) -> uint32_t {
@@ -755,58 +784,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < nloop && ok; c++) chunk(c, false);
         if (MODE == MODE_MINE_OUT && ok) chunk(nch - 1, true);
         if (!ok) break;
-        __threadfence();                       // this unit's reductions are visible before the hand-off
+        // every thread's reductions of this unit are visible, then each thread hashes one tile.
+        // The buffer is cleared as it is read; its next user (two units on) starts only after the
+        // next unit's hand-off, which every thread reaches after its clears.
+        __threadfence();
         mbar_arrive(&bars->hash_ready[buf]);
+        ok = warp_wait(&bars->hash_ready[buf], (local >> 1) & 1, abort_flag, p.status);
+        if (!ok) break;
+        hash_tile(p, msg, m0, n0, threadIdx.x);
       } else {
         consume(a0, col0, true);
       }
-    }
-  } else if (C::HASH) {
-    // ------------------------------------------------------------ hash warps
-    const int hw = warp - kEpiWarps;
-    uint32_t key[8], tgt[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) { key[i] = p.key[i]; tgt[i] = p.target[i]; }
-    int local = 0;
-    for (int u = blockIdx.x; u < p.nunits; u += gridDim.x, local++) {
-      int m0, n0;
-      unit_coords(p, u, C::UM, m0, n0);
-      const int buf = local & 1;
-      uint32_t* const msg = msg_cta + buf * kMsgWords;
-      if (!warp_wait(&bars->hash_ready[buf], (local >> 1) & 1, abort_flag, p.status)) break;
-      for (int slot = hw * 32 + lane; slot < C::TILES; slot += kHashWarps * 32) {
-        const int ln = slot & 31, cbk = (slot >> 5) & 3, rb = (slot >> 7) & 1, a = slot >> 8;
-        const int row_off = m0 + a * 128 + rb * 64 + (ln >> 2);
-        const int col_off = n0 + cbk * 64 + 2 * (ln & 3);
-        uint32_t w[16], hv[8];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          w[i] = __ldcg(msg + i * kMaxTiles + slot);
-          __stcg(msg + i * kMaxTiles + slot, 0u);   // clear for the unit after next
-        }
-        if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) continue;
-        b3::hash64<true>(key, w, hv, p.one);
-        bool le = true, decided = false;
-#pragma unroll
-        for (int i = 7; i >= 0; i--) {
-          if (!decided && hv[i] != tgt[i]) {
-            le = hv[i] < tgt[i];
-            decided = true;
-          }
-        }
-        if (le) {
-          const uint32_t ws = atomicAdd(p.wins, 1u);
-          if (ws < (uint32_t)p.max_wins) {
-            uint32_t* rec = p.wins + 1 + (uint64_t)ws * UWC_WIN_WORDS;
-            rec[0] = (uint32_t)row_off;
-            rec[1] = (uint32_t)col_off;
-#pragma unroll
-            for (int i = 0; i < 8; i++) rec[2 + i] = hv[i];
-          }
-        }
-      }
-      __threadfence();
-      mbar_arrive(&bars->hash_free[buf]);
     }
   }
 
