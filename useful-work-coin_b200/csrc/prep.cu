@@ -18,7 +18,7 @@ constexpr int kPitch = 5;            // uint4 per staged 64-byte block (80 B pit
 // Level-wise pairwise merge of `count` chaining values in shared memory, the odd trailing node
 // carried up unchanged: this builds BLAKE3's left-balanced tree as long as the group starts at a
 // multiple of a power of two >= its size. ROOT goes on the last merge when `is_root`.
-__device__ void merge_cvs(uint32_t* cv, int count, const uint32_t* key, bool is_root) {
+__device__ void merge_cvs(uint32_t* cv, int count, const uint32_t* key, bool is_root, uint32_t one) {
   const int tid = threadIdx.x;
   while (count > 1) {
     const int pairs = count >> 1, odd = count & 1;
@@ -28,7 +28,7 @@ __device__ void merge_cvs(uint32_t* cv, int count, const uint32_t* key, bool is_
 #pragma unroll
       for (int i = 0; i < 16; i++) msg[i] = cv[2 * tid * 8 + i];
       const uint32_t fl = b3::PARENT | b3::KEYED | ((is_root && count == 2) ? b3::ROOT : 0u);
-      b3::compress(key, msg, 0, 64, fl, res);
+      b3::compress<true>(key, msg, 0, 64, fl, res, one);
     }
     __syncthreads();
     if (tid < pairs) {
@@ -48,7 +48,7 @@ __device__ void merge_cvs(uint32_t* cv, int count, const uint32_t* key, bool is_
 // Chaining values of 128 consecutive chunks, merged to one subtree CV per CTA.
 __global__ void __launch_bounds__(kChunksPerCta) k_b3_chunks(const uint8_t* __restrict__ data, uint64_t nchunks,
                                                               const uint32_t* __restrict__ key,
-                                                              uint32_t* __restrict__ cvs_out) {
+                                                              uint32_t* __restrict__ cvs_out, uint32_t one) {
   __shared__ __align__(16) uint4 stage[2][kChunksPerCta * kPitch];
   __shared__ uint32_t cvs[kChunksPerCta * 8];
   const int tid = threadIdx.x;
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kChunksPerCta) k_b3_chunks(const uint8_t* __re
       }
       const uint32_t fl = b3::KEYED | (blk == 0 ? b3::CHUNK_START : 0u) | (blk == 15 ? b3::CHUNK_END : 0u) |
                           ((blk == 15 && nchunks == 1) ? b3::ROOT : 0u);
-      b3::compress(cv, msg, base + tid, 64, fl, cv);
+      b3::compress<true>(cv, msg, base + tid, 64, fl, cv, one);
     }
     __syncthreads();
   }
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kChunksPerCta) k_b3_chunks(const uint8_t* __re
     for (int i = 0; i < 8; i++) cvs[tid * 8 + i] = cv[i];
   }
   __syncthreads();
-  merge_cvs(cvs, count, k8, gridDim.x == 1 && nchunks > 1);
+  merge_cvs(cvs, count, k8, gridDim.x == 1 && nchunks > 1, one);
   if (tid < 8) cvs_out[(uint64_t)blockIdx.x * 8 + tid] = cvs[tid];
 }
 
@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(512) k_b3_reduce(const uint32_t* __restrict__ 
                                                    const uint32_t* __restrict__ key, uint32_t* __restrict__ out,
                                                    int final_level, const uint32_t* __restrict__ prefix,
                                                    const uint32_t* __restrict__ salt, uint32_t dim,
-                                                   uint32_t* __restrict__ root_out, uint32_t* __restrict__ seed_out) {
+                                                   uint32_t* __restrict__ root_out, uint32_t* __restrict__ seed_out,
+                                                   uint32_t one) {
   __shared__ uint32_t cvs[kReduceGroup * 8];
   const uint32_t base = blockIdx.x * kReduceGroup;
   const int cnt = (int)min((uint32_t)kReduceGroup, count - base);
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(512) k_b3_reduce(const uint32_t* __restrict__ 
 #pragma unroll
   for (int i = 0; i < 8; i++) k8[i] = key[i];
   __syncthreads();
-  merge_cvs(cvs, cnt, k8, final_level != 0);
+  merge_cvs(cvs, cnt, k8, final_level != 0, one);
   if (!final_level) {
     if (threadIdx.x < 8) out[(uint64_t)blockIdx.x * 8 + threadIdx.x] = cvs[threadIdx.x];
     return;
@@ -127,10 +128,10 @@ __global__ void __launch_bounds__(512) k_b3_reduce(const uint32_t* __restrict__ 
 #pragma unroll
       for (int i = 0; i < 8; i++) { msg[i] = root[i]; msg[8 + i] = 0u; s8[i] = salt[i]; }
       msg[8] = dim;
-      b3::hash64(s8, msg, bound);
+      b3::hash64<true>(s8, msg, bound, one);
 #pragma unroll
       for (int i = 0; i < 8; i++) { msg[i] = prefix[i]; msg[8 + i] = bound[i]; }
-      b3::hash64(nullptr, msg, seed);
+      b3::hash64<true>(nullptr, msg, seed, one);
 #pragma unroll
       for (int i = 0; i < 8; i++) seed_out[i] = seed[i];
     }
@@ -386,18 +387,18 @@ int uwc_b3_root_and_seed(const void* data, uint64_t nbytes, const uint32_t* key,
   cudaStream_t st = (cudaStream_t)stream;
   const uint64_t nch = nbytes / 1024;
   uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;
-  k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch);
+  k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch, 1u);
   uint32_t* cur = scratch;
   uint32_t* nxt = scratch + 8 * cnt;
   while (cnt > (uint64_t)kReduceGroup) {
     const uint64_t groups = (cnt + kReduceGroup - 1) / kReduceGroup;
     k_b3_reduce<<<(unsigned)groups, 512, 0, st>>>(cur, (uint32_t)cnt, key, nxt, 0, nullptr, nullptr, 0, nullptr,
-                                                  nullptr);
+                                                  nullptr, 1u);
     cur = nxt;
     nxt += 8 * groups;
     cnt = groups;
   }
-  k_b3_reduce<<<1, 512, 0, st>>>(cur, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out);
+  k_b3_reduce<<<1, 512, 0, st>>>(cur, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out, 1u);
   return uwc_launch_status();
 }
 
@@ -530,7 +531,7 @@ extern "C" int uwc_b3_root_and_seed_noalloc(const void* data, uint64_t nbytes, c
   cudaStream_t st = (cudaStream_t)stream;
   const uint64_t nch = nbytes / 1024;
   const uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;   // <= kNoAllocMaxCtas
-  k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch);
-  k_b3_reduce<<<1, 512, 0, st>>>(scratch, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out);
+  k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch, 1u);
+  k_b3_reduce<<<1, 512, 0, st>>>(scratch, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out, 1u);
   return uwc_launch_status();
 }
