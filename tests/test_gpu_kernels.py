@@ -118,6 +118,27 @@ def test_noise_rows_ranks_against_oracle(ops, r):
     assert int(mx.item()) == int(want_mx[0])
 
 
+@pytest.mark.parametrize("rows,k,r,ecopy", [(8, 1024, 64, False), (200, 1040, 64, True), (8192, 4096, 64, False),
+                                            (40000, 64, 128, True), (1776, 272, 256, True)])
+def test_noise_add_against_oracle(ops, rows, k, r, ecopy):
+    """The noising-only kernel (no projection): persistent CTAs with uneven row shares, shares longer
+    than one staged group (40000 rows), and the E copy into every correction limb."""
+    rng = np.random.default_rng(rows + k + r)
+    A = rng.integers(-64, 65, size=(rows, k), dtype=np.int8)
+    E = rng.integers(-32, 32, size=(rows, r), dtype=np.int8)
+    Pn = O.perm_packed(O.SEED_LABEL_A, rng.bytes(32), k, r)
+    L = 2 if ecopy else 0
+    want_corr = np.zeros((L, rows, 2 * r), np.int8) if ecopy else None
+    want_dst = O.noise_rows(A, r, E=E, Pn=Pn, want_dst=True, corr=want_corr, ecopy_off=r if ecopy else -1)
+    t = lambda x: torch.from_numpy(x.view(np.int32) if x.dtype == np.uint32 else x).cuda()
+    dst = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    corr = torch.zeros((L, rows, 2 * r), dtype=torch.int8, device="cuda") if ecopy else None
+    ops.noise_rows(t(A), rows, k, r, E=t(E), Pn=t(Pn), dst=dst, corr=corr, ecopy_off=r if ecopy else -1)
+    assert np.array_equal(dst.cpu().numpy(), want_dst)
+    if ecopy:
+        assert np.array_equal(corr.cpu().numpy(), want_corr)
+
+
 def test_proj_matrix_and_tensor_core_projection(ops):
     rng = np.random.default_rng(11)
     rows, k, r = 256, 2048, 128

@@ -189,57 +189,66 @@ __global__ void __launch_bounds__(128) k_noise_perm(uint32_t* __restrict__ out, 
 // ------------------------------------------------------------------ noise_rows
 namespace {
 constexpr int kNrRows = 8;  // rows per CTA
-constexpr int kNaRows = 16; // rows per CTA of the noising-only kernel
+constexpr int kNaRows = 32;      // rows per staged group of the noising-only kernel
+constexpr int kNaCtasPerSm = 4;  // its resident CTAs per SM (persistent grid, <= 64 registers)
 }
 
-// Noising only (no projection): dst = src + E[:, first] - E[:, second], row by row. Thread q owns
-// 16 consecutive columns for all kNaRows rows of its CTA: their permutation pairs stay in
-// registers, A is read and ApEA written in coalesced 16-byte vectors, E rows sit in shared memory.
+// Noising only (no projection): dst = src + E[:, first] - E[:, second], row by row. Persistent
+// CTAs (a few per SM) each take an even share of the rows, so no second partial wave leaves most
+// SMs idle; the share is walked in groups of kNaRows rows whose E rows are staged in shared memory.
+// Thread q owns 16 consecutive columns: their permutation pairs stay in registers for the CTA's
+// whole share, A is read and ApEA written in coalesced 16-byte vectors.
 // Values stay in int8 without wrapping for |src| <= 64, |E| <= 32 (kernels.cu:310-372).
-__global__ void __launch_bounds__(256) k_noise_add(const int8_t* __restrict__ src, int rows, int k, int r,
-                                                   const int8_t* __restrict__ E, const uint32_t* __restrict__ Pn,
-                                                   int8_t* __restrict__ dst, int8_t* __restrict__ corr, int ecopy_off,
-                                                   int lmax) {
-  __shared__ int8_t Es[kNaRows * 256];
-  const int row0 = blockIdx.x * kNaRows;
-  const int nr = min(kNaRows, rows - row0);
-  for (int i = threadIdx.x; i < nr * r; i += blockDim.x) Es[i] = E[(uint64_t)row0 * r + i];
-  __syncthreads();
-  if (corr && ecopy_off >= 0) {
-    // the E half of every correction limb: [X_li | E] (kernels.cu:360-368)
-    const uint64_t limb_stride = (uint64_t)rows * 2 * r;
-    for (int i = threadIdx.x; i < nr * r; i += blockDim.x) {
-      const int rr = i / r, j = i - rr * r;
-      for (int li = 0; li < lmax; li++) corr[li * limb_stride + (uint64_t)(row0 + rr) * 2 * r + ecopy_off + j] = Es[i];
+__global__ void __launch_bounds__(256, kNaCtasPerSm) k_noise_add(const int8_t* __restrict__ src, int rows, int k,
+                                                                 int r, const int8_t* __restrict__ E,
+                                                                 const uint32_t* __restrict__ Pn,
+                                                                 int8_t* __restrict__ dst, int8_t* __restrict__ corr,
+                                                                 int ecopy_off, int lmax) {
+  __shared__ __align__(16) int8_t Es[kNaRows * 256];
+  const int r0 = (int)((int64_t)blockIdx.x * rows / gridDim.x);
+  const int r1 = (int)((int64_t)(blockIdx.x + 1) * rows / gridDim.x);
+  const int nq = k >> 4;
+  for (int g0 = r0; g0 < r1; g0 += kNaRows) {
+    const int nr = min(kNaRows, r1 - g0);
+    if (g0 != r0) __syncthreads();   // the previous group's E rows are no longer read
+    for (int i = threadIdx.x; i < nr * r; i += blockDim.x) Es[i] = E[(uint64_t)g0 * r + i];
+    __syncthreads();
+    if (corr && ecopy_off >= 0) {
+      // the E half of every correction limb: [X_li | E] (kernels.cu:360-368)
+      const uint64_t limb_stride = (uint64_t)rows * 2 * r;
+      for (int i = threadIdx.x; i < nr * r; i += blockDim.x) {
+        const int rr = i / r, j = i - rr * r;
+        for (int li = 0; li < lmax; li++) corr[li * limb_stride + (uint64_t)(g0 + rr) * 2 * r + ecopy_off + j] = Es[i];
+      }
     }
-  }
-  for (int q = threadIdx.x; q < (k >> 4); q += blockDim.x) {
-    uint32_t pf[16];
-    const uint4* pn4 = reinterpret_cast<const uint4*>(Pn + 16 * q);
-#pragma unroll
-    for (int v = 0; v < 4; v++) {
-      const uint4 p = __ldg(pn4 + v);
-      pf[4 * v] = p.x; pf[4 * v + 1] = p.y; pf[4 * v + 2] = p.z; pf[4 * v + 3] = p.w;
-    }
-#pragma unroll 4
-    for (int rr = 0; rr < nr; rr++) {
-      const uint64_t off = (uint64_t)(row0 + rr) * k + 16 * q;
-      const uint4 w = __ldcs(reinterpret_cast<const uint4*>(src + off));
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-      const int8_t* er = Es + rr * r;
-      uint32_t o[4];
+    for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+      uint32_t pf[16];
+      const uint4* pn4 = reinterpret_cast<const uint4*>(Pn + 16 * q);
 #pragma unroll
       for (int v = 0; v < 4; v++) {
-        uint32_t ov = 0;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const uint32_t p = pf[4 * v + j];
-          const int nv = (int)(int8_t)(ws[v] >> (8 * j)) + (int)er[p & 0xFFFFu] - (int)er[p >> 16];
-          ov |= (uint32_t)(uint8_t)(int8_t)nv << (8 * j);
-        }
-        o[v] = ov;
+        const uint4 p = __ldg(pn4 + v);
+        pf[4 * v] = p.x; pf[4 * v + 1] = p.y; pf[4 * v + 2] = p.z; pf[4 * v + 3] = p.w;
       }
-      __stcs(reinterpret_cast<uint4*>(dst + off), make_uint4(o[0], o[1], o[2], o[3]));
+#pragma unroll 4
+      for (int rr = 0; rr < nr; rr++) {
+        const uint64_t off = (uint64_t)(g0 + rr) * k + 16 * q;
+        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(src + off));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const int8_t* er = Es + rr * r;
+        uint32_t o[4];
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+          uint32_t ov = 0;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const uint32_t p = pf[4 * v + j];
+            const int nv = (int)(int8_t)(ws[v] >> (8 * j)) + (int)er[p & 0xFFFFu] - (int)er[p >> 16];
+            ov |= (uint32_t)(uint8_t)(int8_t)nv << (8 * j);
+          }
+          o[v] = ov;
+        }
+        __stcs(reinterpret_cast<uint4*>(dst + off), make_uint4(o[0], o[1], o[2], o[3]));
+      }
     }
   }
 }
@@ -435,8 +444,8 @@ int uwc_noise_rows(const int8_t* src, int rows, int k, int r, const int8_t* E, c
   if ((((uintptr_t)src) | ((uintptr_t)dst) | ((uintptr_t)Pn) | ((uintptr_t)Pp)) & 15) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (dst && !Pp) {
-    k_noise_add<<<(rows + kNaRows - 1) / kNaRows, 256, 0, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, corr,
-                                                                                 ecopy_off, lmax);
+    const int grid = std::min(rows, uwc_num_sms() * kNaCtasPerSm);
+    k_noise_add<<<grid, 256, 0, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, corr, ecopy_off, lmax);
     return uwc_launch_status();
   }
   const int smem = kNrRows * 256 + kNrRows * r * 4;
