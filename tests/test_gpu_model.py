@@ -37,9 +37,13 @@ def test_attention_prefill_golden(dev, mg, tag):
 
 @pytest.mark.parametrize("B,start,Tq,H,Hkv,maxlen", [(3, 299, 1, 4, 2, 320), (2, 100, 5, 8, 2, 128),
                                                       (1, 0, 70, 2, 2, 70), (2, 1000, 17, 4, 4, 1040),
-                                                      (1, 2175, 1, 16, 8, 2176)])
+                                                      (1, 2175, 1, 16, 8, 2176), (2, 0, 1, 2, 2, 16),
+                                                      (1, 5, 1, 8, 2, 8), (2, 1100, 1, 8, 1, 1104),
+                                                      (1, 4095, 1, 4, 1, 4096)])
 def test_attention_cache_vs_oracle(dev, B, start, Tq, H, Hkv, maxlen):
-    """New tokens at positions start .. start+Tq-1 over a KV cache (decode and chunked prefill)."""
+    """New tokens at positions start .. start+Tq-1 over a KV cache (decode and chunked prefill).
+    Tq = 1 runs the cluster decode kernel: 1, 2, 4 and 8 query heads per KV head, and key counts
+    below the cluster size (CTAs without keys) as well as across several V tiles per CTA."""
     import torch
 
     import detq as D

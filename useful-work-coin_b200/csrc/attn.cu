@@ -15,10 +15,14 @@
 // 14-bit integer probabilities; V is staged per 64-key tile transposed (dims x keys) so the P V
 // dot products run four keys per dp4a. Keys and values are read with strides, so the same kernel
 // serves the prefill layout (token-major, the detgpu call) and a KV cache (head-major, decode).
+// A decode token (Tq = 1) runs k_attn_decode instead: a cluster of 8 CTAs per (sequence, KV head)
+// splits the keys and combines its reductions through distributed shared memory.
 #include <algorithm>
 #include <mutex>
 #include <set>
 #include <utility>
+
+#include <cooperative_groups.h>
 
 #include "det_math.cuh"
 #include "uwc_device.cuh"
@@ -272,6 +276,259 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
   }
 }
 
+// ---- decode: one query token per sequence (Tq = 1), the keys split over a cluster of CTAs.
+// A cluster of kDecCluster CTAs serves one (sequence, KV head) pair and all HPG = H / Hkv query
+// heads that read it, so each key and value row is loaded once per token. CTA `rank` owns keys
+// [rank S / C, (rank + 1) S / C). The softmax's four row reductions (max, max of e, the exact int64
+// sum, max of P * sv) and the int64 P V partials combine across the cluster through distributed
+// shared memory: max and integer addition are exact in any order, so the result is bit-identical
+// to the single-CTA kernel and to detrt.
+constexpr int kDecCluster = 8;
+
+// the four reductions' exchange slots (one per reduction, so no slot is rewritten) and the partials
+template <int HPG>
+struct DecShared {
+  float red[3][8];         // per-warp partials of the three maxima (one slot set each: no reuse)
+  long long redl[2][8];    // per-warp partials of the row sum (and of its rare second pass)
+  float xf[3][HPG];        // row max, max of e, max of P * sv: this CTA's values
+  long long xl[2][HPG];    // exact row sum at the presumed shift (and at the true one): this CTA's value
+  float sp[HPG];
+  long long part[HPG][kHd];  // this CTA's P V partial, read by the cluster's final reduction
+};
+
+// Global -> shared copies that bypass registers (cp.async), issued in commit groups; a thread
+// waits for its own groups, a barrier then publishes them to the CTA.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int HPG>
+__global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThreads)
+    k_attn_decode(const AttnArgs a, int lpitch) {
+  constexpr int NW = kAttnThreads / 32, WPR = NW / HPG;
+  static_assert(HPG >= 1 && HPG <= NW && NW % HPG == 0, "query heads per KV head");
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint32_t* vrows = reinterpret_cast<uint32_t*>(sm);                               // lpitch x 32 words
+  float* sc = reinterpret_cast<float*>(sm + (size_t)lpitch * kHd);                 // HPG x lpitch
+  float* svs = sc + (size_t)HPG * lpitch;                                          // lpitch value scales
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(svs + lpitch);                      // HPG x 32 words
+  long long* s_out = reinterpret_cast<long long*>(qrow + HPG * 32);                // NW x 128
+  __shared__ DecShared<HPG> ds;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = warp / WPR, part = warp % WPR;
+  const int rank = (int)cluster.block_rank();
+  const int pair = blockIdx.x / kDecCluster;
+  const int b = pair / a.Hkv, g = pair % a.Hkv;
+  const int start = a.start_dev ? __ldg(a.start_dev) : a.start;
+  const int S = start + 1;
+  const int k0 = (int)((long long)rank * S / kDecCluster), k1 = (int)((long long)(rank + 1) * S / kDecCluster);
+  const int nk = k1 - k0;
+  const int8_t* kb = a.kc + b * a.kv_seq + g * a.kv_head;
+  const int8_t* vb = a.vc + b * a.kv_seq + g * a.kv_head;
+  const float* ksb = a.ks + b * a.s_seq + g * a.s_head;
+  const float* vsb = a.vs + b * a.s_seq + g * a.s_head;
+  const int h0 = g * HPG;
+
+  // Loads in the order they are needed: the thread's first key row (registers), then by cp.async
+  // the query rows (group 1), the value scales (group 2) and the value rows (group 3), which
+  // stream into shared memory while the scores and the softmax run.
+  uint32_t kw[32];
+  float ksj = 0.f;
+  auto load_key = [&](int jl) {
+    const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)(k0 + jl) * a.kv_tok);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint4 v = __ldg(kp + i);
+      kw[4 * i] = v.x; kw[4 * i + 1] = v.y; kw[4 * i + 2] = v.z; kw[4 * i + 3] = v.w;
+    }
+    ksj = __ldg(ksb + (size_t)(k0 + jl) * a.s_tok);
+  };
+  if (tid < nk) load_key(tid);
+  for (int i = tid; i < HPG * 8; i += kAttnThreads)
+    cp_async16(qrow + 4 * i, a.qq + ((size_t)b * a.H + h0 + (i >> 3)) * kHd + (i & 7) * 16);
+  cp_async_commit();
+  for (int j = tid; j < nk; j += kAttnThreads) cp_async4(svs + j, vsb + (size_t)(k0 + j) * a.s_tok);
+  cp_async_commit();
+  for (int i = tid; i < nk * 8; i += kAttnThreads)
+    cp_async16(vrows + (size_t)(i >> 3) * 32 + (i & 7) * 4, vb + (size_t)(k0 + (i >> 3)) * a.kv_tok + (i & 7) * 16);
+  cp_async_commit();
+  cp_async_wait<2>();   // the query rows
+  __syncthreads();
+
+  // ---- scores of this CTA's keys for every query head of the group
+  for (int jl = tid; jl < nk; jl += kAttnThreads) {
+    if (jl != tid) load_key(jl);
+#pragma unroll
+    for (int rr = 0; rr < HPG; rr++) {
+      const uint4* qv = reinterpret_cast<const uint4*>(qrow + rr * 32);
+      int dot = 0;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const uint4 qw = qv[i];
+        dot = __dp4a((int)kw[4 * i], (int)qw.x, dot);
+        dot = __dp4a((int)kw[4 * i + 1], (int)qw.y, dot);
+        dot = __dp4a((int)kw[4 * i + 2], (int)qw.z, dot);
+        dot = __dp4a((int)kw[4 * i + 3], (int)qw.w, dot);
+      }
+      const float qsr = __ldg(a.qs + (size_t)b * a.H + h0 + rr);
+      sc[rr * lpitch + jl] = __fmul_rn(__fmul_rn(__fmul_rn((float)dot, qsr), ksj), a.inv_sqrt_hd);
+    }
+  }
+  __syncthreads();
+
+  // row reduction over this CTA (the row's WPR warps), then over the cluster
+  float* row = sc + r * lpitch;
+  const int j0 = 32 * part + lane, js = 32 * WPR;
+  auto cta_max = [&](float v, int slot) -> float {
+    v = warp_maxf(v);
+    if (lane == 0) ds.red[slot][warp] = v;
+    __syncthreads();
+    float m = ds.red[slot][r * WPR];
+#pragma unroll
+    for (int i = 1; i < WPR; i++) m = fmaxf(m, ds.red[slot][r * WPR + i]);
+    return m;
+  };
+  auto cluster_max = [&](float v, int slot) -> float {
+    v = cta_max(v, slot);
+    if (part == 0 && lane == 0) ds.xf[slot][r] = v;
+    cluster.sync();
+#pragma unroll
+    for (int q = 0; q < kDecCluster; q++) v = fmaxf(v, cluster.map_shared_rank(&ds.xf[slot][r], q)[0]);
+    return v;
+  };
+  // this CTA's exact fixed-point sum of the row's e at shift sh, into exchange slot `slot`
+  auto cta_sum = [&](int sh, int slot) {
+    long long acc = 0;
+    if (sh <= 100) {                 // |e| 2^sh stays a normal float below 2^62: exact in fp32
+      const float up = pow2f(sh);
+      for (int j = j0; j < nk; j += js) acc += __float2ll_rn(__fmul_rn(row[j], up));
+    } else {
+      const double up = pow2d(sh);
+      for (int j = j0; j < nk; j += js) acc += fixed_term(row[j], up);
+    }
+    acc = warp_sumll(acc);
+    if (lane == 0) ds.redl[slot][warp] = acc;
+    __syncthreads();
+    if (part == 0 && lane == 0) {
+      long long t = 0;
+#pragma unroll
+      for (int i = 0; i < WPR; i++) t += ds.redl[slot][r * WPR + i];
+      ds.xl[slot][r] = t;
+    }
+  };
+  float mx = __int_as_float(0xff800000);
+  for (int j = j0; j < nk; j += js) mx = fmaxf(mx, row[j]);
+  mx = cluster_max(mx, 0);
+  float emax = 0.f;
+  for (int j = j0; j < nk; j += js) {
+    const float e = det_exp(__fsub_rn(row[j], mx));
+    row[j] = e;
+    emax = fmaxf(emax, e);
+  }
+  // The sum's shift follows from the row's max of e, which is det_exp(0) = 1 (the max score's own
+  // term) unless another term rounds to 2 or more: the sum at that presumed shift travels with the
+  // max of e in one exchange, and only a different true shift (uniform over the cluster) costs a
+  // second exchange. Either way the sum is the one at the true shift.
+  const int sh_guess = fixed_shift(1.0f, kMaxKeysLog2);
+  emax = cta_max(emax, 1);
+  if (part == 0 && lane == 0) ds.xf[1][r] = emax;
+  cta_sum(sh_guess, 0);
+  cp_async_wait<1>();   // the value scales, read after this exchange
+  cluster.sync();
+#pragma unroll
+  for (int q = 0; q < kDecCluster; q++) emax = fmaxf(emax, cluster.map_shared_rank(&ds.xf[1][r], q)[0]);
+  const int sh = fixed_shift(emax, kMaxKeysLog2);
+  long long acc = 0;
+  if (__syncthreads_or(sh != sh_guess)) {
+    cta_sum(sh, 1);
+    cluster.sync();
+#pragma unroll
+    for (int q = 0; q < kDecCluster; q++) acc += cluster.map_shared_rank(&ds.xl[1][r], q)[0];
+  } else {
+#pragma unroll
+    for (int q = 0; q < kDecCluster; q++) acc += cluster.map_shared_rank(&ds.xl[0][r], q)[0];
+  }
+  const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+  float pmax = 0.f;
+  for (int j = j0; j < nk; j += js) {
+    const float pv = __fmul_rn(__fdiv_rn(row[j], den), svs[j]);
+    row[j] = pv;
+    pmax = fmaxf(pmax, pv);
+  }
+  pmax = cluster_max(pmax, 2);
+  const float sp = __fdiv_rn(fmaxf(pmax, 1e-30f), (float)kPLevels);
+  const int nk4 = (nk + 3) & ~3;
+  for (int j = j0; j < nk4; j += js) {
+    int pi = 0;
+    if (j < nk) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels);
+    reinterpret_cast<int*>(row)[j] = pi;
+  }
+  if (lane == 0 && part == 0) ds.sp[r] = sp;
+  cp_async_wait<0>();   // the value rows
+  __syncthreads();
+
+  // ---- P V over this CTA's keys, straight from the staged value rows: lane l owns dims 4l..4l+3;
+  // four keys' words are transposed in registers so each dp4a adds four keys' hi (resp. lo) limbs
+  // times one dim's values: exact int32 partial sums (|sum| < 127 * 127 * S), combined as
+  // (hi << 7) + lo in int64.
+  int acc_hi[4] = {0, 0, 0, 0}, acc_lo[4] = {0, 0, 0, 0};
+  const int4* prow = reinterpret_cast<const int4*>(row);
+#pragma unroll 4
+  for (int kg = part; kg < nk4 / 4; kg += WPR) {
+    const int4 p4 = prow[kg];
+    const uint32_t lo4 =
+        __byte_perm(__byte_perm(p4.x, p4.y, 0x0040), __byte_perm(p4.z, p4.w, 0x0040), 0x5410) & 0x7F7F7F7Fu;
+    const uint32_t hi4 = __byte_perm(__byte_perm(p4.x << 1, p4.y << 1, 0x0051),
+                                     __byte_perm(p4.z << 1, p4.w << 1, 0x0051), 0x5410);
+    const uint32_t* vr = vrows + (size_t)(4 * kg) * 32 + lane;
+    const uint32_t w0 = vr[0], w1 = vr[32], w2 = vr[64], w3 = vr[96];
+    const uint32_t lo01 = __byte_perm(w0, w1, 0x5140), hi01 = __byte_perm(w0, w1, 0x7362);
+    const uint32_t lo23 = __byte_perm(w2, w3, 0x5140), hi23 = __byte_perm(w2, w3, 0x7362);
+    const uint32_t d4[4] = {__byte_perm(lo01, lo23, 0x5410), __byte_perm(lo01, lo23, 0x7632),
+                            __byte_perm(hi01, hi23, 0x5410), __byte_perm(hi01, hi23, 0x7632)};
+#pragma unroll
+    for (int y = 0; y < 4; y++) {
+      acc_hi[y] = __dp4a((int)hi4, (int)d4[y], acc_hi[y]);
+      acc_lo[y] = __dp4a((int)lo4, (int)d4[y], acc_lo[y]);
+    }
+  }
+#pragma unroll
+  for (int y = 0; y < 4; y++) s_out[warp * kHd + 4 * lane + y] = ((long long)acc_hi[y] << 7) + acc_lo[y];
+  __syncthreads();
+  for (int i = tid; i < HPG * kHd; i += kAttnThreads) {
+    const int rr = i / kHd, d = i % kHd;
+    long long t = 0;
+#pragma unroll
+    for (int w = 0; w < WPR; w++) t += s_out[(rr * WPR + w) * kHd + d];
+    ds.part[rr][d] = t;
+  }
+  cluster.sync();
+  // the cluster's CTAs split the HPG x 128 outputs; each sums its share over the cluster
+  for (int i = rank * kAttnThreads + tid; i < HPG * kHd; i += kDecCluster * kAttnThreads) {
+    const int rr = i / kHd, d = i % kHd;
+    long long t = 0;
+#pragma unroll
+    for (int q = 0; q < kDecCluster; q++) t += cluster.map_shared_rank(&ds.part[rr][d], q)[0];
+    a.out[((size_t)b * a.H + h0 + rr) * kHd + d] = __fmul_rn(__ll2float_rn(t), ds.sp[rr]);
+  }
+  cluster.sync();   // no CTA leaves while another may still read its shared memory
+}
+
+// value rows, scores, value scales, query rows, per-warp P V partials
+size_t dec_smem(int HPG, int lpitch) {
+  return (size_t)lpitch * kHd + (size_t)HPG * lpitch * 4 + (size_t)lpitch * 4 + (size_t)HPG * 128 +
+         (size_t)(kAttnThreads / 32) * kHd * 8;
+}
+
 // det_rmsnorm (core.py:151-159) of one row per CTA, float32 out.
 template <int NT>
 __global__ void __launch_bounds__(NT) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, int k,
@@ -377,9 +634,19 @@ int smem_optin(const void* kernel, int bytes) {
 template <int QT>
 int launch_attn(const AttnArgs& a, int B, int spitch, cudaStream_t st) {
   const int smem = (int)attn_smem(QT, spitch);
-  const int rc = smem_optin((const void*)k_attention<QT>, smem);
+  const int rc = smem_optin((const void*)k_attention<QT>, smem + 1024);   // + its static reduction slots
   if (rc != UWC_OK) return rc;
   k_attention<QT><<<dim3(B * a.H, (a.Tq + QT - 1) / QT), kAttnThreads, smem, st>>>(a, spitch);
+  return uwc_launch_status();
+}
+
+template <int HPG>
+int launch_decode(const AttnArgs& a, int B, int lpitch, cudaStream_t st) {
+  const int smem = (int)dec_smem(HPG, lpitch);
+  // the opt-in covers the static reduction slots too (their sum passes 48 KiB before the dynamic part does)
+  const int rc = smem_optin((const void*)k_attn_decode<HPG>, smem + (int)sizeof(DecShared<HPG>));
+  if (rc != UWC_OK) return rc;
+  k_attn_decode<HPG><<<B * a.Hkv * kDecCluster, kAttnThreads, smem, st>>>(a, lpitch);
   return uwc_launch_status();
 }
 
@@ -402,6 +669,21 @@ int attention_impl(const int8_t* qq, const float* qs, const int8_t* kc, const fl
   AttnArgs a{qq, qs, kc, ks, vc, vs, kv_seq, kv_tok, kv_head, s_seq, s_tok, s_head, Tq, start, H, Hkv, inv_sqrt_hd,
              out, start_dev};
   cudaStream_t st = (cudaStream_t)stream;
+  if (Tq == 1 && (long long)B * Hkv * kDecCluster <= 0x7fffffffLL) {
+    // decode: the keys split over a cluster, all query heads of a KV head in one cluster
+    const int per = (S + kDecCluster - 1) / kDecCluster;
+    const int lpitch = (per + kTileKeys - 1) / kTileKeys * kTileKeys;
+    const int hpg = H / Hkv;
+    if (dec_smem(hpg, lpitch) <= (size_t)kAttnSmemMax) {
+      switch (hpg) {
+        case 1: return launch_decode<1>(a, B, lpitch, st);
+        case 2: return launch_decode<2>(a, B, lpitch, st);
+        case 4: return launch_decode<4>(a, B, lpitch, st);
+        case 8: return launch_decode<8>(a, B, lpitch, st);
+        default: break;
+      }
+    }
+  }
   // the widest query block whose score rows fit in shared memory (and not wider than Tq needs)
   const int want = Tq >= 8 ? 8 : Tq >= 4 ? 4 : Tq >= 2 ? 2 : 1;
   for (int QT = want; QT >= 1; QT >>= 1) {
