@@ -44,7 +44,7 @@ WORKLOADS = {
                                      "128-token greedy decode (configs[3])"),
 }
 # DRAM bytes per launch of the dominant kernel from one ncu capture (committed summary under profiles/)
-TRAFFIC = {"c3-mine": 148.2e6 + 6.4e6}
+TRAFFIC = {"c3-mine": 148.7e6 + 4.0e6}
 # Llama-3.1-8B linears of one layer: (name, n, k, kind); qkv n = (32 + 2 * 8) * 128
 C5_LINEARS = [("qkv", 6144, 4096, "col"), ("o", 4096, 4096, "row"), ("gate_up", 28672, 4096, "col"),
               ("down", 4096, 14336, "row")]
