@@ -340,17 +340,24 @@ class MinedWeight:
         """What a pure noise miner runs per attempt batch: commit A, noise it, hashed GEMM, no output.
 
         No projections (X, Y) and no denoise, since nobody needs C (ops.py:349-364)."""
+        b = self._buf(A.shape[0])
+        self.mine_prepare(A, b["a_seed"], b["ApEA"], b["wins"], b["EAL"], b["PA"], b["scratch"])
+        self.mine_gemm(b["ApEA"], b["a_seed"], b["wins"])
+
+    def mine_prepare(self, A, a_seed, ApEA, wins, EAL, PA, scratch):
+        """The first half of noise_mine: commit to A (a_seed), its noise EAL and P_A, ApEA = A + noise,
+        and the win counter zeroed. Writes only the given buffers."""
         m, k = A.shape
-        r = self.r
-        dev = A.device
-        b = self._buf(m)
-        c = consts(dev)
-        b3_root_and_seed(A.view(-1), self.job_key, prefix=self.b_seed, salt=c["SALT_A"], dim=m,
-                         seed_out=b["a_seed"], scratch=b["scratch"])
-        noise_uniform(b["EAL"], c["LABEL_A"], b["a_seed"], zero_me=b["wins"], zero_n=1)
-        noise_perm(b["PA"], k, r, c["LABEL_A"], b["a_seed"])
-        noise_rows(A, m, k, r, E=b["EAL"], Pn=b["PA"], dst=b["ApEA"])
-        gemm(b["ApEA"], self.BpEBt, r=r, flags=FLAG_HASH, key=b["a_seed"], target=self.target, wins=b["wins"],
+        c = consts(A.device)
+        b3_root_and_seed(A.view(-1), self.job_key, prefix=self.b_seed, salt=c["SALT_A"], dim=m, seed_out=a_seed,
+                         scratch=scratch)
+        noise_uniform(EAL, c["LABEL_A"], a_seed, zero_me=wins, zero_n=1)
+        noise_perm(PA, k, self.r, c["LABEL_A"], a_seed)
+        noise_rows(A, m, k, self.r, E=EAL, Pn=PA, dst=ApEA)
+
+    def mine_gemm(self, ApEA, a_seed, wins):
+        """The second half of noise_mine: the hashed GEMM of a prepared attempt."""
+        gemm(ApEA, self.BpEBt, r=self.r, flags=FLAG_HASH, key=a_seed, target=self.target, wins=wins,
              max_wins=self.max_wins)
 
     def win_count(self, m: int) -> int:
