@@ -203,6 +203,26 @@ int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const flo
                   const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq, long long kv_tok,
                   long long kv_head, long long s_seq, long long s_tok, long long s_head, float inv_sqrt_hd,
                   float* out, void* stream);
+/* uwc_attention for many query rows on the tensor cores: S = Q K^T and O = [P_hi; P_lo] V as
+ * batched tcgen05 int8 GEMMs (uwc_gemm_batched), the scale chain and softmax per query row between
+ * them; the same bits as uwc_attention (exact integer sums). Same arguments plus a device
+ * workspace of uwc_attention_tc_workspace_bytes(B, Tq, start, H, Hkv) bytes (16-byte aligned).
+ * start + Tq <= 131072 (the P V limb sums stay below 2^31) and 4 (start + Tq) floats of shared
+ * memory per query row. Replaces the same call as uwc_attention (runtime/detgpu/kernels.py
+ * attention, the prefill form). */
+uint64_t uwc_attention_tc_workspace_bytes(int B, int Tq, int start, int H, int Hkv);
+int uwc_attention_tc(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                     const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq, long long kv_tok,
+                     long long kv_head, long long s_seq, long long s_tok, long long s_head, float inv_sqrt_hd,
+                     float* out, void* workspace, uint64_t workspace_bytes, void* stream);
+/* Batched exact int8 GEMM, int32 out: out[bt] (m x n, contiguous per batch) = A[bt] B[bt / b_bdiv]^T
+ * for bt < nbatch, A[bt] the m x k rows from row bt * a_brows of A, B[g] the n x k rows from row
+ * g * b_brows of B (both k-contiguous, row length k; k % 16 == 0, n % 4 == 0). causal 1 computes
+ * only the 128 x 256 output blocks some row sees (row t sees columns j <= cshift + t); causal 2
+ * stops a 128-row block's k range after column cshift + (m0 % qrows) + 127 (A stacks two qrows-row
+ * halves). No counterpart in the reference (its attention is SIMT, runtime/detgpu/kernels.py). */
+int uwc_gemm_batched(const int8_t* A, const int8_t* B, int m, int n, int k, int nbatch, long long a_brows,
+                     long long b_brows, int b_bdiv, int causal, int cshift, int qrows, int32_t* out, void* stream);
 /* uwc_attention with the start position read from device memory (*start <= max_start), so one
  * CUDA graph serves every decode step; shared memory is sized for max_start + Tq keys. No
  * counterpart in the reference (its decode runs eagerly, runtime/detrt/qwen3.py:315-329). */

@@ -723,6 +723,258 @@ __global__ void __launch_bounds__(256) k_kv_append(const int8_t* __restrict__ kq
 }
 }  // namespace
 
+// ------------------------------------------------------------------ prefill on the tensor cores
+// The same attention for many query rows as three passes around two exact int8 GEMMs on tcgen05
+// (uwc_gemm_batched): S = Q K^T in int32 (causal blocks only), then per query row the fp32 scale
+// chain and the softmax -> 14-bit P as two 7-bit limbs [P_hi; P_lo], then O = [P_hi; P_lo] V in
+// int32 and o = fmul(float((hi << 7) + lo), sp). The integer sums are exact, so the output is the
+// same bits as k_attention. Query batch bt = b * H + h reads KV head g = h / (H / Hkv).
+extern "C" int uwc_gemm_batched(const int8_t* A, const int8_t* B, int m, int n, int k, int nbatch, long long a_brows,
+                                long long b_brows, int b_bdiv, int causal, int cshift, int qrows, int32_t* out,
+                                void* stream);
+namespace {
+constexpr int kTcRowsPerCta = 4;   // query rows per softmax CTA (one warp each)
+
+struct TcLayout {
+  int nb, nkv, Tp, Sp, Sn;
+  size_t qh, kh, vt, ksc, vsc, sint, pst, o32, sp, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+TcLayout tc_layout(int B, int Tq, int start, int H, int Hkv) {
+  TcLayout L{};
+  L.nb = B * H;
+  L.nkv = B * Hkv;
+  L.Tp = (Tq + 127) / 128 * 128;
+  const int S = start + Tq;
+  L.Sp = (S + 127) / 128 * 128;
+  L.Sn = (S + 3) / 4 * 4;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { const size_t at = o; o = align256(o + bytes); return at; };
+  L.qh = take((size_t)L.nb * L.Tp * kHd);
+  L.kh = take((size_t)L.nkv * L.Sp * kHd);
+  L.vt = take((size_t)L.nkv * kHd * L.Sp);
+  L.ksc = take((size_t)L.nkv * L.Sp * 4);
+  L.vsc = take((size_t)L.nkv * L.Sp * 4);
+  L.sint = take((size_t)L.nb * L.Tp * L.Sn * 4);
+  L.pst = take((size_t)L.nb * 2 * L.Tp * L.Sp);
+  L.o32 = take((size_t)L.nb * 2 * L.Tp * kHd * 4);
+  L.sp = take((size_t)L.nb * L.Tp * 4);
+  L.total = o;
+  return L;
+}
+
+// Query rows head-major: Qh[b * H + h][t] = q(b * Tq + t, h), 16 bytes per thread.
+__global__ void k_tc_gather_q(const int8_t* __restrict__ qq, int B, int Tq, int H, int Tp, int8_t* __restrict__ qh) {
+  const long long n = (long long)B * H * Tq * 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int part = (int)(i & 7);
+    const long long row = i >> 3;                 // (b, h, t)
+    const int t = (int)(row % Tq);
+    const long long bh = row / Tq;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    const uint4 v = reinterpret_cast<const uint4*>(qq + ((size_t)(b * Tq + t) * H + h) * kHd)[part];
+    reinterpret_cast<uint4*>(qh + ((size_t)bh * Tp + t) * kHd)[part] = v;
+  }
+}
+
+// Keys and the key / value scales per KV head: Kh[b * Hkv + g][j], KS, VS, for j < S.
+__global__ void k_tc_gather_k(const int8_t* __restrict__ kc, const float* __restrict__ ks, const float* __restrict__ vs,
+                              int B, int S, int Hkv, long long kv_seq, long long kv_tok, long long kv_head,
+                              long long s_seq, long long s_tok, long long s_head, int Sp, int8_t* __restrict__ kh,
+                              float* __restrict__ ksc, float* __restrict__ vsc) {
+  const long long n = (long long)B * Hkv * S * 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int part = (int)(i & 7);
+    const long long row = i >> 3;                 // (b, g, j)
+    const int j = (int)(row % S);
+    const long long bg = row / S;
+    const int g = (int)(bg % Hkv), b = (int)(bg / Hkv);
+    const uint4 v = *reinterpret_cast<const uint4*>(kc + b * kv_seq + j * kv_tok + g * kv_head + part * 16);
+    reinterpret_cast<uint4*>(kh + ((size_t)bg * Sp + j) * kHd)[part] = v;
+    if (part == 0) {
+      ksc[(size_t)bg * Sp + j] = ks[b * s_seq + j * s_tok + g * s_head];
+      vsc[(size_t)bg * Sp + j] = vs[b * s_seq + j * s_tok + g * s_head];
+    }
+  }
+}
+
+// Values transposed per KV head: Vt[b * Hkv + g][d][j] (keys contiguous: the P V GEMM's k axis).
+// One CTA per (KV head, 64-key tile): the tile is staged in shared memory, then written per dim.
+__global__ void __launch_bounds__(256) k_tc_transpose_v(const int8_t* __restrict__ vc, int B, int S, int Hkv,
+                                                        long long kv_seq, long long kv_tok, long long kv_head, int Sp,
+                                                        int8_t* __restrict__ vt) {
+  __shared__ uint32_t tile[64][kHd / 4 + 1];
+  const int bg = blockIdx.y, j0 = blockIdx.x * 64;
+  const int g = bg % Hkv, b = bg / Hkv;
+  for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+    const int jj = i >> 5, w = i & 31, j = j0 + jj;
+    tile[jj][w] = j < S ? *reinterpret_cast<const uint32_t*>(vc + b * kv_seq + j * kv_tok + g * kv_head + 4 * w) : 0u;
+  }
+  __syncthreads();
+  // thread: dim d, 4 consecutive keys -> one word of Vt
+  for (int i = threadIdx.x; i < kHd * 16; i += 256) {
+    const int d = i >> 4, kq = i & 15;
+    uint32_t o = 0;
+#pragma unroll
+    for (int x = 0; x < 4; x++) o |= ((tile[4 * kq + x][d >> 2] >> (8 * (d & 3))) & 0xFFu) << (8 * x);
+    if (j0 + 4 * kq < Sp) *reinterpret_cast<uint32_t*>(vt + ((size_t)bg * kHd + d) * Sp + j0 + 4 * kq) = o;
+  }
+}
+
+// One warp per query row (batch bt, row t): the scale chain and softmax of k_attention on the
+// int32 dots of S, the 14-bit P written as hi limbs (row t of the batch's P block) and lo limbs (row
+// Tp + t), zero from key start + t + 1 up to the end of the P V GEMM's k range for t's row block.
+__global__ void __launch_bounds__(kTcRowsPerCta * 32) k_tc_softmax(const int32_t* __restrict__ sint,
+                                                                   const float* __restrict__ qs,
+                                                                   const float* __restrict__ ksc,
+                                                                   const float* __restrict__ vsc, int B, int Tq,
+                                                                   int start, int H, int Hkv, int Tp, int Sp, int Sn,
+                                                                   float inv_sqrt_hd, int8_t* __restrict__ pst,
+                                                                   float* __restrict__ spo) {
+  extern __shared__ __align__(16) float tc_rows[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long gr = (long long)blockIdx.x * kTcRowsPerCta + warp;   // (bt, t)
+  if (gr >= (long long)B * H * Tq) return;
+  const int t = (int)(gr % Tq);
+  const int bt = (int)(gr / Tq);
+  const int b = bt / H, h = bt % H, bg = b * Hkv + h / (H / Hkv);
+  float* row = tc_rows + (size_t)warp * Sp;
+  const int n = start + t + 1;                                    // keys this row sees
+  const int kcap = min(Sp, (start + (t / 128) * 128 + 128 + 127) / 128 * 128);
+  const int32_t* srow = sint + ((size_t)bt * Tp + t) * Sn;
+  const float* ksr = ksc + (size_t)bg * Sp;
+  const float* vsr = vsc + (size_t)bg * Sp;
+  const float qsr = qs[(size_t)(b * Tq + t) * H + h];
+  float mx = __int_as_float(0xff800000);
+  for (int j = lane; j < n; j += 32) {
+    const float v = __fmul_rn(__fmul_rn(__fmul_rn((float)__ldg(srow + j), qsr), __ldg(ksr + j)), inv_sqrt_hd);
+    row[j] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = warp_maxf(mx);
+  float emax = 0.f;
+  for (int j = lane; j < n; j += 32) {
+    const float e = det_exp(__fsub_rn(row[j], mx));
+    row[j] = e;
+    emax = fmaxf(emax, e);
+  }
+  emax = warp_maxf(emax);
+  const int sh = fixed_shift(emax, kMaxKeysLog2);
+  long long acc = 0;
+  if (sh <= 100) {                 // |e| 2^sh stays a normal float below 2^62: exact in fp32
+    const float up = pow2f(sh);
+    for (int j = lane; j < n; j += 32) acc += __float2ll_rn(__fmul_rn(row[j], up));
+  } else {
+    const double up = pow2d(sh);
+    for (int j = lane; j < n; j += 32) acc += fixed_term(row[j], up);
+  }
+  acc = warp_sumll(acc);
+  const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+  float pmax = 0.f;
+  for (int j = lane; j < n; j += 32) {
+    const float pv = __fmul_rn(__fdiv_rn(row[j], den), __ldg(vsr + j));
+    row[j] = pv;
+    pmax = fmaxf(pmax, pv);
+  }
+  pmax = warp_maxf(pmax);
+  const float sp = __fdiv_rn(fmaxf(pmax, 1e-30f), (float)kPLevels);
+  __syncwarp();
+  // four consecutive keys per lane and step: one word of hi limbs, one of lo limbs
+  int8_t* phi = pst + ((size_t)bt * 2 * Tp + t) * Sp;
+  int8_t* plo = phi + (size_t)Tp * Sp;
+  for (int j = 4 * lane; j < kcap; j += 128) {
+    uint32_t hw = 0, lw = 0;
+#pragma unroll
+    for (int x = 0; x < 4; x++) {
+      int pi = 0;
+      if (j + x < n) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j + x], sp)), 0.f), (float)kPLevels);
+      hw |= (uint32_t)(pi >> 7) << (8 * x);
+      lw |= (uint32_t)(pi & 127) << (8 * x);
+    }
+    *reinterpret_cast<uint32_t*>(phi + j) = hw;
+    *reinterpret_cast<uint32_t*>(plo + j) = lw;
+  }
+  if (lane == 0) spo[(size_t)bt * Tp + t] = sp;
+}
+
+// o(b * Tq + t, h, d) = fmul(float((hi << 7) + lo), sp), hi / lo the int32 P V rows t and Tp + t.
+__global__ void k_tc_combine(const int32_t* __restrict__ o32, const float* __restrict__ spi, int B, int Tq, int H,
+                             int Tp, float* __restrict__ out) {
+  const long long n = (long long)B * H * Tq * (kHd / 4);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int d4 = (int)(i % (kHd / 4));
+    const long long row = i / (kHd / 4);          // (bt, t)
+    const int t = (int)(row % Tq);
+    const long long bt = row / Tq;
+    const int h = (int)(bt % H), b = (int)(bt / H);
+    const int4 hi = reinterpret_cast<const int4*>(o32 + ((size_t)bt * 2 * Tp + t) * kHd)[d4];
+    const int4 lo = reinterpret_cast<const int4*>(o32 + ((size_t)bt * 2 * Tp + Tp + t) * kHd)[d4];
+    const float sp = spi[(size_t)bt * Tp + t];
+    float4 o;
+    o.x = __fmul_rn(__ll2float_rn(((long long)hi.x << 7) + lo.x), sp);
+    o.y = __fmul_rn(__ll2float_rn(((long long)hi.y << 7) + lo.y), sp);
+    o.z = __fmul_rn(__ll2float_rn(((long long)hi.z << 7) + lo.z), sp);
+    o.w = __fmul_rn(__ll2float_rn(((long long)hi.w << 7) + lo.w), sp);
+    reinterpret_cast<float4*>(out + ((size_t)(b * Tq + t) * H + h) * kHd)[d4] = o;
+  }
+}
+}  // namespace
+
+extern "C" uint64_t uwc_attention_tc_workspace_bytes(int B, int Tq, int start, int H, int Hkv) {
+  if (B <= 0 || Tq <= 0 || start < 0 || H <= 0 || Hkv <= 0) return 0;
+  return tc_layout(B, Tq, start, H, Hkv).total;
+}
+
+extern "C" int uwc_attention_tc(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
+                                const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq,
+                                long long kv_tok, long long kv_head, long long s_seq, long long s_tok,
+                                long long s_head, float inv_sqrt_hd, float* out, void* workspace,
+                                uint64_t workspace_bytes, void* stream) {
+  if (!qq || !qs || !kc || !ks || !vc || !vs || !out || !workspace) return UWC_ERR_ARG;
+  if (B <= 0 || Tq <= 0 || start < 0 || H <= 0 || Hkv <= 0 || H % Hkv) return UWC_ERR_SHAPE;
+  if ((long long)start + Tq > 131072) return UWC_ERR_SHAPE;   // P V limb sums stay below 2^31
+  if ((((uintptr_t)qq) | ((uintptr_t)kc) | ((uintptr_t)vc) | ((uintptr_t)out) | ((uintptr_t)workspace)) & 15)
+    return UWC_ERR_ALIGN;
+  if (kv_tok % 16 || kv_head % 16 || kv_seq % 16) return UWC_ERR_ALIGN;
+  const TcLayout L = tc_layout(B, Tq, start, H, Hkv);
+  if (workspace_bytes < L.total) return UWC_ERR_SCRATCH;
+  const size_t smem = (size_t)kTcRowsPerCta * L.Sp * 4;
+  if (smem > (size_t)kAttnSmemMax) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  int rc = smem_optin((const void*)k_tc_softmax, (int)smem);
+  if (rc != UWC_OK) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int8_t* qh = reinterpret_cast<int8_t*>(ws + L.qh);
+  int8_t* kh = reinterpret_cast<int8_t*>(ws + L.kh);
+  int8_t* vt = reinterpret_cast<int8_t*>(ws + L.vt);
+  float* ksc = reinterpret_cast<float*>(ws + L.ksc);
+  float* vsc = reinterpret_cast<float*>(ws + L.vsc);
+  int32_t* sint = reinterpret_cast<int32_t*>(ws + L.sint);
+  int8_t* pst = reinterpret_cast<int8_t*>(ws + L.pst);
+  int32_t* o32 = reinterpret_cast<int32_t*>(ws + L.o32);
+  float* spb = reinterpret_cast<float*>(ws + L.sp);
+  const int S = start + Tq, grid = uwc_num_sms() * 8;
+  k_tc_gather_q<<<grid, 256, 0, st>>>(qq, B, Tq, H, L.Tp, qh);
+  k_tc_gather_k<<<grid, 256, 0, st>>>(kc, ks, vs, B, S, Hkv, kv_seq, kv_tok, kv_head, s_seq, s_tok, s_head, L.Sp, kh,
+                                      ksc, vsc);
+  k_tc_transpose_v<<<dim3(L.Sp / 64, L.nkv), 256, 0, st>>>(vc, B, S, Hkv, kv_seq, kv_tok, kv_head, L.Sp, vt);
+  if ((rc = uwc_launch_status()) != UWC_OK) return rc;
+  const int hpg = H / Hkv;
+  rc = uwc_gemm_batched(qh, kh, L.Tp, L.Sn, kHd, L.nb, L.Tp, L.Sp, hpg, 1, start, 0, sint, stream);
+  if (rc != UWC_OK) return rc;
+  const long long rows = (long long)L.nb * Tq;
+  k_tc_softmax<<<(unsigned)((rows + kTcRowsPerCta - 1) / kTcRowsPerCta), kTcRowsPerCta * 32, smem, st>>>(
+      sint, qs, ksc, vsc, B, Tq, start, H, Hkv, L.Tp, L.Sp, L.Sn, inv_sqrt_hd, pst, spb);
+  if ((rc = uwc_launch_status()) != UWC_OK) return rc;
+  rc = uwc_gemm_batched(pst, vt, 2 * L.Tp, kHd, L.Sp, L.nb, 2LL * L.Tp, kHd, hpg, 2, start, L.Tp, o32, stream);
+  if (rc != UWC_OK) return rc;
+  k_tc_combine<<<grid, 256, 0, st>>>(o32, spb, B, Tq, H, L.Tp, out);
+  return uwc_launch_status();
+}
+
 extern "C" int uwc_attention(const int8_t* qq, const float* qs, const int8_t* kc, const float* ks, const int8_t* vc,
                              const float* vs, int B, int Tq, int start, int H, int Hkv, long long kv_seq,
                              long long kv_tok, long long kv_head, long long s_seq, long long s_tok, long long s_head,

@@ -82,6 +82,13 @@ struct Params {
   void* out;
   uint32_t* status;
   uint32_t one;      // 1, opaque to the compiler (multiply-add additions in the tile hash)
+  // Batched PLAIN launches (nbatch > 1 or causal): batch bt reads A rows bt * a_brows + [0, m) and
+  // B rows (bt / b_bdiv) * b_brows + [0, n), and writes its m x n int32 block at out + bt * m * n.
+  // causal 1 (Q K^T): block (m0, n0) runs only if some row t in [m0, m0 + 128) sees a column of it
+  // (column j visible to row t when j <= cshift + t). causal 2 (P V, A = [P_hi; P_lo] rows of qrows
+  // each): the k range stops after the last key row (m0 % qrows) + 127 sees.
+  int nbatch, b_bdiv, causal, cshift, qrows, units_per_batch;
+  long long a_brows, b_brows;
 };
 
 // R: hash chunk width in k (64, 128, 256), or 0 for no hashing.
@@ -131,10 +138,39 @@ __device__ __forceinline__ void unit_coords(const Params& p, int u, int UM, int&
   n0 = (in / gsz) * kUN;
 }
 
+// Causal Q K^T: the column blocks row block mb needs (the first n0 past cshift + mb*128 + 127 is out).
+__device__ __forceinline__ int causal_nblocks(const Params& p, int mb) {
+  return min(p.nn, (p.cshift + mb * 128 + 128 + kUN - 1) / kUN);
+}
+
 // Unit u of a split-K PLAIN launch: output block (unit_coords of u % (nm * nn)) and the k-block
-// range [kb0, kb0 + nkb) of split u / (nm * nn). Without splitting, the whole k.
+// range [kb0, kb0 + nkb) of split u / (nm * nn). Without splitting, the whole k. Batched
+// launches: batch bt = u / units_per_batch, then the block within the batch (causal: row blocks
+// in order, each with its visible column blocks).
 __device__ __forceinline__ void unit_span(const Params& p, int u, int UM, int kblocks, int& m0, int& n0, int& kb0,
-                                          int& nkb) {
+                                          int& nkb, int& bt) {
+  bt = 0;
+  if (p.units_per_batch > 0) {
+    bt = u / p.units_per_batch;
+    int r = u - bt * p.units_per_batch;
+    kb0 = 0;
+    nkb = kblocks;
+    if (p.causal == 1) {
+      int mb = 0;
+      for (; mb + 1 < p.nm; mb++) {
+        const int c = causal_nblocks(p, mb);
+        if (r < c) break;
+        r -= c;
+      }
+      m0 = mb * 128;
+      n0 = r * kUN;
+      return;
+    }
+    m0 = (r % p.nm) * 128;
+    n0 = (r / p.nm) * kUN;
+    if (p.causal == 2) nkb = min(kblocks, (p.cshift + m0 % p.qrows + 128 + kKB - 1) / kKB);
+    return;
+  }
   if (p.nsplit > 1) {
     const int nmn = p.nm * p.nn, ks = u / nmn;
     unit_coords(p, u - ks * nmn, UM, m0, n0);
@@ -375,8 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool leader = elect_one();
       uint32_t gk = 0;
       for (int u = blockIdx.x; u < p.nunits && !__any_sync(0xffffffffu, *abort_flag); u += gridDim.x) {
-        int m0, n0, kb0, nkb;
-        unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
+        int m0, n0, kb0, nkb, bt;
+        unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb, bt);
         const int ncorr = C::CORR ? L * cblocks : 0;
         const int nblk = ncorr + nkb;
         for (int b = 0; b < nblk; b++, gk++) {
@@ -393,8 +429,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sB, &tmCB, &bars->full[s], kb * kKB, li * p.n + n0);
           } else {
             const int kb = kb0 + b - ncorr;
-            tma_load_2d(sA, &tmA, &bars->full[s], kb * kKB, m0);
-            tma_load_2d(sB, &tmB, &bars->full[s], kb * kKB, n0);
+            tma_load_2d(sA, &tmA, &bars->full[s], kb * kKB, (int)(bt * p.a_brows) + m0);
+            tma_load_2d(sB, &tmB, &bars->full[s], kb * kKB, (int)((bt / p.b_bdiv) * p.b_brows) + n0);
           }
         }
       }
@@ -413,8 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t smem_base = smem_u32(smem);
       constexpr uint32_t id_acc = idesc_i8(128, C::ACC_N);
       for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
-        int m0, n0, kb0, nkb;
-        unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
+        int m0, n0, kb0, nkb, bt;
+        unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb, bt);
         // ---- correction accumulator R (FWD): Horner over limbs, highest limb first
         if (C::CORR && L > 0) {
           // MODE_CORR with up to two limbs keeps each limb's product in its own 256 columns (the
@@ -531,8 +567,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < p.nunits && ok; u += gridDim.x, local++) {
-      int m0, n0, kb0, nkb;
-      unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb);
+      int m0, n0, kb0, nkb, bt;
+      unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb, bt);
       if (MODE == MODE_PLAIN) {
         const int b = local & 1;
         ok = warp_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status);
@@ -565,7 +601,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int pass = 0; pass < 8; pass++) {
               const int rl = pass * 4 + (lane >> 3), r = m0 + 32 * q + rl;
               const uint32_t* t = tile + rl * 33 + cl;
-              if (r < p.m && c < p.n) store4(p, r, c, (int32_t)t[0], (int32_t)t[1], (int32_t)t[2], (int32_t)t[3]);
+              if (r < p.m && c < p.n)
+                store4(p, bt * p.m + r, c, (int32_t)t[0], (int32_t)t[1], (int32_t)t[2], (int32_t)t[3]);
             }
             __syncwarp();
           } else {
@@ -899,6 +936,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   p.msgbuf = static_cast<uint32_t*>(workspace);
   p.status = uwc_status_ptr();
   p.one = 1u;
+  p.b_bdiv = 1;
   p.nn = (n + kUN - 1) / kUN;
   cudaStream_t st = (cudaStream_t)stream;
 
@@ -979,4 +1017,45 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   q.nm = (m + 127) / 128;
   q.nunits = q.nm * q.nn;
   return launch<MODE_CORR, 0>(q, ta, tb, tca, tcb, st);
+}
+
+// Batched exact int8 GEMM, int32 out: out[bt] (m x n) = A[bt] B[bt / b_bdiv]^T for bt < nbatch, A[bt]
+// the m x k rows from row bt * a_brows, B[g] the n x k rows from row g * b_brows (both k-contiguous
+// row-major with row length k). causal: 0 all blocks; 1 skip 128 x 256 blocks no row sees (row t
+// sees columns j <= cshift + t); 2 stop each row block's k range after key cshift + (m0 % qrows) + 127
+// (A = [P_hi; P_lo] of qrows rows each). The attention's Q K^T (causal 1) and P V (causal 2).
+extern "C" int uwc_gemm_batched(const int8_t* A, const int8_t* B, int m, int n, int k, int nbatch, long long a_brows,
+                                long long b_brows, int b_bdiv, int causal, int cshift, int qrows, int32_t* out,
+                                void* stream) {
+  if (!A || !B || !out || nbatch <= 0 || b_bdiv <= 0 || causal < 0 || causal > 2 || cshift < 0) return UWC_ERR_ARG;
+  if (m <= 0 || n <= 0 || k <= 0 || k % 16 || n % 4 || a_brows < m || b_brows < n) return UWC_ERR_SHAPE;
+  if (causal == 2 && (qrows <= 0 || qrows % 128 || m % qrows)) return UWC_ERR_SHAPE;
+  if ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)out)) & 15) return UWC_ERR_ALIGN;
+  const long long arows = (long long)(nbatch - 1) * a_brows + m, brows = (long long)((nbatch - 1) / b_bdiv) * b_brows + n;
+  if (arows > 0x7fffffffLL || brows > 0x7fffffffLL) return UWC_ERR_SHAPE;
+  UWC_CHECK_DEVICE();
+  Params p{};
+  p.m = m; p.n = n; p.k = k; p.r = 0;
+  p.out_mode = UWC_OUT_I32; p.out = out;
+  p.status = uwc_status_ptr();
+  p.one = 1u;
+  p.nsplit = 1;
+  p.kps = (k + kKB - 1) / kKB;
+  p.nm = (m + 127) / 128;
+  p.nn = (n + kUN - 1) / kUN;
+  p.nbatch = nbatch; p.a_brows = a_brows; p.b_brows = b_brows; p.b_bdiv = b_bdiv;
+  p.causal = causal; p.cshift = cshift; p.qrows = qrows;
+  int per = p.nm * p.nn;
+  if (causal == 1) {
+    per = 0;
+    for (int mb = 0; mb < p.nm; mb++) per += std::min(p.nn, (cshift + mb * 128 + 128 + kUN - 1) / kUN);
+  }
+  p.units_per_batch = per;
+  if ((long long)per * nbatch > 0x7fffffffLL) return UWC_ERR_SHAPE;
+  p.nunits = per * nbatch;
+  CUtensorMap ta, tb;
+  int rc = uwc_make_tmap_2d(&ta, A, (uint64_t)arows, (uint64_t)k, (uint64_t)k, 128, kKB);
+  if (rc == UWC_OK) rc = uwc_make_tmap_2d(&tb, B, (uint64_t)brows, (uint64_t)k, (uint64_t)k, kUN, kKB);
+  if (rc != UWC_OK) return rc;
+  return launch<MODE_PLAIN, 0>(p, ta, tb, ta, tb, (cudaStream_t)stream);
 }

@@ -45,6 +45,10 @@ SIGNATURES = {
                             _P]),
     "uwc_attention": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _I64,
                              _F32, _P, _P]),
+    "uwc_attention_tc_workspace_bytes": (_U64, [_I32, _I32, _I32, _I32, _I32]),
+    "uwc_attention_tc": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64,
+                                _I64, _F32, _P, _P, _U64, _P]),
+    "uwc_gemm_batched": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I64, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "uwc_attention_at": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64,
                                 _I64, _I64, _F32, _P, _P]),
     "uwc_kv_append": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),

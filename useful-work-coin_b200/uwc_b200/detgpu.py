@@ -165,16 +165,40 @@ def mlp_residual(gu, down, w_norm: torch.Tensor, r1: torch.Tensor, eps: float) -
     return dequant_residual(det.int_gemm(q4, down.Wq), s4, down.sw, r1)
 
 
-def _attn(qq, qs, kc, ks, vc, vs, B, Tq, start, H, Hkv, strides, inv_sqrt_hd) -> torch.Tensor:
+TC_MIN_ROWS = 128        # query rows per sequence from which attention runs its GEMMs on tcgen05
+_TC_WS: dict = {}         # device -> workspace of the tensor-core attention (grown on demand)
+
+
+def _tc_workspace(device, nbytes: int) -> torch.Tensor:
+    ws = _TC_WS.get(str(device))
+    if ws is None or ws.numel() < nbytes:
+        _TC_WS[str(device)] = ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws
+
+
+def _attn(qq, qs, kc, ks, vc, vs, B, Tq, start, H, Hkv, strides, inv_sqrt_hd, path: str = "auto") -> torch.Tensor:
+    """path: "simt" (one CTA per block of query rows, dp4a dots), "tc" (Q K^T and P V as batched
+    tcgen05 GEMMs), or "auto" (tc from TC_MIN_ROWS query rows per sequence). Same bits either way."""
     assert qq.dtype == torch.int8 and qq.shape[-1] == 128 and qq.is_contiguous(), (qq.dtype, qq.shape)
     out = torch.empty((B * Tq, H * 128), dtype=torch.float32, device=qq.device)
+    S = start + Tq
+    tc = path == "tc" or (path == "auto" and Tq >= TC_MIN_ROWS and S <= 12800)
+    if tc:
+        need = int(lib().uwc_attention_tc_workspace_bytes(B, Tq, start, H, Hkv))
+        ws = _tc_workspace(qq.device, need)
+        check(lib().uwc_attention_tc(_p(qq), _p(_f32(qs)), _p(kc), _p(ks), _p(vc), _p(vs), B, Tq, start, H, Hkv,
+                                     *strides, float(inv_sqrt_hd), _p(out), _p(ws), ws.numel(), _stream()),
+              "attention_tc")
+        _count(7)
+        return out
     check(lib().uwc_attention(_p(qq), _p(_f32(qs)), _p(kc), _p(ks), _p(vc), _p(vs), B, Tq, start, H, Hkv, *strides,
                               float(inv_sqrt_hd), _p(out), _stream()), "attention")
     _count()
     return out
 
 
-def attention(qq, qs, kq, ks, vq, vs, B: int, T: int, H: int, Hkv: int, inv_sqrt_hd_f32: float) -> torch.Tensor:
+def attention(qq, qs, kq, ks, vq, vs, B: int, T: int, H: int, Hkv: int, inv_sqrt_hd_f32: float,
+              path: str = "auto") -> torch.Tensor:
     """runtime/detgpu/kernels.py attention: detrt's attention of B sequences of T tokens from
     quantized q, k, v -- qq (N, H, 128), kq and vq (N, Hkv, 128) int8, qs (N, H, 1), ks and vs
     (N, Hkv, 1) float32, N = B * T. Returns o as (N, H * 128) float32."""
@@ -182,11 +206,11 @@ def attention(qq, qs, kq, ks, vq, vs, B: int, T: int, H: int, Hkv: int, inv_sqrt
     kq, vq = i8(kq), i8(vq)
     ks, vs = _f32(ks), _f32(vs)
     strides = (T * Hkv * 128, Hkv * 128, 128, T * Hkv, Hkv, 1)
-    return _attn(i8(qq), qs, kq, ks, vq, vs, B, T, 0, H, Hkv, strides, inv_sqrt_hd_f32)
+    return _attn(i8(qq), qs, kq, ks, vq, vs, B, T, 0, H, Hkv, strides, inv_sqrt_hd_f32, path)
 
 
 def attention_cache(qq, qs, cache: dict, B: int, Tq: int, start: int, H: int, Hkv: int,
-                    inv_sqrt_hd_f32: float) -> torch.Tensor:
+                    inv_sqrt_hd_f32: float, path: str = "auto") -> torch.Tensor:
     """Attention of Tq new tokens per sequence (positions start .. start + Tq - 1) over a KV cache
     laid out as runtime/detrt/qwen3.py new_cache: k, v (B, Hkv, maxlen, 128) int8, sk, sv
     (B, Hkv, maxlen, 1) float32, already holding keys 0 .. start + Tq - 1 (qwen3.py:254-283)."""
@@ -195,7 +219,7 @@ def attention_cache(qq, qs, cache: dict, B: int, Tq: int, start: int, H: int, Hk
     maxlen = k.shape[2]
     assert start + Tq <= maxlen
     strides = (Hkv * maxlen * 128, 128, maxlen * 128, Hkv * maxlen, 1, maxlen)
-    return _attn(qq.contiguous(), qs, k, sk, v, sv, B, Tq, start, H, Hkv, strides, inv_sqrt_hd_f32)
+    return _attn(qq.contiguous(), qs, k, sk, v, sv, B, Tq, start, H, Hkv, strides, inv_sqrt_hd_f32, path)
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
