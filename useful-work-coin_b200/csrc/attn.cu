@@ -826,6 +826,9 @@ __global__ void __launch_bounds__(256) k_tc_transpose_v(const int8_t* __restrict
 // One warp per query row (batch bt, row t): the scale chain and softmax of k_attention on the
 // int32 dots of S, the 14-bit P written as hi limbs (row t of the batch's P block) and lo limbs (row
 // Tp + t), zero from key start + t + 1 up to the end of the P V GEMM's k range for t's row block.
+// Each lane takes four consecutive keys per step (16-byte loads of S and the key scales). The
+// exponentials and the exact sum share one pass at the shift of det_exp(0) = 1 (the row maximum's
+// own term); a row whose max of e has another exponent sums again at its true shift.
 __global__ void __launch_bounds__(kTcRowsPerCta * 32) k_tc_softmax(const int32_t* __restrict__ sint,
                                                                    const float* __restrict__ qs,
                                                                    const float* __restrict__ ksc,
@@ -842,41 +845,67 @@ __global__ void __launch_bounds__(kTcRowsPerCta * 32) k_tc_softmax(const int32_t
   const int b = bt / H, h = bt % H, bg = b * Hkv + h / (H / Hkv);
   float* row = tc_rows + (size_t)warp * Sp;
   const int n = start + t + 1;                                    // keys this row sees
+  const int n4 = (n + 3) & ~3;                                    // <= Sn <= Sp
   const int kcap = min(Sp, (start + (t / 128) * 128 + 128 + 127) / 128 * 128);
   const int32_t* srow = sint + ((size_t)bt * Tp + t) * Sn;
   const float* ksr = ksc + (size_t)bg * Sp;
   const float* vsr = vsc + (size_t)bg * Sp;
   const float qsr = qs[(size_t)(b * Tq + t) * H + h];
   float mx = __int_as_float(0xff800000);
-  for (int j = lane; j < n; j += 32) {
-    const float v = __fmul_rn(__fmul_rn(__fmul_rn((float)__ldg(srow + j), qsr), __ldg(ksr + j)), inv_sqrt_hd);
-    row[j] = v;
-    mx = fmaxf(mx, v);
+  for (int j = 4 * lane; j < n4; j += 128) {
+    const int4 d = __ldg(reinterpret_cast<const int4*>(srow + j));
+    const float4 kk = __ldg(reinterpret_cast<const float4*>(ksr + j));
+    float4 v;
+    v.x = __fmul_rn(__fmul_rn(__fmul_rn((float)d.x, qsr), kk.x), inv_sqrt_hd);
+    v.y = __fmul_rn(__fmul_rn(__fmul_rn((float)d.y, qsr), kk.y), inv_sqrt_hd);
+    v.z = __fmul_rn(__fmul_rn(__fmul_rn((float)d.z, qsr), kk.z), inv_sqrt_hd);
+    v.w = __fmul_rn(__fmul_rn(__fmul_rn((float)d.w, qsr), kk.w), inv_sqrt_hd);
+    *reinterpret_cast<float4*>(row + j) = v;
+    mx = fmaxf(mx, v.x);
+    if (j + 1 < n) mx = fmaxf(mx, v.y);
+    if (j + 2 < n) mx = fmaxf(mx, v.z);
+    if (j + 3 < n) mx = fmaxf(mx, v.w);
   }
   mx = warp_maxf(mx);
+  const int sh_guess = fixed_shift(1.0f, kMaxKeysLog2);
+  const float up_guess = pow2f(sh_guess);
   float emax = 0.f;
-  for (int j = lane; j < n; j += 32) {
-    const float e = det_exp(__fsub_rn(row[j], mx));
-    row[j] = e;
-    emax = fmaxf(emax, e);
+  long long acc = 0;
+  for (int j = 4 * lane; j < n4; j += 128) {
+    float4 e = *reinterpret_cast<const float4*>(row + j);
+    e.x = det_exp(__fsub_rn(e.x, mx));
+    e.y = j + 1 < n ? det_exp(__fsub_rn(e.y, mx)) : 0.f;
+    e.z = j + 2 < n ? det_exp(__fsub_rn(e.z, mx)) : 0.f;
+    e.w = j + 3 < n ? det_exp(__fsub_rn(e.w, mx)) : 0.f;
+    *reinterpret_cast<float4*>(row + j) = e;
+    emax = fmaxf(fmaxf(emax, fmaxf(e.x, e.y)), fmaxf(e.z, e.w));
+    acc += __float2ll_rn(__fmul_rn(e.x, up_guess)) + __float2ll_rn(__fmul_rn(e.y, up_guess)) +
+           __float2ll_rn(__fmul_rn(e.z, up_guess)) + __float2ll_rn(__fmul_rn(e.w, up_guess));
   }
   emax = warp_maxf(emax);
   const int sh = fixed_shift(emax, kMaxKeysLog2);
-  long long acc = 0;
-  if (sh <= 100) {                 // |e| 2^sh stays a normal float below 2^62: exact in fp32
-    const float up = pow2f(sh);
-    for (int j = lane; j < n; j += 32) acc += __float2ll_rn(__fmul_rn(row[j], up));
-  } else {
-    const double up = pow2d(sh);
-    for (int j = lane; j < n; j += 32) acc += fixed_term(row[j], up);
+  if (sh != sh_guess) {            // warp-uniform: the sum again at the true shift
+    acc = 0;
+    if (sh <= 100) {               // |e| 2^sh stays a normal float below 2^62: exact in fp32
+      const float up = pow2f(sh);
+      for (int j = lane; j < n; j += 32) acc += __float2ll_rn(__fmul_rn(row[j], up));
+    } else {
+      const double up = pow2d(sh);
+      for (int j = lane; j < n; j += 32) acc += fixed_term(row[j], up);
+    }
   }
   acc = warp_sumll(acc);
   const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
   float pmax = 0.f;
-  for (int j = lane; j < n; j += 32) {
-    const float pv = __fmul_rn(__fdiv_rn(row[j], den), __ldg(vsr + j));
-    row[j] = pv;
-    pmax = fmaxf(pmax, pv);
+  for (int j = 4 * lane; j < n4; j += 128) {
+    float4 e = *reinterpret_cast<const float4*>(row + j);
+    const float4 sv = __ldg(reinterpret_cast<const float4*>(vsr + j));
+    e.x = __fmul_rn(__fdiv_rn(e.x, den), sv.x);
+    e.y = j + 1 < n ? __fmul_rn(__fdiv_rn(e.y, den), sv.y) : 0.f;
+    e.z = j + 2 < n ? __fmul_rn(__fdiv_rn(e.z, den), sv.z) : 0.f;
+    e.w = j + 3 < n ? __fmul_rn(__fdiv_rn(e.w, den), sv.w) : 0.f;
+    *reinterpret_cast<float4*>(row + j) = e;
+    pmax = fmaxf(fmaxf(pmax, fmaxf(e.x, e.y)), fmaxf(e.z, e.w));
   }
   pmax = warp_maxf(pmax);
   const float sp = __fdiv_rn(fmaxf(pmax, 1e-30f), (float)kPLevels);
@@ -886,12 +915,16 @@ __global__ void __launch_bounds__(kTcRowsPerCta * 32) k_tc_softmax(const int32_t
   int8_t* plo = phi + (size_t)Tp * Sp;
   for (int j = 4 * lane; j < kcap; j += 128) {
     uint32_t hw = 0, lw = 0;
+    if (j < n) {
+      const float4 pv = *reinterpret_cast<const float4*>(row + j);
+      const float pvs[4] = {pv.x, pv.y, pv.z, pv.w};
 #pragma unroll
-    for (int x = 0; x < 4; x++) {
-      int pi = 0;
-      if (j + x < n) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j + x], sp)), 0.f), (float)kPLevels);
-      hw |= (uint32_t)(pi >> 7) << (8 * x);
-      lw |= (uint32_t)(pi & 127) << (8 * x);
+      for (int x = 0; x < 4; x++) {
+        int pi = 0;
+        if (j + x < n) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(pvs[x], sp)), 0.f), (float)kPLevels);
+        hw |= (uint32_t)(pi >> 7) << (8 * x);
+        lw |= (uint32_t)(pi & 127) << (8 * x);
+      }
     }
     *reinterpret_cast<uint32_t*>(phi + j) = hw;
     *reinterpret_cast<uint32_t*>(plo + j) = lw;
