@@ -32,10 +32,74 @@ namespace {
 constexpr int kRowThreads = 256;      // threads per row CTA (1024 for few-row calls)
 constexpr int kMaxRowSmem = 200 * 1024;   // k <= 51200 floats per row
 
+// One bs = 32 E block per warp, E consecutive elements per lane in registers: stages h < E pair
+// elements of a lane, stages h >= E pair lane l with lane l ^ (h / E) (the lower lane keeps a + b,
+// the upper a - b, a the lower element): the same pairs, operands and roundings as the staged
+// transform below.
+template <int E>
+__device__ __forceinline__ void fwht_block_lane(float* blk) {
+  const int lane = threadIdx.x & 31;
+  float v[E];
+  float* p = blk + E * lane;
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < E / 4; i++) {
+      const float4 x = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; i++) v[i] = p[i];
+  }
+#pragma unroll
+  for (int h = 1; h < E; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < E; i++) {
+      if (i & h) continue;
+      const float a = v[i], b = v[i + h];
+      v[i] = __fadd_rn(a, b);
+      v[i + h] = __fsub_rn(a, b);
+    }
+  }
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const bool upper = lane & d;
+#pragma unroll
+    for (int i = 0; i < E; i++) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+      v[i] = upper ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
+    }
+  }
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < E / 4; i++)
+      reinterpret_cast<float4*>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; i++) p[i] = v[i];
+  }
+}
+
+template <int NT, int E>
+__device__ void fwht_row_warp(float* row, int k) {
+  const int nblk = k / (32 * E);
+  for (int blk = threadIdx.x >> 5; blk < nblk; blk += NT / 32) fwht_block_lane<E>(row + (size_t)blk * 32 * E);
+  __syncthreads();
+}
+
 // In-place unnormalized block Walsh-Hadamard transform of a shared-memory row (core.py:171-185):
-// stages h = 1, 2, 4, ... < bs, pairs (i, i + h) of each 2h-block -> (a + b, a - b).
+// stages h = 1, 2, 4, ... < bs, pairs (i, i + h) of each 2h-block -> (a + b, a - b). Blocks of 32
+// to 512 elements run one per warp in registers (fwht_block_lane), others staged in shared memory.
 template <int NT>
 __device__ void fwht_row(float* row, int k, int bs) {
+  switch (bs) {
+    case 512: fwht_row_warp<NT, 16>(row, k); return;
+    case 256: fwht_row_warp<NT, 8>(row, k); return;
+    case 128: fwht_row_warp<NT, 4>(row, k); return;
+    case 64: fwht_row_warp<NT, 2>(row, k); return;
+    case 32: fwht_row_warp<NT, 1>(row, k); return;
+    default: break;
+  }
   for (int lh = 0; (1 << lh) < bs; lh++) {
     const int h = 1 << lh;
     for (int p = threadIdx.x; p < (k >> 1); p += NT) {
