@@ -129,10 +129,14 @@ __device__ void quant_row64(const float* row, int k, int bs, float amax, int8_t*
   if (threadIdx.x == 0) *scale_out = bs > 1 ? __fmul_rn(s, __fdiv_rn(1.0f, __fsqrt_rn((float)bs))) : s;
 }
 
+// k % 4 == 0 (every caller checks): four elements per thread and step
 template <int NT>
 __device__ float row_absmax(const float* row, int k, float* red) {
   float mx = 0.f;
-  for (int i = threadIdx.x; i < k; i += NT) mx = fmaxf(mx, fabsf(row[i]));
+  for (int i = 4 * threadIdx.x; i < k; i += 4 * NT) {
+    const float4 v = *reinterpret_cast<const float4*>(row + i);
+    mx = fmaxf(fmaxf(mx, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+  }
   return block_maxf<NT>(mx, red);
 }
 
@@ -188,19 +192,36 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ 
   __shared__ long long redl[NT / 32];
   const int r = blockIdx.x;
   load_row<NT, false>(x, r, k, row);
+  // four elements per thread and step (k % 4 == 0)
   float mx = 0.f;
-  for (int i = threadIdx.x; i < k; i += NT) mx = fmaxf(mx, __fmul_rn(row[i], row[i]));
+  for (int i = 4 * threadIdx.x; i < k; i += 4 * NT) {
+    const float4 v = *reinterpret_cast<const float4*>(row + i);
+    mx = fmaxf(fmaxf(mx, fmaxf(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y))),
+               fmaxf(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
+  }
   mx = block_maxf<NT>(mx, red);
   int e;
   frexpf(mx, &e);
   const int sh = min(max((62 - L) - e, -1000), 1000);
   const double up = pow2d(sh);
   long long acc = 0;
-  for (int i = threadIdx.x; i < k; i += NT) acc += __double2ll_rn((double)__fmul_rn(row[i], row[i]) * up);
+  for (int i = 4 * threadIdx.x; i < k; i += 4 * NT) {
+    const float4 v = *reinterpret_cast<const float4*>(row + i);
+    acc += __double2ll_rn((double)__fmul_rn(v.x, v.x) * up) + __double2ll_rn((double)__fmul_rn(v.y, v.y) * up) +
+           __double2ll_rn((double)__fmul_rn(v.z, v.z) * up) + __double2ll_rn((double)__fmul_rn(v.w, v.w) * up);
+  }
   acc = block_sumll<NT>(acc, redl);
   const float ss = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
   const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_d), eps)));
-  for (int i = threadIdx.x; i < k; i += NT) row[i] = __fmul_rn(__fmul_rn(row[i], rr), w[i]);
+  for (int i = 4 * threadIdx.x; i < k; i += 4 * NT) {
+    float4 v = *reinterpret_cast<const float4*>(row + i);
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(w + i));
+    v.x = __fmul_rn(__fmul_rn(v.x, rr), wv.x);
+    v.y = __fmul_rn(__fmul_rn(v.y, rr), wv.y);
+    v.z = __fmul_rn(__fmul_rn(v.z, rr), wv.z);
+    v.w = __fmul_rn(__fmul_rn(v.w, rr), wv.w);
+    *reinterpret_cast<float4*>(row + i) = v;
+  }
   __syncthreads();
   if (bs > 1) fwht_row<NT>(row, k, bs);
   const float am = row_absmax<NT>(row, k, red);
@@ -224,7 +245,20 @@ __global__ void __launch_bounds__(NT) k_swiglu_quant(const int32_t* __restrict__
   const int r = blockIdx.x;
   const float s = s3[r];
   const int32_t* ar = acc + (uint64_t)r * 2 * I;
-  for (int i = threadIdx.x; i < I; i += NT) row[i] = swiglu_at(ar, s, sw, I, i);
+  // four elements per thread and step (I % 4 == 0): 16-byte loads of the gate and up halves
+  for (int i = 4 * threadIdx.x; i < I; i += 4 * NT) {
+    const int4 g4 = __ldg(reinterpret_cast<const int4*>(ar + i)), u4 = __ldg(reinterpret_cast<const int4*>(ar + I + i));
+    const float4 sg = __ldg(reinterpret_cast<const float4*>(sw + i)), su = __ldg(reinterpret_cast<const float4*>(sw + I + i));
+    const int gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+    const float sgv[4] = {sg.x, sg.y, sg.z, sg.w}, suv[4] = {su.x, su.y, su.z, su.w};
+    float o[4];
+#pragma unroll
+    for (int x = 0; x < 4; x++) {
+      const float g = deq(gv[x], s, sgv[x]), u = deq(uv[x], s, suv[x]);
+      o[x] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, det_exp(-g))), u);
+    }
+    *reinterpret_cast<float4*>(row + i) = make_float4(o[0], o[1], o[2], o[3]);
+  }
   __syncthreads();
   if (bs > 1) fwht_row<NT>(row, I, bs);
   const float am = row_absmax<NT>(row, I, red);
@@ -404,7 +438,7 @@ extern "C" int uwc_quant_act_global(const float* x, int m, int k, int bs, const 
 extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, int bs, double eps, int8_t* q,
                                  float* scale, void* stream) {
   if (!x || !w || !q || !scale || m < 0 || k <= 0 || k % 4 || !bs_ok(k, bs)) return UWC_ERR_ARG;
-  if (!aligned16(x) || ((uintptr_t)q & 3)) return UWC_ERR_ALIGN;
+  if (!aligned16(x) || !aligned16(w) || ((uintptr_t)q & 3)) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
@@ -425,7 +459,7 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
 extern "C" int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float* sw, int m, int I, int bs, int8_t* q,
                                 float* scale, void* stream) {
   if (!acc || !s3 || !sw || !q || !scale || m < 0 || I <= 0 || I % 4 || !bs_ok(I, bs)) return UWC_ERR_ARG;
-  if ((uintptr_t)q & 3) return UWC_ERR_ALIGN;
+  if (((uintptr_t)q & 3) || !aligned16(acc) || !aligned16(sw)) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
   if (few_rows(m)) {
