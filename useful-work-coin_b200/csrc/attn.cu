@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
   if (live)
     for (int j = j0; j < Sp; j += js) {
       int pi = 0;
-      if (j < S) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels);
+      if (j < S) pi = int_of_small(fminf(fmaxf(rint_small(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels));
       reinterpret_cast<int*>(row)[j] = pi;
     }
   if (lane == 0 && part == 0) s_sp[r] = sp;
@@ -469,7 +469,7 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThrea
   const int nk4 = (nk + 3) & ~3;
   for (int j = j0; j < nk4; j += js) {
     int pi = 0;
-    if (j < nk) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels);
+    if (j < nk) pi = int_of_small(fminf(fmaxf(rint_small(__fdiv_rn(row[j], sp)), 0.f), (float)kPLevels));
     reinterpret_cast<int*>(row)[j] = pi;
   }
   if (lane == 0 && part == 0) ds.sp[r] = sp;
@@ -856,10 +856,11 @@ __global__ void __launch_bounds__(kTcRowsPerCta * 32) k_tc_softmax(const int32_t
     const int4 d = __ldg(reinterpret_cast<const int4*>(srow + j));
     const float4 kk = __ldg(reinterpret_cast<const float4*>(ksr + j));
     float4 v;
-    v.x = __fmul_rn(__fmul_rn(__fmul_rn((float)d.x, qsr), kk.x), inv_sqrt_hd);
-    v.y = __fmul_rn(__fmul_rn(__fmul_rn((float)d.y, qsr), kk.y), inv_sqrt_hd);
-    v.z = __fmul_rn(__fmul_rn(__fmul_rn((float)d.z, qsr), kk.z), inv_sqrt_hd);
-    v.w = __fmul_rn(__fmul_rn(__fmul_rn((float)d.w, qsr), kk.w), inv_sqrt_hd);
+    // float(dot) exactly: |dot| <= 127 * 127 * 128 < 2^22
+    v.x = __fmul_rn(__fmul_rn(__fmul_rn(float_of_small(d.x), qsr), kk.x), inv_sqrt_hd);
+    v.y = __fmul_rn(__fmul_rn(__fmul_rn(float_of_small(d.y), qsr), kk.y), inv_sqrt_hd);
+    v.z = __fmul_rn(__fmul_rn(__fmul_rn(float_of_small(d.z), qsr), kk.z), inv_sqrt_hd);
+    v.w = __fmul_rn(__fmul_rn(__fmul_rn(float_of_small(d.w), qsr), kk.w), inv_sqrt_hd);
     *reinterpret_cast<float4*>(row + j) = v;
     mx = fmaxf(mx, v.x);
     if (j + 1 < n) mx = fmaxf(mx, v.y);
@@ -921,7 +922,8 @@ __global__ void __launch_bounds__(kTcRowsPerCta * 32) k_tc_softmax(const int32_t
 #pragma unroll
       for (int x = 0; x < 4; x++) {
         int pi = 0;
-        if (j + x < n) pi = (int)fminf(fmaxf(rintf(__fdiv_rn(pvs[x], sp)), 0.f), (float)kPLevels);
+        // pv / sp <= 16383 (1 + 2^-22): rint_small and int_of_small are exact here
+        if (j + x < n) pi = int_of_small(fminf(fmaxf(rint_small(__fdiv_rn(pvs[x], sp)), 0.f), (float)kPLevels));
         hw |= (uint32_t)(pi >> 7) << (8 * x);
         lw |= (uint32_t)(pi & 127) << (8 * x);
       }

@@ -17,17 +17,31 @@ constexpr float kTiny = (float)1e-8;
 __device__ __forceinline__ float pow2f(int n) { return __int_as_float((n + 127) << 23); }
 __device__ __forceinline__ double pow2d(int n) { return __longlong_as_double((long long)(n + 1023) << 52); }
 
+// Integer rounding on the FMA / ALU pipes instead of the conversion unit. Adding 1.5 * 2^23 puts
+// an |x| < 2^22 into the binade whose ulp is 1, so the addition itself rounds x to an integer in
+// the chosen direction (exactly), and that integer is the low mantissa bits of the sum.
+constexpr float kRoundMagic = 12582912.0f;    // 1.5 * 2^23
+constexpr int kRoundMagicBits = 0x4B400000;   // its bit pattern
+__device__ __forceinline__ float floor_small(float x) { return __fsub_rn(__fadd_rd(x, kRoundMagic), kRoundMagic); }
+__device__ __forceinline__ int floor_small_int(float x) { return __float_as_int(__fadd_rd(x, kRoundMagic)) - kRoundMagicBits; }
+__device__ __forceinline__ float rint_small(float x) { return __fsub_rn(__fadd_rn(x, kRoundMagic), kRoundMagic); }
+// an integer-valued |x| < 2^22 as int
+__device__ __forceinline__ int int_of_small(float x) { return __float_as_int(__fadd_rn(x, kRoundMagic)) - kRoundMagicBits; }
+// float(d) for |d| < 2^22 (exact: no rounding happens)
+__device__ __forceinline__ float float_of_small(int d) { return __fsub_rn(__int_as_float(kRoundMagicBits + d), kRoundMagic); }
+
 // detrt.core.det_exp (core.py:111-127): 2^(z log2 e) as 2^n * poly(f), one rounding per op.
+// After the range clamp |t| < 128, so floor(t) comes from floor_small.
 __device__ __forceinline__ float det_exp(float z) {
   float t = __fmul_rn(z, kLog2e);
   const bool under = t < -126.0f, over = t >= 128.0f;
   if (under || over || isnan(t)) t = 0.0f;
-  const float n = floorf(t);
+  const float n = floor_small(t);
   const float f = __fsub_rn(t, n);
   float p = kExp2[7];
 #pragma unroll
   for (int i = 6; i >= 0; i--) p = __fadd_rn(__fmul_rn(p, f), kExp2[i]);
-  float r = __fmul_rn(p, pow2f((int)n));
+  float r = __fmul_rn(p, pow2f(floor_small_int(t)));
   if (under) r = 0.0f;
   if (over) r = __int_as_float(0x7f800000);
   if (isnan(z)) r = z;

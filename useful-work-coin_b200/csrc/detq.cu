@@ -121,8 +121,9 @@ __device__ void quant_row64(const float* row, int k, int bs, float amax, int8_t*
     uint32_t o = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const float v = fminf(fmaxf(rintf(__fdiv_rn(row[i + j], s)), -64.f), 64.f);
-      o |= ((uint32_t)(uint8_t)(int8_t)(int)v) << (8 * j);
+      // |row / s| <= 64 (1 + 2^-22): rint_small and int_of_small are exact here
+      const float v = fminf(fmaxf(rint_small(__fdiv_rn(row[i + j], s)), -64.f), 64.f);
+      o |= ((uint32_t)(uint8_t)(int8_t)int_of_small(v)) << (8 * j);
     }
     *reinterpret_cast<uint32_t*>(q + i) = o;
   }
