@@ -110,3 +110,45 @@ def test_glue_helpers():
     # penalized bound picks the smaller of the two (pearl_glue.py:55-62)
     t = glue.nbits_to_target(0x1E00FFFF)
     assert glue.jackpot_bound(0x1E00FFFF, 2048, 128, 4) == min(t * 128 * 2048, t * 128 * 16 * 4)
+
+
+def test_attention_and_batched_gemm_validation_needs_no_device():
+    from uwc_b200 import _lib
+    L = _lib.lib()
+    f = ctypes.c_void_p(0x1000)
+    gb = lambda *a: L.uwc_gemm_batched(f, f, *a, f, None)
+    assert gb(128, 258, 128, 2, 128, 258, 1, 0, 0, 0) == _lib.ERR_SHAPE      # n % 4
+    assert gb(128, 256, 120, 2, 128, 256, 1, 0, 0, 0) == _lib.ERR_SHAPE      # k % 16
+    assert gb(128, 256, 128, 2, 100, 256, 1, 0, 0, 0) == _lib.ERR_SHAPE      # a_brows < m
+    assert gb(256, 128, 256, 2, 256, 128, 1, 2, 0, 100) == _lib.ERR_SHAPE    # qrows % 128
+    assert gb(128, 256, 128, 2, 128, 256, 0, 0, 0, 0) == _lib.ERR_ARG        # b_bdiv
+    assert gb(128, 256, 128, 2, 128, 256, 1, 3, 0, 0) == _lib.ERR_ARG        # causal mode
+    at = lambda B, Tq, start, H, Hkv, ws: L.uwc_attention_tc(f, f, f, f, f, f, B, Tq, start, H, Hkv, 1 << 20, 128, 1 << 16,
+                                                             1 << 13, 1, 1 << 9, 0.088, f, f, ws, None)
+    assert at(2, 256, 0, 6, 4, 1 << 40) == _lib.ERR_SHAPE                   # H % Hkv
+    assert at(1, 1024, 131000, 2, 2, 1 << 40) == _lib.ERR_SHAPE             # start + Tq > 2^17
+    need = L.uwc_attention_tc_workspace_bytes(2, 256, 0, 4, 2)
+    assert need > 0 and at(2, 256, 0, 4, 2, need - 1) == _lib.ERR_SCRATCH
+
+
+def test_attention_tc_workspace_and_path_selection():
+    """The tensor-core attention's workspace (query / key / transposed value gathers, key and
+    value scales, int32 scores, P limbs, int32 P V rows, P scales, each 256-byte aligned) and the
+    automatic choice between it and the SIMT kernel."""
+    from uwc_b200 import detgpu
+    from uwc_b200._lib import lib
+    up = lambda x, a: (x + a - 1) // a * a
+    for B, Tq, start, H, Hkv in ((8, 2048, 0, 16, 8), (2, 300, 40, 4, 2), (1, 129, 1000, 8, 1)):
+        nb, nkv, Tp, S = B * H, B * Hkv, up(Tq, 128), start + Tq
+        Sp, Sn = up(S, 128), up(S, 4)
+        parts = [nb * Tp * 128, nkv * Sp * 128, nkv * 128 * Sp, nkv * Sp * 4, nkv * Sp * 4, nb * Tp * Sn * 4,
+                 nb * 2 * Tp * Sp, nb * 2 * Tp * 128 * 4, nb * Tp * 4]
+        assert lib().uwc_attention_tc_workspace_bytes(B, Tq, start, H, Hkv) == sum(up(p, 256) for p in parts)
+    assert detgpu.use_tensor_cores(8, 2048, 0, 16, 8)                       # the C4 prefill
+    assert not detgpu.use_tensor_cores(8, 127, 0, 16, 8)                    # short prefills
+    assert not detgpu.use_tensor_cores(8, 1, 2100, 16, 8)                   # decode
+    assert not detgpu.use_tensor_cores(1, 13000, 0, 16, 8)                  # scores beyond shared memory
+    assert not detgpu.use_tensor_cores(64, 8192, 0, 32, 8)                  # workspace above the cap
+    assert detgpu.use_tensor_cores(1, 1, 0, 2, 2, "tc") and not detgpu.use_tensor_cores(8, 2048, 0, 16, 8, "simt")
+    with pytest.raises(ValueError):
+        detgpu.use_tensor_cores(1, 1, 0, 2, 2, "fast")

@@ -166,7 +166,22 @@ def mlp_residual(gu, down, w_norm: torch.Tensor, r1: torch.Tensor, eps: float) -
 
 
 TC_MIN_ROWS = 128        # query rows per sequence from which attention runs its GEMMs on tcgen05
+TC_MAX_KEYS = 12800      # the tensor-core softmax keeps 4 query rows' scores in shared memory
+TC_MAX_WORKSPACE = 24 << 30   # larger calls (long prompts times many heads) run the SIMT kernel
 _TC_WS: dict = {}         # device -> workspace of the tensor-core attention (grown on demand)
+
+
+def use_tensor_cores(B: int, Tq: int, start: int, H: int, Hkv: int, path: str = "auto") -> bool:
+    """Whether attention of Tq query rows per sequence runs on the tensor-core path: forced by
+    path "tc" / "simt", else from TC_MIN_ROWS rows while the keys fit the softmax pass's shared
+    memory and the workspace (int32 scores, P limbs) stays within TC_MAX_WORKSPACE bytes."""
+    if path in ("tc", "simt"):
+        return path == "tc"
+    if path != "auto":
+        raise ValueError(f"attention path {path!r}")
+    if Tq < TC_MIN_ROWS or start + Tq > TC_MAX_KEYS:
+        return False
+    return int(lib().uwc_attention_tc_workspace_bytes(B, Tq, start, H, Hkv)) <= TC_MAX_WORKSPACE
 
 
 def _tc_workspace(device, nbytes: int) -> torch.Tensor:
@@ -181,9 +196,7 @@ def _attn(qq, qs, kc, ks, vc, vs, B, Tq, start, H, Hkv, strides, inv_sqrt_hd, pa
     tcgen05 GEMMs), or "auto" (tc from TC_MIN_ROWS query rows per sequence). Same bits either way."""
     assert qq.dtype == torch.int8 and qq.shape[-1] == 128 and qq.is_contiguous(), (qq.dtype, qq.shape)
     out = torch.empty((B * Tq, H * 128), dtype=torch.float32, device=qq.device)
-    S = start + Tq
-    tc = path == "tc" or (path == "auto" and Tq >= TC_MIN_ROWS and S <= 12800)
-    if tc:
+    if use_tensor_cores(B, Tq, start, H, Hkv, path):
         need = int(lib().uwc_attention_tc_workspace_bytes(B, Tq, start, H, Hkv))
         ws = _tc_workspace(qq.device, need)
         check(lib().uwc_attention_tc(_p(qq), _p(_f32(qs)), _p(kc), _p(ks), _p(vc), _p(vs), B, Tq, start, H, Hkv,
