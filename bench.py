@@ -666,11 +666,13 @@ def run_b200(a, world, rank, local):
 
 def main():
     a = parse()
+    if a.impl == "reference":
+        # host cores only: no device and no process group; rank 0 runs and prints, the others exit
+        run_reference(a, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
     world, rank, local = dist_setup(a.gpus)
     try:
-        if a.impl == "reference":
-            run_reference(a, world, rank)
-        elif a.workload.startswith("c5"):
+        if a.workload.startswith("c5"):
             run_c5(a, world, rank, local)
         elif a.workload.startswith("c4"):
             run_c4(a, world, rank, local)
