@@ -30,7 +30,7 @@ def sha(x) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("UWC_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("UWC_REFERENCE"), required="UWC_REFERENCE" not in os.environ)
     a = ap.parse_args()
     sys.path.insert(0, os.path.join(a.reference, "miner", "ampere"))
     import torch
