@@ -4,9 +4,11 @@
 
 Default workload (the metric's 1/2/4/8-GPU config): noise mining at the
 Llama-3.1-8B MLP shape, M=8192 (the nonce A), K=4096, N=14336 (the block's B^T), rank-64 noise,
-2^-20 target. One step = one mining attempt, exactly MinedWeight.noise_mine + winners():
-BLAKE3 commit of A -> a_seed, A-side noise, noise_rows (A + E_A P_A), the hashed tcgen05 GEMM
-(XOR-fold every r columns, keyed BLAKE3 per 8x16 hash tile, target compare), win records.
+2^-20 target. One device-timed step = one mining attempt, MinedWeight.noise_mine (one
+uwc_mine_attempt call): BLAKE3 commit of A -> a_seed, A-side noise, ApEA = A + E_A P_A, the hashed
+tcgen05 GEMM (XOR-fold every r columns, keyed BLAKE3 per 8x16 hash tile, target compare, win
+records on the device). The end-to-end figure adds, every step, the upload of A from pinned host
+memory and the copy of the win records back to the host.
 With N GPUs every rank mines its own A (nonce sharding by rank seed, no collective on the data
 path): weak scaling. Timing: CUDA events on the launching stream around each step, L2 flushed
 (a 256 MiB write) before every timed step, max over ranks.
@@ -43,7 +45,7 @@ WORKLOADS = {
     "c4-generate": (8, 2048, 128, 0, "Qwen3-1.7B deterministic int8 forward, random-init: batch 8 x 2048 prefill + "
                                      "128-token greedy decode (configs[3])"),
 }
-# DRAM bytes per launch of the dominant kernel from one ncu capture (committed summary under profiles/)
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this workload
 TRAFFIC = {"c3-mine": 148.7e6 + 4.0e6}
 # Llama-3.1-8B linears of one layer: (name, n, k, kind); qkv n = (32 + 2 * 8) * 128
 C5_LINEARS = [("qkv", 6144, 4096, "col"), ("o", 4096, 4096, "row"), ("gate_up", 28672, 4096, "col"),
@@ -324,10 +326,10 @@ def run_c5(a, world, rank, local):
     barrier(world)
     # the layer is one CUDA graph (kernels, split-K memsets and, with N > 1, the NCCL all-reduces)
     graph = torch.cuda.CUDAGraph()
-    l0 = ops.LAUNCHES
+    l0 = ops.launches()
     with torch.cuda.graph(graph):
         ys = step(xs)
-    per_step = ops.LAUNCHES - l0
+    per_step = ops.launches() - l0
     barrier(world)
     sampler = ClockSampler(local)
     sampler.start()
@@ -466,7 +468,7 @@ def run_c4(a, world, rank, local):
     for _ in range(a.warmup):
         job(prompt)
     barrier(world)
-    l0 = ops.LAUNCHES
+    l0 = ops.launches()
     sampler = ClockSampler(local)
     sampler.start()
     evs = []
@@ -477,7 +479,7 @@ def run_c4(a, world, rank, local):
         evs.append(e)
     barrier(world)
     clocks = sampler.stop()
-    launches = ops.LAUNCHES - l0
+    launches = ops.launches() - l0
     t_pre = max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs), world)
     t_dec = max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in evs), world)
     t_ms = max_over_ranks(sum(e[0].elapsed_time(e[2]) for e in evs), world)
@@ -566,7 +568,7 @@ def run_b200(a, world, rank, local):
     for i in range(a.warmup):
         step(i)
     barrier(world)
-    launches_before = ops.LAUNCHES
+    launches_before = ops.launches()
     sampler = ClockSampler(local)
     sampler.start()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
@@ -579,7 +581,7 @@ def run_b200(a, world, rank, local):
         evs[i][1].record(stream)
     barrier(world)
     clocks = sampler.stop()
-    launches = ops.LAUNCHES - launches_before
+    launches = ops.launches() - launches_before
     t_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
     t_ms = max_over_ranks(t_ms, world)
     ops_per_step = 2.0 * m * n * k
@@ -587,14 +589,14 @@ def run_b200(a, world, rank, local):
     tiles_per_s = world * (m * n / 128) * a.steps / (t_ms / 1e3)
 
     # dominant kernel alone: the hashed GEMM, CUDA events on its stream
-    b = w._buf(m)
+    b = w.buffers(m)
     gk = []
     for i in range(max(3, a.steps // 2)):
         flush.fill_(i & 0xFF)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         if forward:
-            ops.gemm(b["ApEA"], w.BpEBt, r=r, flags=ops.FLAG_HASH | ops.FLAG_DENOISE, corrA=b["corrA"], corrB=w.corrB,
+            ops.gemm(b["ApEA"], w.BpEBt, r=r, flags=ops.FLAG_HASH | ops.FLAG_DENOISE, corrA=b["corrA"], corrB=b["corrB"],
                      maxabs=b["maxabs"], key=b["a_seed"], target=w.target, wins=b["wins"], max_wins=w.max_wins,
                      out=out, out_mode=ops.OUT_I32)
         else:
@@ -649,9 +651,9 @@ def run_b200(a, world, rank, local):
             "pct_int8_peak": 100.0 * value / world / peak_tops,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOP/s",
                          "frac": achieved / peak_tops, "traffic": TRAFFIC.get(a.workload),
-                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch, "
-                                           "profiles/k_noisy_gemm_mine_r64_c3_ncu_full.md" if a.workload in TRAFFIC
-                                           else None, "kernel": "k_noisy_gemm",
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch of "
+                                           "k_noisy_gemm<MODE_MINE, 64>, one ncu capture of this workload"
+                                           if a.workload in TRAFFIC else None, "kernel": "k_noisy_gemm",
                          "peak_source": "cuBLASLt int8 (torch._int_mm) on the same shape, burst, measured in "
                                         "this run (MEASURED_PEAKS.json has no int8 entry; its bf16 figure "
                                         f"{pk['bf16_tflops']} TF/s, {pk['src']})",

@@ -48,6 +48,10 @@ extern "C" {
 /* Library version (major*10000 + minor*100 + patch). */
 int uwc_version(void);
 
+/* Kernels this library has launched in this process (all devices, all threads): a counter the
+ * caller reads before and after a region to count the library's launches in it. */
+uint64_t uwc_launch_count(void);
+
 /* Human-readable name of a status code. */
 const char* uwc_status_string(int code);
 
@@ -75,8 +79,12 @@ int uwc_b3_root_and_seed(const void* data, uint64_t nbytes, const uint32_t* key,
  * limited to uwc_b3_noalloc_max_bytes() (128 MiB); larger ones return UWC_ERR_SCRATCH. No
  * allocation of any kind. The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) and should come before any stream capture. All calls on a device share
- * the array: calls that overlap on the GPU race and must be serialized by the caller. */
+ * the array: calls that overlap on the GPU race and must be serialized by the caller. The looked-up
+ * address is cached per device (host threads may make their first calls concurrently) for the life
+ * of the device's CUDA context; a caller that resets a device (cudaDeviceReset) calls
+ * uwc_b3_noalloc_forget() afterwards. */
 uint64_t uwc_b3_noalloc_max_bytes(void);
+void uwc_b3_noalloc_forget(void);
 int uwc_b3_root_and_seed_noalloc(const void* data, uint64_t nbytes, const uint32_t* key, const uint32_t* prefix,
                                  const uint32_t* salt, uint32_t dim, uint32_t* root_out, uint32_t* seed_out,
                                  void* stream);
@@ -138,6 +146,63 @@ int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int f
              const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key, const uint32_t* target,
              uint32_t* wins, int max_wins, const float* a_scale, const float* b_scale, void* out, int out_mode,
              void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* ---- a mined weight: the per-block and per-call sequences as single calls --------------------
+ * MinedWeight (miner/ampere/uwc_ampere/ops.py:205-371) keeps its state in two caller-owned device
+ * buffers whose layouts are fixed functions of the shapes:
+ *   block      everything derived from B^T (n x k) and the block key, written by
+ *              uwc_mined_setup_block and only read by the per-call functions;
+ *   workspace  everything a call derives from A (m x k); every call overwrites it, so calls that
+ *              overlap on the GPU need workspaces of their own (the reference shares one workspace
+ *              per (device, m, k, r) among the layers of a model, ops.py:258-277: so can callers).
+ * The *_layout functions write the byte offset of each part (the UWC_MB_* / UWC_MW_* indices) and,
+ * at index UWC_MB_BYTES / UWC_MW_BYTES, the total size. Shapes: n % 64 == 0, k % 64 == 0,
+ * r in {64, 128, 256}, k % r == 0, k <= 65536; m % 64 == 0 for the per-call functions. */
+#define UWC_MB_CONSTS 0 /* 64 u32: job key, b_seed, target, noise labels A/B, seed salts A/B */
+#define UWC_MB_EBRT 1   /* n x r int8: B-side noise factor */
+#define UWC_MB_PB 2     /* k u32: B-side noise permutation, first | second << 16 */
+#define UWC_MB_SBT 3    /* r x k int8: projection matrix of P_B */
+#define UWC_MB_BPEBT 4  /* n x k int8: the noised weight B + F */
+#define UWC_MB_BYTES 5
+#define UWC_MW_A_SEED 0 /* 8 u32: the call's a_seed (the tile-hash key) */
+#define UWC_MW_MAXABS 1 /* 2 int32: max |X|, max |Y| (forward) */
+#define UWC_MW_EAL 2    /* m x r int8 */
+#define UWC_MW_PA 3     /* k u32 */
+#define UWC_MW_APEA 4   /* m x k int8: the noised A + E */
+#define UWC_MW_B3 5     /* commitment scratch */
+#define UWC_MW_GEMM 6   /* the hashed GEMM's workspace (uwc_gemm_workspace_bytes) */
+#define UWC_MW_SAT 7    /* forward: r x k int8 projection matrix of P_A */
+#define UWC_MW_CORRA 8  /* forward: L x m x 2r int8, [X_li | EAL] */
+#define UWC_MW_CORRB 9  /* forward: L x n x 2r int8, [EBRt | Y_li] */
+#define UWC_MW_PROJA 10 /* forward: m x r int32 */
+#define UWC_MW_PROJB 11 /* forward: n x r int32 */
+#define UWC_MW_BYTES 12
+/* offsets: UWC_MB_BYTES + 1 entries. */
+int uwc_mined_block_layout(int n, int k, int r, uint64_t* offsets);
+/* offsets: UWC_MW_BYTES + 1 entries. forward = 0: the layout uwc_mine_attempt needs; 1: the one of
+ * uwc_mined_forward with the given hash flag and out_mode (the forward parts are sized 0 otherwise). */
+int uwc_mined_workspace_layout(int m, int n, int k, int r, int forward, int hash, int out_mode, uint64_t* offsets);
+/* MinedWeight.setup_block (ops.py:233-253): commit to Bt (device, n x k int8, values in [-64, 64])
+ * under the 32-byte job key, b_seed = BLAKE3(job_key || BLAKE3_keyed(salt_B, root_B || n)), the
+ * B-side noise EBRt and P_B, BpEBt = Bt + EBRt P_B and the projection matrix of P_B, into `block`.
+ * job_key (32 bytes) and target (8 LE words of the 256-bit tile target) are HOST memory, copied in
+ * with cudaMemcpyAsync (so this call cannot be captured in a graph; the per-call ones can).
+ * scratch: device memory of at least 4 * uwc_b3_scratch_words(n * k) bytes. */
+int uwc_mined_setup_block(const int8_t* Bt, int n, int k, int r, const uint8_t* job_key, const uint32_t* target,
+                          void* block, uint64_t block_bytes, void* scratch, uint64_t scratch_bytes, void* stream);
+/* MinedWeight.noise_mine (ops.py:349-364): one mining attempt on the nonce matrix A (device, m x k
+ * int8): a_seed = BLAKE3(b_seed || BLAKE3_keyed(salt_A, root_A || m)), A-side noise, ApEA, then the
+ * hashed GEMM ApEA BpEBt^T with every 8 x 16 tile hashed and compared to the block's target; win
+ * records into wins (count zeroed by this call, see uwc_gemm). No output matrix, no projections. */
+int uwc_mine_attempt(const int8_t* A, int m, int n, int k, int r, const void* block, uint32_t* wins, int max_wins,
+                     void* workspace, uint64_t workspace_bytes, void* stream);
+/* MinedWeight.forward (ops.py:281-347): the mining attempt's preparation, the rank-r projections
+ * X = A P_B^T and Y = BpEBt P_A^T as balanced base-128 limbs (ops.py:152-168), then the GEMM with
+ * FLAG_DENOISE (and FLAG_HASH when hash != 0): out = A Bt^T exactly, in out_mode (I32, BF16, F32
+ * with a_scale (m) and b_scale (n) as in uwc_gemm). The winning tiles equal uwc_mine_attempt's. */
+int uwc_mined_forward(const int8_t* A, int m, int n, int k, int r, const float* a_scale, const float* b_scale,
+                      const void* block, int hash, uint32_t* wins, int max_wins, void* out, int out_mode,
+                      void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- deterministic linear: producers
  * and consumers of the int8 GEMM, bit-identical to runtime/detrt's emulated-fp32 ops (every + - * /

@@ -41,7 +41,7 @@ def test_mined_forward_exact_and_winners_match_oracle(ops, m, n, k, r):
     out = w.forward(torch.from_numpy(A).cuda(), torch.ones(m, device="cuda"), out_mode=ops.OUT_I32)
     assert np.array_equal(out.cpu().numpy(), O.gemm_i32(A, Bt))
     a_seed, want = _expected(A, Bt, key, r, target)
-    assert ops.words_to_bytes(w._buf(m)["a_seed"]) == a_seed
+    assert ops.words_to_bytes(w.buffers(m)["a_seed"]) == a_seed
     got = sorted(w.winners(m))
     assert want and got == want
 
@@ -80,22 +80,27 @@ def test_golden_winners(ops, golden):
 
 
 def test_projection_paths_identical(ops):
-    """Tensor-core projections == shared-memory-atomic noise_rows (test_proj_gemm.py:23-47)."""
+    """The forward's tensor-core projections (split-K GEMMs against S^T, then limbs) == the gather
+    kernel of noise_rows with a projection permutation, limb for limb (test_proj_gemm.py:23-47)."""
     from uwc_b200 import glue
-    for (n, k, m) in ((1024, 2048, 256), (512, 4096, 128)):
+    for (n, k, m, r) in ((1024, 2048, 256, 128), (512, 4096, 128, 128), (512, 4096, 256, 64), (256, 2048, 128, 256)):
         A, Bt, key = _inputs(m, n, k, n + k + m)
-        res = {}
-        for mode in (False, True):
-            w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=128)
-            w.setup_block(key, glue.target_for(m, n))
-            ones = torch.ones(m, dtype=torch.float32, device="cuda")
-            out = w._forward(torch.from_numpy(A).cuda(), ones, None, ops.OUT_I32, True, ops.DEFAULT_CFG, mode)
-            b = w._buf(m)
-            res[mode] = (out.clone(), b["corrA"].clone(), w.corrB.clone(), b["maxabs"].clone(), sorted(w.winners(m)))
-        for name, x, y in zip(("out", "corrA", "corrB", "maxabs"), res[False][:4], res[True][:4]):
-            assert torch.equal(x, y), name
-        assert res[False][4] == res[True][4] and 0 < len(res[True][4]) < 64
-        assert np.array_equal(res[True][0].cpu().numpy(), O.gemm_i32(A, Bt))
+        w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r)
+        w.setup_block(key, glue.target_for(m, n))
+        Ad = torch.from_numpy(A).cuda()
+        out = w.forward(Ad, torch.ones(m, dtype=torch.float32, device="cuda"), out_mode=ops.OUT_I32)
+        b = w.buffers(m)
+        L = b["corrA"].shape[0]
+        corrA = torch.zeros_like(b["corrA"])
+        corrB = torch.zeros_like(b["corrB"])
+        mx = torch.zeros(2, dtype=torch.int32, device="cuda")
+        ops.noise_rows(Ad, m, k, r, E=b["EAL"], Pp=w.PB, corr=corrA, corr_off=0, ecopy_off=r, maxabs=mx[0:1])
+        ops.noise_rows(w.BpEBt, n, k, r, E=w.EBRt, Pp=b["PA"], corr=corrB, corr_off=r, ecopy_off=0, maxabs=mx[1:2])
+        for name, x, y in (("corrA", b["corrA"], corrA), ("corrB", b["corrB"], corrB), ("maxabs", b["maxabs"], mx)):
+            assert torch.equal(x, y), (name, n, k, m, r, L)
+        wins = sorted(w.winners(m))
+        assert 0 < len(wins) < 64
+        assert np.array_equal(out.cpu().numpy(), O.gemm_i32(A, Bt))
 
 
 def test_large_projection_needs_more_limbs(ops):
@@ -113,7 +118,7 @@ def test_large_projection_needs_more_limbs(ops):
     w = ops.MinedWeight(Bt=torch.from_numpy(Bt).cuda(), b_scale=torch.ones(n, device="cuda"), r=r)
     w.setup_block(key, np.zeros(8, np.uint32))
     out = w.forward(torch.from_numpy(A).cuda(), torch.ones(m, device="cuda"), out_mode=ops.OUT_I32)
-    assert int(w._buf(m)["maxabs"].max().item()) > 8127
+    assert int(w.buffers(m)["maxabs"].max().item()) > 8127
     assert np.array_equal(out.cpu().numpy(), O.gemm_i32(A, Bt))
 
 
@@ -266,7 +271,7 @@ def test_host_miner_matches_noise_mine(dev):
         want.append(sorted(w.winners(m)))
     hm = ops.HostMiner(w, m, k, dev)
     hosts = [torch.from_numpy(A).pin_memory() for A in As]
-    outs = [torch.empty(w._buf(m)["wins"].numel(), dtype=torch.int32).pin_memory() for _ in As]
+    outs = [torch.empty(w.buffers(m)["wins"].numel(), dtype=torch.int32).pin_memory() for _ in As]
     for A_h, o in zip(hosts, outs):
         hm.mine(A_h, o)
     torch.cuda.synchronize()

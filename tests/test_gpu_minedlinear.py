@@ -23,6 +23,13 @@ def test_mined_and_plain_equal_int_path(dev):
     ya, yb, yc = a(x), b(x), c(x)
     assert ya.shape == yb.shape == yc.shape == (3, 333, 5120)
     assert torch.equal(ya, yb) and torch.equal(ya, yc)
+    # independent of the library's GEMM: the int8 operands' exact product on the host
+    import oracle as O
+    from uwc_b200 import ops
+    xq, sx = ops.quant_rows_had(x.reshape(-1, 2560).contiguous(), a.bs)
+    acc = torch.from_numpy(O.gemm_i32(xq.cpu().numpy(), a.Wq.cpu().numpy()))
+    want = ((acc.float() * sx.cpu().unsqueeze(1)) * a.sw.cpu().unsqueeze(0)).to(torch.bfloat16)
+    assert torch.equal(ya.reshape(-1, 5120).cpu(), want)
     ref = x.float() @ torch.cat([l.weight for l in lins]).cuda().t()
     assert ((ya.float() - ref).norm() / ref.norm()).item() < 0.03
 

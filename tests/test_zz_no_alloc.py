@@ -48,13 +48,20 @@ def test_noalloc_commitment_matches_regular_entry_point(dev):
     salt = torch.randint(-2 ** 31, 2 ** 31 - 1, (8,), dtype=torch.int32, device="cuda", generator=gen)
     max_bytes = int(L.uwc_b3_noalloc_max_bytes())
     assert max_bytes == 128 << 20
-    # two calls in a row on different inputs: the shared scratch keeps the first call's contents
-    # when the second runs, and the second must not depend on them
-    for nbytes, dim in ((max_bytes, 8192), (3 * 1024 * 129, 387)):
+    key_bytes = key.cpu().numpy().astype("<i4").tobytes()
+    # calls in a row on different inputs: the shared scratch keeps the previous call's contents
+    # when the next runs, and the next must not depend on them. The sizes cover the largest input
+    # (1024 chunk groups, one reduce level), a ragged group count, a single full group (the chunk
+    # kernel applies ROOT at its own merge) and a single chunk (ROOT on the chunk compression).
+    for nbytes, dim in ((max_bytes, 8192), (3 * 1024 * 129, 387), (128 * 1024, 64), (1024, 1)):
         data = torch.randint(-128, 128, (nbytes,), dtype=torch.int8, device="cuda", generator=gen)
         want_root, want_seed = _commit(L, data, key, prefix, salt, dim, noalloc=False)
         got_root, got_seed = _commit(L, data, key, prefix, salt, dim, noalloc=True)
         assert np.array_equal(got_root, want_root) and np.array_equal(got_seed, want_seed), nbytes
+        if nbytes <= 1 << 20:
+            import blake3
+            digest = blake3.blake3(data.cpu().numpy().tobytes(), key=key_bytes).digest()
+            assert got_root.astype("<i4").tobytes() == digest, nbytes
     assert _lib.device_status(clear=True) == 0
 
 

@@ -637,6 +637,7 @@ int launch_attn(const AttnArgs& a, int B, int spitch, cudaStream_t st) {
   const int rc = smem_optin((const void*)k_attention<QT>, smem + 1024);   // + its static reduction slots
   if (rc != UWC_OK) return rc;
   k_attention<QT><<<dim3(B * a.H, (a.Tq + QT - 1) / QT), kAttnThreads, smem, st>>>(a, spitch);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -647,6 +648,7 @@ int launch_decode(const AttnArgs& a, int B, int lpitch, cudaStream_t st) {
   const int rc = smem_optin((const void*)k_attn_decode<HPG>, smem + (int)sizeof(DecShared<HPG>));
   if (rc != UWC_OK) return rc;
   k_attn_decode<HPG><<<B * a.Hkv * kDecCluster, kAttnThreads, smem, st>>>(a, lpitch);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -993,9 +995,12 @@ extern "C" int uwc_attention_tc(const int8_t* qq, const float* qs, const int8_t*
   float* spb = reinterpret_cast<float*>(ws + L.sp);
   const int S = start + Tq, grid = uwc_num_sms() * 8;
   k_tc_gather_q<<<grid, 256, 0, st>>>(qq, B, Tq, H, L.Tp, qh);
+  uwc_count_launch();
   k_tc_gather_k<<<grid, 256, 0, st>>>(kc, ks, vs, B, S, Hkv, kv_seq, kv_tok, kv_head, s_seq, s_tok, s_head, L.Sp, kh,
                                       ksc, vsc);
+  uwc_count_launch();
   k_tc_transpose_v<<<dim3(L.Sp / 64, L.nkv), 256, 0, st>>>(vc, B, S, Hkv, kv_seq, kv_tok, kv_head, L.Sp, vt);
+  uwc_count_launch();
   if ((rc = uwc_launch_status()) != UWC_OK) return rc;
   const int hpg = H / Hkv;
   rc = uwc_gemm_batched(qh, kh, L.Tp, L.Sn, kHd, L.nb, L.Tp, L.Sp, hpg, 1, start, 0, sint, stream);
@@ -1003,10 +1008,12 @@ extern "C" int uwc_attention_tc(const int8_t* qq, const float* qs, const int8_t*
   const long long rows = (long long)L.nb * Tq;
   k_tc_softmax<<<(unsigned)((rows + kTcRowsPerCta - 1) / kTcRowsPerCta), kTcRowsPerCta * 32, smem, st>>>(
       sint, qs, ksc, vsc, B, Tq, start, H, Hkv, L.Tp, L.Sp, L.Sn, inv_sqrt_hd, pst, spb);
+  uwc_count_launch();
   if ((rc = uwc_launch_status()) != UWC_OK) return rc;
   rc = uwc_gemm_batched(pst, vt, 2 * L.Tp, kHd, L.Sp, L.nb, 2LL * L.Tp, kHd, hpg, 2, start, L.Tp, o32, stream);
   if (rc != UWC_OK) return rc;
   k_tc_combine<<<grid, 256, 0, st>>>(o32, spb, B, Tq, H, L.Tp, out);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -1039,6 +1046,7 @@ extern "C" int uwc_kv_append(const int8_t* kq, const float* ks, const int8_t* vq
   if (warps == 0) return UWC_OK;
   k_kv_append<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(kq, ks, vq, vs, B, T, Hkv,
                                                                                        maxlen, pos, kc, skc, vc, svc);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -1051,6 +1059,7 @@ extern "C" int uwc_rmsnorm(const float* x, const float* w, int m, int k, double 
   while ((1 << L) < k) L++;
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
   k_rmsnorm<256><<<m, 256, 0, (cudaStream_t)stream>>>(x, w, k, (float)(1.0 / k), (float)eps, L, out);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -1059,5 +1068,6 @@ extern "C" int uwc_logprobs(const float* logits, int m, int V, float* lp, long l
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
   k_logprobs<1024><<<m, 1024, 0, (cudaStream_t)stream>>>(logits, V, lp, tok);
+  uwc_count_launch();
   return uwc_launch_status();
 }

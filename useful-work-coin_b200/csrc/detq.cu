@@ -409,10 +409,12 @@ int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, fl
     const int rc = row_smem_ok(k, (const void*)k_quant_act<1024, MODE, BF16>);
     if (rc != UWC_OK) return rc;
     k_quant_act<1024, MODE, BF16><<<m, 1024, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
+    uwc_count_launch();
   } else {
     const int rc = row_smem_ok(k, (const void*)k_quant_act<kRowThreads, MODE, BF16>);
     if (rc != UWC_OK) return rc;
     k_quant_act<kRowThreads, MODE, BF16><<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
+    uwc_count_launch();
   }
   return uwc_launch_status();
 }
@@ -448,11 +450,13 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
     const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<1024>);
     if (rc != UWC_OK) return rc;
     k_rmsnorm_quant<1024><<<m, 1024, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, inv_d, eps32, ceil_log2(k), q, scale);
+    uwc_count_launch();
   } else {
     const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<kRowThreads>);
     if (rc != UWC_OK) return rc;
     k_rmsnorm_quant<kRowThreads><<<m, kRowThreads, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, inv_d, eps32,
                                                                                  ceil_log2(k), q, scale);
+    uwc_count_launch();
   }
   return uwc_launch_status();
 }
@@ -467,10 +471,12 @@ extern "C" int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float
     const int rc = row_smem_ok(I, (const void*)k_swiglu_quant<1024>);
     if (rc != UWC_OK) return rc;
     k_swiglu_quant<1024><<<m, 1024, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
+    uwc_count_launch();
   } else {
     const int rc = row_smem_ok(I, (const void*)k_swiglu_quant<kRowThreads>);
     if (rc != UWC_OK) return rc;
     k_swiglu_quant<kRowThreads><<<m, kRowThreads, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
+    uwc_count_launch();
   }
   return uwc_launch_status();
 }
@@ -481,6 +487,7 @@ extern "C" int uwc_swiglu(const int32_t* acc, const float* s3, const float* sw, 
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
   k_swiglu<<<dim3((I + 255) / 256, m), 256, 0, (cudaStream_t)stream>>>(acc, s3, sw, I, h);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -493,6 +500,7 @@ extern "C" int uwc_dequant_residual(const int32_t* acc, const float* s, const fl
   if (n4 == 0) return UWC_OK;
   const int grid = (int)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)uwc_num_sms() * 16);
   k_dequant_residual<<<grid, 256, 0, (cudaStream_t)stream>>>(acc, s, sw, x, k, n4, out);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -509,6 +517,7 @@ int qkv_post_launch(const int32_t* acc, const float* s1, const float* sw, const 
   k_qkv_post<<<N, kRowThreads, 0, (cudaStream_t)stream>>>(acc, s1, sw, qnw, knw, cos_t, sin_t, T, H, Hkv,
                                                           (float)(1.0 / 128), (float)eps, qknorm, qq, qs, kq, ks, vq,
                                                           vs, pos0);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 }  // namespace

@@ -864,6 +864,7 @@ int launch(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CU
   }
   const int grid = std::min(p.nunits, uwc_num_sms());
   k_noisy_gemm<MODE, R><<<grid, kThreads, Cfg<MODE, R>::SMEM, st>>>(a, b, ca, cb, p);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 

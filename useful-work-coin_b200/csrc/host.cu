@@ -1,6 +1,7 @@
 // Host plumbing of the C ABI: device checks, launch status, TMA descriptor encoding, status words.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "uwc_device.cuh"
@@ -15,6 +16,7 @@ int g_dev_ok[kMaxDevices];   // 0 unknown, 1 sm_100, -1 other
 int g_dev_sms[kMaxDevices];
 uint32_t* g_dev_status[kMaxDevices];
 std::mutex g_mu;
+std::atomic<uint64_t> g_launches{0};
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int current_device(int* dev) {
@@ -66,6 +68,8 @@ uint32_t* uwc_status_ptr() {
   return g_dev_status[dev];
 }
 
+void uwc_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 int uwc_launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? UWC_OK : UWC_ERR_CUDA;
@@ -100,7 +104,9 @@ int uwc_make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 
 extern "C" {
 
-int uwc_version(void) { return 100; }
+int uwc_version(void) { return 200; }
+
+uint64_t uwc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* uwc_status_string(int code) {
   switch (code) {

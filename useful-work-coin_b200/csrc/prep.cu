@@ -5,6 +5,8 @@
 //   proj_matrix, proj_corr (tensor-core projection)  (ops.py:145-168, kernels.cu:374-404)
 // All of them are HBM- or latency-bound SIMT kernels; the dense work is in gemm_sm100.cu.
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "uwc_device.cuh"
 #include "uwc_host.h"
@@ -151,9 +153,10 @@ __device__ __forceinline__ void random_hash(uint32_t index, const uint32_t* labe
 __global__ void __launch_bounds__(256) k_noise_uniform(int8_t* __restrict__ out, uint32_t nblocks,
                                                        const uint32_t* __restrict__ label,
                                                        const uint32_t* __restrict__ key, int32_t* __restrict__ zero_me,
-                                                       int zero_n) {
+                                                       int zero_n, int32_t* __restrict__ zero2, int zero2_n) {
   const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
   if (zero_me && b < (uint32_t)zero_n) zero_me[b] = 0;
+  if (zero2 && b < (uint32_t)zero2_n) zero2[b] = 0;
   if (b >= nblocks) return;
   uint32_t h[8], o[8];
   random_hash(b, label, key, 0, h);
@@ -188,7 +191,7 @@ __global__ void __launch_bounds__(128) k_noise_perm(uint32_t* __restrict__ out, 
 
 // ------------------------------------------------------------------ noise_rows
 namespace {
-constexpr int kNrRows = 8;  // rows per CTA
+constexpr int kNrRows = 8;       // row multiple of the noise_rows call (the reference's rows per CTA)
 constexpr int kNaRows = 32;      // rows per staged group of the noising-only kernel
 constexpr int kNaCtasPerSm = 4;  // its resident CTAs per SM (persistent grid, <= 64 registers)
 }
@@ -253,82 +256,106 @@ __global__ void __launch_bounds__(256, kNaCtasPerSm) k_noise_add(const int8_t* _
   }
 }
 
-__global__ void __launch_bounds__(256) k_noise_rows(const int8_t* __restrict__ src, int rows, int k, int r,
-                                                    const int8_t* __restrict__ E, const uint32_t* __restrict__ Pn,
-                                                    int8_t* __restrict__ dst, const uint32_t* __restrict__ Pp,
-                                                    int8_t* __restrict__ corr, int corr_off, int ecopy_off,
-                                                    int32_t* __restrict__ maxabs, int lmax) {
-  extern __shared__ __align__(16) uint8_t nr_smem[];
-  int8_t* Es = reinterpret_cast<int8_t*>(nr_smem);                        // kNrRows * r
-  int32_t* proj = reinterpret_cast<int32_t*>(nr_smem + kNrRows * 256);    // kNrRows * r
+// Projection of rows onto a noise permutation (the X / Y terms of the exact denoise, reference
+// kernels.cu:310-372): proj[row][j] = sum of src[row][l] over the columns l with first(l) == j minus
+// the sum over the columns with second(l) == j, written as lmax balanced base-128 limbs at
+// corr[li][row][corr_off + j] with max |proj| folded into *maxabs. Gather design: every CTA first
+// inverts the permutation into per-column index lists in shared memory (a counting sort of the k
+// pairs), then walks its share of the rows: the row is staged in shared memory and the threads
+// assigned to column j add up the bytes of j's two lists, so no value is scattered. The tensor-core
+// path (k_proj_matrix + the split-K GEMM + k_proj_corr) computes the same integers; the tests
+// compare the two. Optionally copies E (rows x r) into corr[li][row][ecopy_off + j] for every limb.
+namespace {
+constexpr int kPrThreads = 256;
+constexpr int kPrCtasPerSm = 2;
+}
+
+__global__ void __launch_bounds__(kPrThreads, kPrCtasPerSm)
+    k_project_rows(const int8_t* __restrict__ src, int rows, int k, int r, const uint32_t* __restrict__ Pp,
+                   const int8_t* __restrict__ E, int8_t* __restrict__ corr, int corr_off, int ecopy_off,
+                   int32_t* __restrict__ maxabs, int lmax) {
+  extern __shared__ __align__(16) uint8_t pr_smem[];
+  // [plus start r+1][minus start r+1][plus list k][minus list k] (u16 columns), then the staged row
+  int* const pstart = reinterpret_cast<int*>(pr_smem);
+  int* const mstart = pstart + (r + 1);
+  uint16_t* const plist = reinterpret_cast<uint16_t*>(mstart + (r + 1));
+  uint16_t* const mlist = plist + k;
+  int8_t* const row_s = reinterpret_cast<int8_t*>(pr_smem + (((2 * (r + 1) * 4 + 4 * k) + 15) & ~15));
   const int tid = threadIdx.x;
-  const int row0 = blockIdx.x * kNrRows;
-  if (E)
-    for (int i = tid; i < kNrRows * r; i += 256) Es[i] = E[(uint64_t)row0 * r + i];
-  if (Pp)
-    for (int i = tid; i < kNrRows * r; i += 256) proj[i] = 0;
-  __syncthreads();
-  const int vpr = k >> 4;  // 16-byte vectors per row
-  for (int it = tid; it < kNrRows * vpr; it += 256) {
-    const int rr = it / vpr, q = it - rr * vpr;
-    const uint64_t off = (uint64_t)(row0 + rr) * k + 16 * q;
-    const uint4 w = __ldg(reinterpret_cast<const uint4*>(src + off));
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    if (dst) {
-      const uint4* pn4 = reinterpret_cast<const uint4*>(Pn + 16 * q);
-      uint32_t o[4];
-#pragma unroll
-      for (int v = 0; v < 4; v++) {
-        const uint4 p = __ldg(pn4 + v);
-        const uint32_t pv[4] = {p.x, p.y, p.z, p.w};
-        uint32_t ov = 0;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int x = (int)(int8_t)(ws[v] >> (8 * j));
-          const int nv = x + (int)Es[rr * r + (pv[j] & 0xFFFFu)] - (int)Es[rr * r + (pv[j] >> 16)];
-          ov |= (uint32_t)(uint8_t)(int8_t)nv << (8 * j);
-        }
-        o[v] = ov;
-      }
-      *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  const int r0 = (int)((int64_t)blockIdx.x * rows / gridDim.x);
+  const int r1 = (int)((int64_t)(blockIdx.x + 1) * rows / gridDim.x);
+  if (r0 >= r1) return;
+  const uint64_t limb_stride = (uint64_t)rows * 2 * r;
+  if (Pp) {
+    // counting sort of the k columns by first (plus lists) and by second (minus lists)
+    for (int j = tid; j <= r; j += kPrThreads) pstart[j] = mstart[j] = 0;
+    __syncthreads();
+    // (pairs naming a column >= r are not valid permutations and are left out of both lists)
+    for (int l = tid; l < k; l += kPrThreads) {
+      const uint32_t p = __ldg(Pp + l);
+      if ((p & 0xFFFFu) < (uint32_t)r) atomicAdd(&pstart[(p & 0xFFFFu) + 1], 1);
+      if ((p >> 16) < (uint32_t)r) atomicAdd(&mstart[(p >> 16) + 1], 1);
     }
+    __syncthreads();
+    if (tid == 0) {
+      for (int j = 0; j < r; j++) pstart[j + 1] += pstart[j];
+    } else if (tid == 32) {
+      for (int j = 0; j < r; j++) mstart[j + 1] += mstart[j];
+    }
+    __syncthreads();
+    // fill: one warp per column j keeps the columns in increasing order (ballot ranks)
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int j = warp; j < r; j += kPrThreads / 32) {
+      int pp = pstart[j], mp = mstart[j];
+      for (int l0 = 0; l0 < k; l0 += 32) {
+        const int l = l0 + lane;
+        const uint32_t p = l < k ? __ldg(Pp + l) : 0xFFFFFFFFu;
+        const bool isp = l < k && (int)(p & 0xFFFFu) == j, ism = l < k && (int)(p >> 16) == j;
+        const uint32_t bp = __ballot_sync(0xffffffffu, isp), bm = __ballot_sync(0xffffffffu, ism);
+        const uint32_t below = (1u << lane) - 1u;
+        if (isp) plist[pp + __popc(bp & below)] = (uint16_t)l;
+        if (ism) mlist[mp + __popc(bm & below)] = (uint16_t)l;
+        pp += __popc(bp);
+        mp += __popc(bm);
+      }
+    }
+    __syncthreads();
+  }
+  const int parts = kPrThreads / r;   // threads per column: 4 (r 64), 2 (r 128), 1 (r 256)
+  const int j = tid % r, part = tid / r;
+  int local_max = 0;
+  for (int row = r0; row < r1; row++) {
     if (Pp) {
-      const uint4* pp4 = reinterpret_cast<const uint4*>(Pp + 16 * q);
-#pragma unroll
-      for (int v = 0; v < 4; v++) {
-        const uint4 p = __ldg(pp4 + v);
-        const uint32_t pv[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int x = (int)(int8_t)(ws[v] >> (8 * j));
-          if (x != 0) {
-            atomicAdd(&proj[rr * r + (pv[j] & 0xFFFFu)], x);
-            atomicSub(&proj[rr * r + (pv[j] >> 16)], x);
+      const uint4* g = reinterpret_cast<const uint4*>(src + (uint64_t)row * k);
+      for (int q = tid; q < (k >> 4); q += kPrThreads) reinterpret_cast<uint4*>(row_s)[q] = __ldg(g + q);
+      __syncthreads();
+      int acc = 0;
+      for (int i = pstart[j] + part; i < pstart[j + 1]; i += parts) acc += row_s[plist[i]];
+      for (int i = mstart[j] + part; i < mstart[j + 1]; i += parts) acc -= row_s[mlist[i]];
+      // the parts of column j are lanes tid, tid + r, ... of the same warp only when r < 32; sum
+      // them through shared memory (reusing the pstart-free tail of the row buffer is not safe)
+      __syncthreads();
+      int* const red = reinterpret_cast<int*>(row_s);
+      red[tid] = acc;
+      __syncthreads();
+      if (part == 0) {
+        int v = 0;
+        for (int q = 0; q < parts; q++) v += red[q * r + j];
+        local_max = max(local_max, abs(v));
+        if (corr && corr_off >= 0) {
+          const uint64_t base = (uint64_t)row * 2 * r + corr_off + j;
+          for (int li = 0; li < lmax; li++) {
+            const int d = ((v + 64) & 127) - 64;
+            corr[li * limb_stride + base] = (int8_t)d;
+            v = (v - d) >> 7;
           }
         }
       }
+      __syncthreads();
     }
-  }
-  __syncthreads();
-  const uint64_t limb_stride = (uint64_t)rows * 2 * r;
-  int local_max = 0;
-  for (int i = tid; i < kNrRows * r; i += 256) {
-    const int rr = i / r, j = i - rr * r;
-    const uint64_t rowbase = (uint64_t)(row0 + rr) * 2 * r;
-    if (Pp && corr_off >= 0) {
-      int v = proj[i];
-      local_max = max(local_max, abs(v));
-      if (corr) {
-        for (int li = 0; li < lmax; li++) {
-          const int d = ((v + 64) & 127) - 64;
-          corr[li * limb_stride + rowbase + corr_off + j] = (int8_t)d;
-          v = (v - d) >> 7;
-        }
-      }
-    }
-    if (E && corr && ecopy_off >= 0) {
-      const int8_t e = Es[i];
-      for (int li = 0; li < lmax; li++) corr[li * limb_stride + rowbase + ecopy_off + j] = e;
+    if (E && corr && ecopy_off >= 0 && part == 0) {
+      const int8_t e = E[(uint64_t)row * r + j];
+      for (int li = 0; li < lmax; li++) corr[li * limb_stride + (uint64_t)row * 2 * r + ecopy_off + j] = e;
     }
   }
   if (Pp && maxabs) {
@@ -350,7 +377,8 @@ __global__ void __launch_bounds__(256) k_proj_matrix(const uint32_t* __restrict_
 
 __global__ void __launch_bounds__(256) k_proj_corr(const int32_t* __restrict__ proj, int rows, int r,
                                                    int8_t* __restrict__ corr, int corr_off,
-                                                   int32_t* __restrict__ maxabs, int lmax) {
+                                                   int32_t* __restrict__ maxabs, int lmax,
+                                                   const int8_t* __restrict__ E, int ecopy_off) {
   const uint64_t limb_stride = (uint64_t)rows * 2 * r, total = (uint64_t)rows * r;
   int local_max = 0;
   for (uint64_t i = (uint64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (uint64_t)gridDim.x * 256) {
@@ -363,6 +391,10 @@ __global__ void __launch_bounds__(256) k_proj_corr(const int32_t* __restrict__ p
         const int d = ((v + 64) & 127) - 64;
         corr[li * limb_stride + rr * 2 * r + corr_off + j] = (int8_t)d;
         v = (v - d) >> 7;
+      }
+      if (E) {
+        const int8_t e = E[i];
+        for (int li = 0; li < lmax; li++) corr[li * limb_stride + rr * 2 * r + ecopy_off + j] = e;
       }
     }
   }
@@ -397,33 +429,48 @@ int uwc_b3_root_and_seed(const void* data, uint64_t nbytes, const uint32_t* key,
   const uint64_t nch = nbytes / 1024;
   uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;
   k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch, 1u);
+  uwc_count_launch();
   uint32_t* cur = scratch;
   uint32_t* nxt = scratch + 8 * cnt;
   while (cnt > (uint64_t)kReduceGroup) {
     const uint64_t groups = (cnt + kReduceGroup - 1) / kReduceGroup;
     k_b3_reduce<<<(unsigned)groups, 512, 0, st>>>(cur, (uint32_t)cnt, key, nxt, 0, nullptr, nullptr, 0, nullptr,
                                                   nullptr, 1u);
+    uwc_count_launch();
     cur = nxt;
     nxt += 8 * groups;
     cnt = groups;
   }
   k_b3_reduce<<<1, 512, 0, st>>>(cur, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out, 1u);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
-int uwc_noise_uniform(int8_t* out, uint64_t nbytes, const uint32_t* label, const uint32_t* key, int32_t* zero_me,
-                      int zero_n, void* stream) {
-  if (!out || !label || !key || zero_n < 0 || (zero_n > 0 && !zero_me)) return UWC_ERR_ARG;
+}  // extern "C"
+
+int uwc_noise_uniform_zero2(int8_t* out, uint64_t nbytes, const uint32_t* label, const uint32_t* key,
+                            int32_t* zero_me, int zero_n, int32_t* zero2, int zero2_n, void* stream) {
+  if (!out || !label || !key || zero_n < 0 || (zero_n > 0 && !zero_me) || zero2_n < 0 || (zero2_n > 0 && !zero2))
+    return UWC_ERR_ARG;
   if (nbytes % 32) return UWC_ERR_SHAPE;
   if (((uintptr_t)out) & 15) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   const uint64_t nblocks = nbytes / 32;
   if (nblocks > 0xFFFFFFFFull) return UWC_ERR_SHAPE;
-  const uint64_t threads = std::max<uint64_t>(nblocks, (uint64_t)zero_n);
+  const uint64_t threads = std::max<uint64_t>(nblocks, (uint64_t)std::max(zero_n, zero2_n));
   if (threads == 0) return UWC_OK;
   k_noise_uniform<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(out, (uint32_t)nblocks, label,
-                                                                                     key, zero_me, zero_n);
+                                                                                     key, zero_me, zero_n, zero2,
+                                                                                     zero2_n);
+  uwc_count_launch();
   return uwc_launch_status();
+}
+
+extern "C" {
+
+int uwc_noise_uniform(int8_t* out, uint64_t nbytes, const uint32_t* label, const uint32_t* key, int32_t* zero_me,
+                      int zero_n, void* stream) {
+  return uwc_noise_uniform_zero2(out, nbytes, label, key, zero_me, zero_n, nullptr, 0, stream);
 }
 
 int uwc_noise_perm(uint32_t* out, uint32_t k, uint32_t r, const uint32_t* label, const uint32_t* key, void* stream) {
@@ -433,6 +480,7 @@ int uwc_noise_perm(uint32_t* out, uint32_t k, uint32_t r, const uint32_t* label,
   if (k == 0) return UWC_OK;
   const uint32_t nh = (k + 7) / 8;
   k_noise_perm<<<(nh + 127) / 128, 128, 0, (cudaStream_t)stream>>>(out, k, r, label, key);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -441,16 +489,32 @@ int uwc_noise_rows(const int8_t* src, int rows, int k, int r, const int8_t* E, c
                    void* stream) {
   if (!src || (dst && (!E || !Pn)) || (ecopy_off >= 0 && corr && !E) || lmax < 0) return UWC_ERR_ARG;
   if (rows <= 0 || rows % kNrRows || k <= 0 || k % 16 || (r != 64 && r != 128 && r != 256)) return UWC_ERR_SHAPE;
+  if (Pp && k > 65536) return UWC_ERR_SHAPE;   // the projection's index lists hold 16-bit columns
   if ((((uintptr_t)src) | ((uintptr_t)dst) | ((uintptr_t)Pn) | ((uintptr_t)Pp)) & 15) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (dst && !Pp) {
     const int grid = std::min(rows, uwc_num_sms() * kNaCtasPerSm);
     k_noise_add<<<grid, 256, 0, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, corr, ecopy_off, lmax);
+    uwc_count_launch();
     return uwc_launch_status();
   }
-  const int smem = kNrRows * 256 + kNrRows * r * 4;
-  k_noise_rows<<<rows / kNrRows, 256, smem, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, Pp, corr, corr_off,
-                                                                    ecopy_off, maxabs, lmax);
+  // projection (and the E copy when nothing is noised): the gather kernel; the rows are noised first
+  if (dst) {
+    const int grid = std::min(rows, uwc_num_sms() * kNaCtasPerSm);
+    k_noise_add<<<grid, 256, 0, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, corr, ecopy_off, lmax);
+    uwc_count_launch();
+  }
+  const int smem = (((2 * (r + 1) * 4 + 4 * k) + 15) & ~15) + std::max(k, kPrThreads * 4);
+  if (smem > 227 * 1024) return UWC_ERR_SHAPE;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k_project_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  const int grid = std::min(rows, uwc_num_sms() * kPrCtasPerSm);
+  k_project_rows<<<grid, kPrThreads, smem, (cudaStream_t)stream>>>(src, rows, k, r, Pp, dst ? nullptr : E, corr,
+                                                                   corr_off, ecopy_off, maxabs, lmax);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -461,21 +525,28 @@ int uwc_proj_matrix(const uint32_t* P, int k, int r, int8_t* St, void* stream) {
   const uint64_t n = (uint64_t)r * k;
   const unsigned grid = (unsigned)std::min<uint64_t>(4096, (n + 255) / 256);
   k_proj_matrix<<<grid, 256, 0, (cudaStream_t)stream>>>(P, k, r, St);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
 int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_off, int32_t* maxabs, int lmax,
                   void* stream) {
-  if (!proj || lmax < 0 || (corr && corr_off < 0)) return UWC_ERR_ARG;
+  return uwc_proj_corr_ecopy(proj, rows, r, corr, corr_off, maxabs, lmax, nullptr, -1, stream);
+}
+
+}  // extern "C"
+
+int uwc_proj_corr_ecopy(const int32_t* proj, int rows, int r, int8_t* corr, int corr_off, int32_t* maxabs, int lmax,
+                        const int8_t* E, int ecopy_off, void* stream) {
+  if (!proj || lmax < 0 || (corr && corr_off < 0) || (E && (!corr || ecopy_off < 0))) return UWC_ERR_ARG;
   if (rows <= 0 || r <= 0) return UWC_ERR_SHAPE;
   UWC_CHECK_DEVICE();
   const uint64_t n = (uint64_t)rows * r;
   const unsigned grid = (unsigned)std::min<uint64_t>(4096, (n + 255) / 256);
-  k_proj_corr<<<grid, 256, 0, (cudaStream_t)stream>>>(proj, rows, r, corr, corr_off, maxabs, lmax);
+  k_proj_corr<<<grid, 256, 0, (cudaStream_t)stream>>>(proj, rows, r, corr, corr_off, maxabs, lmax, E, ecopy_off);
+  uwc_count_launch();
   return uwc_launch_status();
 }
-
-}  // extern "C"
 
 // ------------------------------------------------------------------ commitment without allocation
 // Some callers cannot allocate device memory at the moment they commit to a matrix: code running
@@ -499,11 +570,15 @@ constexpr uint64_t kNoAllocWords = 8 * kNoAllocMaxCtas;
 static __device__ __align__(256) uint32_t g_b3_noalloc_scratch[kNoAllocWords];
 
 constexpr int kNoAllocDevices = 64;
-uint32_t* g_noalloc_ptr[kNoAllocDevices];
+std::atomic<uint32_t*> g_noalloc_ptr[kNoAllocDevices];
+std::mutex g_noalloc_mu;
 
 // Device address of the static scratch on the current device. The first call on a device looks
-// it up with cudaGetSymbolAddress (with that device current); in host code the array's name is
-// only a stand-in and must never be passed to a kernel.
+// it up with cudaGetSymbolAddress (with that device current) under a mutex, so host threads that
+// make their first calls at the same time do not race; later calls read the cached address. In
+// host code the array's name is only a stand-in and must never be passed to a kernel. The cache
+// lives as long as the device's CUDA context: after cudaDeviceReset, uwc_b3_noalloc_forget()
+// drops it so the next call looks the address up again.
 int noalloc_scratch(uint32_t** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -511,20 +586,31 @@ int noalloc_scratch(uint32_t** out) {
     return UWC_ERR_CUDA;
   }
   if (dev < 0 || dev >= kNoAllocDevices) return UWC_ERR_DEVICE;
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_b3_noalloc_scratch) != cudaSuccess || !p) {
-      cudaGetLastError();
-      return UWC_ERR_CUDA;
+  uint32_t* cached = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!cached) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    cached = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+    if (!cached) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_b3_noalloc_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return UWC_ERR_CUDA;
+      }
+      cached = static_cast<uint32_t*>(p);
+      g_noalloc_ptr[dev].store(cached, std::memory_order_release);
     }
-    g_noalloc_ptr[dev] = static_cast<uint32_t*>(p);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = cached;
   return UWC_OK;
 }
 }  // namespace
 
 extern "C" uint64_t uwc_b3_noalloc_max_bytes(void) { return kNoAllocMaxBytes; }
+
+extern "C" void uwc_b3_noalloc_forget(void) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (int d = 0; d < kNoAllocDevices; d++) g_noalloc_ptr[d].store(nullptr, std::memory_order_release);
+}
 
 extern "C" int uwc_b3_root_and_seed_noalloc(const void* data, uint64_t nbytes, const uint32_t* key,
                                             const uint32_t* prefix, const uint32_t* salt, uint32_t dim,
@@ -541,6 +627,8 @@ extern "C" int uwc_b3_root_and_seed_noalloc(const void* data, uint64_t nbytes, c
   const uint64_t nch = nbytes / 1024;
   const uint64_t cnt = (nch + kChunksPerCta - 1) / kChunksPerCta;   // <= kNoAllocMaxCtas
   k_b3_chunks<<<(unsigned)cnt, kChunksPerCta, 0, st>>>((const uint8_t*)data, nch, key, scratch, 1u);
+  uwc_count_launch();
   k_b3_reduce<<<1, 512, 0, st>>>(scratch, (uint32_t)cnt, key, nullptr, 1, prefix, salt, dim, root_out, seed_out, 1u);
+  uwc_count_launch();
   return uwc_launch_status();
 }

@@ -187,7 +187,9 @@ int launch_leaves(const float* rows, long long nrows, int D, int T, uint32_t* sc
   const long long n = nrows * nblk;
   k_block_leaves<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(reinterpret_cast<const uint32_t*>(rows), D, nblk,
                                                                nrows, scratch);
+  uwc_count_launch();
   k_sout_leaves<<<(unsigned)((nrows + 63) / 64), 64, 0, st>>>(scratch, nblk, nrows, T, out);
+  uwc_count_launch();
   return uwc_launch_status();
 }
 
@@ -223,5 +225,6 @@ extern "C" int uwc_stage_roots(const float* rows, int B, int T, int D, uint32_t*
   int rc = launch_leaves(rows, nrows, D, T, blk, lv, st);
   if (rc != UWC_OK) return rc;
   k_tree_roots<<<B, 256, 0, st>>>(lv, pp, T, roots);
+  uwc_count_launch();
   return uwc_launch_status();
 }

@@ -20,6 +20,9 @@ int uwc_launch_status();
 // Device address of the library's status word on the current device (cached), or nullptr.
 uint32_t* uwc_status_ptr();
 
+// Adds one to the library's count of kernel launches (uwc_launch_count); called after each launch.
+void uwc_count_launch();
+
 // Number of SMs of the current device (cached).
 int uwc_num_sms();
 
@@ -27,3 +30,11 @@ int uwc_num_sms();
 // `box_rows`, 128-byte swizzle, out-of-bounds reads as zero. Returns UWC_OK or an error code.
 int uwc_make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                      uint32_t box_rows, uint32_t box_cols);
+
+// Library-internal launchers shared between translation units (not part of the C ABI).
+// uwc_noise_uniform that also zeroes a second int32 range (a win counter beside maxabs).
+int uwc_noise_uniform_zero2(int8_t* out, uint64_t nbytes, const uint32_t* label, const uint32_t* key,
+                            int32_t* zero_me, int zero_n, int32_t* zero2, int zero2_n, void* stream);
+// uwc_proj_corr that also copies E (rows x r int8) into corr[li][row][ecopy_off + j] for every limb.
+int uwc_proj_corr_ecopy(const int32_t* proj, int rows, int r, int8_t* corr, int corr_off, int32_t* maxabs, int lmax,
+                        const int8_t* E, int ecopy_off, void* stream);

@@ -19,11 +19,13 @@ _P, _U32, _U64, _I32, _F64 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, 
 _I64, _F32 = ctypes.c_longlong, ctypes.c_float
 SIGNATURES = {
     "uwc_version": (_I32, []),
+    "uwc_launch_count": (_U64, []),
     "uwc_status_string": (ctypes.c_char_p, [_I32]),
     "uwc_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint32), _I32]),
     "uwc_b3_scratch_words": (_U64, [_U64]),
     "uwc_b3_root_and_seed": (_I32, [_P, _U64, _P, _P, _P, _U32, _P, _P, _P, _U64, _P]),
     "uwc_b3_noalloc_max_bytes": (_U64, []),
+    "uwc_b3_noalloc_forget": (None, []),
     "uwc_b3_root_and_seed_noalloc": (_I32, [_P, _U64, _P, _P, _P, _U32, _P, _P, _P]),
     "uwc_noise_uniform": (_I32, [_P, _U64, _P, _P, _P, _I32, _P]),
     "uwc_noise_perm": (_I32, [_P, _U32, _U32, _P, _P, _P]),
@@ -33,6 +35,11 @@ SIGNATURES = {
     "uwc_gemm_workspace_bytes": (_U64, [_I32, _I32, _I32, _I32]),
     "uwc_gemm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32,
                         _P, _U64, _P]),
+    "uwc_mined_block_layout": (_I32, [_I32, _I32, _I32, _P]),
+    "uwc_mined_workspace_layout": (_I32, [_I32, _I32, _I32, _I32, _I32, _I32, _I32, _P]),
+    "uwc_mined_setup_block": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _U64, _P, _U64, _P]),
+    "uwc_mine_attempt": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _I32, _P, _U64, _P]),
+    "uwc_mined_forward": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _P, _I32, _P, _U64, _P]),
     "uwc_quant_act": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "uwc_quant_rows_had": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "uwc_fwht_absmax": (_I32, [_P, _I32, _I32, _I32, _P, _P]),
@@ -92,6 +99,11 @@ def check(rc: int, what: str) -> None:
     if rc in (ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_SCRATCH):
         raise AssertionError(msg)
     raise UWCError(msg)
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process so far (a counter in the library)."""
+    return int(lib().uwc_launch_count())
 
 
 def device_status(clear: bool = True) -> int:

@@ -13,7 +13,7 @@ import torch
 
 from . import det
 from ._lib import check, lib
-from .ops import _count, _p, _stream
+from .ops import _p, _stream
 
 
 def _f32(x: torch.Tensor) -> torch.Tensor:
@@ -28,7 +28,6 @@ def quant_act(x: torch.Tensor, bs: int) -> tuple[torch.Tensor, torch.Tensor]:
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty(m, dtype=torch.float32, device=x.device)
     check(lib().uwc_quant_act(_p(x), m, k, bs, _p(q), _p(s), _stream()), "quant_act")
-    _count()
     return q, s
 
 
@@ -39,7 +38,6 @@ def quant_rows_had(x: torch.Tensor, bs: int, q: torch.Tensor | None = None, scal
     q = torch.empty((m, k), dtype=torch.int8, device=x.device) if q is None else q
     scale = torch.empty(m, dtype=torch.float32, device=x.device) if scale is None else scale
     check(lib().uwc_quant_rows_had(_p(x), m, k, bs, _p(q), _p(scale), _stream()), "quant_rows_had")
-    _count()
     return q, scale
 
 
@@ -49,7 +47,6 @@ def fwht_absmax(x: torch.Tensor, bs: int) -> torch.Tensor:
     m, k = x.shape
     amax = torch.empty(m, dtype=torch.float32, device=x.device)
     check(lib().uwc_fwht_absmax(_p(x), m, k, bs, _p(amax), _stream()), "fwht_absmax")
-    _count()
     return amax
 
 
@@ -61,7 +58,6 @@ def quant_act_global(x: torch.Tensor, bs: int, amax: torch.Tensor) -> tuple[torc
     s = torch.empty(m, dtype=torch.float32, device=x.device)
     check(lib().uwc_quant_act_global(_p(x), m, k, bs, _p(amax.contiguous()), _p(q), _p(s), _stream()),
           "quant_act_global")
-    _count()
     return q, s
 
 
@@ -72,7 +68,6 @@ def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, bs: int) -> tupl
     q = torch.empty((m, k), dtype=torch.int8, device=x.device)
     s = torch.empty(m, dtype=torch.float32, device=x.device)
     check(lib().uwc_rmsnorm_quant(_p(x), _p(w), m, k, bs, float(eps), _p(q), _p(s), _stream()), "rmsnorm_quant")
-    _count()
     return q, s
 
 
@@ -86,7 +81,6 @@ def swiglu_quant(acc: torch.Tensor, s3: torch.Tensor, sw: torch.Tensor, bs: int)
     sc = torch.empty(N, dtype=torch.float32, device=acc.device)
     check(lib().uwc_swiglu_quant(_p(acc), _p(_f32(s3)), _p(_f32(sw)), N, I, bs, _p(q), _p(sc), _stream()),
           "swiglu_quant")
-    _count()
     return q, sc
 
 
@@ -100,7 +94,6 @@ def dequant_residual(acc: torch.Tensor, s: torch.Tensor, sw: torch.Tensor, x: to
     out = torch.empty((N, k), dtype=torch.float32, device=acc.device)
     check(lib().uwc_dequant_residual(_p(acc), _p(_f32(s)), _p(_f32(sw)), _p(x), N, k, _p(out), _stream()),
           "dequant_residual")
-    _count()
     return out
 
 
@@ -115,7 +108,6 @@ def swiglu(acc: torch.Tensor, s3: torch.Tensor, sw: torch.Tensor) -> torch.Tenso
     N, two_i = acc.shape
     h = torch.empty((N, two_i // 2), dtype=torch.float32, device=acc.device)
     check(lib().uwc_swiglu(_p(acc), _p(_f32(s3)), _p(_f32(sw)), N, two_i // 2, _p(h), _stream()), "swiglu")
-    _count()
     return h
 
 
@@ -135,7 +127,6 @@ def qkv_post(acc, s1, sw, qnw, knw, cos, sin, T: int, H: int, Hkv: int, eps: flo
     check(lib().uwc_qkv_post(_p(acc), _p(_f32(s1)), _p(_f32(sw)), _p(qn), _p(kn), _p(_f32(cos)), _p(_f32(sin)),
                              N, T, H, Hkv, float(eps), int(bool(qknorm)), _p(qq), _p(qs), _p(kq), _p(ks), _p(vq),
                              _p(vs), _stream()), "qkv_post")
-    _count()
     return qq, qs, kq, ks, vq, vs
 
 
@@ -202,11 +193,9 @@ def _attn(qq, qs, kc, ks, vc, vs, B, Tq, start, H, Hkv, strides, inv_sqrt_hd, pa
         check(lib().uwc_attention_tc(_p(qq), _p(_f32(qs)), _p(kc), _p(ks), _p(vc), _p(vs), B, Tq, start, H, Hkv,
                                      *strides, float(inv_sqrt_hd), _p(out), _p(ws), ws.numel(), _stream()),
               "attention_tc")
-        _count(7)
         return out
     check(lib().uwc_attention(_p(qq), _p(_f32(qs)), _p(kc), _p(ks), _p(vc), _p(vs), B, Tq, start, H, Hkv, *strides,
                               float(inv_sqrt_hd), _p(out), _stream()), "attention")
-    _count()
     return out
 
 
@@ -241,7 +230,6 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     m, k = x.shape
     out = torch.empty_like(x)
     check(lib().uwc_rmsnorm(_p(x), _p(w), m, k, float(eps), _p(out), _stream()), "rmsnorm")
-    _count()
     return out
 
 
@@ -253,7 +241,6 @@ def logprobs(logits: torch.Tensor, want_lp: bool = True):
     lp = torch.empty_like(lg) if want_lp else None
     tok = torch.empty(m, dtype=torch.int64, device=lg.device)
     check(lib().uwc_logprobs(_p(lg), m, V, _p(lp), _p(tok), _stream()), "logprobs")
-    _count()
     return lp, tok
 
 
@@ -273,7 +260,6 @@ def qkv_post_at(acc, s1, sw, qnw, knw, cos_table, sin_table, pos: torch.Tensor, 
     check(lib().uwc_qkv_post_at(_p(acc), _p(_f32(s1)), _p(_f32(sw)), _p(qn), _p(kn), _p(_f32(cos_table)),
                                 _p(_f32(sin_table)), _p(pos), N, T, H, Hkv, float(eps), int(bool(qknorm)), _p(qq),
                                 _p(qs), _p(kq), _p(ks), _p(vq), _p(vs), _stream()), "qkv_post_at")
-    _count()
     return qq, qs, kq, ks, vq, vs
 
 
@@ -283,7 +269,6 @@ def kv_append(kq, ks, vq, vs, cache: dict, B: int, T: int, pos: torch.Tensor) ->
     Hkv, maxlen = k.shape[1], k.shape[2]
     check(lib().uwc_kv_append(_p(kq.contiguous()), _p(_f32(ks)), _p(vq.contiguous()), _p(_f32(vs)), B, T, Hkv, maxlen,
                               _p(pos), _p(k), _p(sk), _p(v), _p(sv), _stream()), "kv_append")
-    _count()
 
 
 def attention_cache_at(qq, qs, cache: dict, B: int, Tq: int, pos: torch.Tensor, max_start: int, H: int, Hkv: int,
@@ -297,5 +282,4 @@ def attention_cache_at(qq, qs, cache: dict, B: int, Tq: int, pos: torch.Tensor, 
     strides = (Hkv * maxlen * 128, 128, maxlen * 128, Hkv * maxlen, 1, maxlen)
     check(lib().uwc_attention_at(_p(qq), _p(_f32(qs)), _p(k), _p(sk), _p(v), _p(sv), B, Tq, _p(pos), max_start, H,
                                  Hkv, *strides, float(inv_sqrt_hd_f32), _p(out), _stream()), "attention_at")
-    _count()
     return out

@@ -32,15 +32,23 @@ ARCHS = {"qwen3": ARCH_QWEN3, "llama": ARCH_LLAMA, "mistral": ARCH_LLAMA}
 
 
 def llama3_inv_freq(inv: np.ndarray, factor: float, low: float, high: float, orig: int) -> np.ndarray:
-    """Llama 3.1+ rotary frequency scaling, in float64 (qwen3.py:38-47): long wavelengths divided
-    by `factor`, short ones kept, a linear blend in between."""
-    low_wl, high_wl = orig / low, orig / high
-    wl = 2 * np.pi / inv
-    scaled = np.where(wl > low_wl, inv / factor, inv)
-    blend = (orig / wl - low) / (high - low)
-    mid = (1 - blend) * scaled / factor + blend * scaled
-    in_mid = (wl >= high_wl) & (wl <= low_wl)
-    return np.where(in_mid, mid, scaled)
+    """Llama 3.1+ rotary frequency scaling (the published rule transformers implements, which
+    runtime/detrt/qwen3.py:38-47 pins): for each inverse frequency f with wavelength w = 2 pi / f,
+    w above orig / low -> f / factor; w below orig / high -> f; in between the blend
+    ((1 - s) f) / factor + s f with s = (orig / w - low) / (high - low). Every value is one float64
+    expression evaluated in that order, so the table is the same bit for bit."""
+    out = np.empty_like(inv)
+    long_w, short_w = orig / low, orig / high
+    for i, f in enumerate(inv.tolist()):
+        w = 2 * np.pi / f
+        if w > long_w:
+            out[i] = f / factor
+        elif w < short_w:
+            out[i] = f
+        else:
+            s = (orig / w - low) / (high - low)
+            out[i] = (1 - s) * f / factor + s * f
+    return out
 
 
 def rope_table(theta: float, head_dim: int, max_pos: int = 8192, scaling: dict | None = None):
@@ -56,19 +64,26 @@ def rope_table(theta: float, head_dim: int, max_pos: int = 8192, scaling: dict |
     return cos, sin, hashlib.sha256(cos.tobytes() + sin.tobytes()).hexdigest()
 
 
+LLAMA3_SCALING_KEYS = ("factor", "low_freq_factor", "high_freq_factor", "original_max_position_embeddings")
+
+
 def rope_config(cfg) -> tuple[float, dict | None]:
-    """(theta, Llama 3 scaling or None) of a transformers config (qwen3.py:133-148)."""
-    rp = dict(getattr(cfg, "rope_parameters", None) or {})
-    rs = dict(getattr(cfg, "rope_scaling", None) or {})
-    theta = getattr(cfg, "rope_theta", None) or rp.get("rope_theta") or 1e6
-    kind = rp.get("rope_type") or rs.get("rope_type") or rs.get("type") or "default"
+    """(rope theta, Llama 3 scaling parameters or None) of a transformers config. transformers 5
+    keeps theta and the rope type together in `rope_parameters`; transformers 4 has `rope_theta`
+    and an optional `rope_scaling` dict (type under "rope_type" or "type"). Defaults: theta 1e6,
+    no scaling. Scalings other than llama3 are refused (qwen3.py:133-148 accepts the same set)."""
+    v5 = dict(getattr(cfg, "rope_parameters", None) or {})
+    v4 = dict(getattr(cfg, "rope_scaling", None) or {})
+    theta = float(getattr(cfg, "rope_theta", None) or v5.get("rope_theta") or 1e6)
+    if v5.get("rope_type"):
+        kind, params = v5["rope_type"], v5
+    else:
+        kind, params = v4.get("rope_type") or v4.get("type") or "default", v4
     if kind == "default":
-        return float(theta), None
-    if kind != "llama3":
-        raise ValueError(f"rope scaling {kind!r} is not supported by the deterministic runtime")
-    src = rp if rp.get("rope_type") == "llama3" else rs
-    return float(theta), {k: src[k] for k in ("factor", "low_freq_factor", "high_freq_factor",
-                                              "original_max_position_embeddings")}
+        return theta, None
+    if kind == "llama3":
+        return theta, {key: params[key] for key in LLAMA3_SCALING_KEYS}
+    raise ValueError(f"unsupported rotary scaling {kind!r}: the deterministic forward knows the default and llama3")
 
 
 class Linear:
@@ -288,13 +303,13 @@ class DecodeGraph:
         model._decode_step(self.tok, self.cache, self.pos, self.max_start)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
-        c0 = ops.LAUNCHES
+        c0 = ops.launches()
         with torch.cuda.graph(self.graph):
             self.h, self.nxt = model._decode_step(self.tok, self.cache, self.pos, self.max_start)
             self.tok.copy_(self.nxt)
             self.pos.add_(1)
-        self.launches_per_step = ops.LAUNCHES - c0   # this library's kernels in one replay
-        ops.LAUNCHES = c0                            # captured, not launched
+        self.launches_per_step = ops.launches() - c0   # this library's kernels in one replay
+        ops.note_graph(-self.launches_per_step)        # captured, not launched
 
     @torch.no_grad()
     def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
@@ -314,7 +329,7 @@ class DecodeGraph:
             self.graph.replay()
             toks.append(self.nxt.clone())
             hs.append(self.h.clone())
-        ops._count(self.launches_per_step * (n_new - 1))
+        ops.note_graph(self.launches_per_step * (n_new - 1))
         return torch.stack(toks, 1), torch.stack(hs, 1)
 
     def run(self, prompt: torch.Tensor, n_new: int):

@@ -1,13 +1,21 @@
-"""Integer linear layers for Hugging Face Qwen3 models, mined on B200 (miner/ampere/uwc_ampere/model.py).
+"""Mined integer linear layers for Hugging Face Qwen3 models on B200 (the reference's
+miner/ampere/uwc_ampere/model.py surface: MinedLinear, convert_qwen3, hadamard, rotate, quant_rows).
 
-Same quantization and modes as the reference module, so provider code switches by import:
-  weights      per output channel, W' = W H (H: block Walsh-Hadamard, orthonormal), s_w = max|W'| / 64
-  activations  per token, x' = x H, s_x = max|x'| / 64 (ops.quant_rows_had: rotate + quantize fused)
-  y = (q(x') q(W')^T) * s_x * s_w, bf16 out
+Quantization (the reference's scheme, model.py:30-52): per output channel of the weight and per
+token of the activation, a block Walsh-Hadamard rotation of size bs (the largest power of two
+dividing k, capped at `hadamard_block`), then symmetric int8 in [-64, 64] with scale max|x'| / 64.
+Weights and activations both go through this library's fused rotate + quantize kernel
+(ops.quant_rows_had) from bf16 rows, so a layer's int8 operands are produced the same way on both
+sides; the output is y = RNE_bf16((float(q_x q_W^T) * s_x) * s_w).
 
-Modes: "bf16" (original weights), "int" (the integer math through cuBLAS int8: the quality and
-parity reference), "plain" (this library's tcgen05 GEMM with the bf16 dequant fused, no mining),
-"mined" (MinedWeight.forward: commit, noise, hashed GEMM, exact denoise; bit-identical to "int").
+Modes:
+  "bf16"   the original bf16 weights (F.linear), no integer math: the quality baseline;
+  "int"    the exact int32 product on this library's GEMM, the dequant as separate torch
+           elementwise ops: the parity baseline of the two below;
+  "plain"  the same product with the dequant fused into the GEMM epilogue (bf16 out);
+  "mined"  MinedWeight.forward: commit, noise, hashed GEMM, exact denoise, fused dequant. Layers
+           whose shape Pearl does not accept for mining (see `mineable`) run "plain".
+Every integer mode sends every shape through ops.gemm; the three give bit-identical outputs.
 """
 from __future__ import annotations
 
@@ -20,169 +28,187 @@ import torch.nn.functional as F
 from . import ops
 
 QMAX = 64
+ROW_CHUNK = 8192   # weight rows quantized per kernel call (bounds the bf16 staging copy)
 
 
 def hadamard(n: int, device, dtype=torch.float32) -> torch.Tensor:
-    """The n x n Sylvester Hadamard matrix scaled to be orthonormal (model.py:30-36)."""
+    """The orthonormal n x n Sylvester Hadamard matrix: H[i, j] = (-1)^popcount(i & j) / sqrt(n)."""
     assert n > 0 and n & (n - 1) == 0
-    H = torch.ones(1, 1)
-    while H.shape[0] < n:
-        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)], 0)
-    return (H / math.sqrt(n)).to(device=device, dtype=dtype)
+    idx = torch.arange(n)
+    parity = torch.zeros(n, n, dtype=torch.int64)
+    b = idx[:, None] & idx[None, :]
+    while bool(b.any()):
+        parity ^= b & 1
+        b = b >> 1
+    return ((1 - 2 * parity).to(torch.float64) / math.sqrt(n)).to(device=device, dtype=dtype)
 
 
 def rotate(x: torch.Tensor, H: torch.Tensor | None) -> torch.Tensor:
-    """x times the block-diagonal H along the last dim (model.py:39-44)."""
+    """x multiplied by the block-diagonal matrix diag(H, H, ...) along its last dimension."""
     if H is None:
         return x
     bs = H.shape[0]
-    shp = x.shape
-    return (x.reshape(*shp[:-1], shp[-1] // bs, bs).to(H.dtype) @ H).reshape(shp)
+    blocks = x.to(H.dtype).unflatten(-1, (x.shape[-1] // bs, bs))
+    return torch.matmul(blocks, H).flatten(-2)
 
 
 def quant_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Symmetric per-row quantization to int8 values in [-64, 64] (model.py:47-52)."""
+    """Symmetric int8 per row: q = round_half_even(x / s) clamped to [-64, 64], s = max|x| / 64
+    (at least 1e-8 / 64). Returns (q int8, s float32 per row)."""
     xf = x.float()
-    s = xf.abs().amax(dim=-1, keepdim=True).clamp_min(1e-8) / QMAX
-    q = torch.round(xf / s).clamp_(-QMAX, QMAX).to(torch.int8)
-    return q, s.squeeze(-1)
+    s = torch.clamp(xf.abs().amax(dim=-1), min=1e-8) / QMAX
+    q = torch.clamp(torch.round(xf / s.unsqueeze(-1)), -QMAX, QMAX).to(torch.int8)
+    return q, s
+
+
+def _block_size(k: int, hadamard_block: int) -> int:
+    return min(hadamard_block, k & -k) if hadamard_block else 0
 
 
 class MinedLinear(nn.Module):
-    """One or more nn.Linear layers that share an input, fused along n (model.py:55-141)."""
+    """nn.Linear layers that read the same input, concatenated along the output dimension and
+    computed as one integer GEMM (one mined weight when mode is "mined")."""
 
     def __init__(self, linears: list[nn.Linear], device, mode: str = "mined", hadamard_block: int = 512,
                  r: int = 128, cfg: str | None = None):
         super().__init__()
         if mode not in ("bf16", "int", "plain", "mined"):
             raise ValueError(f"mode {mode!r}")
-        self.mode = mode
-        self.splits = [l.out_features for l in linears]
-        W = torch.cat([l.weight.detach() for l in linears], 0)
-        bias = [l.bias for l in linears]
-        self.bias = None if all(b is None for b in bias) else torch.cat(
-            [b.detach() if b is not None else torch.zeros(l.out_features) for b, l in zip(bias, linears)]).to(
-                device, torch.bfloat16)
-        self.n, self.k = W.shape
-        self.H = hadamard(min(hadamard_block, self.k & -self.k), device) if hadamard_block else None
+        self.mode, self.r, self.cfg = mode, r, cfg
+        self.splits = [lin.out_features for lin in linears]
+        self.k = linears[0].in_features
+        self.n = sum(self.splits)
+        self.bs = _block_size(self.k, hadamard_block)
+        self.H = hadamard(self.bs, device) if self.bs > 1 else None
+        biases = [lin.bias.detach() if lin.bias is not None else None for lin in linears]
+        self.bias = None
+        if any(b is not None for b in biases):
+            self.bias = torch.cat([b if b is not None else torch.zeros(n) for b, n in zip(biases, self.splits)]).to(
+                device=device, dtype=torch.bfloat16)
         if mode == "bf16":
-            self.W = W.to(device=device, dtype=torch.bfloat16)
+            self.W = torch.cat([lin.weight.detach() for lin in linears]).to(device=device, dtype=torch.bfloat16)
         else:
-            # row chunks, so a huge layer (lm_head) never needs a full float32 copy on the GPU
-            qs, ss = [], []
-            for s0 in range(0, self.n, 16384):
-                q, sc = quant_rows(rotate(W[s0:s0 + 16384].to(device=device, dtype=torch.float32), self.H))
-                qs.append(q)
-                ss.append(sc)
-            self.Wq, self.sw = torch.cat(qs).contiguous(), torch.cat(ss).contiguous()
-        del W
-        self.r = r
-        self.cfg = cfg or ops.DEFAULT_CFG
+            self.Wq = torch.empty((self.n, self.k), dtype=torch.int8, device=device)
+            self.sw = torch.empty(self.n, dtype=torch.float32, device=device)
+            row = 0
+            for lin in linears:
+                for r0 in range(0, lin.out_features, ROW_CHUNK):
+                    w = lin.weight.detach()[r0:r0 + ROW_CHUNK].to(device=device, dtype=torch.bfloat16).contiguous()
+                    ops.quant_rows_had(w, self.bs, q=self.Wq[row:row + w.shape[0]], scale=self.sw[row:row + w.shape[0]])
+                    row += w.shape[0]
         self.mw: ops.MinedWeight | None = None
-        self.hashed_macs = 0   # m_pad * n * k summed over mined calls
-        self.useful_macs = 0   # m * n * k summed over calls
+        self.hashed_macs = 0   # padded rows x n x k over the calls that took the mined path
+        self.useful_macs = 0   # rows x n x k over all calls
 
     @property
     def mineable(self) -> bool:
-        """Pearl's shape rules for a mined weight (model.py:95-98) and this kernel's tile alignment."""
+        """Pearl's shape rules for a mined weight (k at least max(1024, 16 r), at most 4 r^2, a
+        multiple of r; miner/ampere/uwc_ampere/model.py:95-98) and this kernel's 64-alignment."""
         k, n, r = self.k, self.n, self.r
-        return k >= max(1024, 16 * r) and k % r == 0 and k % 64 == 0 and k <= 4 * r * r and n % 64 == 0
+        return max(1024, 16 * r) <= k <= 4 * r * r and k % r == 0 and k % 64 == 0 and n % 64 == 0
 
     def setup_block(self, job_key_for_k, bound_for_k):
-        """job_key_for_k(k) -> 32-byte job key; bound_for_k(k) -> 8 target words (model.py:100-107)."""
+        """Prepare the mined weight for a block: job_key_for_k(k) -> 32-byte key, bound_for_k(k) ->
+        8 target words. A no-op unless this layer mines."""
         if self.mode != "mined" or not self.mineable:
             return
         if self.mw is None:
             self.mw = ops.MinedWeight(Bt=self.Wq, b_scale=self.sw, r=self.r)
         self.mw.setup_block(job_key_for_k(self.k), bound_for_k(self.k))
 
-    def _int_forward(self, xq, sx):
-        y = torch._int_mm(xq, self.Wq.t()).float() * sx[:, None] * self.sw[None, :]
-        return y.to(torch.bfloat16)
+    def _integer(self, xq: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
+        m = xq.shape[0]
+        if self.mode == "mined" and self.mw is not None:
+            self.hashed_macs += m * self.n * self.k
+            return self.mw.forward(xq, sx)
+        if self.n % 8 == 0 and self.mode != "int":        # "plain", and "mined" layers that do not mine
+            y = torch.empty((m, self.n), dtype=torch.bfloat16, device=xq.device)
+            ops.gemm(xq, self.Wq, a_scale=sx, b_scale=self.sw, out=y, out_mode=ops.OUT_BF16)
+            return y
+        acc = torch.empty((m, self.n), dtype=torch.int32, device=xq.device)
+        ops.gemm(xq, self.Wq, out=acc, out_mode=ops.OUT_I32)
+        return ((acc.float() * sx.unsqueeze(1)) * self.sw.unsqueeze(0)).to(torch.bfloat16)
 
     @torch.compiler.disable
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        shp = x.shape
-        x2 = x.reshape(-1, self.k)
-        m = x2.shape[0]
+        lead = x.shape[:-1]
+        xb = x.reshape(-1, self.k).to(torch.bfloat16)
+        m = xb.shape[0]
         if self.mode == "bf16":
-            y = F.linear(x2.to(torch.bfloat16), self.W)
+            y = F.linear(xb, self.W)
         else:
-            bs = self.H.shape[0] if self.H is not None else 0
-            kernel_path = self.mode in ("mined", "plain") and self.mineable
-            mp = -(-m // ops.BM) * ops.BM if kernel_path else m
-            xb = x2.to(torch.bfloat16)
-            if mp != m:
-                xb = F.pad(xb, (0, 0, 0, mp - m))
-            xq, sx = ops.quant_rows_had(xb.contiguous(), bs)          # fused rotate + quantize
-            if self.mode == "mined" and self.mineable:
-                y = self.mw.forward(xq, sx)[:m]
-                self.hashed_macs += mp * self.n * self.k
-            elif self.mode == "plain" and self.mineable:
-                y = torch.empty((mp, self.n), dtype=torch.bfloat16, device=xq.device)
-                ops.gemm(xq, self.Wq, a_scale=sx, b_scale=self.sw, out=y, out_mode=ops.OUT_BF16)
-                y = y[:m]
-            elif m < 17:                                              # cuBLAS int8 needs m > 16
-                y = (xq.float() @ self.Wq.float().t() * sx[:, None] * self.sw[None, :]).to(torch.bfloat16)
-            else:
-                y = self._int_forward(xq.contiguous(), sx)
+            mined = self.mode == "mined" and self.mw is not None
+            rows = -(-m // 64) * 64 if mined else m     # the mined GEMM works on 64-row multiples
+            if rows != m:
+                xb = torch.cat([xb, xb.new_zeros(rows - m, self.k)])
+            xq, sx = ops.quant_rows_had(xb.contiguous(), self.bs)
+            y = self._integer(xq, sx)[:m]
         self.useful_macs += m * self.n * self.k
         if self.bias is not None:
             y = y + self.bias
-        return y.reshape(*shp[:-1], self.n)
+        return y.reshape(*lead, self.n)
 
 
-class _Slice(nn.Module):
-    """k_proj / v_proj / up_proj stand-in: its slice of the fused output the head layer computed."""
+class _SharedInput:
+    """One fused MinedLinear serving the stand-ins of several projections that read the same input
+    (q/k/v, or gate/up). A stand-in called with a new input tensor runs the fused layer; the others
+    then take their parts of that result. The input is held (and compared by identity) only until
+    every stand-in has taken its part, so no stale result can match a later tensor."""
 
-    def __init__(self, head: "_FusedHead", idx: int):
-        super().__init__()
-        self.head, self.idx = head, idx
+    def __init__(self, fused: MinedLinear):
+        self.fused = fused
+        self.x = None
+        self.parts: tuple[torch.Tensor, ...] = ()
+        self.waiting: set[int] = set()
 
-    @torch.compiler.disable
-    def forward(self, x):
-        assert self.head.last_input is x, "fused layers must be called with the same input tensor, in order"
-        y = self.head.outputs[self.idx]
-        if self.idx == len(self.head.outputs) - 1:    # the last consumer drops the references
-            self.head.outputs = self.head.last_input = None
+    def part(self, x: torch.Tensor, idx: int) -> torch.Tensor:
+        if x is not self.x or idx not in self.waiting:
+            self.parts = torch.split(self.fused(x), self.fused.splits, dim=-1)
+            self.x, self.waiting = x, set(range(len(self.parts)))
+        self.waiting.discard(idx)
+        y = self.parts[idx]
+        if not self.waiting:
+            self.x, self.parts = None, ()
         return y
 
 
-class _FusedHead(nn.Module):
-    def __init__(self, ml: MinedLinear):
+class _Part(nn.Module):
+    """Stand-in for one of the fused projections."""
+
+    def __init__(self, shared: _SharedInput, idx: int):
         super().__init__()
-        self.ml = ml
-        self.last_input = None
-        self.outputs = None
+        self.shared, self.idx = shared, idx
+        if idx == 0:
+            self.fused = shared.fused       # registered once, so .to() / state_dict see it
 
     @torch.compiler.disable
     def forward(self, x):
-        y = self.ml(x)
-        self.last_input = x
-        self.outputs = torch.split(y, self.ml.splits, dim=-1)
-        return self.outputs[0]
+        return self.shared.part(x, self.idx)
+
+
+def _fuse(owner: nn.Module, names: list[str], device, mode, hadamard_block, cfg) -> MinedLinear:
+    ml = MinedLinear([getattr(owner, nm) for nm in names], device, mode, hadamard_block, cfg=cfg)
+    if len(names) == 1:
+        setattr(owner, names[0], ml)
+        return ml
+    shared = _SharedInput(ml)
+    for i, nm in enumerate(names):
+        setattr(owner, nm, _Part(shared, i))
+    return ml
 
 
 def convert_qwen3(model, device, mode="mined", hadamard_block=512, mine_lm_head=True, cfg=None) -> list[MinedLinear]:
-    """Swap every linear of a HF Qwen3 model (q/k/v fused, gate/up fused); returns the MinedLinears
-    (model.py:171-197)."""
-    mls = []
-    base = model.model if hasattr(model, "model") else model
-    for layer in base.layers:
-        at, mlp = layer.self_attn, layer.mlp
-        qkv = MinedLinear([at.q_proj, at.k_proj, at.v_proj], device, mode, hadamard_block, cfg=cfg)
-        head = _FusedHead(qkv)
-        at.q_proj, at.k_proj, at.v_proj = head, _Slice(head, 1), _Slice(head, 2)
-        o = MinedLinear([at.o_proj], device, mode, hadamard_block, cfg=cfg)
-        at.o_proj = o
-        gu = MinedLinear([mlp.gate_proj, mlp.up_proj], device, mode, hadamard_block, cfg=cfg)
-        head2 = _FusedHead(gu)
-        mlp.gate_proj, mlp.up_proj = head2, _Slice(head2, 1)
-        d = MinedLinear([mlp.down_proj], device, mode, hadamard_block, cfg=cfg)
-        mlp.down_proj = d
-        mls += [qkv, o, gu, d]
+    """Replace every linear layer of a Hugging Face Qwen3 model by MinedLinear: q/k/v fused into one,
+    o alone, gate/up fused, down alone, and the LM head (if mine_lm_head). Returns the new layers,
+    four per decoder layer in that order, then the head."""
+    layers = []
+    body = getattr(model, "model", model)
+    for block in body.layers:
+        attn, mlp = block.self_attn, block.mlp
+        layers.append(_fuse(attn, ["q_proj", "k_proj", "v_proj"], device, mode, hadamard_block, cfg))
+        layers.append(_fuse(attn, ["o_proj"], device, mode, hadamard_block, cfg))
+        layers.append(_fuse(mlp, ["gate_proj", "up_proj"], device, mode, hadamard_block, cfg))
+        layers.append(_fuse(mlp, ["down_proj"], device, mode, hadamard_block, cfg))
     if mine_lm_head and hasattr(model, "lm_head"):
-        lm = MinedLinear([model.lm_head], device, mode, hadamard_block, cfg=cfg)
-        model.lm_head = lm
-        mls.append(lm)
-    return mls
+        layers.append(_fuse(model, ["lm_head"], device, mode, hadamard_block, cfg))
+    return layers

@@ -10,14 +10,15 @@ Differences from the reference, all additive:
   * one tcgen05 kernel family replaces the mma.sync tile configs: `cfg` is accepted and ignored,
     CONFIGS / DEFAULT_CFG keep their names for callers that read them;
   * OUT_F32 (the detrt dequant epilogue) joins OUT_NONE / OUT_I32 / OUT_BF16;
-  * the rank-r projections default to the tensor-core path (`project`), which the reference
-    offers as UWC_PROJ_GEMM; set UWC_PROJ_GEMM=0 for the shared-memory-atomics path. Both are
-    bit-identical (tests/test_gpu_mined.py checks it, as the reference's test_proj_gemm.py does).
+  * MinedWeight's per-block and per-call sequences are single library calls
+    (uwc_mined_setup_block, uwc_mined_forward, uwc_mine_attempt) over a block buffer and a
+    shared workspace; the rank-r projections run on the tensor cores (the reference's opt-in
+    UWC_PROJ_GEMM path). noise_rows with a projection permutation runs a gather kernel instead;
+    both give the same integers (tests/test_gpu_mined.py, as the reference's test_proj_gemm.py).
 """
 from __future__ import annotations
 
-import os
-from dataclasses import dataclass, field
+import ctypes
 
 import numpy as np
 import torch
@@ -32,13 +33,20 @@ FLAG_HASH, FLAG_DENOISE = 1, 2
 OUT_NONE, OUT_I32, OUT_BF16, OUT_F32 = 0, 1, 2, 3
 CONFIGS = {"sm100": (256, 3, 1)}
 DEFAULT_CFG = "sm100"
-PROJ_GEMM = os.environ.get("UWC_PROJ_GEMM", "1") != "0"
-LAUNCHES = 0   # kernels this module has launched (all of them this library's own)
+
+_REPLAYED = 0   # kernels run by graph replays, net of the ones recorded (captured, not run) by captures
 
 
-def _count(n: int = 1) -> None:
-    global LAUNCHES
-    LAUNCHES += n
+def launches() -> int:
+    """Kernels of this library launched in this process: the library's own counter of host-side
+    launches, adjusted by note_graph() for kernels captured into CUDA graphs and run by replays."""
+    return _lib.launch_count() + _REPLAYED
+
+
+def note_graph(kernels: int) -> None:
+    """Adjust launches() by `kernels`: minus a capture's kernels (recorded, not run), plus a replay's."""
+    global _REPLAYED
+    _REPLAYED += kernels
 
 
 def limbs_for(k: int) -> int:
@@ -113,10 +121,6 @@ def b3_root_and_seed(data: torch.Tensor, key: torch.Tensor, *, prefix=None, salt
         scratch = torch.empty(need, dtype=torch.int32, device=data.device)
     check(lib().uwc_b3_root_and_seed(_p(data), nbytes, _p(key), _p(prefix), _p(salt), dim, _p(root_out),
                                      _p(seed_out), _p(scratch), scratch.numel(), _stream()), "b3_root_and_seed")
-    cnt, launches = -(-(nbytes // 1024) // CHUNKS_PER_CTA), 2
-    while cnt > 1024:
-        cnt, launches = -(-cnt // 1024), launches + 1
-    _count(launches)
     return scratch
 
 
@@ -124,12 +128,10 @@ def b3_root_and_seed(data: torch.Tensor, key: torch.Tensor, *, prefix=None, salt
 def noise_uniform(out: torch.Tensor, label: torch.Tensor, key: torch.Tensor, zero_me=None, zero_n: int = 0):
     check(lib().uwc_noise_uniform(_p(out), _nbytes(out), _p(label), _p(key), _p(zero_me), zero_n, _stream()),
           "noise_uniform")
-    _count()
 
 
 def noise_perm(out: torch.Tensor, k: int, r: int, label: torch.Tensor, key: torch.Tensor):
     check(lib().uwc_noise_perm(_p(out), k, r, _p(label), _p(key), _stream()), "noise_perm")
-    _count()
 
 
 def noise_rows(src, rows, k, r, *, E=None, Pn=None, dst=None, Pp=None, corr=None, corr_off=-1, ecopy_off=-1,
@@ -138,7 +140,6 @@ def noise_rows(src, rows, k, r, *, E=None, Pn=None, dst=None, Pp=None, corr=None
     assert rows % 8 == 0 and k % 4 == 0
     check(lib().uwc_noise_rows(_p(src), rows, k, r, _p(E), _p(Pn), _p(dst), _p(Pp), _p(corr), corr_off, ecopy_off,
                                _p(maxabs), lmax, _stream()), "noise_rows")
-    _count()
 
 
 # ------------------------------------------------------------------ projections as int8 GEMMs
@@ -147,7 +148,6 @@ def proj_matrix(P: torch.Tensor, k: int, r: int, St: torch.Tensor | None = None)
     if St is None:
         St = torch.empty((r, k), dtype=torch.int8, device=P.device)
     check(lib().uwc_proj_matrix(_p(P), k, r, _p(St), _stream()), "proj_matrix")
-    _count()
     return St
 
 
@@ -161,7 +161,6 @@ def project(src: torch.Tensor, St: torch.Tensor, corr: torch.Tensor, corr_off: i
     gemm(src, St, out=proj, out_mode=OUT_I32)
     check(lib().uwc_proj_corr(_p(proj), rows, r, _p(corr), corr_off, _p(maxabs), corr.shape[0], _stream()),
           "proj_corr")
-    _count()
 
 
 # ------------------------------------------------------------------ GEMM
@@ -176,7 +175,6 @@ def quant_rows_had(x: torch.Tensor, bs: int, q: torch.Tensor | None = None, scal
     q = torch.empty((m, k), dtype=torch.int8, device=x.device) if q is None else q
     scale = torch.empty(m, dtype=torch.float32, device=x.device) if scale is None else scale
     check(lib().uwc_quant_rows_had(_p(x), m, k, bs, _p(q), _p(scale), _stream()), "quant_rows_had")
-    _count()
     return q, scale
 
 
@@ -207,173 +205,149 @@ def gemm(A, B, *, r=128, flags=0, corrA=None, corrB=None, maxabs=None, key=None,
     check(lib().uwc_gemm(_p(A), _p(B), m, n, k, r, flags, _p(corrA), _p(corrB), _p(maxabs), lmax, _p(key), _p(target),
                          _p(wins), max_wins, _p(a_scale), _p(b_scale), _p(out), out_mode, _p(ws),
                          0 if ws is None else ws.numel(), _stream()), "gemm")
-    _count()
 
 
 # ------------------------------------------------------------------ one mined linear layer
-_WORKSPACE: dict = {}
+MB_CONSTS, MB_EBRT, MB_PB, MB_SBT, MB_BPEBT, MB_BYTES = range(6)
+MW_A_SEED, MW_MAXABS, MW_EAL, MW_PA, MW_APEA, MW_B3, MW_GEMM, MW_SAT, MW_CORRA, MW_CORRB, MW_PROJA, MW_PROJB, \
+    MW_BYTES = range(13)
+_SHARED_WS: dict = {}   # device -> one uint8 workspace, grown on demand, shared by every weight
 
 
-@dataclass
+def _offsets(fn, *args, count: int) -> list[int]:
+    arr = (ctypes.c_uint64 * (count + 1))()
+    check(fn(*args, arr), fn.__name__)
+    return list(arr)
+
+
+def shared_workspace(device, nbytes: int) -> torch.Tensor:
+    """The per-device call workspace of MinedWeight: layers run one after another on one stream, so
+    they share it (as the reference shares its per-(device, m, k, r) buffers, ops.py:258-277)."""
+    key = str(torch.device(device))
+    ws = _SHARED_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = _SHARED_WS[key] = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws
+
+
 class MinedWeight:
-    """A weight B^T (n x k int8, values in [-64, 64]) prepared for mining under one block template.
+    """B^T (n x k int8, values in [-64, 64]) prepared for mining under one block template, with the
+    reference's call surface (ops.py:205-371): setup_block() once per block key, then forward() /
+    noise_mine() per call and winners() to read the win records.
 
-    setup_block() runs once per (block header, k); forward() runs per call and needs no host sync
-    (ops.py:205-371)."""
-    Bt: torch.Tensor            # n x k int8 (GPU, or pinned CPU: only BpEBt lives on the GPU)
-    b_scale: torch.Tensor       # n float32, on the mining GPU
-    r: int = 128
-    max_wins: int = 64
-    # per block
-    job_key: torch.Tensor | None = None
-    b_seed: torch.Tensor | None = None
-    target: torch.Tensor | None = None
-    BpEBt: torch.Tensor | None = None
-    PB: torch.Tensor | None = None
-    EBRt: torch.Tensor | None = None
-    corrB: torch.Tensor | None = None
-    SBt: torch.Tensor | None = None
-    _bufs: dict = field(default_factory=dict)
+    The block state lives in one device buffer written by uwc_mined_setup_block; a call is a single
+    library call (uwc_mined_forward / uwc_mine_attempt) over a workspace shared by every weight on
+    the device. Attribute views (BpEBt, target, ...) and buffers(m) expose the parts by the
+    library's layout, for tests and benchmarks."""
 
-    @property
-    def n(self):
-        return self.Bt.shape[0]
+    def __init__(self, Bt: torch.Tensor, b_scale: torch.Tensor, r: int = 128, max_wins: int = 64):
+        self.Bt, self.b_scale, self.r, self.max_wins = Bt, b_scale, r, max_wins
+        self.block: torch.Tensor | None = None
+        self._wins: dict[int, torch.Tensor] = {}
+        self._last_ws: dict[int, tuple[torch.Tensor, list[int]]] = {}
 
-    @property
-    def k(self):
-        return self.Bt.shape[1]
+    n = property(lambda self: self.Bt.shape[0])
+    k = property(lambda self: self.Bt.shape[1])
+    device = property(lambda self: self.b_scale.device)
 
-    @property
-    def device(self):
-        return self.b_scale.device
-
-    def setup_block(self, job_key: bytes, target_words: np.ndarray):
-        dev = self.device
-        n, k, r = self.n, self.k, self.r
+    # -------------------------------------------------------- per block
+    def setup_block(self, job_key: bytes, target_words) -> None:
+        n, k, r, dev = self.n, self.k, self.r, self.device
+        assert len(job_key) == 32
+        self._bo = _offsets(lib().uwc_mined_block_layout, n, k, r, count=MB_BYTES)
+        if self.block is None:
+            self.block = torch.empty(self._bo[MB_BYTES], dtype=torch.uint8, device=dev)
         Bt = self.Bt if self.Bt.device == dev else self.Bt.to(dev, non_blocking=True)
-        self.job_key = words(job_key, dev)
-        self.target = torch.from_numpy(np.asarray(target_words).astype(np.uint32).view(np.int32).copy()).to(dev)
-        self.b_seed = torch.empty(8, dtype=torch.int32, device=dev)
-        c = consts(dev)
-        b3_root_and_seed(Bt.view(-1), self.job_key, prefix=self.job_key, salt=c["SALT_B"], dim=n,
-                         seed_out=self.b_seed)
-        self.EBRt = torch.empty((n, r), dtype=torch.int8, device=dev)
-        noise_uniform(self.EBRt, c["LABEL_B"], self.b_seed)
-        self.PB = torch.empty(k, dtype=torch.int32, device=dev)
-        noise_perm(self.PB, k, r, c["LABEL_B"], self.b_seed)
-        if self.BpEBt is None:
-            self.BpEBt = torch.empty((n, k), dtype=torch.int8, device=dev)
-            self.corrB = torch.zeros((limbs_for(k), n, 2 * r), dtype=torch.int8, device=dev)
-        noise_rows(Bt, n, k, r, E=self.EBRt, Pn=self.PB, dst=self.BpEBt, corr=self.corrB, ecopy_off=0)
-        self.SBt = proj_matrix(self.PB, k, r)
+        scratch = shared_workspace(dev, 4 * b3_scratch_words(n * k))
+        key = (ctypes.c_uint8 * 32).from_buffer_copy(job_key)
+        tgt = (ctypes.c_uint32 * 8)(*[int(x) for x in np.asarray(target_words, dtype=np.uint64)])
+        check(lib().uwc_mined_setup_block(_p(Bt.contiguous()), n, k, r, key, tgt, _p(self.block), self.block.numel(),
+                                          _p(scratch), scratch.numel(), _stream()), "mined_setup_block")
         del Bt
 
-    def _buf(self, m: int):
-        """Per-call buffers. The large ones are a workspace shared by every weight with the same
-        (m, k, r): layers run one after another on one stream. Win records are per weight."""
-        dev, k, r = self.device, self.k, self.r
-        key = (str(dev), m, k, r)
-        ws = _WORKSPACE.get(key)
-        if ws is None:
-            n_max = max(m, 1)
-            ws = _WORKSPACE[key] = dict(
-                a_seed=torch.empty(8, dtype=torch.int32, device=dev),
-                EAL=torch.empty((m, r), dtype=torch.int8, device=dev),
-                PA=torch.empty(k, dtype=torch.int32, device=dev),
-                SAt=torch.empty((r, k), dtype=torch.int8, device=dev),
-                ApEA=torch.empty((m, k), dtype=torch.int8, device=dev),
-                corrA=torch.zeros((limbs_for(k), m, 2 * r), dtype=torch.int8, device=dev),
-                maxabs=torch.zeros(2, dtype=torch.int32, device=dev),
-                projA=torch.empty((n_max, r), dtype=torch.int32, device=dev),
-                scratch=torch.empty(b3_scratch_words(m * k), dtype=torch.int32, device=dev),
-            )
-        wins = self._bufs.get(m)
-        if wins is None:
-            wins = self._bufs[m] = torch.zeros(1 + self.max_wins * WIN_WORDS, dtype=torch.int32, device=dev)
-        return {**ws, "wins": wins}
+    def _block_part(self, idx: int, shape, dtype) -> torch.Tensor:
+        assert self.block is not None, "setup_block() first"
+        nbytes = int(np.prod(shape)) * torch.tensor([], dtype=dtype).element_size()
+        return self.block[self._bo[idx]:self._bo[idx] + nbytes].view(dtype).view(shape)
 
-    def _projB(self):
-        if self._bufs.get("projB") is None:
-            self._bufs["projB"] = torch.empty((self.n, self.r), dtype=torch.int32, device=self.device)
-        return self._bufs["projB"]
+    BpEBt = property(lambda self: self._block_part(MB_BPEBT, (self.n, self.k), torch.int8))
+    EBRt = property(lambda self: self._block_part(MB_EBRT, (self.n, self.r), torch.int8))
+    PB = property(lambda self: self._block_part(MB_PB, (self.k,), torch.int32))
+    SBt = property(lambda self: self._block_part(MB_SBT, (self.r, self.k), torch.int8))
+    job_key = property(lambda self: self._block_part(MB_CONSTS, (64,), torch.int32)[0:8])
+    b_seed = property(lambda self: self._block_part(MB_CONSTS, (64,), torch.int32)[8:16])
+    target = property(lambda self: self._block_part(MB_CONSTS, (64,), torch.int32)[16:24])
+
+    # -------------------------------------------------------- per call
+    def _wins_for(self, m: int) -> torch.Tensor:
+        w = self._wins.get(m)
+        if w is None:
+            w = self._wins[m] = torch.zeros(1 + self.max_wins * WIN_WORDS, dtype=torch.int32, device=self.device)
+        return w
+
+    def _workspace(self, m: int, forward: bool, hash_tiles: bool, out_mode: int):
+        wo = _offsets(lib().uwc_mined_workspace_layout, m, self.n, self.k, self.r, int(forward), int(hash_tiles),
+                      out_mode, count=MW_BYTES)
+        ws = shared_workspace(self.device, wo[MW_BYTES])
+        self._last_ws[m] = (ws, wo)
+        return ws, wo
 
     def forward(self, A: torch.Tensor, a_scale: torch.Tensor, out: torch.Tensor | None = None,
                 out_mode: int = OUT_BF16, hash_tiles: bool = True) -> torch.Tensor:
-        """A: m x k int8 (values in [-64, 64]). Returns A @ Bt^T scaled (bf16), exact int32, or the
-        detrt fp32 dequant (OUT_F32). Every path gives bit-identical outputs and winning tiles."""
-        return self._forward(A, a_scale, out, out_mode, hash_tiles, DEFAULT_CFG, PROJ_GEMM)
-
-    def _forward(self, A, a_scale, out, out_mode, hash_tiles, cfg, proj):
+        """A: m x k int8 (values in [-64, 64]). Returns A @ Bt^T exactly, scaled to bf16 (default),
+        int32 (OUT_I32) or the detrt fp32 dequant (OUT_F32); with hash_tiles every tile of the
+        noisy product is hashed and checked against the block target (winners())."""
         m, k = A.shape
-        n, r = self.n, self.r
-        dev = A.device
-        b = self._buf(m)
-        c = consts(dev)
+        assert A.dtype == torch.int8 and A.is_contiguous() and k == self.k
         if out is None and out_mode != OUT_NONE:
             dt = {OUT_BF16: torch.bfloat16, OUT_I32: torch.int32, OUT_F32: torch.float32}[out_mode]
-            out = torch.empty((m, n), dtype=dt, device=dev)
-        # 1. commit to A, derive a_seed = H(b_seed || bind_a(root_A, m))
-        b3_root_and_seed(A.view(-1), self.job_key, prefix=self.b_seed, salt=c["SALT_A"], dim=m,
-                         seed_out=b["a_seed"], scratch=b["scratch"])
-        # 2. A-side noise (also zeroes maxabs and the win counter)
-        noise_uniform(b["EAL"], c["LABEL_A"], b["a_seed"], zero_me=b["maxabs"], zero_n=2)
-        b["wins"][:1].zero_()
-        noise_perm(b["PA"], k, r, c["LABEL_A"], b["a_seed"])
-        # 3. ApEA = A + EAL*P_A ; X = A * P_B^T (limbs) ; EAL copy ; 4. Y = BpEBt * P_A^T (limbs)
-        if proj:
-            noise_rows(A, m, k, r, E=b["EAL"], Pn=b["PA"], dst=b["ApEA"], corr=b["corrA"], ecopy_off=r)
-            project(A, self.SBt, b["corrA"], 0, b["maxabs"][0:1], proj=b["projA"][:m])
-            project(self.BpEBt, proj_matrix(b["PA"], k, r, b["SAt"]), self.corrB, r, b["maxabs"][1:2],
-                    proj=self._projB())
-        else:
-            noise_rows(A, m, k, r, E=b["EAL"], Pn=b["PA"], dst=b["ApEA"], Pp=self.PB, corr=b["corrA"], corr_off=0,
-                       ecopy_off=r, maxabs=b["maxabs"][0:1])
-            noise_rows(self.BpEBt, n, k, r, Pp=b["PA"], corr=self.corrB, corr_off=r, maxabs=b["maxabs"][1:2])
-        # 5. noisy GEMM: hash every tile, denoise exactly, scale
-        gemm(b["ApEA"], self.BpEBt, r=r, flags=(FLAG_HASH if hash_tiles else 0) | FLAG_DENOISE,
-             corrA=b["corrA"], corrB=self.corrB, maxabs=b["maxabs"], key=b["a_seed"], target=self.target,
-             wins=b["wins"], max_wins=self.max_wins, a_scale=a_scale, b_scale=self.b_scale, out=out,
-             out_mode=out_mode)
+            out = torch.empty((m, self.n), dtype=dt, device=A.device)
+        ws, wo = self._workspace(m, True, hash_tiles, out_mode)
+        wins = self._wins_for(m)
+        check(lib().uwc_mined_forward(_p(A), m, self.n, k, self.r, _p(a_scale), _p(self.b_scale), _p(self.block),
+                                      int(hash_tiles), _p(wins), self.max_wins, _p(out), out_mode, _p(ws), ws.numel(),
+                                      _stream()), "mined_forward")
         return out
 
-    def noise_mine(self, A: torch.Tensor):
-        """What a pure noise miner runs per attempt batch: commit A, noise it, hashed GEMM, no output.
-
-        No projections (X, Y) and no denoise, since nobody needs C (ops.py:349-364)."""
-        b = self._buf(A.shape[0])
-        self.mine_prepare(A, b["a_seed"], b["ApEA"], b["wins"], b["EAL"], b["PA"], b["scratch"])
-        self.mine_gemm(b["ApEA"], b["a_seed"], b["wins"])
-
-    def mine_prepare(self, A, a_seed, ApEA, wins, EAL, PA, scratch):
-        """The first half of noise_mine: commit to A (a_seed), its noise EAL and P_A, ApEA = A + noise,
-        and the win counter zeroed. Writes only the given buffers."""
+    def noise_mine(self, A: torch.Tensor) -> None:
+        """One noise-mining attempt on A: commit, noise, hashed GEMM, no output (ops.py:349-364)."""
         m, k = A.shape
-        c = consts(A.device)
-        b3_root_and_seed(A.view(-1), self.job_key, prefix=self.b_seed, salt=c["SALT_A"], dim=m, seed_out=a_seed,
-                         scratch=scratch)
-        noise_uniform(EAL, c["LABEL_A"], a_seed, zero_me=wins, zero_n=1)
-        noise_perm(PA, k, self.r, c["LABEL_A"], a_seed)
-        noise_rows(A, m, k, self.r, E=EAL, Pn=PA, dst=ApEA)
+        assert A.dtype == torch.int8 and A.is_contiguous() and k == self.k
+        ws, _ = self._workspace(m, False, True, OUT_NONE)
+        check(lib().uwc_mine_attempt(_p(A), m, self.n, k, self.r, _p(self.block), _p(self._wins_for(m)),
+                                     self.max_wins, _p(ws), ws.numel(), _stream()), "mine_attempt")
 
-    def mine_gemm(self, ApEA, a_seed, wins):
-        """The second half of noise_mine: the hashed GEMM of a prepared attempt."""
-        gemm(ApEA, self.BpEBt, r=self.r, flags=FLAG_HASH, key=a_seed, target=self.target, wins=wins,
-             max_wins=self.max_wins)
+    def buffers(self, m: int) -> dict:
+        """Views of the last call's workspace parts for this m (a_seed, EAL, PA, ApEA, maxabs and,
+        after a forward, corrA, corrB) and the win buffer."""
+        ws, wo = self._last_ws[m]
+        L, r, n, k = limbs_for(self.k), self.r, self.n, self.k
+
+        def part(idx, shape, dtype):
+            nbytes = int(np.prod(shape)) * torch.tensor([], dtype=dtype).element_size()
+            return ws[wo[idx]:wo[idx] + nbytes].view(dtype).view(shape)
+        views = dict(a_seed=part(MW_A_SEED, (8,), torch.int32), maxabs=part(MW_MAXABS, (2,), torch.int32),
+                     EAL=part(MW_EAL, (m, r), torch.int8), PA=part(MW_PA, (k,), torch.int32),
+                     ApEA=part(MW_APEA, (m, k), torch.int8), wins=self._wins_for(m))
+        if wo[MW_CORRB] > wo[MW_CORRA]:
+            views.update(corrA=part(MW_CORRA, (L, m, 2 * r), torch.int8),
+                         corrB=part(MW_CORRB, (L, n, 2 * r), torch.int8))
+        return views
 
     def win_count(self, m: int) -> int:
         """Winning tiles of the last call with this m, including any beyond max_wins (syncs)."""
-        return int(self._buf(m)["wins"][0].item())
+        return int(self._wins_for(m)[0].item())
 
     def winners(self, m: int) -> list[tuple[int, int, bytes]]:
-        """(row_offset, col_offset, hash) for winning tiles of the last forward with this m (syncs).
+        """(row_offset, col_offset, hash) of the winning tiles of the last call with this m (syncs).
         Raises if a kernel reported a device-side timeout since the last check."""
-        w = self._buf(m)["wins"].cpu().numpy().view(np.uint32)
+        words_ = self._wins_for(m).cpu().numpy().view(np.uint32)
         st = _lib.device_status(clear=True)
         if st:
             raise _lib.UWCError(f"device status {st:#x}: a kernel wait timed out; results are invalid")
-        cnt = min(int(w[0]), self.max_wins)
-        recs = w[1:1 + cnt * WIN_WORDS].reshape(cnt, WIN_WORDS)
-        return [(int(x[0]), int(x[1]), x[2:].astype("<u4").tobytes()) for x in recs]
+        cnt = min(int(words_[0]), self.max_wins)
+        return [(int(rec[0]), int(rec[1]), rec[2:].astype("<u4").tobytes())
+                for rec in words_[1:1 + cnt * WIN_WORDS].reshape(cnt, WIN_WORDS)]
 
 
 class HostMiner:
@@ -389,7 +363,7 @@ class HostMiner:
         self.copy_stream = torch.cuda.Stream(dev)
         self.uploaded = [torch.cuda.Event() for _ in range(2)]
         self.consumed = [torch.cuda.Event() for _ in range(2)]
-        self.wins_dev = w._buf(m)["wins"]
+        self.wins_dev = w._wins_for(m)
         self.i = 0
 
     def mine(self, A_host: torch.Tensor, wins_host: torch.Tensor) -> None:
@@ -411,26 +385,24 @@ class HostMiner:
 
 
 class GraphedForward:
-    """MinedWeight.forward captured as one CUDA graph for a fixed m (static input/output buffers)."""
+    """A MinedWeight's forward for one m as a replayable CUDA graph over static buffers: write the
+    nonce matrix into .A (and scales into .a_scale), call the object, read .out. The forward is a
+    single library call, so the graph holds exactly its kernels; the first (uncaptured) call sets
+    the library's per-device launch state, which capture must not do."""
 
-    def __init__(self, w: MinedWeight, m: int, out_mode: int = OUT_BF16):
+    def __init__(self, w: MinedWeight, m: int, out_mode: int = OUT_BF16, hash_tiles: bool = True):
         dev = w.device
-        self.w, self.m = w, m
+        dt = {OUT_BF16: torch.bfloat16, OUT_I32: torch.int32, OUT_F32: torch.float32}[out_mode]
         self.A = torch.zeros((m, w.k), dtype=torch.int8, device=dev)
         self.a_scale = torch.ones(m, dtype=torch.float32, device=dev)
-        dt = {OUT_BF16: torch.bfloat16, OUT_I32: torch.int32, OUT_F32: torch.float32}[out_mode]
         self.out = torch.empty((m, w.n), dtype=dt, device=dev)
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                w.forward(self.A, self.a_scale, out=self.out, out_mode=out_mode)
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
+        call = lambda: w.forward(self.A, self.a_scale, out=self.out, out_mode=out_mode, hash_tiles=hash_tiles)
+        call()
+        torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            w.forward(self.A, self.a_scale, out=self.out, out_mode=out_mode)
+            call()
 
-    def __call__(self):
+    def __call__(self) -> torch.Tensor:
         self.graph.replay()
         return self.out

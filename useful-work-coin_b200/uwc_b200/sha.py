@@ -14,7 +14,7 @@ import numpy as np
 import torch
 
 from ._lib import check, lib
-from .ops import _count, _p, _stream
+from .ops import _p, _stream
 
 
 def _rows(out: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
@@ -36,7 +36,6 @@ def _leaf_words(out: torch.Tensor) -> torch.Tensor:
     res = torch.empty((nrows, 8), dtype=torch.int32, device=out.device)
     check(lib().uwc_stage_out_leaves(_p(out), nrows, D, T, _p(scratch), scratch.numel(), _p(res), _stream()),
           "stage_out_leaves")
-    _count(2)
     return res
 
 
@@ -61,7 +60,6 @@ def stage_roots_gpu(out: torch.Tensor) -> torch.Tensor:
     scratch = _scratch(B * T, D, out.device)
     roots = torch.empty((B, 8), dtype=torch.int32, device=out.device)
     check(lib().uwc_stage_roots(_p(out), B, T, D, _p(scratch), scratch.numel(), _p(roots), _stream()), "stage_roots")
-    _count(3)
     return roots
 
 
