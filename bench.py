@@ -535,6 +535,71 @@ def run_c4(a, world, rank, local):
 
 
 # ------------------------------------------------------------------ GPU arm, NoisyGEMM
+def tc_peak_i8(stream, iters=20000):
+    """This GPU's int8 tensor-core rate right now: back-to-back tcgen05.mma kind::i8 on every SM
+    (uwc_peak_i8), best of three launches after a warm-up. TOP/s."""
+    import torch
+
+    from uwc_b200 import _lib
+    L = _lib.lib()
+    best = 0.0
+    for i in range(4):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        _lib.check(L.uwc_peak_i8(iters, stream.cuda_stream), "peak_i8")
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if i:
+            best = max(best, L.uwc_peak_i8_ops(iters) / (e0.elapsed_time(e1) / 1e3) / 1e12)
+    return best
+
+
+REF_KERNEL = os.path.join(ROOT, "baseline", "_ref", "libref_noisy_gemm.so")
+
+
+def ref_gpu_kernel(stream, A, B, m, n, k, r, flags, key, target, max_wins, flush, reps, corrA=None, corrB=None,
+                   maxabs=None, out=None):
+    """The reference's own GPU NoisyGEMM (its kernels.cu, built for sm_100a by
+    baseline/build_ref_kernel.py) on the same operands, launched as its ops.gemm does. Returns
+    (mean ms, win buffer) or None when the build is absent (it needs the reference checkout)."""
+    import ctypes
+
+    import torch
+    if not os.path.exists(REF_KERNEL):
+        return None
+    L = ctypes.CDLL(REF_KERNEL)
+    P, I = ctypes.c_void_p, ctypes.c_int
+    L.ref_noisy_gemm.argtypes = [P, P, I, I, I, I, P, P, P, P, P, P, I, P, P, P, I, I, I, P]
+    bm, bn, bk = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    L.ref_noisy_gemm_config(ctypes.byref(bm), ctypes.byref(bn), ctypes.byref(bk))
+    assert m % bm.value == 0 and n % bn.value == 0 and k % bk.value == 0 and k % r == 0
+    wins = torch.zeros(1 + max_wins * 10, dtype=torch.int32, device=A.device)
+    ptr = lambda t: None if t is None else t.data_ptr()
+    lmax = corrA.shape[0] if corrA is not None else 0
+    call = lambda: L.ref_noisy_gemm(A.data_ptr(), B.data_ptr(), m, n, k, r, ptr(corrA), ptr(corrB), ptr(maxabs),
+                                    key.data_ptr(), target.data_ptr(), wins.data_ptr(), max_wins, None, None,
+                                    ptr(out), 1 if out is not None else 0, flags, lmax, stream.cuda_stream)
+    ts = []
+    for i in range(reps + 2):
+        flush.fill_(i & 0xFF)
+        wins.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        rc = call()
+        e1.record(stream)
+        assert rc == 0, f"reference kernel launch failed ({rc})"
+        ts.append((e0, e1))
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in ts[2:]), wins
+
+
+def win_records(wins, max_wins):
+    import numpy as np
+    w = wins.cpu().numpy().view(np.uint32)
+    cnt = min(int(w[0]), max_wins)
+    return sorted(map(tuple, w[1:1 + cnt * 10].reshape(-1, 10).tolist()))
+
+
 def run_b200(a, world, rank, local):
     import numpy as np
     import torch
@@ -572,7 +637,6 @@ def run_b200(a, world, rank, local):
     sampler = ClockSampler(local)
     sampler.start()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
-    gemm_evs = []
     barrier(world)
     for i in range(a.steps):
         flush.fill_(i & 0xFF)                                       # L2 flush, outside the timed window
@@ -588,27 +652,65 @@ def run_b200(a, world, rank, local):
     value = world * ops_per_step * a.steps / (t_ms / 1e3) / 1e12
     tiles_per_s = world * (m * n / 128) * a.steps / (t_ms / 1e3)
 
-    # dominant kernel alone: the hashed GEMM, CUDA events on its stream
+    # dominant kernel alone: the hashed GEMM of the last step's prepared operands, CUDA events on
+    # its stream, L2 flushed before each launch (the first launches warm up, untimed)
     b = w.buffers(m)
+    flags = ops.FLAG_HASH | (ops.FLAG_DENOISE if forward else 0)
+    gemm_kw = dict(r=r, flags=flags, key=b["a_seed"], target=w.target, wins=b["wins"], max_wins=w.max_wins)
+    if forward:
+        gemm_kw.update(corrA=b["corrA"], corrB=b["corrB"], maxabs=b["maxabs"], out=out, out_mode=ops.OUT_I32)
     gk = []
-    for i in range(max(3, a.steps // 2)):
+    nk = max(5, a.steps)
+    for i in range(nk + 2):
         flush.fill_(i & 0xFF)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        if forward:
-            ops.gemm(b["ApEA"], w.BpEBt, r=r, flags=ops.FLAG_HASH | ops.FLAG_DENOISE, corrA=b["corrA"], corrB=b["corrB"],
-                     maxabs=b["maxabs"], key=b["a_seed"], target=w.target, wins=b["wins"], max_wins=w.max_wins,
-                     out=out, out_mode=ops.OUT_I32)
-        else:
-            ops.gemm(b["ApEA"], w.BpEBt, r=r, flags=ops.FLAG_HASH, key=b["a_seed"], target=w.target, wins=b["wins"],
-                     max_wins=w.max_wins)
+        ops.gemm(b["ApEA"], w.BpEBt, **gemm_kw)
         e1.record(stream)
         gk.append((e0, e1))
     torch.cuda.synchronize()
-    gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gk)
+    gemm_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in gk[2:])
+    ours_wins = win_records(b["wins"], w.max_wins)
     pk = peaks()
-    peak_tops = int8_peak(m, n, k, flush)
     achieved = ops_per_step / (gemm_ms / 1e3) / 1e12
+
+    # the reference's own GPU kernel on the same operands (rank 0; same key, target, corrections)
+    ref = None
+    if rank == 0:
+        ref_out = torch.empty_like(out) if forward else None
+        res = ref_gpu_kernel(stream, b["ApEA"], w.BpEBt, m, n, k, r, flags, b["a_seed"], w.target, w.max_wins, flush,
+                             max(5, a.steps // 2), corrA=b["corrA"] if forward else None,
+                             corrB=b["corrB"] if forward else None, maxabs=b["maxabs"] if forward else None,
+                             out=ref_out)
+        if res is not None:
+            ref_ms, ref_wins = res
+            ref = {"kernel": "noisy_gemm (miner/ampere/uwc_ampere/kernels.cu, mma.sync), nvcc sm_100a, "
+                             "-DSTAGES=3 -DBN_=128 -DMINB=2 (the reference's default CONFIGS entry)",
+                   "ms": ref_ms, "tops": ops_per_step / (ref_ms / 1e3) / 1e12, "ours_ms": gemm_ms,
+                   "speedup": ref_ms / gemm_ms,
+                   "same_win_records": win_records(ref_wins, w.max_wins) == ours_wins}
+            if forward:
+                ref["same_output"] = bool(torch.equal(ref_out, out))
+        else:
+            ref = {"unavailable": "baseline/_ref/libref_noisy_gemm.so not built (needs the reference checkout)"}
+    peak_live = tc_peak_i8(stream)
+    peak_cublas = int8_peak(m, n, k, flush)
+
+    # sustained: the same step back to back for >= 3 s (no flushes), median clock beside it
+    n_sus = max(20, int(3.2e3 / max(t_ms / a.steps, 1e-3)))
+    sampler2 = ClockSampler(local)
+    sampler2.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n_sus):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks2 = sampler2.stop()
+    sus_ms = e0.elapsed_time(e1)
+    sustained = {"steps": n_sus, "seconds": sus_ms / 1e3, "value": ops_per_step * n_sus / (sus_ms / 1e3) / 1e12,
+                 "unit": UNIT, "sm_mhz_median": clocks2.get("sm_mhz"), "reasons": clocks2.get("reasons"),
+                 "clock_samples": clocks2.get("samples")}
 
     # e2e through the public API with host buffers: pinned A in, win records out, every step.
     # Mining uses ops.HostMiner (the upload of attempt i + 1 overlaps attempt i); the timed region
@@ -637,6 +739,21 @@ def run_b200(a, world, rank, local):
     barrier(world)
     t2 = max_over_ranks(e0.elapsed_time(e1), world)
     e2e = world * ops_per_step * a.steps / (t2 / 1e3) / 1e12
+    # the host-to-device rate this GPU got for pinned uploads of A (the e2e limiter at scale)
+    h2d = torch.empty_like(As[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(5):
+        h2d.copy_(A_host[i % 2], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    h2d_gbs = 5 * m * k / (e0.elapsed_time(e1) / 1e3) / 1e9
+    h2d_all = [h2d_gbs]
+    if world > 1:
+        import torch.distributed as dist
+        lst = [None] * world
+        dist.all_gather_object(lst, h2d_gbs)
+        h2d_all = lst
     status = _lib.device_status(clear=True)
 
     if rank != 0:
@@ -648,19 +765,26 @@ def run_b200(a, world, rank, local):
                        "parallelism": f"nonce-sharded x{world}", "l2": "flushed (256 MiB write) before each step",
                        "target": "2^-20 per hash tile"},
             "tiles_hashed_per_s": tiles_per_s,
-            "pct_int8_peak": 100.0 * value / world / peak_tops,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOP/s",
-                         "frac": achieved / peak_tops, "traffic": TRAFFIC.get(a.workload),
-                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch of "
-                                           "k_noisy_gemm<MODE_MINE, 64>, one ncu capture of this workload"
-                                           if a.workload in TRAFFIC else None, "kernel": "k_noisy_gemm",
-                         "peak_source": "cuBLASLt int8 (torch._int_mm) on the same shape, burst, measured in "
-                                        "this run (MEASURED_PEAKS.json has no int8 entry; its bf16 figure "
-                                        f"{pk['bf16_tflops']} TF/s, {pk['src']})",
-                         "kernel_ms": gemm_ms, "nominal_int8_tops": 4500.0},
+            "pct_int8_peak": 100.0 * value / world / peak_live,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_live, "unit": "TOP/s",
+                         "frac": achieved / peak_live, "traffic": TRAFFIC.get(a.workload),
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch of the hashed "
+                                           "GEMM, one ncu capture of this workload" if a.workload in TRAFFIC else None,
+                         "kernel": "k_noisy_gemm", "kernel_ms": gemm_ms,
+                         "peak_source": "live tcgen05.mma kind::i8 back-to-back rate on this GPU in this run "
+                                        "(uwc_peak_i8, burst); MEASURED_PEAKS.json has no int8 entry",
+                         "frac_vs_cublaslt": achieved / peak_cublas, "cublaslt_int8_tops": peak_cublas,
+                         "frac_vs_nominal": achieved / 4500.0, "nominal_int8_tops": 4500.0,
+                         "bf16_measured_tflops": pk["bf16_tflops"]},
+            "ref_gpu_kernel": ref,
+            "sustained": sustained,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": m * k,
-                    "d2h_bytes_per_step": wins_host[0].numel() * 4},
+                    "d2h_bytes_per_step": wins_host[0].numel() * 4,
+                    "h2d_gbs_per_rank": h2d_all,
+                    "limiter": "the per-attempt upload of A (m x k int8) from pinned host memory"},
             "gpu_launches": launches, "clocks": clocks, "device_status": status}
+    if forward:
+        line["ops_executed_per_step"] = 2.0 * m * n * (k + 2 * r * int(b["corrA"].shape[0]))
     if not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(m, n, k, r)
     print(json.dumps(line), flush=True)

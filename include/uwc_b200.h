@@ -45,6 +45,15 @@ extern "C" {
 #define UWC_OUT_F32 3 /* new: detrt dequant y = fmul(fmul(float(acc), a_scale[i]), b_scale[j]) (qwen3.py:125) */
 #define UWC_WIN_WORDS 10
 
+/* Test hooks of the error path (no counterpart in the reference). UWC_HOOK_WAIT_NS sets the bound of
+ * every wait inside the GEMM kernels (value in ns; 0 restores the default of 1 s);
+ * UWC_HOOK_WITHHOLD = 1 makes later GEMM launches issue no copies, so their first wait runs out and
+ * the kernel unwinds with UWC_DEV_TIMEOUT in uwc_device_status (0 restores normal launches).
+ * Process-wide; for tests only. Returns UWC_OK or UWC_ERR_ARG. */
+#define UWC_HOOK_WAIT_NS 1
+#define UWC_HOOK_WITHHOLD 2
+int uwc_test_hook(int hook, long long value);
+
 /* Library version (major*10000 + minor*100 + patch). */
 int uwc_version(void);
 
@@ -203,6 +212,15 @@ int uwc_mine_attempt(const int8_t* A, int m, int n, int k, int r, const void* bl
 int uwc_mined_forward(const int8_t* A, int m, int n, int k, int r, const float* a_scale, const float* b_scale,
                       const void* block, int hash, uint32_t* wins, int max_wins, void* out, int out_mode,
                       void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* ---- measurement --------------------------------------------------------------------------
+ * The tensor core's int8 rate on the current device (no reference counterpart: a roofline
+ * denominator). uwc_peak_i8 launches one CTA per SM, each issuing iters x 8 back-to-back
+ * tcgen05.mma kind::i8 (M 128, N 256, K 32) from fixed shared-memory tiles into two TMEM
+ * accumulators; time it with events on `stream`. uwc_peak_i8_ops(iters): its int8 operations
+ * (2 per multiply-add). iters in [1, 131072]. */
+int uwc_peak_i8(int iters, void* stream);
+double uwc_peak_i8_ops(int iters);
 
 /* ---------------------------------------------------------------- deterministic linear: producers
  * and consumers of the int8 GEMM, bit-identical to runtime/detrt's emulated-fp32 ops (every + - * /

@@ -2,25 +2,31 @@
 // tcgen05.mma kind::i8, TMEM accumulators and TMA-fed 128-byte-swizzled shared-memory stages.
 //
 // Reference semantics: noisy_gemm (miner/ampere/uwc_ampere/kernels.cu:482-715), launched by
-// ops.gemm (ops.py:185-198). Three schedules share one persistent, warp-specialized kernel,
+// ops.gemm (ops.py:185-198). Five schedules share one persistent, warp-specialized kernel,
 // specialized at compile time on the schedule and on the hash chunk width r:
 //
-//   MODE_MINE  FLAG_HASH (MinedWeight.noise_mine, ops.py:349-364; MODE_MINE_OUT also stores the
-//              finished product, for MinedWeight.forward, ops.py:316-347). A work unit is a
-//              256 x 256 output block held as two 128 x 256 TMEM accumulators X (rows 0-127) and
-//              Y (rows 128-255) sharing the B tile. Per r-column chunk of k the MMA warp issues X
-//              then Y, so each accumulator's running sum is read by the epilogue while the tensor
-//              core works on the other.
-//   MODE_FWD   FLAG_DENOISE without FLAG_HASH (MinedWeight.forward with hash_tiles=False).
-//              A unit is a 128 x 256 block held as two 128 x 128 accumulators (column halves)
-//              plus a 128 x 256 correction accumulator R = sum_li 128^li corrA[li] corrB[li]^T,
-//              built before the main loop by Horner steps (R <<= 7 done by the epilogue in TMEM).
-//              The output is acc - R, exact in int32.
-//   MODE_CORR  second pass of a hashed, denoised call: only the correction accumulator R (same
-//              Horner build), then out = acc - R with acc read back from the int32 product that
-//              MODE_MINE_OUT stored. Hashing thus always runs on the mining schedule.
-//   MODE_PLAIN no flags: a 128 x 256 block per unit, two accumulators used alternately across
-//              units so the store of one unit overlaps the main loop of the next.
+//   MODE_MINE      FLAG_HASH without an output (MinedWeight.noise_mine, ops.py:349-364). A work
+//                  unit is a 256 x 256 output block held as two 128 x 256 TMEM accumulators X (rows
+//                  0-127) and Y (rows 128-255) sharing the B tile. Per r-column chunk of k the MMA
+//                  warp issues X then Y, so each accumulator's running sum is read by the epilogue
+//                  while the tensor core works on the other.
+//   MODE_MINE_FWD  FLAG_HASH with an output (MinedWeight.forward, ops.py:316-347): the mining
+//                  schedule, and in the same kernel the output. At the last snapshot, already in
+//                  registers for the hash, each thread stores its raw int32 row (into its own output
+//                  row, or a per-CTA staging block for bf16). With FLAG_DENOISE the freed accumulator
+//                  then receives the correction R = sum_li 128^li corrA[li] corrB[li]^T by Horner
+//                  steps (the epilogue shifts R by 7 bits in TMEM between limbs) and the thread
+//                  writes out = raw - R, scaled; without it, the scaled raw row. The raw row is
+//                  reread by the thread that wrote it microseconds earlier (from L2), never as an
+//                  m x n matrix pass over HBM.
+//   MODE_FWD       FLAG_DENOISE without FLAG_HASH (MinedWeight.forward with hash_tiles=False).
+//                  A unit is a 128 x 256 block held as two 128 x 128 accumulators (column halves)
+//                  plus a 128 x 256 correction accumulator R built before the main loop (Horner).
+//                  The output is acc - R, exact in int32.
+//   MODE_CORR      the scaling pass of a split-K plain GEMM with an fp32 / bf16 output: out =
+//                  scale(acc) with acc read back from the summed int32 partials.
+//   MODE_PLAIN     no flags: a 128 x 256 block per unit, two accumulators used alternately across
+//                  units so the store of one unit overlaps the main loop of the next.
 //
 // The MMA issue loop is fully unrolled per 128-byte k-block stage: the tensor core only runs at
 // its rate when tcgen05.mma instructions are issued back to back.
@@ -33,9 +39,12 @@
 // Rows 32-63 of a 64-row block live in the next quadrant (the next warp). XOR and rotl are linear
 // over GF(2): the reference's msg[c % 16] = rotl(msg[c % 16], 13) ^ x_c equals the XOR over the
 // chunks of slot s of rotl(x_c, 13 * (updates of slot s after c)). So every epilogue thread
-// pre-rotates its chunk contribution and red.global.xor's it into the unit's message buffer
-// (caller workspace, double-buffered per CTA): no message state in registers, and the two
-// quadrant halves of a tile combine in the same word.
+// pre-rotates its chunk contribution and XOR-reduces it into the unit's message buffer in shared
+// memory (red.shared.xor; 512 tiles x 16 words = 32 KiB): no message state in registers, no
+// traffic to L2 (reductions into global memory cost a third of the kernel's time at r = 64,
+// measured), and the two quadrant halves of a tile combine in the same word. Two CTA-wide
+// hand-offs per unit order the reductions before the tile hashes and the hashes (which clear the
+// words) before the next unit's reductions.
 //
 // Warp roles (576 threads, one CTA per SM, all 512 TMEM columns):
 //   0..15   epilogue: warp w reads TMEM lanes 32*(w%4).. and the 64-column block w/4; at the end
@@ -44,13 +53,14 @@
 //   16      TMA producer (one elected lane issues)
 //   17      MMA issuer (one lane issues); allocates and frees TMEM
 #include <algorithm>
+#include <atomic>
 
 #include "uwc_device.cuh"
 #include "uwc_host.h"
 
 namespace {
 
-enum Mode { MODE_PLAIN = 0, MODE_MINE = 1, MODE_FWD = 2, MODE_CORR = 3, MODE_MINE_OUT = 4 };
+enum Mode { MODE_PLAIN = 0, MODE_MINE = 1, MODE_FWD = 2, MODE_CORR = 3, MODE_MINE_FWD = 4 };
 
 constexpr int kEpiWarps = 16;
 constexpr int kProducerWarp = kEpiWarps;               // 16
@@ -59,7 +69,8 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;           // 576
 constexpr int kKB = 128;                                // K bytes per stage (one 128-byte swizzle row)
 constexpr int kUN = 256;                                // output columns per unit
 constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
-constexpr int kMsgWords = kMaxTiles * 16;               // one unit's tile messages (32 KiB)
+constexpr int kMsgWords = kMaxTiles * 16;               // one unit's tile messages (32 KiB, shared memory)
+constexpr int kStageRows = 256;                         // rows of a unit's raw-product staging block
 constexpr int kBarBytes = 256;
 
 struct Params {
@@ -75,13 +86,15 @@ struct Params {
   const uint32_t* key;
   const uint32_t* target;
   uint32_t* wins;
-  uint32_t* msgbuf;        // workspace: per CTA 2 x kMsgWords words of tile messages
-  const int32_t* acc_in;   // MODE_CORR: the uncorrected int32 product, m x n
+  int32_t* stage;          // MODE_MINE_FWD with a bf16 output: per CTA a 256 x 256 int32 block
+  const int32_t* acc_in;   // MODE_CORR: the summed int32 split-K product, m x n
   const float* a_scale;
   const float* b_scale;
   void* out;
   uint32_t* status;
   uint32_t one;      // 1, opaque to the compiler (multiply-add additions in the tile hash)
+  uint64_t wait_ns;  // bound of every wait (1 s; shortened by the test hook)
+  int withhold;      // test hook: the producer issues no copies, so the first wait runs out
   // Batched PLAIN launches (nbatch > 1 or causal): batch bt reads A rows bt * a_brows + [0, m) and
   // B rows (bt / b_bdiv) * b_brows + [0, n), and writes its m x n int32 block at out + bt * m * n.
   // causal 1 (Q K^T): block (m0, n0) runs only if some row t in [m0, m0 + 128) sees a column of it
@@ -95,21 +108,20 @@ struct Params {
 template <int MODE, int R>
 struct Cfg {
   static constexpr bool HASH = R != 0;
-  static constexpr bool MINE = MODE == MODE_MINE || MODE == MODE_MINE_OUT;   // the mining schedule
+  static constexpr bool MINE = MODE == MODE_MINE || MODE == MODE_MINE_FWD;   // the mining schedule
   static constexpr int UM = MINE ? 256 : 128;                    // output rows per unit
   static constexpr int NACC = MODE == MODE_PLAIN ? 1 : 2;
   static constexpr int ACC_N = MODE == MODE_FWD ? 128 : 256;    // MMA N per accumulator
-  static constexpr bool CORR = MODE == MODE_FWD || MODE == MODE_CORR;  // builds the correction R
+  static constexpr bool CORR = MODE == MODE_FWD || MODE == MODE_CORR;  // R built before the main loop
   static constexpr int A_BYTES = UM * kKB;
   static constexpr int STAGE = A_BYTES + kUN * kKB;              // 64 KiB (MINE) / 48 KiB
-  // MODE_MINE_OUT and MODE_CORR trade stages for the epilogue's tiles (below)
-  static constexpr int NST = MODE == MODE_MINE || MODE == MODE_PLAIN ? 3 : (MODE == MODE_MINE_OUT || MODE == MODE_CORR ? 2 : 4);
+  static constexpr int NST = MINE || MODE == MODE_PLAIN ? 3 : (MODE == MODE_CORR ? 2 : 4);
   // Per epilogue warp a padded 32 x 33-word shared-memory tile that turns thread-per-row data into
-  // row-contiguous global accesses (MODE_CORR's read-back and stores, MODE_MINE_OUT's and
-  // MODE_PLAIN's stores).
+  // row-contiguous global accesses (MODE_CORR's read-back and stores, MODE_PLAIN's stores).
   static constexpr int TILE_WORDS = 32 * 33;
-  static constexpr int TILE_BYTES = MODE == MODE_FWD || MODE == MODE_MINE ? 0 : kEpiWarps * TILE_WORDS * 4;
-  static constexpr int SMEM = NST * STAGE + TILE_BYTES + kBarBytes + 1024;  // +1024: manual alignment
+  static constexpr int TILE_BYTES = MODE == MODE_CORR || MODE == MODE_PLAIN ? kEpiWarps * TILE_WORDS * 4 : 0;
+  static constexpr int MSG_BYTES = HASH ? kMsgWords * 4 : 0;     // the unit's tile messages
+  static constexpr int SMEM = NST * STAGE + TILE_BYTES + MSG_BYTES + kBarBytes + 1024;  // +1024: alignment
   static constexpr int PARTS = R == 64 ? 2 : 1;                  // chunks per stage
   static constexpr int SPAN = R == 256 ? 2 : 1;                  // stages per chunk
   static constexpr int ACC_WARPS = MODE == MODE_FWD ? kEpiWarps / 2 : kEpiWarps;  // readers per acc
@@ -122,7 +134,10 @@ struct Bars {
   uint64_t acc_full[4];
   uint64_t acc_empty[4];
   uint64_t r_full, r_scaled, r_empty;
-  uint64_t hash_ready[2];   // per message buffer: every epilogue thread's XOR reductions landed
+  uint64_t c_ready[2];      // MODE_MINE_FWD, per accumulator: a Horner step of R has landed in TMEM
+  uint64_t c_shifted[2];    // MODE_MINE_FWD, per accumulator: the epilogue shifted R by 7 bits
+  uint64_t hash_ready;      // every epilogue thread's XOR reductions of the unit landed
+  uint64_t hash_done;       // every tile of the unit hashed and its message words cleared
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -251,6 +266,35 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int c0, co
   }
 }
 
+// store_row32 converting in place: v (32 int32 of one row, columns c0..c0+31 < n, n % 64 == 0)
+// is overwritten with the output words, so no second 32-register array is live (the mining
+// schedule's epilogue holds a whole 64-column snapshot when it stores).
+__device__ __forceinline__ void store_row32_inplace(const Params& p, int row, int c0, uint32_t* v) {
+  if (p.out_mode == UWC_OUT_NONE || row >= p.m || c0 >= p.n) return;
+  if (p.out_mode == UWC_OUT_BF16) {
+    const float sx = p.a_scale[row];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float f0 = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i]), sx), __ldg(p.b_scale + c0 + 2 * i));
+      const float f1 = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i + 1]), sx), __ldg(p.b_scale + c0 + 2 * i + 1));
+      v[i] = bf16_rne(f0) | (bf16_rne(f1) << 16);
+    }
+    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (uint64_t)row * p.n + c0);
+#pragma unroll
+    for (int i = 0; i < 4; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    return;
+  }
+  if (p.out_mode == UWC_OUT_F32) {
+    const float sx = p.a_scale[row];
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+      v[i] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), sx), __ldg(p.b_scale + c0 + i)));
+  }
+  uint4* o = reinterpret_cast<uint4*>(static_cast<uint32_t*>(p.out) + (uint64_t)row * p.n + c0);
+#pragma unroll
+  for (int i = 0; i < 8; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
 // Four consecutive outputs of one row (c % 4 == 0, n % 4 == 0) in the chosen format.
 __device__ __forceinline__ void store4(const Params& p, int row, int c, int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
   if (p.out_mode == UWC_OUT_I32) {
@@ -301,16 +345,22 @@ __device__ __forceinline__ uint32_t reduce_scatter4(const uint32_t* pt, int lane
   return k0 ^ k1 ^ send ^ __shfl_xor_sync(0xffffffffu, send, 8);
 }
 
-// Keyed BLAKE3 of hash tile `slot` of a finished unit's message buffer, target compare and win
-// record (kernels.cu:574-596). Slot bits: lane-in-group (5), 64-column block (2), 64-row half (1),
-// 128-row accumulator (1); the message words of a slot are kMaxTiles apart. Clears the words.
+// XOR into a shared-memory word (the tile messages of the unit being mined).
+__device__ __forceinline__ void red_xor_shared(uint32_t* addr, uint32_t v) {
+  asm volatile("red.shared.xor.b32 [%0], %1;" ::"r"(smem_u32(addr)), "r"(v) : "memory");
+}
+
+// Keyed BLAKE3 of hash tile `slot` of a finished unit's message buffer (shared memory), target
+// compare and win record (kernels.cu:574-596). Slot bits: lane-in-group (5), 64-column block (2),
+// 64-row half (1), 128-row accumulator (1); the message words of a slot are kMaxTiles apart.
+// Clears the words for the next unit.
 __device__ __forceinline__ void hash_tile(const Params& p, uint32_t* msg, int m0, int n0, int slot) {
   const int ln = slot & 31, cbk = (slot >> 5) & 3, rb = (slot >> 7) & 1, a = slot >> 8;
   uint32_t w[16], hv[8], key[8];
 #pragma unroll
   for (int i = 0; i < 16; i++) {
-    w[i] = __ldcg(msg + i * kMaxTiles + slot);
-    __stcg(msg + i * kMaxTiles + slot, 0u);   // clear for the unit after next
+    w[i] = msg[i * kMaxTiles + slot];
+    msg[i * kMaxTiles + slot] = 0u;
   }
   if (m0 + a * 128 + rb * 64 >= p.m || n0 + cbk * 64 >= p.n) return;
 #pragma unroll
@@ -337,10 +387,20 @@ __device__ __forceinline__ void hash_tile(const Params& p, uint32_t* msg, int m0
   }
 }
 
+// 64 consecutive int32 of one row (both halves of a thread's snapshot) to global memory, raw.
+__device__ __forceinline__ void store_raw64(int32_t* dst, const uint32_t* v, const uint32_t* v2) {
+  uint4* o = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 8; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+#pragma unroll
+  for (int i = 0; i < 8; i++) o[8 + i] = make_uint4(v2[4 * i], v2[4 * i + 1], v2[4 * i + 2], v2[4 * i + 3]);
+}
+
 // Warp-wide bounded wait: every lane polls the barrier (measured faster to wake than one polling
 // lane plus a warp sync) and the warp agrees on the verdict.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status));
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status,
+                                          uint64_t wait_ns) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, wait_ns));
 }
 
 template <int MODE, int R>
@@ -348,10 +408,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     k_noisy_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmCA, const __grid_constant__ CUtensorMap tmCB, const Params p) {
   using C = Cfg<MODE, R>;
+  constexpr bool FWDH = MODE == MODE_MINE_FWD;   // the hashed forward: output (and correction) in the same pass
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint32_t* const tiles = reinterpret_cast<uint32_t*>(smem + C::NST * C::STAGE);
-  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE + C::TILE_BYTES);
+  uint32_t* const msg = reinterpret_cast<uint32_t*>(smem + C::NST * C::STAGE + C::TILE_BYTES);
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::NST * C::STAGE + C::TILE_BYTES + C::MSG_BYTES);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -364,31 +426,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int a = 0; a < 2; a++) {
       mbar_init(&bars->acc_full[a], 1);
       mbar_init(&bars->acc_empty[a], C::ACC_WARPS);
-      // message hand-offs are signalled by every lane that wrote (arrival counts in threads)
-      mbar_init(&bars->hash_ready[a], kEpiWarps * 32);
+      mbar_init(&bars->c_ready[a], 1);
+      mbar_init(&bars->c_shifted[a], kEpiWarps);
     }
+    // message hand-offs are signalled by every epilogue thread (arrival counts in threads)
+    mbar_init(&bars->hash_ready, kEpiWarps * 32);
+    mbar_init(&bars->hash_done, kEpiWarps * 32);
     mbar_init(&bars->r_full, 1);
     mbar_init(&bars->r_scaled, kEpiWarps);
     mbar_init(&bars->r_empty, kEpiWarps);
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
-    bars->L = C::CORR ? limbs_from_maxabs(p) : 0;
+    bars->L = C::CORR || FWDH ? limbs_from_maxabs(p) : 0;
     mbar_fence_init();
   }
   if (warp == kMmaWarp) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
-  uint32_t* const msg_cta = C::HASH ? p.msgbuf + (uint64_t)blockIdx.x * (2 * kMsgWords) : nullptr;
   if (C::HASH && warp < kEpiWarps) {
-    uint4* z = reinterpret_cast<uint4*>(msg_cta);
-    for (int i = threadIdx.x; i < 2 * kMsgWords / 4; i += kEpiWarps * 32) __stcg(z + i, make_uint4(0, 0, 0, 0));
-    __threadfence();
+    uint4* z = reinterpret_cast<uint4*>(msg);
+    for (int i = threadIdx.x; i < kMsgWords / 4; i += kEpiWarps * 32) z[i] = make_uint4(0, 0, 0, 0);
   }
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (C::CORR && p.denoise) {
+    if ((C::CORR || FWDH) && p.denoise) {
       tma_prefetch_desc(&tmCA);
       tma_prefetch_desc(&tmCB);
     }
@@ -401,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k = p.k;
   const int kblocks = MODE == MODE_CORR ? 0 : (k + kKB - 1) / kKB;
   const int nch = C::HASH ? k / R : 1;                         // snapshots per accumulator per unit
-  const int cblocks = C::CORR ? (2 * p.r) / kKB : 1;  // k-blocks per correction limb
+  const int cblocks = C::CORR || FWDH ? (2 * p.r) / kKB : 1;  // k-blocks per correction limb
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
@@ -410,21 +473,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       const bool leader = elect_one();
       uint32_t gk = 0;
-      for (int u = blockIdx.x; u < p.nunits && !__any_sync(0xffffffffu, *abort_flag); u += gridDim.x) {
+      // (test hook: with `withhold` no copy is issued and the MMA warp's first wait runs out)
+      for (int u = blockIdx.x; u < p.nunits && !p.withhold && !__any_sync(0xffffffffu, *abort_flag); u += gridDim.x) {
         int m0, n0, kb0, nkb, bt;
         unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb, bt);
+        // correction blocks: before the main loop (FWD, CORR) or after it (MINE_FWD)
         const int ncorr = C::CORR ? L * cblocks : 0;
-        const int nblk = ncorr + nkb;
+        const int npost = FWDH ? L * cblocks : 0;
+        const int nblk = ncorr + nkb + npost;
         for (int b = 0; b < nblk; b++, gk++) {
           const int s = gk % C::NST;
           const uint32_t ph = (gk / C::NST) & 1;
-          if (!warp_wait(&bars->empty[s], ph ^ 1, abort_flag, p.status)) break;
+          if (!warp_wait(&bars->empty[s], ph ^ 1, abort_flag, p.status, p.wait_ns)) break;
           uint8_t* sA = smem + s * C::STAGE;
           uint8_t* sB = sA + C::A_BYTES;
           if (!leader) continue;
           mbar_expect_tx(&bars->full[s], C::STAGE);
-          if (b < ncorr) {
-            const int li = L - 1 - b / cblocks, kb = b % cblocks;
+          if (b < ncorr || b >= ncorr + nkb) {
+            const int bb = b < ncorr ? b : b - ncorr - nkb;
+            const int li = L - 1 - bb / cblocks, kb = bb % cblocks;
             tma_load_2d(sA, &tmCA, &bars->full[s], kb * kKB, li * p.m + m0);
             tma_load_2d(sB, &tmCB, &bars->full[s], kb * kKB, li * p.n + n0);
           } else {
@@ -443,6 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool leader = elect_one();
       uint32_t gk = 0;                      // k-blocks consumed (ring position)
       uint32_t snaps[2] = {0, 0};           // snapshots produced per accumulator
+      uint32_t writes[2] = {0, 0};          // MINE: waits for a free accumulator (snapshots + corrections)
+      uint32_t shifted[2] = {0, 0};         // MINE_FWD: waits for the epilogue's Horner shifts
       uint32_t r_scaled_waits = 0;
       int local = 0;
       bool ok = true;
@@ -459,14 +528,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int li = L - 1; li >= 0 && ok; li--) {
             const uint32_t tR = tmem + (direct ? 256 * li : 256);
             if (li == L - 1)
-              ok = warp_wait(&bars->r_empty, (local & 1) ^ 1, abort_flag, p.status);
+              ok = warp_wait(&bars->r_empty, (local & 1) ^ 1, abort_flag, p.status, p.wait_ns);
             else if (!direct)
-              ok = warp_wait(&bars->r_scaled, r_scaled_waits++ & 1, abort_flag, p.status);
+              ok = warp_wait(&bars->r_scaled, r_scaled_waits++ & 1, abort_flag, p.status, p.wait_ns);
             if (!ok) break;
             tc_fence_after();
             for (int kb = 0; kb < cblocks && ok; kb++, gk++) {
               const int s = gk % C::NST;
-              ok = warp_wait(&bars->full[s], (gk / C::NST) & 1, abort_flag, p.status);
+              ok = warp_wait(&bars->full[s], (gk / C::NST) & 1, abort_flag, p.status, p.wait_ns);
               if (!ok) break;
               tc_fence_after();
               const uint32_t aA = smem_base + s * C::STAGE, aB = aA + C::A_BYTES;
@@ -489,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < nkb && ok; kb++) {   // kb counts from this unit's first k-block
           const uint32_t g = gk0 + kb;
           const int s = g % C::NST;
-          ok = warp_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status);
+          ok = warp_wait(&bars->full[s], (g / C::NST) & 1, abort_flag, p.status, p.wait_ns);
           if (!ok) break;
           tc_fence_after();
           const uint32_t aA = smem_base + s * C::STAGE;
@@ -504,7 +573,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int a = 0; a < C::NACC; a++) {
                 if (a >= nacc) break;
                 if (cstart) {
-                  ok = warp_wait(&bars->acc_empty[a], (snaps[a] & 1) ^ 1, abort_flag, p.status);
+                  const uint32_t w = C::MINE ? writes[a]++ : snaps[a];
+                  ok = warp_wait(&bars->acc_empty[a], (w & 1) ^ 1, abort_flag, p.status, p.wait_ns);
                   if (!ok) break;
                   tc_fence_after();
                 }
@@ -530,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int ba = MODE == MODE_PLAIN ? pbuf : a;
               if (kb == 0) {
                 const uint32_t uses = MODE == MODE_PLAIN ? (uint32_t)(local >> 1) : snaps[a];
-                ok = warp_wait(&bars->acc_empty[ba], (uses & 1) ^ 1, abort_flag, p.status);
+                ok = warp_wait(&bars->acc_empty[ba], (uses & 1) ^ 1, abort_flag, p.status, p.wait_ns);
                 if (!ok) break;
                 tc_fence_after();
               }
@@ -551,10 +621,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mma_commit(&bars->empty[s]);
         }
         gk = gk0 + nkb;
+        // ---- MINE_FWD: the correction R of each finished accumulator, into its own columns:
+        // highest limb first (accumulate off), the epilogue shifts R by 7 bits before each lower
+        // limb accumulates on top (Horner), c_ready after each limb
+        if (FWDH && L > 0) {
+          for (int li = L - 1; li >= 0 && ok; li--) {
+            for (int kb = 0; kb < cblocks && ok; kb++, gk++) {
+              const int s = gk % C::NST;
+              ok = warp_wait(&bars->full[s], (gk / C::NST) & 1, abort_flag, p.status, p.wait_ns);
+              if (!ok) break;
+              tc_fence_after();
+              const uint32_t aA = smem_base + s * C::STAGE;
+              const uint64_t adesc = sdesc_sw128(aA), bdesc = sdesc_sw128(aA + C::A_BYTES);
+              for (int a = 0; a < nacc && ok; a++) {
+                if (kb == 0) {
+                  if (li == L - 1)   // the last snapshot's release
+                    ok = warp_wait(&bars->acc_empty[a], (writes[a]++ & 1) ^ 1, abort_flag, p.status, p.wait_ns);
+                  else
+                    ok = warp_wait(&bars->c_shifted[a], shifted[a]++ & 1, abort_flag, p.status, p.wait_ns);
+                  if (!ok) break;
+                  tc_fence_after();
+                }
+                if (leader) {
+#pragma unroll
+                  for (int ks = 0; ks < 4; ks++)
+                    mma_i8(tmem + a * 256, adesc + a * (128 * kKB / 16) + 2 * ks, bdesc + 2 * ks, id_acc,
+                           (li == L - 1 && kb == 0 && ks == 0) ? 0u : 1u);
+                  if (kb == cblocks - 1) mma_commit(&bars->c_ready[a]);
+                }
+              }
+              if (!ok) break;
+              if (leader) mma_commit(&bars->empty[s]);
+            }
+          }
+        }
       }
       // drain: every MMA issued by the leader has completed before TMEM is released
       if (leader) mma_commit(&bars->drain);
-      warp_wait(&bars->drain, 0, abort_flag, p.status);
+      warp_wait(&bars->drain, 0, abort_flag, p.status, p.wait_ns);
     }
   } else if (warp < kEpiWarps) {
     // ------------------------------------------------------------ epilogue warps
@@ -563,6 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // message slot of this thread's tile after the reduce-scatter: g = lane % 8, t = lane / 8
     const int tslot = (lane & 7) * 4 + (lane >> 3);
     uint32_t snaps[2] = {0, 0};
+    uint32_t cready[2] = {0, 0};    // MINE_FWD: c_ready waits per accumulator
     uint32_t r_waits = 0;
     int local = 0;
     bool ok = true;
@@ -571,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       unit_span(p, u, C::UM, kblocks, m0, n0, kb0, nkb, bt);
       if (MODE == MODE_PLAIN) {
         const int b = local & 1;
-        ok = warp_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status);
+        ok = warp_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status, p.wait_ns);
         if (!ok) break;
         tc_fence_after();
         const uint32_t col = tmem + b * 256 + cb * 64;
@@ -615,21 +720,158 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
-      // MINE: accumulators X (a = 0) and Y (a = 1), this warp's 64 columns cb*64 of each.
-      // FWD: accumulator a = cb / 2 (column half), its columns (cb % 2) * 64.
-      const bool hasY = C::MINE && m0 + 128 < p.m;
-      const int a0 = C::MINE ? 0 : (cb >> 1);
-      const uint32_t col0 = tmem + lane_base + (C::MINE ? cb * 64 : a0 * 128 + (cb & 1) * 64);
-      const uint32_t col1 = tmem + lane_base + 256 + cb * 64;
-      const int buf = local & 1;
-      uint32_t* const msg = msg_cta + buf * kMsgWords;
-      // row half of the 128-row accumulator this quadrant belongs to, for the message slot
-      const int rb = q >> 1;
+      if (C::MINE) {
+        // ---- the mining schedules: accumulators X (a = 0, rows m0..m0+127) and Y (a = 1), this
+        // warp's 32 rows (quadrant q) x 64 columns (block cb) of each
+        const bool hasY = m0 + 128 < p.m;
+        const uint32_t colX = tmem + lane_base + cb * 64;
+        const int rb = q >> 1;   // 64-row half of the 128-row accumulator, for the message slot
+        const int slot[2] = {((0 * 2 + rb) * 4 + cb) * 32 + tslot, ((1 * 2 + rb) * 4 + cb) * 32 + tslot};
+        const int c0 = n0 + cb * 64;
+        auto row_of = [&](int a) { return m0 + a * 128 + 32 * q + lane; };
+        // where a forward keeps the thread's raw product row until it is corrected / scaled: its
+        // own output row (int32 / fp32 outputs), or the CTA's staging block (bf16)
+        auto raw_of = [&](int a) -> int32_t* {
+          if (p.out_mode == UWC_OUT_BF16)
+            return p.stage + ((uint64_t)blockIdx.x * kStageRows + a * 128 + 32 * q + lane) * kUN + cb * 64;
+          return static_cast<int32_t*>(p.out) + (uint64_t)row_of(a) * p.n + c0;
+        };
+        // consume one snapshot of accumulator a: read 64 values, release the accumulator, fold
+        auto consume = [&](int a, bool last) -> uint32_t {
+          ok = warp_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status, p.wait_ns);
+          if (!ok) return 0u;
+          snaps[a]++;
+          tc_fence_after();
+          uint32_t v[32], v2[32];
+          tmem_ld_32x32b_x32(colX + a * 256, v);
+          tmem_ld_32x32b_x32(colX + a * 256 + 32, v2);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
+          uint32_t pt[4] = {0u, 0u, 0u, 0u};
+          fold_row32(v, pt);
+          fold_row32(v2, pt);
+          // the last snapshot of a forward: the raw row goes out (the int32 output itself when
+          // nothing is subtracted or scaled), to be finished after the unit's hashes
+          if (FWDH && last && row_of(a) < p.m && c0 < p.n) store_raw64(raw_of(a), v, v2);
+          return reduce_scatter4(pt, lane);
+        };
+        // the previous unit's tile hashes clear the message words this unit reduces into
+        bool clear_pending = local > 0;
+        auto chunk = [&](int c, bool last) {
+          const int sl = c & 15;
+          // slot sl is updated again by chunks c + 16, c + 32, ... < nch: the contribution of
+          // chunk c is rotated 13 bits for each of those later updates
+          const int rot = (13 * ((nch - 1 - c) >> 4)) & 31;
+#pragma unroll
+          for (int a = 0; a < 2; a++) {
+            if (a == 1 && !hasY) break;
+            const uint32_t x = consume(a, last);
+            if (!ok) break;
+            if (clear_pending) {
+              ok = warp_wait(&bars->hash_done, (local - 1) & 1, abort_flag, p.status, p.wait_ns);
+              clear_pending = false;
+              if (!ok) break;
+            }
+            red_xor_shared(msg + sl * kMaxTiles + slot[a], __funnelshift_l(x, x, rot));
+          }
+        };
+        // the last chunk of a forward (which also writes the output) is peeled off the loop
+        for (int c = 0; c < (FWDH ? nch - 1 : nch) && ok; c++) chunk(c, false);
+        if (FWDH && ok) chunk(nch - 1, true);
+        if (!ok) break;
+        // every thread's reductions of this unit are in shared memory: each thread hashes one tile
+        mbar_arrive(&bars->hash_ready);
+        ok = warp_wait(&bars->hash_ready, local & 1, abort_flag, p.status, p.wait_ns);
+        if (!ok) break;
+        hash_tile(p, msg, m0, n0, threadIdx.x);
+        mbar_arrive(&bars->hash_done);   // waited on before the next unit's first reduction
+        if (FWDH && L == 0 && p.out_mode != UWC_OUT_I32) {
+          // no correction: scale the raw rows (the accumulators were released at their last read)
+#pragma unroll
+          for (int a = 0; a < 2; a++) {
+            if (a == 1 && !hasY) break;
+            if (row_of(a) >= p.m || c0 >= p.n) continue;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; hh++) {
+              uint32_t w[32];
+              const uint4* src = reinterpret_cast<const uint4*>(raw_of(a) + hh * 32);
+#pragma unroll
+              for (int i = 0; i < 8; i++) {
+                const uint4 t = __ldcg(src + i);
+                w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+              }
+              store_row32_inplace(p, row_of(a), c0 + hh * 32, w);
+            }
+          }
+        }
+        if (FWDH && L > 0) {
+          // the correction: shift R by 7 bits between limbs (Horner), then out = raw - R
+          for (int step = 0; step + 1 < L && ok; step++) {
+#pragma unroll
+            for (int a = 0; a < 2; a++) {
+              if ((a == 1 && !hasY) || !ok) break;
+              ok = warp_wait(&bars->c_ready[a], cready[a]++ & 1, abort_flag, p.status, p.wait_ns);
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll 1
+              for (int hh = 0; hh < 2; hh++) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(colX + a * 256 + hh * 32, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++) v[i] <<= 7;
+                tmem_st_32x32b_x32(colX + a * 256 + hh * 32, v);
+              }
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars->c_shifted[a]);
+            }
+          }
+#pragma unroll
+          for (int a = 0; a < 2; a++) {
+            if ((a == 1 && !hasY) || !ok) break;
+            ok = warp_wait(&bars->c_ready[a], cready[a]++ & 1, abort_flag, p.status, p.wait_ns);
+            if (!ok) break;
+            tc_fence_after();
+            const bool live = row_of(a) < p.m && c0 < p.n;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; hh++) {
+              uint32_t rr[32];
+              tmem_ld_32x32b_x32(colX + a * 256 + hh * 32, rr);
+              tmem_wait_ld();
+              if (live) {
+                // the raw row this thread stored at the last snapshot (program order: its own writes)
+                const uint4* src = reinterpret_cast<const uint4*>(raw_of(a) + hh * 32);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                  const uint4 t = __ldcg(src + i);
+                  rr[4 * i] = t.x - rr[4 * i];
+                  rr[4 * i + 1] = t.y - rr[4 * i + 1];
+                  rr[4 * i + 2] = t.z - rr[4 * i + 2];
+                  rr[4 * i + 3] = t.w - rr[4 * i + 3];
+                }
+                store_row32_inplace(p, row_of(a), c0 + hh * 32, rr);
+              }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty[a]);   // the accumulator is free for the next unit
+          }
+        }
+        continue;
+      }
+
+      // ---- FWD (a = cb / 2, the column half; this warp's columns (cb % 2) * 64) and CORR
+      const int a0 = cb >> 1;
+      const uint32_t col0 = tmem + lane_base + a0 * 128 + (cb & 1) * 64;
 
       if (C::CORR && !(MODE == MODE_CORR && L <= 2)) {
         // Horner: R <<= 7 between limbs (all 16 warps, 64 columns of R each)
         for (int step = 0; step + 1 < L && ok; step++) {
-          ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
+          ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status, p.wait_ns);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
@@ -650,10 +892,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
       if (MODE == MODE_CORR) {
-        // out = acc - R (R = 0 without denoising), acc read back from the int32 matrix the
-        // mining pass stored, then scaled / converted to the output format
+        // out = acc - R (R = 0 without denoising), acc read back from the summed int32 product,
+        // then scaled / converted to the output format
         if (L > 0) {
-          ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
+          ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status, p.wait_ns);
           if (!ok) break;
           tc_fence_after();
         }
@@ -715,122 +957,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
-      // consume one snapshot of accumulator `a` at TMEM address `col`; returns this thread's fold
-      auto consume = [&](int a, uint32_t col, bool last) -> uint32_t {
-        ok = warp_wait(&bars->acc_full[a], snaps[a] & 1, abort_flag, p.status);
-        if (!ok) return 0u;
-        snaps[a]++;
+      // FWD: the unit's only snapshot: out = acc - R for this warp's 32 rows x 64 columns
+      ok = warp_wait(&bars->acc_full[a0], snaps[a0] & 1, abort_flag, p.status, p.wait_ns);
+      if (!ok) break;
+      snaps[a0]++;
+      tc_fence_after();
+      if (L > 0) {
+        ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status, p.wait_ns);
+        if (!ok) break;
         tc_fence_after();
-        uint32_t pt[4] = {0u, 0u, 0u, 0u};
-        uint32_t v[32], v2[32];
-        if (C::HASH) {
-          // both halves in flight at once; the accumulator is released as soon as they landed
-          tmem_ld_32x32b_x32(col, v);
-          tmem_ld_32x32b_x32(col + 32, v2);
-          tmem_wait_ld();
-        }
-        if (MODE == MODE_FWD && last) {
-          if (C::HASH) {
-            fold_row32(v, pt);
-            fold_row32(v2, pt);
-          }
-          // output: acc - R for this warp's 32 rows x 64 columns, then release acc and R
-          if (L > 0) {
-            ok = warp_wait(&bars->r_full, r_waits++ & 1, abort_flag, p.status);
-            if (!ok) return 0u;
-            tc_fence_after();
-          }
-          if (p.out_mode != UWC_OUT_NONE) {
+      }
+      if (p.out_mode != UWC_OUT_NONE) {
 #pragma unroll 1
-            for (int hh = 0; hh < 2; hh++) {
-              uint32_t w[32];
-              tmem_ld_32x32b_x32(col + hh * 32, w);
+        for (int hh = 0; hh < 2; hh++) {
+          uint32_t w[32];
+          tmem_ld_32x32b_x32(col0 + hh * 32, w);
+          tmem_wait_ld();
+          if (L > 0) {
+#pragma unroll
+            for (int qq = 0; qq < 2; qq++) {
+              uint32_t rr[16];
+              tmem_ld_32x32b_x16(tmem + 256 + cb * 64 + hh * 32 + qq * 16 + lane_base, rr);
               tmem_wait_ld();
-              if (L > 0) {
 #pragma unroll
-                for (int qq = 0; qq < 2; qq++) {
-                  uint32_t rr[16];
-                  tmem_ld_32x32b_x16(tmem + 256 + cb * 64 + hh * 32 + qq * 16 + lane_base, rr);
-                  tmem_wait_ld();
-#pragma unroll
-                  for (int i = 0; i < 16; i++) w[qq * 16 + i] -= rr[i];
-                }
-              }
-              store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + hh * 32, reinterpret_cast<const int32_t*>(w));
+              for (int i = 0; i < 16; i++) w[qq * 16 + i] -= rr[i];
             }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&bars->acc_empty[a]);
-            if (L > 0) mbar_arrive(&bars->r_empty);
-          }
-        } else {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
-          if (C::HASH) {
-            fold_row32(v, pt);
-            fold_row32(v2, pt);
-          }
-          if (MODE == MODE_MINE_OUT && last) {
-            // the finished product, raw int32, staged through this warp's shared-memory tile so the
-            // stores are row-contiguous (4 rows x 128 bytes per instruction)
-            uint32_t* const tile = tiles + warp * C::TILE_WORDS;
-            const int r0 = m0 + a * 128 + 32 * q, cl = 4 * (lane & 7);
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-              const uint32_t* src = hh ? v2 : v;
-#pragma unroll
-              for (int j = 0; j < 32; j++) tile[lane * 33 + j] = src[j];
-              __syncwarp();
-              const int c = n0 + cb * 64 + hh * 32 + cl;
-#pragma unroll
-              for (int pass = 0; pass < 8; pass++) {
-                const int rl = pass * 4 + (lane >> 3), row = r0 + rl;
-                const uint32_t* t = tile + rl * 33 + cl;
-                if (row < p.m && c < p.n)
-                  *reinterpret_cast<uint4*>(static_cast<int32_t*>(p.out) + (uint64_t)row * p.n + c) =
-                      make_uint4(t[0], t[1], t[2], t[3]);
-              }
-              __syncwarp();
-            }
-          }
+          store_row32(p, m0 + 32 * q + lane, n0 + cb * 64 + hh * 32, reinterpret_cast<const int32_t*>(w));
         }
-        return C::HASH ? reduce_scatter4(pt, lane) : 0u;
-      };
-
-      if (C::HASH) {
-        const int slot0 = ((0 * 2 + rb) * 4 + cb) * 32 + tslot, slot1 = ((1 * 2 + rb) * 4 + cb) * 32 + tslot;
-        // slot s = c % 16 is updated again by the chunks c + 16, c + 32, ... < nch: the
-        // contribution of chunk c is rotated 13 bits for each of those later updates
-        auto chunk = [&](int c, bool last) {
-          const int s = c & 15;
-          const int rot = (13 * ((nch - 1 - c) >> 4)) & 31;
-          const uint32_t x = consume(a0, col0, last);
-          if (!ok) return;
-          red_xor(msg + s * kMaxTiles + slot0, __funnelshift_l(x, x, rot));
-          if (hasY) {
-            const uint32_t y = consume(1, col1, last);
-            if (!ok) return;
-            red_xor(msg + s * kMaxTiles + slot1, __funnelshift_l(y, y, rot));
-          }
-        };
-        // the last chunk of MINE_OUT (which also stores the product) is peeled off the loop
-        const int nloop = MODE == MODE_MINE_OUT ? nch - 1 : nch;
-        for (int c = 0; c < nloop && ok; c++) chunk(c, false);
-        if (MODE == MODE_MINE_OUT && ok) chunk(nch - 1, true);
-        if (!ok) break;
-        // every thread's reductions of this unit are visible, then each thread hashes one tile.
-        // The buffer is cleared as it is read; its next user (two units on) starts only after the
-        // next unit's hand-off, which every thread reaches after its clears.
-        __threadfence();
-        mbar_arrive(&bars->hash_ready[buf]);
-        ok = warp_wait(&bars->hash_ready[buf], (local >> 1) & 1, abort_flag, p.status);
-        if (!ok) break;
-        hash_tile(p, msg, m0, n0, threadIdx.x);
-      } else {
-        consume(a0, col0, true);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars->acc_empty[a0]);
+        if (L > 0) mbar_arrive(&bars->r_empty);
       }
     }
   }
@@ -848,9 +1008,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
+// Test hooks (uwc_test_hook): the bound of every wait, and whether launches withhold their copies.
+std::atomic<uint64_t> g_wait_ns{0};
+std::atomic<int> g_withhold{0};
+
 template <int MODE, int R>
-int launch(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& ca, const CUtensorMap& cb,
+int launch(Params p, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& ca, const CUtensorMap& cb,
            cudaStream_t st) {
+  const uint64_t ns = g_wait_ns.load();
+  p.wait_ns = ns ? ns : UWC_WAIT_TIMEOUT_NS;
+  p.withhold = g_withhold.load();
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -879,13 +1046,11 @@ int launch_r(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const 
 }  // namespace
 
 namespace {
-// Workspace layout: tile messages (hashed calls), then the int32 product when a hashed call writes
-// bf16 (the second pass reads it back; I32 / F32 outputs hold it in place).
-uint64_t msg_bytes(int flags) {
-  return (flags & UWC_FLAG_HASH) ? (uint64_t)uwc_num_sms() * 2 * kMsgWords * 4 : 0;
-}
-bool needs_acc_buffer(int flags, int out_mode) {
-  return (flags & UWC_FLAG_HASH) && out_mode == UWC_OUT_BF16;
+// Workspace of a hashed call with a bf16 output: one 256 x 256 int32 staging block per CTA (the
+// raw product waits there for its correction and scaling; a bf16 output has no room for it).
+uint64_t stage_bytes(int flags, int out_mode) {
+  const bool staged = (flags & UWC_FLAG_HASH) && out_mode == UWC_OUT_BF16;
+  return staged ? (uint64_t)uwc_num_sms() * kStageRows * kUN * 4 : 0;
 }
 // Skinny plain GEMMs (decode-sized m, tensor-parallel shards of n) have fewer 128 x 256 output
 // blocks than half the SMs: they split k across units and add int32 partials.
@@ -895,9 +1060,20 @@ bool split_k(int m, int n) {
 }
 }  // namespace
 
+extern "C" int uwc_test_hook(int hook, long long value) {
+  if (hook == UWC_HOOK_WAIT_NS && value >= 0) {
+    g_wait_ns.store((uint64_t)value);
+    return UWC_OK;
+  }
+  if (hook == UWC_HOOK_WITHHOLD && (value == 0 || value == 1)) {
+    g_withhold.store((int)value);
+    return UWC_OK;
+  }
+  return UWC_ERR_ARG;
+}
+
 extern "C" uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mode) {
-  uint64_t bytes = msg_bytes(flags);
-  if (needs_acc_buffer(flags, out_mode) && m > 0 && n > 0) bytes += (uint64_t)m * n * 4;
+  uint64_t bytes = stage_bytes(flags, out_mode);
   // split-K with a scaled output: the int32 product is summed here, then scaled by a second pass
   if (!flags && (out_mode == UWC_OUT_F32 || out_mode == UWC_OUT_BF16) && m > 0 && n > 0 && split_k(m, n))
     bytes += (uint64_t)m * n * 4;
@@ -934,7 +1110,6 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   p.hash = hash; p.denoise = denoise; p.lmax = lmax; p.out_mode = out_mode; p.max_wins = max_wins;
   p.maxabs = maxabs; p.key = key; p.target = target; p.wins = wins;
   p.a_scale = a_scale; p.b_scale = b_scale; p.out = out;
-  p.msgbuf = static_cast<uint32_t*>(workspace);
   p.status = uwc_status_ptr();
   p.one = 1u;
   p.b_bdiv = 1;
@@ -948,7 +1123,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   if (rc == UWC_OK) rc = uwc_make_tmap_2d(&tb, B, (uint64_t)n, (uint64_t)k, (uint64_t)k, kUN, kKB);
   if (rc != UWC_OK) return rc;
   if (denoise) {
-    rc = uwc_make_tmap_2d(&tca, corrA, (uint64_t)lmax * m, (uint64_t)2 * r, (uint64_t)2 * r, 128, kKB);
+    rc = uwc_make_tmap_2d(&tca, corrA, (uint64_t)lmax * m, (uint64_t)2 * r, (uint64_t)2 * r, UM, kKB);
     if (rc == UWC_OK) rc = uwc_make_tmap_2d(&tcb, corrB, (uint64_t)lmax * n, (uint64_t)2 * r, (uint64_t)2 * r, kUN, kKB);
     if (rc != UWC_OK) return rc;
   } else {
@@ -970,8 +1145,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     const int splits = std::min(kblocks, std::max(1, uwc_num_sms() / p.nunits));
     p.kps = (kblocks + splits - 1) / splits;
     p.nsplit = (kblocks + p.kps - 1) / p.kps;
-    int32_t* acc = out_mode == UWC_OUT_I32 ? static_cast<int32_t*>(out)
-                                           : reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + msg_bytes(flags));
+    int32_t* acc = out_mode == UWC_OUT_I32 ? static_cast<int32_t*>(out) : static_cast<int32_t*>(workspace);
     if (cudaMemsetAsync(acc, 0, (size_t)m * n * 4, st) != cudaSuccess) {
       cudaGetLastError();
       return UWC_ERR_CUDA;
@@ -991,33 +1165,16 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     return launch<MODE_CORR, 0>(q, ta, tb, tca, tcb, st);
   }
 
-  // Hashed: the mining schedule hashes every tile. With an output it also stores the finished
-  // product as raw int32, into `out` (I32 / F32 outputs, rewritten in place) or into the workspace
-  // (BF16); a second pass then writes out = acc - R (R = 0 without denoising), scaled.
-  int32_t* acc = nullptr;
-  if (out_mode != UWC_OUT_NONE) {
-    acc = needs_acc_buffer(flags, out_mode)
-              ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + msg_bytes(flags))
-              : static_cast<int32_t*>(out);
-    p.out = acc;
-    p.out_mode = UWC_OUT_I32;
-  }
+  // Hashed: the mining schedule hashes every tile; with an output the same kernel writes it (and
+  // subtracts the correction first when denoising)
   p.nm = (m + 255) / 256;
   p.nunits = p.nm * p.nn;
-  rc = out_mode == UWC_OUT_NONE ? launch_r<MODE_MINE>(p, ta, tb, tca, tcb, st)
-                                : launch_r<MODE_MINE_OUT>(p, ta, tb, tca, tcb, st);
-  const bool second_pass = out_mode != UWC_OUT_NONE && (denoise || out_mode != UWC_OUT_I32);
-  if (rc != UWC_OK || !second_pass) return rc;
-
-  Params q = p;
-  q.hash = 0;
-  q.nsplit = 1;
-  q.out = out;
-  q.out_mode = out_mode;
-  q.acc_in = acc;
-  q.nm = (m + 127) / 128;
-  q.nunits = q.nm * q.nn;
-  return launch<MODE_CORR, 0>(q, ta, tb, tca, tcb, st);
+  if (out_mode == UWC_OUT_NONE) {
+    p.denoise = 0;
+    return launch_r<MODE_MINE>(p, ta, tb, tca, tcb, st);
+  }
+  p.stage = stage_bytes(flags, out_mode) ? static_cast<int32_t*>(workspace) : nullptr;
+  return launch_r<MODE_MINE_FWD>(p, ta, tb, tca, tcb, st);
 }
 
 // Batched exact int8 GEMM, int32 out: out[bt] (m x n) = A[bt] B[bt / b_bdiv]^T for bt < nbatch, A[bt]

@@ -156,16 +156,17 @@ UWC_DEVI bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity. Returns false (and raises the CTA's abort
-// flag and the device status) after UWC_WAIT_TIMEOUT_NS, or as soon as another thread of the CTA
-// has raised the abort flag.
-UWC_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
+// flag and the device status) after timeout_ns (default UWC_WAIT_TIMEOUT_NS), or as soon as another
+// thread of the CTA has raised the abort flag.
+UWC_DEVI bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status,
+                        uint64_t timeout_ns = UWC_WAIT_TIMEOUT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > UWC_WAIT_TIMEOUT_NS) {
+      if (globaltimer() - t0 > timeout_ns) {
         *abort_flag = 1;
         set_status(status, UWC_DEV_TIMEOUT);
         return false;

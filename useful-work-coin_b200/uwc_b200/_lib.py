@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(HERE, "libuwcb200.so")
 
 OK, ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_CUDA, ERR_DEVICE, ERR_SCRATCH = range(7)
 DEV_TIMEOUT = 1
+HOOK_WAIT_NS, HOOK_WITHHOLD = 1, 2
 
 # (name, restype, argtypes) for every function declared in include/uwc_b200.h
 _P, _U32, _U64, _I32, _F64 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_double
@@ -20,6 +21,7 @@ _I64, _F32 = ctypes.c_longlong, ctypes.c_float
 SIGNATURES = {
     "uwc_version": (_I32, []),
     "uwc_launch_count": (_U64, []),
+    "uwc_test_hook": (_I32, [_I32, _I64]),
     "uwc_status_string": (ctypes.c_char_p, [_I32]),
     "uwc_device_status": (_I32, [ctypes.POINTER(ctypes.c_uint32), _I32]),
     "uwc_b3_scratch_words": (_U64, [_U64]),
@@ -40,6 +42,8 @@ SIGNATURES = {
     "uwc_mined_setup_block": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _U64, _P, _U64, _P]),
     "uwc_mine_attempt": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _I32, _P, _U64, _P]),
     "uwc_mined_forward": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _P, _I32, _P, _U64, _P]),
+    "uwc_peak_i8": (_I32, [_I32, _P]),
+    "uwc_peak_i8_ops": (ctypes.c_double, [_I32]),
     "uwc_quant_act": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "uwc_quant_rows_had": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "uwc_fwht_absmax": (_I32, [_P, _I32, _I32, _I32, _P, _P]),

@@ -33,13 +33,28 @@ def linear_f32(q: torch.Tensor, s_x: torch.Tensor, Wq: torch.Tensor, s_w: torch.
 
 
 def patch_detlinear(DetLinear) -> None:
-    """Route DetLinear.int_gemm (qwen3.py:106-119) through this library for CUDA devices, the way
-    runtime/agent/mining.py:49-65 monkey-patches it; the CPU path stays the reference's."""
+    """Route DetLinear.int_gemm (runtime/detrt/qwen3.py:106-119) through this library on CUDA devices,
+    the way runtime/agent/mining.py:49-65 patches it for mining: a layer that mines with one of this
+    library's MinedWeights (lin.mine and lin.mw) runs the hashed forward on its rows padded to a
+    multiple of 64 (int32 out, unit scales); any other CUDA layer gets the exact int32 q @ Wq^T of
+    the tcgen05 GEMM. CPU layers keep the reference's own float64 path. The original method stays
+    reachable as DetLinear._orig_int_gemm; patching twice is a no-op."""
+    if getattr(DetLinear, "_uwc_b200_patched", False):
+        return
     orig = DetLinear.int_gemm
 
     def int_gemm_b200(self, q):
         if self.device.type != "cuda":
             return orig(self, q)
+        mw = getattr(self, "mw", None)
+        if getattr(self, "mine", False) and isinstance(mw, ops.MinedWeight):
+            m = q.shape[0]
+            mp = -(-m // 64) * 64
+            qp = torch.nn.functional.pad(q, (0, 0, 0, mp - m)) if mp != m else q
+            ones = torch.ones(mp, dtype=torch.float32, device=q.device)
+            return mw.forward(qp.contiguous(), ones, out_mode=ops.OUT_I32)[:m]
         return int_gemm(q, self.Wq)
 
+    DetLinear._orig_int_gemm = orig
     DetLinear.int_gemm = int_gemm_b200
+    DetLinear._uwc_b200_patched = True
