@@ -66,7 +66,8 @@ def test_patched_int_gemm_on_gpu(dev):
     mw = ops.MinedWeight(Bt=torch.from_numpy(Wq).cuda(), b_scale=torch.ones(512, device="cuda"), r=128)
     mw.setup_block(bytes(range(32)), glue.target_for(64, 512, 4))
     mined = Layer(torch.from_numpy(Wq).cuda(), "cuda", mw=mw)
-    got = mined.int_gemm(torch.from_numpy(q).cuda())
-    assert got.shape == (37, 512) and np.array_equal(got.cpu().numpy(), want)
+    qm = rng.integers(-64, 65, (37, 2048), dtype=np.int8)   # mined operands stay in [-64, 64] (quant_sym(64))
+    got = mined.int_gemm(torch.from_numpy(qm).cuda())
+    assert got.shape == (37, 512) and np.array_equal(got.cpu().numpy(), O.gemm_i32(qm, Wq))
     cpu = Layer(torch.from_numpy(Wq), "cpu")
     assert np.array_equal(cpu.int_gemm(torch.from_numpy(q)).numpy().astype(np.int64), want)

@@ -73,6 +73,11 @@ constexpr int kMsgWords = kMaxTiles * 16;               // one unit's tile messa
 constexpr int kStageRows = 256;                         // rows of a unit's raw-product staging block
 constexpr int kBarBytes = 256;
 
+// The epilogue's tensor-memory hand-offs (accumulator free, R shifted, R consumed) order only TMEM
+// accesses, so they arrive relaxed: a releasing arrive would first wait for the thread's earlier
+// output stores and message reductions, holding the tensor core back (measured at r = 64).
+#define ACC_ARRIVE mbar_arrive_relaxed
+
 struct Params {
   int m, n, k, r;
   int hash;         // FLAG_HASH
@@ -716,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->acc_empty[b]);
+        if (lane == 0) ACC_ARRIVE(&bars->acc_empty[b]);
         continue;
       }
 
@@ -748,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->acc_empty[a]);
+          if (lane == 0) ACC_ARRIVE(&bars->acc_empty[a]);
           uint32_t pt[4] = {0u, 0u, 0u, 0u};
           fold_row32(v, pt);
           fold_row32(v2, pt);
@@ -827,7 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem_wait_st();
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(&bars->c_shifted[a]);
+              if (lane == 0) ACC_ARRIVE(&bars->c_shifted[a]);
             }
           }
 #pragma unroll
@@ -858,7 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc_empty[a]);   // the accumulator is free for the next unit
+            if (lane == 0) ACC_ARRIVE(&bars->acc_empty[a]);   // the accumulator is free for the next unit
           }
         }
         continue;
@@ -887,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->r_scaled);
+          if (lane == 0) ACC_ARRIVE(&bars->r_scaled);
         }
         if (!ok) break;
       }
@@ -952,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (L > 0) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars->r_empty);
+          if (lane == 0) ACC_ARRIVE(&bars->r_empty);
         }
         continue;
       }
@@ -989,8 +994,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bars->acc_empty[a0]);
-        if (L > 0) mbar_arrive(&bars->r_empty);
+        ACC_ARRIVE(&bars->acc_empty[a0]);
+        if (L > 0) ACC_ARRIVE(&bars->r_empty);
       }
     }
   }

@@ -140,6 +140,12 @@ UWC_DEVI void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.clus
 UWC_DEVI void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Arrive without release semantics: for hand-offs that only order tensor-memory accesses (a TMEM
+// read finished with tcgen05.wait::ld, then tcgen05.fence::before_thread_sync) and must not wait
+// for this thread's earlier global or shared-memory writes to complete, as a release would.
+UWC_DEVI void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 UWC_DEVI void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
