@@ -145,11 +145,12 @@ int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_o
  *                            (same expression in fp32, the detrt dequant).
  * Without flags any m >= 1 works (rows past m are read as zero and not stored); k % 16 == 0.
  * workspace: device memory of at least uwc_gemm_workspace_bytes(m, n, flags, out_mode) bytes,
- *            16-byte aligned, any contents (the kernels clear what they use); unused (may be NULL)
- *            when that size is 0 (no FLAG_HASH). A hashed call with a BF16 output keeps the int32
- *            product there (m * n * 4 bytes) for its second (correction / scaling) pass; with I32
- *            / F32 outputs it is kept in `out` and rewritten in place. Hashed calls that overlap
- *            on the GPU must not share a workspace. */
+ *            16-byte aligned, any contents; unused (may be NULL) when that size is 0. Hashed calls
+ *            without an output need none (the tile messages live in shared memory). A hashed call
+ *            with an output runs as one kernel and stages each unit's raw int32 product there
+ *            (256 KiB per SM) until the unit's tile hashes and correction are done; a plain
+ *            split-K call with an F32 / BF16 output sums its int32 partials there (m * n * 4
+ *            bytes). Calls that overlap on the GPU must not share a workspace. */
 uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mode);
 int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
              const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key, const uint32_t* target,

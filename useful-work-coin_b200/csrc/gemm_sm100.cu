@@ -70,7 +70,7 @@ constexpr int kKB = 128;                                // K bytes per stage (on
 constexpr int kUN = 256;                                // output columns per unit
 constexpr int kMaxTiles = 512;                          // hash tiles per unit (MINE)
 constexpr int kMsgWords = kMaxTiles * 16;               // one unit's tile messages (32 KiB, shared memory)
-constexpr int kStageRows = 256;                         // rows of a unit's raw-product staging block
+constexpr int kStageWords = 2 * kEpiWarps * 32 * 64;   // a unit's raw products: 2 accumulators x 512 threads x 64
 constexpr int kBarBytes = 256;
 
 // The epilogue's tensor-memory hand-offs (accumulator free, R shifted, R consumed) order only TMEM
@@ -91,7 +91,7 @@ struct Params {
   const uint32_t* key;
   const uint32_t* target;
   uint32_t* wins;
-  int32_t* stage;          // MODE_MINE_FWD with a bf16 output: per CTA a 256 x 256 int32 block
+  int32_t* stage;          // MODE_MINE_FWD: per CTA kStageWords int32 (the unit's raw products, thread-interleaved)
   const int32_t* acc_in;   // MODE_CORR: the summed int32 split-K product, m x n
   const float* a_scale;
   const float* b_scale;
@@ -143,6 +143,7 @@ struct Bars {
   uint64_t c_shifted[2];    // MODE_MINE_FWD, per accumulator: the epilogue shifted R by 7 bits
   uint64_t hash_ready;      // every epilogue thread's XOR reductions of the unit landed
   uint64_t hash_done;       // every tile of the unit hashed and its message words cleared
+  uint64_t tiles_done;      // MINE_FWD: the output pass's transpose tiles (in the message buffer) re-zeroed
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -271,35 +272,6 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int c0, co
   }
 }
 
-// store_row32 converting in place: v (32 int32 of one row, columns c0..c0+31 < n, n % 64 == 0)
-// is overwritten with the output words, so no second 32-register array is live (the mining
-// schedule's epilogue holds a whole 64-column snapshot when it stores).
-__device__ __forceinline__ void store_row32_inplace(const Params& p, int row, int c0, uint32_t* v) {
-  if (p.out_mode == UWC_OUT_NONE || row >= p.m || c0 >= p.n) return;
-  if (p.out_mode == UWC_OUT_BF16) {
-    const float sx = p.a_scale[row];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const float f0 = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i]), sx), __ldg(p.b_scale + c0 + 2 * i));
-      const float f1 = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[2 * i + 1]), sx), __ldg(p.b_scale + c0 + 2 * i + 1));
-      v[i] = bf16_rne(f0) | (bf16_rne(f1) << 16);
-    }
-    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (uint64_t)row * p.n + c0);
-#pragma unroll
-    for (int i = 0; i < 4; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    return;
-  }
-  if (p.out_mode == UWC_OUT_F32) {
-    const float sx = p.a_scale[row];
-#pragma unroll
-    for (int i = 0; i < 32; i++)
-      v[i] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int32_t)v[i]), sx), __ldg(p.b_scale + c0 + i)));
-  }
-  uint4* o = reinterpret_cast<uint4*>(static_cast<uint32_t*>(p.out) + (uint64_t)row * p.n + c0);
-#pragma unroll
-  for (int i = 0; i < 8; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-}
-
 // Four consecutive outputs of one row (c % 4 == 0, n % 4 == 0) in the chosen format.
 __device__ __forceinline__ void store4(const Params& p, int row, int c, int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
   if (p.out_mode == UWC_OUT_I32) {
@@ -392,13 +364,35 @@ __device__ __forceinline__ void hash_tile(const Params& p, uint32_t* msg, int m0
   }
 }
 
-// 64 consecutive int32 of one row (both halves of a thread's snapshot) to global memory, raw.
-__device__ __forceinline__ void store_raw64(int32_t* dst, const uint32_t* v, const uint32_t* v2) {
-  uint4* o = reinterpret_cast<uint4*>(dst);
+// A thread's 64 raw values (both halves of its last snapshot) into the CTA's staging block,
+// thread-interleaved: quad i of thread T at uint4 index i * 512 + T, so every store instruction of a
+// warp writes 512 contiguous bytes (a row-major store would touch 32 lines per instruction).
+__device__ __forceinline__ void store_raw64(uint4* stage, int tid, const uint32_t* v, const uint32_t* v2) {
 #pragma unroll
-  for (int i = 0; i < 8; i++) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  for (int i = 0; i < 8; i++) stage[i * 512 + tid] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 #pragma unroll
-  for (int i = 0; i < 8; i++) o[8 + i] = make_uint4(v2[4 * i], v2[4 * i + 1], v2[4 * i + 2], v2[4 * i + 3]);
+  for (int i = 0; i < 8; i++)
+    stage[(8 + i) * 512 + tid] = make_uint4(v2[4 * i], v2[4 * i + 1], v2[4 * i + 2], v2[4 * i + 3]);
+}
+
+// 16 int32 of one row (columns c0..c0+15) converted in place to the output words: I32 as is, F32
+// the detrt dequant, BF16 packed pairs in w[0..7]. Returns the number of 16-byte quads (4 or 2).
+__device__ __forceinline__ int convert16(const Params& p, int row, int c0, uint32_t* w) {
+  if (p.out_mode == UWC_OUT_I32) return 4;
+  const float sx = row < p.m ? p.a_scale[row] : 0.f;
+  if (p.out_mode == UWC_OUT_F32) {
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+      w[i] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int32_t)w[i]), sx), __ldg(p.b_scale + c0 + i)));
+    return 4;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float f0 = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)w[2 * i]), sx), __ldg(p.b_scale + c0 + 2 * i));
+    const float f1 = __fmul_rn(__fmul_rn(__int2float_rn((int32_t)w[2 * i + 1]), sx), __ldg(p.b_scale + c0 + 2 * i + 1));
+    w[i] = bf16_rne(f0) | (bf16_rne(f1) << 16);
+  }
+  return 2;
 }
 
 // Warp-wide bounded wait: every lane polls the barrier (measured faster to wake than one polling
@@ -437,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // message hand-offs are signalled by every epilogue thread (arrival counts in threads)
     mbar_init(&bars->hash_ready, kEpiWarps * 32);
     mbar_init(&bars->hash_done, kEpiWarps * 32);
+    mbar_init(&bars->tiles_done, kEpiWarps * 32);
     mbar_init(&bars->r_full, 1);
     mbar_init(&bars->r_scaled, kEpiWarps);
     mbar_init(&bars->r_empty, kEpiWarps);
@@ -734,12 +729,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int slot[2] = {((0 * 2 + rb) * 4 + cb) * 32 + tslot, ((1 * 2 + rb) * 4 + cb) * 32 + tslot};
         const int c0 = n0 + cb * 64;
         auto row_of = [&](int a) { return m0 + a * 128 + 32 * q + lane; };
-        // where a forward keeps the thread's raw product row until it is corrected / scaled: its
-        // own output row (int32 / fp32 outputs), or the CTA's staging block (bf16)
-        auto raw_of = [&](int a) -> int32_t* {
-          if (p.out_mode == UWC_OUT_BF16)
-            return p.stage + ((uint64_t)blockIdx.x * kStageRows + a * 128 + 32 * q + lane) * kUN + cb * 64;
-          return static_cast<int32_t*>(p.out) + (uint64_t)row_of(a) * p.n + c0;
+        // this thread's raw product slots for accumulator a in the CTA's staging block
+        auto stage_of = [&](int a) {
+          return reinterpret_cast<uint4*>(p.stage + ((uint64_t)blockIdx.x * 2 + a) * (kStageWords / 2));
         };
         // consume one snapshot of accumulator a: read 64 values, release the accumulator, fold
         auto consume = [&](int a, bool last) -> uint32_t {
@@ -757,9 +749,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pt[4] = {0u, 0u, 0u, 0u};
           fold_row32(v, pt);
           fold_row32(v2, pt);
-          // the last snapshot of a forward: the raw row goes out (the int32 output itself when
-          // nothing is subtracted or scaled), to be finished after the unit's hashes
-          if (FWDH && last && row_of(a) < p.m && c0 < p.n) store_raw64(raw_of(a), v, v2);
+          // the last snapshot of a forward: the raw values wait in the staging block until the
+          // unit's hashes are done (and the correction has landed), then go out
+          if (FWDH && last) store_raw64(stage_of(a), threadIdx.x, v, v2);
           return reduce_scatter4(pt, lane);
         };
         // the previous unit's tile hashes clear the message words this unit reduces into
@@ -775,7 +767,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t x = consume(a, last);
             if (!ok) break;
             if (clear_pending) {
-              ok = warp_wait(&bars->hash_done, (local - 1) & 1, abort_flag, p.status, p.wait_ns);
+              // the message words are zero again: hashes done (MINE), transpose tiles re-zeroed (FWD)
+              ok = warp_wait(FWDH ? &bars->tiles_done : &bars->hash_done, (local - 1) & 1, abort_flag, p.status,
+                             p.wait_ns);
               clear_pending = false;
               if (!ok) break;
             }
@@ -791,28 +785,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = warp_wait(&bars->hash_ready, local & 1, abort_flag, p.status, p.wait_ns);
         if (!ok) break;
         hash_tile(p, msg, m0, n0, threadIdx.x);
-        mbar_arrive(&bars->hash_done);   // waited on before the next unit's first reduction
-        if (FWDH && L == 0 && p.out_mode != UWC_OUT_I32) {
-          // no correction: scale the raw rows (the accumulators were released at their last read)
-#pragma unroll
-          for (int a = 0; a < 2; a++) {
-            if (a == 1 && !hasY) break;
-            if (row_of(a) >= p.m || c0 >= p.n) continue;
-#pragma unroll 1
-            for (int hh = 0; hh < 2; hh++) {
-              uint32_t w[32];
-              const uint4* src = reinterpret_cast<const uint4*>(raw_of(a) + hh * 32);
-#pragma unroll
-              for (int i = 0; i < 8; i++) {
-                const uint4 t = __ldcg(src + i);
-                w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
-              }
-              store_row32_inplace(p, row_of(a), c0 + hh * 32, w);
-            }
-          }
-        }
-        if (FWDH && L > 0) {
-          // the correction: shift R by 7 bits between limbs (Horner), then out = raw - R
+        mbar_arrive(&bars->hash_done);   // waited on before the next unit's first reduction (MINE)
+        if (FWDH) {
+          // ---- the output: correction (Horner: shift R by 7 bits between limbs), then out = raw - R,
+          // scaled. The message buffer is idle until the next unit's first reduction: each warp
+          // transposes its rows through 2 KiB of it, so the stores are row-contiguous.
           for (int step = 0; step + 1 < L && ok; step++) {
 #pragma unroll
             for (int a = 0; a < 2; a++) {
@@ -835,36 +812,68 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) ACC_ARRIVE(&bars->c_shifted[a]);
             }
           }
+          if (!ok) break;
+          // every thread has read and cleared its tile's message words
+          ok = warp_wait(&bars->hash_done, local & 1, abort_flag, p.status, p.wait_ns);
+          if (!ok) break;
+          uint4* const tile = reinterpret_cast<uint4*>(msg) + warp * 128;   // 32 rows x 16 words
 #pragma unroll
           for (int a = 0; a < 2; a++) {
             if ((a == 1 && !hasY) || !ok) break;
-            ok = warp_wait(&bars->c_ready[a], cready[a]++ & 1, abort_flag, p.status, p.wait_ns);
-            if (!ok) break;
-            tc_fence_after();
-            const bool live = row_of(a) < p.m && c0 < p.n;
-#pragma unroll 1
-            for (int hh = 0; hh < 2; hh++) {
-              uint32_t rr[32];
-              tmem_ld_32x32b_x32(colX + a * 256 + hh * 32, rr);
-              tmem_wait_ld();
-              if (live) {
-                // the raw row this thread stored at the last snapshot (program order: its own writes)
-                const uint4* src = reinterpret_cast<const uint4*>(raw_of(a) + hh * 32);
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                  const uint4 t = __ldcg(src + i);
-                  rr[4 * i] = t.x - rr[4 * i];
-                  rr[4 * i + 1] = t.y - rr[4 * i + 1];
-                  rr[4 * i + 2] = t.z - rr[4 * i + 2];
-                  rr[4 * i + 3] = t.w - rr[4 * i + 3];
-                }
-                store_row32_inplace(p, row_of(a), c0 + hh * 32, rr);
-              }
+            if (L > 0) {
+              ok = warp_wait(&bars->c_ready[a], cready[a]++ & 1, abort_flag, p.status, p.wait_ns);
+              if (!ok) break;
+              tc_fence_after();
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) ACC_ARRIVE(&bars->acc_empty[a]);   // the accumulator is free for the next unit
+            const uint4* st = stage_of(a);
+#pragma unroll 1
+            for (int sl = 0; sl < 4; sl++) {   // 16-column slices of the warp's 64 columns
+              uint32_t w[16];
+#pragma unroll
+              for (int i = 0; i < 4; i++) {
+                const uint4 t = __ldcg(st + (4 * sl + i) * 512 + threadIdx.x);
+                w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+              }
+              if (L > 0) {
+                uint32_t rr[16];
+                tmem_ld_32x32b_x16(colX + a * 256 + 16 * sl, rr);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) w[i] -= rr[i];
+              }
+              const int nq = convert16(p, row_of(a), c0 + 16 * sl, w);
+              // row `lane` of the tile, quads swizzled by (row >> 1) & 3: conflict-free both ways
+#pragma unroll
+              for (int i = 0; i < 4; i++)
+                if (i < nq) tile[lane * 4 + (i ^ ((lane >> 1) & 3))] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+              __syncwarp();
+              if (c0 < p.n) {
+                // nq lanes per row, 32 / nq rows per instruction, 16 contiguous bytes per lane
+                const int per = 32 / nq;
+#pragma unroll 1
+                for (int r0 = 0; r0 < 32; r0 += per) {
+                  const int tr = r0 + lane / nq, qd = lane % nq, row = m0 + a * 128 + 32 * q + tr;
+                  const uint4 val = tile[tr * 4 + (qd ^ ((tr >> 1) & 3))];
+                  if (row < p.m) {
+                    uint8_t* o = static_cast<uint8_t*>(p.out) +
+                                 ((uint64_t)row * p.n + c0 + 16 * sl) * (p.out_mode == UWC_OUT_BF16 ? 2 : 4);
+                    reinterpret_cast<uint4*>(o)[qd] = val;
+                  }
+                }
+              }
+              __syncwarp();
+            }
+            if (L > 0) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) ACC_ARRIVE(&bars->acc_empty[a]);   // the accumulator is free for the next unit
+            }
           }
+          if (!ok) break;
+          // the tile goes back to zero (message words of the next unit), then the hand-off
+#pragma unroll
+          for (int i = 0; i < 4; i++) tile[lane * 4 + i] = make_uint4(0u, 0u, 0u, 0u);
+          mbar_arrive(&bars->tiles_done);
         }
         continue;
       }
@@ -1051,11 +1060,11 @@ int launch_r(const Params& p, const CUtensorMap& a, const CUtensorMap& b, const 
 }  // namespace
 
 namespace {
-// Workspace of a hashed call with a bf16 output: one 256 x 256 int32 staging block per CTA (the
-// raw product waits there for its correction and scaling; a bf16 output has no room for it).
+// Workspace of a hashed call with an output: per CTA one staging block of kStageWords int32 (a unit's
+// raw products wait there, thread-interleaved, for the unit's hashes and correction; 256 KiB).
 uint64_t stage_bytes(int flags, int out_mode) {
-  const bool staged = (flags & UWC_FLAG_HASH) && out_mode == UWC_OUT_BF16;
-  return staged ? (uint64_t)uwc_num_sms() * kStageRows * kUN * 4 : 0;
+  const bool staged = (flags & UWC_FLAG_HASH) && out_mode != UWC_OUT_NONE;
+  return staged ? (uint64_t)uwc_num_sms() * kStageWords * 4 : 0;
 }
 // Skinny plain GEMMs (decode-sized m, tensor-parallel shards of n) have fewer 128 x 256 output
 // blocks than half the SMs: they split k across units and add int32 partials.
