@@ -46,7 +46,7 @@ WORKLOADS = {
                                      "128-token greedy decode (configs[3])"),
 }
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this workload
-TRAFFIC = {"c3-mine": 148.7e6 + 4.0e6}
+TRAFFIC = {"c3-mine": 146.1e6 + 5.0e6}
 # Llama-3.1-8B linears of one layer: (name, n, k, kind); qkv n = (32 + 2 * 8) * 128
 C5_LINEARS = [("qkv", 6144, 4096, "col"), ("o", 4096, 4096, "row"), ("gate_up", 28672, 4096, "col"),
               ("down", 4096, 14336, "row")]
@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="c3-mine", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-run", action="store_true",
+                    help="only the timed steps and the dominant kernel's timing (no sustained loop, reference "
+                         "kernel, end-to-end or CPU legs): the command the ncu captures under profiles/ use")
     return ap.parse_args()
 
 
@@ -676,7 +679,7 @@ def run_b200(a, world, rank, local):
 
     # the reference's own GPU kernel on the same operands (rank 0; same key, target, corrections)
     ref = None
-    if rank == 0:
+    if rank == 0 and not a.profile_run:
         ref_out = torch.empty_like(out) if forward else None
         res = ref_gpu_kernel(stream, b["ApEA"], w.BpEBt, m, n, k, r, flags, b["a_seed"], w.target, w.max_wins, flush,
                              max(5, a.steps // 2), corrA=b["corrA"] if forward else None,
@@ -695,6 +698,11 @@ def run_b200(a, world, rank, local):
             ref = {"unavailable": "baseline/_ref/libref_noisy_gemm.so not built (needs the reference checkout)"}
     peak_live = tc_peak_i8(stream)
     peak_cublas = int8_peak(m, n, k, flush)
+    if a.profile_run:
+        if rank == 0:
+            print(json.dumps({"profile_run": a.workload, "ms_per_step": t_ms / a.steps, "kernel_ms": gemm_ms,
+                              "value": value, "unit": UNIT}), flush=True)
+        return
 
     # sustained: the same step back to back for >= 3 s (no flushes), median clock beside it
     n_sus = max(20, int(3.2e3 / max(t_ms / a.steps, 1e-3)))
