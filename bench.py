@@ -310,6 +310,16 @@ def run_c5(a, world, rank, local):
     qkv = tp.ColumnParallelLinear(W["qkv"], S["qkv"], bs, rank, world, dev)
     o = tp.RowParallelLinear(W["o"], S["o"], bs, rank, world, dev)
     mlp = tp.TPMLP(W["gate_up"], S["gate_up"], bs, W["down"], S["down"], bs, rank, world, dev)
+    # the same layer on this GPU alone (full weights, a one-rank group: no collectives), the parity
+    # reference of every TP step: integer sums make the two bit-identical
+    solo = None
+    if world > 1:
+        import torch.distributed as dist
+        groups = [dist.new_group([r_]) for r_ in range(world)]
+        solo = groups[rank]
+    o1 = tp.RowParallelLinear(W["o"], S["o"], bs, 0, 1, dev, group=solo)
+    mlp1 = tp.TPMLP(W["gate_up"], S["gate_up"], bs, W["down"], S["down"], bs, 0, 1, dev, group=solo)
+    qkv1 = tp.ColumnParallelLinear(W["qkv"], S["qkv"], bs, 0, 1, dev, group=solo)
     del W
     wn = 1 + 0.1 * torch.randn(D, device=dev, generator=g)
     x = torch.randn(m, D, device=dev, generator=g)
@@ -321,6 +331,20 @@ def run_c5(a, world, rank, local):
         qkv.forward(q1, s1)
         r1 = o.forward(oc, residual=xin)
         return mlp.forward(r1, wn, 1e-5)
+
+    # parity at this N: the TP step's qkv shard and layer output == the one-GPU layer, bit for bit
+    oc_full = torch.randn(m, o.k, device=dev, generator=torch.Generator(device=dev).manual_seed(78))
+    q1, s1 = detgpu.rmsnorm_quant(x, wn, 1e-5, bs)
+    y_tp = mlp.forward(o.forward(oc_full[:, o.lo:o.hi].contiguous(), residual=x), wn, 1e-5)
+    qkv_tp = qkv.forward(q1, s1)
+    y_1 = mlp1.forward(o1.forward(oc_full, residual=x), wn, 1e-5)
+    qkv_1 = qkv1.forward(q1, s1)[:, qkv.lo:qkv.hi]
+    parity = torch.tensor([int(torch.equal(y_tp, y_1) and torch.equal(qkv_tp, qkv_1))], device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(parity, op=dist.ReduceOp.MIN)
+    parity_ok = bool(parity.item())
+    del o1, mlp1, qkv1
 
     stream = torch.cuda.current_stream()
     xs = x.clone()                                   # the captured step's static input
@@ -393,7 +417,8 @@ def run_c5(a, world, rank, local):
                        "parallelism": f"tp{world}", "l2": "flushed (256 MiB write) before each step"},
             "roofline": roof,
             "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": m * D * 4, "d2h_bytes_per_step": m * D * 4},
-            "gpu_launches": launches, "clocks": clocks, "device_status": status}
+            "gpu_launches": launches, "clocks": clocks, "device_status": status,
+            "parity_ok": parity_ok, "parity": "TP step output and qkv shard == the same layer on one GPU, bit for bit"}
     if not a.no_cpu_baseline:
         rows = m if decode else 128
         dt, ops_, nb, th = c5_cpu_sample(rows)

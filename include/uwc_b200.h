@@ -207,7 +207,8 @@ int uwc_mined_setup_block(const int8_t* Bt, int n, int k, int r, const uint8_t* 
 int uwc_mine_attempt(const int8_t* A, int m, int n, int k, int r, const void* block, uint32_t* wins, int max_wins,
                      void* workspace, uint64_t workspace_bytes, void* stream);
 /* MinedWeight.forward (ops.py:281-347): the mining attempt's preparation, the rank-r projections
- * X = A P_B^T and Y = BpEBt P_A^T as balanced base-128 limbs (ops.py:152-168), then the GEMM with
+ * X = A P_B^T and Y = BpEBt P_A^T as balanced base-128 limbs (ops.py:152-168, on the tensor cores:
+ * the reference's UWC_PROJ_GEMM path), then the GEMM with
  * FLAG_DENOISE (and FLAG_HASH when hash != 0): out = A Bt^T exactly, in out_mode (I32, BF16, F32
  * with a_scale (m) and b_scale (n) as in uwc_gemm). The winning tiles equal uwc_mine_attempt's. */
 int uwc_mined_forward(const int8_t* A, int m, int n, int k, int r, const float* a_scale, const float* b_scale,

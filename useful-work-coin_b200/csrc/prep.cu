@@ -256,41 +256,53 @@ __global__ void __launch_bounds__(256, kNaCtasPerSm) k_noise_add(const int8_t* _
   }
 }
 
-// Projection of rows onto a noise permutation (the X / Y terms of the exact denoise, reference
-// kernels.cu:310-372): proj[row][j] = sum of src[row][l] over the columns l with first(l) == j minus
-// the sum over the columns with second(l) == j, written as lmax balanced base-128 limbs at
-// corr[li][row][corr_off + j] with max |proj| folded into *maxabs. Gather design: every CTA first
-// inverts the permutation into per-column index lists in shared memory (a counting sort of the k
-// pairs), then walks its share of the rows: the row is staged in shared memory and the threads
-// assigned to column j add up the bytes of j's two lists, so no value is scattered. The tensor-core
-// path (k_proj_matrix + the split-K GEMM + k_proj_corr) computes the same integers; the tests
-// compare the two. Optionally copies E (rows x r) into corr[li][row][ecopy_off + j] for every limb.
+// One pass over rows of src (reference kernels.cu:310-372, noise_rows): any of
+//   noising      dst = src + E[:, first] - E[:, second] under the permutation Pn;
+//   projection   proj[row][j] = sum of src[row][l] over the columns l with first(l) == j minus the
+//                sum over second(l) == j under Pp (the X / Y terms of the exact denoise), written as
+//                lmax balanced base-128 limbs at corr[li][row][corr_off + j], max |proj| folded into
+//                *maxabs;
+//   E copy       E[row] into corr[li][row][ecopy_off + j] for every limb.
+// Gather design: every CTA first inverts Pp into per-column index lists in shared memory (a counting
+// sort whose positions come from shared-memory counters: the order inside a list is arbitrary and
+// the integer sums do not depend on it), then walks its share of the rows: the row (and its E row)
+// is staged in shared memory, the noised row is written from it, and the threads assigned to
+// column j add up the bytes of j's two lists, so no value is scattered. The tensor-core path
+// (k_proj_matrix + the split-K GEMM + k_proj_corr) computes the same integers; the tests compare them.
 namespace {
 constexpr int kPrThreads = 256;
-constexpr int kPrCtasPerSm = 2;
 }
 
-__global__ void __launch_bounds__(kPrThreads, kPrCtasPerSm)
-    k_project_rows(const int8_t* __restrict__ src, int rows, int k, int r, const uint32_t* __restrict__ Pp,
-                   const int8_t* __restrict__ E, int8_t* __restrict__ corr, int corr_off, int ecopy_off,
-                   int32_t* __restrict__ maxabs, int lmax) {
+__global__ void __launch_bounds__(kPrThreads)
+    k_noise_project(const int8_t* __restrict__ src, int rows, int k, int r, const int8_t* __restrict__ E,
+                    const uint32_t* __restrict__ Pn, int8_t* __restrict__ dst, const uint32_t* __restrict__ Pp,
+                    int8_t* __restrict__ corr, int corr_off, int ecopy_off, int32_t* __restrict__ maxabs, int lmax) {
   extern __shared__ __align__(16) uint8_t pr_smem[];
-  // [plus start r+1][minus start r+1][plus list k][minus list k] (u16 columns), then the staged row
-  int* const pstart = reinterpret_cast<int*>(pr_smem);
-  int* const mstart = pstart + (r + 1);
-  uint16_t* const plist = reinterpret_cast<uint16_t*>(mstart + (r + 1));
+  // [row k][pn k u32 (noising)][plist k u16][mlist k u16][E row 256][red 256 int][pstart r+1]
+  // [mstart r+1][pcur r][mcur r]: every uint4-accessed part starts on a 16-byte boundary (k % 16 == 0)
+  int8_t* const row_s = reinterpret_cast<int8_t*>(pr_smem);
+  uint32_t* const pn_s = reinterpret_cast<uint32_t*>(pr_smem + k);
+  uint16_t* const plist = reinterpret_cast<uint16_t*>(pr_smem + k + (dst ? 4 * k : 0));
   uint16_t* const mlist = plist + k;
-  int8_t* const row_s = reinterpret_cast<int8_t*>(pr_smem + (((2 * (r + 1) * 4 + 4 * k) + 15) & ~15));
+  int8_t* const es = reinterpret_cast<int8_t*>(mlist + k);
+  int* const red = reinterpret_cast<int*>(es + 256);
+  int* const pstart = red + kPrThreads;
+  int* const mstart = pstart + (r + 1);
+  int* const pcur = mstart + (r + 1);
+  int* const mcur = pcur + r;
   const int tid = threadIdx.x;
   const int r0 = (int)((int64_t)blockIdx.x * rows / gridDim.x);
   const int r1 = (int)((int64_t)(blockIdx.x + 1) * rows / gridDim.x);
   if (r0 >= r1) return;
   const uint64_t limb_stride = (uint64_t)rows * 2 * r;
+  if (dst)
+    for (int q = tid; q < (k >> 2); q += kPrThreads)
+      reinterpret_cast<uint4*>(pn_s)[q] = __ldg(reinterpret_cast<const uint4*>(Pn) + q);
   if (Pp) {
-    // counting sort of the k columns by first (plus lists) and by second (minus lists)
+    // counting sort of the k columns by first (plus lists) and by second (minus lists); pairs
+    // naming a column >= r are not valid permutations and are left out of both lists
     for (int j = tid; j <= r; j += kPrThreads) pstart[j] = mstart[j] = 0;
     __syncthreads();
-    // (pairs naming a column >= r are not valid permutations and are left out of both lists)
     for (int l = tid; l < k; l += kPrThreads) {
       const uint32_t p = __ldg(Pp + l);
       if ((p & 0xFFFFu) < (uint32_t)r) atomicAdd(&pstart[(p & 0xFFFFu) + 1], 1);
@@ -303,44 +315,58 @@ __global__ void __launch_bounds__(kPrThreads, kPrCtasPerSm)
       for (int j = 0; j < r; j++) mstart[j + 1] += mstart[j];
     }
     __syncthreads();
-    // fill: one warp per column j keeps the columns in increasing order (ballot ranks)
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int j = warp; j < r; j += kPrThreads / 32) {
-      int pp = pstart[j], mp = mstart[j];
-      for (int l0 = 0; l0 < k; l0 += 32) {
-        const int l = l0 + lane;
-        const uint32_t p = l < k ? __ldg(Pp + l) : 0xFFFFFFFFu;
-        const bool isp = l < k && (int)(p & 0xFFFFu) == j, ism = l < k && (int)(p >> 16) == j;
-        const uint32_t bp = __ballot_sync(0xffffffffu, isp), bm = __ballot_sync(0xffffffffu, ism);
-        const uint32_t below = (1u << lane) - 1u;
-        if (isp) plist[pp + __popc(bp & below)] = (uint16_t)l;
-        if (ism) mlist[mp + __popc(bm & below)] = (uint16_t)l;
-        pp += __popc(bp);
-        mp += __popc(bm);
-      }
+    for (int j = tid; j < r; j += kPrThreads) {
+      pcur[j] = pstart[j];
+      mcur[j] = mstart[j];
     }
     __syncthreads();
+    for (int l = tid; l < k; l += kPrThreads) {
+      const uint32_t p = __ldg(Pp + l);
+      if ((p & 0xFFFFu) < (uint32_t)r) plist[atomicAdd(&pcur[p & 0xFFFFu], 1)] = (uint16_t)l;
+      if ((p >> 16) < (uint32_t)r) mlist[atomicAdd(&mcur[p >> 16], 1)] = (uint16_t)l;
+    }
   }
+  __syncthreads();
   const int parts = kPrThreads / r;   // threads per column: 4 (r 64), 2 (r 128), 1 (r 256)
   const int j = tid % r, part = tid / r;
+  const bool want_e = E && (dst || (corr && ecopy_off >= 0));
   int local_max = 0;
   for (int row = r0; row < r1; row++) {
+    const uint4* g = reinterpret_cast<const uint4*>(src + (uint64_t)row * k);
+    for (int q = tid; q < (k >> 4); q += kPrThreads) reinterpret_cast<uint4*>(row_s)[q] = __ldg(g + q);
+    if (want_e && tid < r / 16)
+      reinterpret_cast<uint4*>(es)[tid] = __ldg(reinterpret_cast<const uint4*>(E + (uint64_t)row * r) + tid);
+    __syncthreads();
+    if (dst) {
+      // values stay in int8 without wrapping for |src| <= 64, |E| <= 32
+      for (int q = tid; q < (k >> 4); q += kPrThreads) {
+        const uint4 w = reinterpret_cast<const uint4*>(row_s)[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+          uint32_t ov = 0;
+#pragma unroll
+          for (int b = 0; b < 4; b++) {
+            const uint32_t pv = pn_s[16 * q + 4 * v + b];
+            const int nv = (int)(int8_t)(ws[v] >> (8 * b)) + (int)es[(pv & 0xFFFFu) & (r - 1)] -
+                           (int)es[(pv >> 16) & (r - 1)];
+            ov |= (uint32_t)(uint8_t)(int8_t)nv << (8 * b);
+          }
+          o[v] = ov;
+        }
+        reinterpret_cast<uint4*>(dst + (uint64_t)row * k)[q] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
     if (Pp) {
-      const uint4* g = reinterpret_cast<const uint4*>(src + (uint64_t)row * k);
-      for (int q = tid; q < (k >> 4); q += kPrThreads) reinterpret_cast<uint4*>(row_s)[q] = __ldg(g + q);
-      __syncthreads();
       int acc = 0;
       for (int i = pstart[j] + part; i < pstart[j + 1]; i += parts) acc += row_s[plist[i]];
       for (int i = mstart[j] + part; i < mstart[j + 1]; i += parts) acc -= row_s[mlist[i]];
-      // the parts of column j are lanes tid, tid + r, ... of the same warp only when r < 32; sum
-      // them through shared memory (reusing the pstart-free tail of the row buffer is not safe)
-      __syncthreads();
-      int* const red = reinterpret_cast<int*>(row_s);
       red[tid] = acc;
       __syncthreads();
       if (part == 0) {
         int v = 0;
-        for (int q = 0; q < parts; q++) v += red[q * r + j];
+        for (int qq = 0; qq < parts; qq++) v += red[qq * r + j];
         local_max = max(local_max, abs(v));
         if (corr && corr_off >= 0) {
           const uint64_t base = (uint64_t)row * 2 * r + corr_off + j;
@@ -351,16 +377,16 @@ __global__ void __launch_bounds__(kPrThreads, kPrCtasPerSm)
           }
         }
       }
-      __syncthreads();
     }
-    if (E && corr && ecopy_off >= 0 && part == 0) {
-      const int8_t e = E[(uint64_t)row * r + j];
-      for (int li = 0; li < lmax; li++) corr[li * limb_stride + (uint64_t)row * 2 * r + ecopy_off + j] = e;
+    if (want_e && corr && ecopy_off >= 0 && tid < r) {
+      const int8_t e = es[tid];
+      for (int li = 0; li < lmax; li++) corr[li * limb_stride + (uint64_t)row * 2 * r + ecopy_off + tid] = e;
     }
+    __syncthreads();   // row_s, es and red are rewritten by the next row
   }
   if (Pp && maxabs) {
 #pragma unroll
-    for (int s = 16; s > 0; s >>= 1) local_max = max(local_max, __shfl_xor_sync(0xffffffffu, local_max, s));
+    for (int sft = 16; sft > 0; sft >>= 1) local_max = max(local_max, __shfl_xor_sync(0xffffffffu, local_max, sft));
     if ((tid & 31) == 0) atomicMax(maxabs, local_max);
   }
 }
@@ -498,22 +524,23 @@ int uwc_noise_rows(const int8_t* src, int rows, int k, int r, const int8_t* E, c
     uwc_count_launch();
     return uwc_launch_status();
   }
-  // projection (and the E copy when nothing is noised): the gather kernel; the rows are noised first
-  if (dst) {
-    const int grid = std::min(rows, uwc_num_sms() * kNaCtasPerSm);
-    k_noise_add<<<grid, 256, 0, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, corr, ecopy_off, lmax);
-    uwc_count_launch();
-  }
-  const int smem = (((2 * (r + 1) * 4 + 4 * k) + 15) & ~15) + std::max(k, kPrThreads * 4);
+  // noising with a projection and / or an E copy: the fused gather kernel, one pass over the rows
+  const int smem = k + (dst ? 4 * k : 0) + 4 * k + 4 * (4 * r + 2) + 256 + 4 * kPrThreads;
   if (smem > 227 * 1024) return UWC_ERR_SHAPE;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k_project_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-    cudaGetLastError();
-    return UWC_ERR_CUDA;
+  static int smem_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || smem_set[dev] < smem)) {
+    if (cudaFuncSetAttribute(k_noise_project, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+      cudaGetLastError();
+      return UWC_ERR_CUDA;
+    }
+    if (dev >= 0 && dev < 64) smem_set[dev] = 227 * 1024;
   }
-  const int grid = std::min(rows, uwc_num_sms() * kPrCtasPerSm);
-  k_project_rows<<<grid, kPrThreads, smem, (cudaStream_t)stream>>>(src, rows, k, r, Pp, dst ? nullptr : E, corr,
-                                                                   corr_off, ecopy_off, maxabs, lmax);
+  const int per_sm = std::max(1, std::min(4, (200 * 1024) / std::max(smem, 1)));
+  const int grid = std::min(rows, uwc_num_sms() * per_sm);
+  k_noise_project<<<grid, kPrThreads, smem, (cudaStream_t)stream>>>(src, rows, k, r, E, Pn, dst, Pp, corr, corr_off,
+                                                                    ecopy_off, maxabs, lmax);
   uwc_count_launch();
   return uwc_launch_status();
 }
