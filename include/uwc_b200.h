@@ -48,10 +48,14 @@ extern "C" {
 /* Test hooks of the error path (no counterpart in the reference). UWC_HOOK_WAIT_NS sets the bound of
  * every wait inside the GEMM kernels (value in ns; 0 restores the default of 1 s);
  * UWC_HOOK_WITHHOLD = 1 makes later GEMM launches issue no copies, so their first wait runs out and
- * the kernel unwinds with UWC_DEV_TIMEOUT in uwc_device_status (0 restores normal launches).
+ * the kernel unwinds with UWC_DEV_TIMEOUT in uwc_device_status (0 restores normal launches);
+ * UWC_HOOK_STREAM_PDL = 0 launches the weight-streaming GEMM and the few-row quantizers without
+ * programmatic dependent launch (1, the default, lets them start while the previous kernel of the
+ * stream finishes).
  * Process-wide; for tests only. Returns UWC_OK or UWC_ERR_ARG. */
 #define UWC_HOOK_WAIT_NS 1
 #define UWC_HOOK_WITHHOLD 2
+#define UWC_HOOK_STREAM_PDL 3
 int uwc_test_hook(int hook, long long value);
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -149,13 +153,37 @@ int uwc_proj_corr(const int32_t* proj, int rows, int r, int8_t* corr, int corr_o
  *            without an output need none (the tile messages live in shared memory). A hashed call
  *            with an output runs as one kernel and stages each unit's raw int32 product there
  *            (256 KiB per SM) until the unit's tile hashes and correction are done; a plain
- *            split-K call with an F32 / BF16 output sums its int32 partials there (m * n * 4
- *            bytes). Calls that overlap on the GPU must not share a workspace. */
+ *            split-K call with an F32 / BF16 output and m > 64 sums its int32 partials there
+ *            (m * n * 4 bytes); plain calls with m <= 64 run the weight-streaming GEMM below and
+ *            need none. Calls that overlap on the GPU must not share a workspace. */
 uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mode);
 int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
              const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key, const uint32_t* target,
              uint32_t* wins, int max_wins, const float* a_scale, const float* b_scale, void* out, int out_mode,
              void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* ---- the weight-streaming GEMM (decode-sized m) -------------------------------------------
+ * New (the reference has no small-m path): out = X W^T for X m x k (1 <= m <= 64), W n x k, int8,
+ * k contiguous, k % 16 == 0, X and W 16-byte aligned. W is read from HBM once: 128-row blocks of W
+ * on the tensor core's M side, X on its N side, k split over a thread-block cluster whose CTAs add
+ * their partial tiles in distributed shared memory. No workspace, no memset, one launch. The
+ * epilogue `epi`:
+ *   UWC_SEPI_I32     int32 out (m x n)                               (DetLinear.int_gemm)
+ *   UWC_SEPI_F32     fmul(fmul(float(acc), x_scale[i]), w_scale[j])   (qwen3.py:125)
+ *   UWC_SEPI_BF16    the same rounded to bf16 (RNE)
+ *   UWC_SEPI_RESID   fadd(resid[i][j], the F32 value), resid m x n fp32 (NULL: the F32 value)
+ *                    (detgpu kernels.py:346-354, the row-parallel output + residual)
+ *   UWC_SEPI_SWIGLU  W = [gate; up], I = n / 2 rows each (n % 128 == 0); out m x I fp32 =
+ *                    fmul(det_silu(g), u) of the dequantized pair (gate row f, up row I + f;
+ *                    w_scale in the same order), detgpu kernels.py:356-396.
+ * uwc_gemm takes this path by itself for plain calls with m <= 64. */
+#define UWC_SEPI_I32 0
+#define UWC_SEPI_F32 1
+#define UWC_SEPI_BF16 2
+#define UWC_SEPI_RESID 3
+#define UWC_SEPI_SWIGLU 4
+int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
+                    const float* w_scale, const float* resid, void* out, int epi, void* stream);
 
 /* ---- a mined weight: the per-block and per-call sequences as single calls --------------------
  * MinedWeight (miner/ampere/uwc_ampere/ops.py:205-371) keeps its state in two caller-owned device

@@ -50,6 +50,11 @@ __device__ __forceinline__ float det_exp(float z) {
 
 __device__ __forceinline__ float deq(int acc, float s, float sw) { return __fmul_rn(__fmul_rn(__int2float_rn(acc), s), sw); }
 
+// detgpu's SwiGLU element (kernels.py:356-396): fmul(g / (1 + det_exp(-g)), u), one rounding per op.
+__device__ __forceinline__ float det_swiglu(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, det_exp(-g))), u);
+}
+
 __device__ __forceinline__ float warp_maxf(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -1077,6 +1077,12 @@ bool split_k(int m, int n) {
 extern "C" int uwc_test_hook(int hook, long long value) {
   if (hook == UWC_HOOK_WAIT_NS && value >= 0) {
     g_wait_ns.store((uint64_t)value);
+    uwc_stream_set_wait_ns((uint64_t)value);
+    return UWC_OK;
+  }
+  if (hook == UWC_HOOK_STREAM_PDL && (value == 0 || value == 1)) {
+    uwc_stream_set_pdl((int)value);
+    uwc_row_set_pdl((int)value);
     return UWC_OK;
   }
   if (hook == UWC_HOOK_WITHHOLD && (value == 0 || value == 1)) {
@@ -1088,6 +1094,7 @@ extern "C" int uwc_test_hook(int hook, long long value) {
 
 extern "C" uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mode) {
   uint64_t bytes = stage_bytes(flags, out_mode);
+  if (!flags && m <= 64) return bytes;   // the weight-streaming GEMM: no workspace
   // split-K with a scaled output: the int32 product is summed here, then scaled by a second pass
   if (!flags && (out_mode == UWC_OUT_F32 || out_mode == UWC_OUT_BF16) && m > 0 && n > 0 && split_k(m, n))
     bytes += (uint64_t)m * n * 4;
@@ -1118,6 +1125,11 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   UWC_CHECK_DEVICE();
   const uint64_t need = uwc_gemm_workspace_bytes(m, n, flags, out_mode);
   if (need && (!workspace || workspace_bytes < need)) return UWC_ERR_SCRATCH;
+  // decode-sized m: W streamed once, k split over a cluster, the output step in its epilogue
+  if (!hash && !denoise && out_mode != UWC_OUT_NONE && uwc_stream_gemm_fits(m, n, k)) {
+    const int epi = out_mode == UWC_OUT_I32 ? UWC_SEPI_I32 : (out_mode == UWC_OUT_F32 ? UWC_SEPI_F32 : UWC_SEPI_BF16);
+    return uwc_gemm_stream(A, B, m, n, k, a_scale, b_scale, nullptr, out, epi, stream);
+  }
 
   Params p{};
   p.m = m; p.n = n; p.k = k; p.r = r;

@@ -132,6 +132,14 @@ UWC_DEVI void set_status(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start before the previous kernel of
+// its stream has finished, once every CTA of that kernel has called pdl_trigger() (or exited).
+// pdl_wait() blocks until the previous kernel has completed and its writes are visible; without a
+// programmatic dependency both are no-ops.
+UWC_DEVI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+UWC_DEVI void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ mbarrier
 UWC_DEVI void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

@@ -38,3 +38,11 @@ int uwc_noise_uniform_zero2(int8_t* out, uint64_t nbytes, const uint32_t* label,
 // uwc_proj_corr that also copies E (rows x r int8) into corr[li][row][ecopy_off + j] for every limb.
 int uwc_proj_corr_ecopy(const int32_t* proj, int rows, int r, int8_t* corr, int corr_off, int32_t* maxabs, int lmax,
                         const int8_t* E, int ecopy_off, void* stream);
+
+// The weight-streaming GEMM (stream_gemm.cu): whether a shape takes it, and its test switches
+// (programmatic dependent launch on / off; the bound of its waits, 0 = default).
+bool uwc_stream_gemm_fits(int m, int n, int k);
+void uwc_stream_set_pdl(int on);
+// Programmatic dependent launch of the few-row quantizers (detq.cu) on / off.
+void uwc_row_set_pdl(int on);
+void uwc_stream_set_wait_ns(uint64_t ns);

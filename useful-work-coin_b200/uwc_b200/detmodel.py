@@ -207,7 +207,7 @@ class DetQwen3:
         cache["sv"][:, :, start:end] = vs.view(B, T, Hkv, 1).transpose(1, 2)
         o = detgpu.attention_cache(qq, qs, cache, B, T, start, H, Hkv, self.inv_sqrt_hd)
         q2, s2 = detgpu.quant_act(o, L["o"].bs)
-        r1 = detgpu.dequant_residual(L["o"].int_gemm(q2), s2, L["o"].sw, x)
+        r1 = detgpu.linear_resid(L["o"], q2, s2, x)
         return detgpu.mlp_residual(L["gu"], L["down"], L["post_norm"], r1, self.eps)
 
     @torch.no_grad()
@@ -250,7 +250,7 @@ class DetQwen3:
             detgpu.kv_append(kq, ks, vq, vs, c, B, 1, pos)
             o = detgpu.attention_cache_at(qq, qs, c, B, 1, pos, max_start, H, Hkv, self.inv_sqrt_hd)
             q2, s2 = detgpu.quant_act(o, L["o"].bs)
-            r1 = detgpu.dequant_residual(L["o"].int_gemm(q2), s2, L["o"].sw, x)
+            r1 = detgpu.linear_resid(L["o"], q2, s2, x)
             x = detgpu.mlp_residual(L["gu"], L["down"], L["post_norm"], r1, self.eps)
         h = detgpu.rmsnorm(x, self.norm, self.eps)
         return h, self.next_tokens(h)

@@ -207,6 +207,28 @@ def gemm(A, B, *, r=128, flags=0, corrA=None, corrB=None, maxabs=None, key=None,
                          0 if ws is None else ws.numel(), _stream()), "gemm")
 
 
+SEPI_I32, SEPI_F32, SEPI_BF16, SEPI_RESID, SEPI_SWIGLU = range(5)
+STREAM_MAX_M = 64
+
+
+def gemm_stream(X, W, epi=SEPI_I32, *, x_scale=None, w_scale=None, resid=None, out=None):
+    """out = X W^T on the weight-streaming GEMM (m <= 64), with the epilogue `epi` (uwc_gemm_stream):
+    SEPI_I32 int32; SEPI_F32 / SEPI_BF16 the dequant fmul(fmul(float(acc), x_scale), w_scale);
+    SEPI_RESID that plus `resid` (fp32 m x n); SEPI_SWIGLU det_silu(gate) * up for W = [gate; up]
+    (n / 2 rows each), m x n/2 fp32."""
+    m, k = X.shape
+    n = W.shape[0]
+    assert X.dtype == torch.int8 and W.dtype == torch.int8 and X.is_contiguous() and W.is_contiguous()
+    if out is None:
+        dt = {SEPI_I32: torch.int32, SEPI_BF16: torch.bfloat16}.get(epi, torch.float32)
+        out = torch.empty((m, n // 2 if epi == SEPI_SWIGLU else n), dtype=dt, device=X.device)
+    f32 = (lambda t: None if t is None else t.contiguous().float())
+    check(lib().uwc_gemm_stream(_p(X), _p(W), m, n, k, _p(f32(x_scale)), _p(f32(w_scale)),
+                                _p(None if resid is None else resid.contiguous()), _p(out), epi, _stream()),
+          "gemm_stream")
+    return out
+
+
 # ------------------------------------------------------------------ one mined linear layer
 MB_CONSTS, MB_EBRT, MB_PB, MB_SBT, MB_BPEBT, MB_BYTES = range(6)
 MW_A_SEED, MW_MAXABS, MW_EAL, MW_PA, MW_APEA, MW_B3, MW_GEMM, MW_SAT, MW_CORRA, MW_CORRB, MW_PROJA, MW_PROJB, \

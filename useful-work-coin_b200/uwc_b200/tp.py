@@ -17,7 +17,10 @@ bit-identical to one device:
                         fp32 SwiGLU, row-parallel down projection with the residual add.
 
 `kernels` is the device backend: by default this library's CUDA kernels (GPUKernels); tests pass
-a CPU stand-in built from the oracle to check the sharding and collectives with gloo ranks.
+a CPU stand-in built from the oracle to check the sharding and collectives with gloo ranks. A
+backend with `fused = True` also offers quant_act, linear_resid and swiglu_linear: decode-sized
+calls then run the output step inside the weight-streaming GEMM (the row-parallel layer on one
+rank, and the gate/up SwiGLU on any number), with the same bits as the separate kernels.
 """
 from __future__ import annotations
 
@@ -43,7 +46,9 @@ def even_bounds(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int
 
 
 class GPUKernels:
-    """The CUDA backend (uwc_b200.detgpu / uwc_b200.det)."""
+    """The CUDA backend (uwc_b200.detgpu / uwc_b200.det / uwc_b200.ops)."""
+
+    fused = True
 
     @staticmethod
     def _mods():
@@ -70,6 +75,28 @@ class GPUKernels:
 
     def dequant_residual(self, acc, s, sw, x):
         return self._mods()[1].dequant_residual(acc, s, sw, x)
+
+    def quant_act(self, x, bs):
+        return self._mods()[1].quant_act(x, bs)
+
+    @staticmethod
+    def _stream(q):
+        from . import ops
+        return ops if q.shape[0] <= ops.STREAM_MAX_M else None
+
+    def linear_resid(self, q, s, Wq, sw, x):
+        """fadd(x, deq(q Wq^T)) (x None: deq alone)."""
+        ops = self._stream(q)
+        if ops is None:
+            return self.dequant_residual(self.int_gemm(q, Wq), s, sw, x)
+        return ops.gemm_stream(q, Wq, ops.SEPI_RESID, x_scale=s, w_scale=sw, resid=x)
+
+    def swiglu_linear(self, q, s, Wq, sw):
+        """det_silu(deq(gate)) * deq(up) of q [gate; up]^T."""
+        ops = self._stream(q)
+        if ops is None or Wq.shape[0] % 128:
+            return self.swiglu(self.int_gemm(q, Wq), s, sw)
+        return ops.gemm_stream(q, Wq, ops.SEPI_SWIGLU, x_scale=s, w_scale=sw)
 
 
 def _default(kernels):
@@ -116,8 +143,15 @@ class RowParallelLinear:
         self.sw = sw.contiguous().to(device)
         self.K = _default(kernels)
 
+    def _solo(self) -> bool:
+        return not (dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1)
+
     def forward(self, x_shard: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
         K = self.K
+        if getattr(K, "fused", False) and self._solo():
+            # one rank: the shard is the whole row, so its own absmax is the row's
+            q, s = K.quant_act(x_shard, self.bs)
+            return K.linear_resid(q, s, self.Wq, self.sw, residual)
         amax = K.fwht_absmax(x_shard, self.bs)
         _all_reduce(amax, dist.ReduceOp.MAX, self.group)
         q, s = K.quant_act_global(x_shard, self.bs, amax)
@@ -143,5 +177,8 @@ class TPMLP:
     def forward(self, r1: torch.Tensor, w_norm: torch.Tensor, eps: float) -> torch.Tensor:
         K = self.K
         q3, s3 = K.rmsnorm_quant(r1, w_norm, eps, self.gu_bs)
-        h = K.swiglu(K.int_gemm(q3, self.gu_Wq), s3, self.gu_sw)
+        if getattr(K, "fused", False):
+            h = K.swiglu_linear(q3, s3, self.gu_Wq, self.gu_sw)
+        else:
+            h = K.swiglu(K.int_gemm(q3, self.gu_Wq), s3, self.gu_sw)
         return self.down.forward(h, residual=r1)
