@@ -295,7 +295,8 @@ def run_c5(a, world, rank, local):
     graph: rmsnorm_quant +
     qkv (column-parallel), o (row-parallel, + residual), then the MLP block (gate/up column-parallel,
     SwiGLU, down row-parallel, + residual). Attention is not part of the path: o_proj reads a seeded
-    activation shard. Every int32 partial product is summed by NCCL all-reduce (exact)."""
+    activation shard. Every int32 partial product is summed over the ranks exactly: at decode inside
+    the quantizer and GEMM kernels over NVLink peer memory (tp.PeerExchange), at prefill by NCCL."""
     import torch
 
     from uwc_b200 import _lib, detgpu, ops, tp
@@ -307,9 +308,11 @@ def run_c5(a, world, rank, local):
     W = {nm: torch.randint(-64, 65, (n, k), dtype=torch.int8, device=dev, generator=g) for nm, n, k, _ in C5_LINEARS}
     S = {nm: torch.rand(n, device=dev, generator=g) * 1e-3 + 1e-5 for nm, n, _, _ in C5_LINEARS}
     D, bs = 4096, 512
+    # decode on several GPUs: the row-parallel all-reduces run inside the kernels over NVLink
+    ex = tp.PeerExchange(64, D, rank, world, dev) if world > 1 and m <= 64 else None
     qkv = tp.ColumnParallelLinear(W["qkv"], S["qkv"], bs, rank, world, dev)
-    o = tp.RowParallelLinear(W["o"], S["o"], bs, rank, world, dev)
-    mlp = tp.TPMLP(W["gate_up"], S["gate_up"], bs, W["down"], S["down"], bs, rank, world, dev)
+    o = tp.RowParallelLinear(W["o"], S["o"], bs, rank, world, dev, exchange=ex)
+    mlp = tp.TPMLP(W["gate_up"], S["gate_up"], bs, W["down"], S["down"], bs, rank, world, dev, exchange=ex)
     # the same layer on this GPU alone (full weights, a one-rank group: no collectives), the parity
     # reference of every TP step: integer sums make the two bit-identical
     solo = None
@@ -393,6 +396,8 @@ def run_c5(a, world, rank, local):
     barrier(world)
     del graph                                        # before the process group goes away
     torch.cuda.synchronize()
+    if ex is not None:
+        ex.close()
     t2 = max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in ev2), world)
     e2e = (wbytes if decode else ops_step) * a.steps / (t2 / 1e3) / (1e9 if decode else 1e12)
     pk = peaks()

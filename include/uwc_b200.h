@@ -176,14 +176,50 @@ int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int f
  *   UWC_SEPI_SWIGLU  W = [gate; up], I = n / 2 rows each (n % 128 == 0); out m x I fp32 =
  *                    fmul(det_silu(g), u) of the dequantized pair (gate row f, up row I + f;
  *                    w_scale in the same order), detgpu kernels.py:356-396.
- * uwc_gemm takes this path by itself for plain calls with m <= 64. */
+ * epi | UWC_SEPI_EARLY_W: W is not written by the kernel launched just before this call on the
+ * stream (static weights), so the call may start streaming W while that kernel finishes.
+ * uwc_gemm takes this path by itself for plain calls with m <= 64 (without UWC_SEPI_EARLY_W). */
 #define UWC_SEPI_I32 0
 #define UWC_SEPI_F32 1
 #define UWC_SEPI_BF16 2
 #define UWC_SEPI_RESID 3
 #define UWC_SEPI_SWIGLU 4
+#define UWC_SEPI_EARLY_W 0x100
 int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
                     const float* w_scale, const float* resid, void* out, int epi, void* stream);
+
+/* ---- tensor-parallel decode over NVLink peer memory ---------------------------------------
+ * New (the reference splits models only into pipeline stages, runtime/detrt/qwen3.py:151-158).
+ * Each rank allocates one exchange buffer (uwc_tp_alloc, zero-filled, same max_m / max_n on every
+ * rank), passes its IPC handle to the others (uwc_ipc_handle, UWC_IPC_HANDLE_BYTES bytes, sent by
+ * the caller's own transport) and maps theirs (uwc_ipc_open). A UwcTP names this rank and every
+ * rank's buffer as mapped here (base[rank] = its own). Every rank must make the same sequence of
+ * uwc_*_tp calls on its buffer, each on its own GPU; a call waits (bounded, UWC_DEV_TIMEOUT) for
+ * the peers' contributions to the same call.
+ *   uwc_quant_act_tp    uwc_quant_act of a row-parallel input shard with the absmax of the whole
+ *                       row: each rank's shard absmax goes to every peer, each takes the maximum
+ *                       (the fwht_absmax + MAX all-reduce + quant_act_global sequence, in one kernel);
+ *                       m <= max_m.
+ *   uwc_gemm_stream_tp  uwc_gemm_stream whose int32 product is summed over the ranks before the
+ *                       epilogue (the row-parallel GEMM + SUM all-reduce + dequant/residual, in
+ *                       one kernel): each rank's partial slices go to every peer, each rank adds
+ *                       them in rank order and writes the full output. m <= max_m, n <= max_n,
+ *                       epi UWC_SEPI_I32 / F32 / BF16 / RESID (| UWC_SEPI_EARLY_W). */
+#define UWC_TP_MAX_WORLD 8
+#define UWC_IPC_HANDLE_BYTES 64
+typedef struct UwcTP {
+  int rank, world, max_m, max_n;
+  void* base[UWC_TP_MAX_WORLD];
+} UwcTP;
+uint64_t uwc_tp_buffer_bytes(int max_m, int max_n);
+int uwc_tp_alloc(int max_m, int max_n, void** buf);
+int uwc_tp_free(void* buf);
+int uwc_ipc_handle(const void* buf, void* handle);
+int uwc_ipc_open(const void* handle, void** peer_buf);
+int uwc_ipc_close(void* peer_buf);
+int uwc_quant_act_tp(const float* x, int m, int k, int bs, int8_t* q, float* scale, const UwcTP* tp, void* stream);
+int uwc_gemm_stream_tp(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
+                       const float* w_scale, const float* resid, void* out, int epi, const UwcTP* tp, void* stream);
 
 /* ---- a mined weight: the per-block and per-call sequences as single calls --------------------
  * MinedWeight (miner/ampere/uwc_ampere/ops.py:205-371) keeps its state in two caller-owned device

@@ -95,8 +95,8 @@ def test_uwc_gemm_routes_small_m(lib):
 
 
 def test_graph_chain_with_pdl_matches_eager(lib):
-    """quant -> stream GEMM -> dequant chains, captured with programmatic dependent launch, replay to
-    the same bits as eager calls launched without it."""
+    """quantizer -> stream GEMM chains, captured with programmatic dependent launch (weights streamed
+    early where the caller allows it), replay to the same bits as eager calls launched without it."""
     ops, detgpu, _lib = lib
     g = torch.Generator(device="cuda").manual_seed(9)
     m, d, n2 = 32, 4096, 8192
@@ -108,9 +108,11 @@ def test_graph_chain_with_pdl_matches_eager(lib):
 
     def chain(xin):
         q, s = detgpu.quant_act(xin, 512)
-        h = ops.gemm_stream(q, W1, ops.SEPI_SWIGLU, x_scale=s, w_scale=s1)
+        h = ops.gemm_stream(q, W1, ops.SEPI_SWIGLU, x_scale=s, w_scale=s1, early_w=True)
         q2, sq2 = detgpu.quant_act(h, 512)
-        return ops.gemm_stream(q2, W2, ops.SEPI_RESID, x_scale=sq2, w_scale=s2, resid=xin)
+        y = ops.gemm_stream(q2, W2, ops.SEPI_RESID, x_scale=sq2, w_scale=s2, resid=xin, early_w=True)
+        q3, sq3 = detgpu.rmsnorm_quant(y, s2 * 1e3, 1e-5, 512)
+        return ops.gemm_stream(q3, W1, ops.SEPI_F32, x_scale=sq3, w_scale=s1)
 
     _lib.lib().uwc_test_hook(_lib.HOOK_STREAM_PDL, 0)
     try:

@@ -1,6 +1,7 @@
-"""Tensor-parallel linears on 2+ GPUs over NCCL with this library's CUDA kernels: the MLP block and
-a row-parallel projection at Llama-3.1-8B widths (hidden 4096, MLP 14336), at decode (M = 32) and
-prefill-like M, bit-identical to the same layer on one GPU. Skipped with fewer than 2 GPUs."""
+"""Tensor-parallel linears on 2+ GPUs with this library's CUDA kernels: the MLP block at
+Llama-3.1-8B widths (hidden 4096, MLP 14336), at decode (M = 32) and prefill-like M, with the
+all-reduces over NCCL and (decode) inside the kernels over NVLink peer memory, eager and as a
+replayed CUDA graph: bit-identical to the same layer on one GPU. Skipped with fewer than 2 GPUs."""
 import datetime
 import os
 import socket
@@ -41,6 +42,34 @@ def _worker(rank, world, port, outdir, Dm, I, ms):
         for m in ms:
             r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
             res[f"y{m}"] = mlp.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
+        # the same block with both all-reduces inside the kernels (NVLink peer exchange): eager calls,
+        # then a CUDA graph replayed several times (the exchange's epochs advance on the device)
+        ex = tp.PeerExchange(64, Dm, rank, world, dev)
+        try:
+            mlpx = tp.TPMLP(gq, gs, 512, dq, ds, 512, rank, world, dev, exchange=ex)
+            for m in ms:
+                r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
+                res[f"x{m}"] = mlpx.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
+            m = ms[0]
+            r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
+            wnd = wn.to(dev)
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                mlpx.forward(r1, wnd, 1e-5)
+            torch.cuda.current_stream().wait_stream(st)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                yg = mlpx.forward(r1, wnd, 1e-5)
+            for i in range(5):
+                graph.replay()
+            torch.cuda.synchronize()
+            res[f"g{m}"] = yg.cpu().numpy()
+            del graph
+            from uwc_b200 import _lib
+            res["status"] = np.array([_lib.device_status(clear=True)])
+        finally:
+            ex.close()
         torch.cuda.synchronize()
         np.savez(os.path.join(outdir, f"rank{rank}.npz"), **res)
     finally:
@@ -69,5 +98,7 @@ def test_tp_mlp_nccl_matches_one_gpu(tmp_path):
         r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).cuda()
         ref = detgpu.mlp_residual(gu, down, wn.cuda(), r1, 1e-5).cpu().numpy()
         for r in range(world):
-            y = np.load(os.path.join(tmp_path, f"rank{r}.npz"))[f"y{m}"]
-            assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), (m, r)
+            got = np.load(os.path.join(tmp_path, f"rank{r}.npz"))
+            assert int(got["status"][0]) == 0, r
+            for key in (f"y{m}", f"x{m}") + ((f"g{m}",) if m == ms[0] else ()):
+                assert np.array_equal(got[key].view(np.uint32), ref.view(np.uint32)), (key, r)

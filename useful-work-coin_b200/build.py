@@ -17,8 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "uwc_b200", "libuwcb200.so")
-SOURCES = ["host.cu", "prep.cu", "gemm_sm100.cu", "mined.cu", "peak.cu", "stream_gemm.cu", "detq.cu", "attn.cu", "sha.cu"]
-HEADERS = ["uwc_device.cuh", "uwc_host.h", "det_math.cuh"]
+SOURCES = ["host.cu", "prep.cu", "gemm_sm100.cu", "mined.cu", "peak.cu", "stream_gemm.cu", "tp.cu", "detq.cu", "attn.cu", "sha.cu"]
+HEADERS = ["uwc_device.cuh", "uwc_host.h", "det_math.cuh", "uwc_tp.cuh"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-cudart", "static"]
 

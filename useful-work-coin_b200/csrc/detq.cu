@@ -18,8 +18,6 @@
 //
 // Row kernels keep one row in shared memory (one CTA of 256 threads per row) and read / write HBM
 // once; they are bandwidth-bound by design.
-#include <cooperative_groups.h>
-
 #include <algorithm>
 #include <atomic>
 #include <mutex>
@@ -29,8 +27,7 @@
 #include "det_math.cuh"
 #include "uwc_device.cuh"
 #include "uwc_host.h"
-
-namespace cg = cooperative_groups;
+#include "uwc_tp.cuh"
 
 namespace {
 
@@ -172,7 +169,11 @@ __global__ void __launch_bounds__(NT) k_quant_act(const void* __restrict__ x, in
                                                            float* __restrict__ amax, int8_t* __restrict__ q,
                                                            float* __restrict__ scale) {
   extern __shared__ float row[];
-  pdl_trigger();   // a weight-streaming GEMM behind this kernel may start fetching its weights
+  // Launched early behind the previous kernel: wait for its writes, then let a weight-streaming GEMM
+  // behind this kernel start fetching its weights. The bf16 form also quantizes weights, so it
+  // never lets its successor start early.
+  pdl_wait();
+  if (!BF16) pdl_trigger();
   __shared__ float red[NT / 32];
   const int r = blockIdx.x;
   load_row<NT, BF16>(x, r, k, row);
@@ -189,12 +190,52 @@ __global__ void __launch_bounds__(NT) k_quant_act(const void* __restrict__ x, in
   quant_row64<NT>(row, k, bs, mx, q + (uint64_t)r * k, scale + r);
 }
 
+// quant_act of a row-parallel shard with the whole row's absmax, exchanged in the kernel: each CTA
+// (one row) publishes its shard's absmax to every rank's exchange buffer as (epoch << 32) | bits,
+// waits for every rank's value of the row, and quantizes with the maximum (the fwht_absmax, MAX
+// all-reduce and quant_act_global sequence: the same maximum, so the same bits).
+template <int NT>
+__global__ void __launch_bounds__(NT) k_quant_act_tp(const float* __restrict__ x, int k, int bs,
+                                                     int8_t* __restrict__ q, float* __restrict__ scale, TPArgs tp,
+                                                     uint32_t* status, uint64_t wait_ns) {
+  extern __shared__ float row[];
+  __shared__ float red[NT / 32];
+  __shared__ float src_max[uwc_tp::kMaxWorld];
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  uint8_t* const mine = tp.base[tp.rank];
+  const uint64_t E = uwc_tp::call_epoch(mine);
+  const int par = (int)(E & 1);
+  load_row<NT, false>(x, r, k, row);
+  if (bs > 1) fwht_row<NT>(row, k, bs);
+  const float mx = row_absmax<NT>(row, k, red);
+  const int p = threadIdx.x;
+  if (p < tp.world)
+    uwc_tp::st_release_sys(uwc_tp::amax_slot(tp.base[p], tp.L, par, tp.rank, r), (E << 32) | __float_as_uint(mx));
+  if (p < tp.world) {
+    bool ok = true;
+    const uint32_t want = (uint32_t)E;
+    const uint64_t v = uwc_tp::wait_value(
+        uwc_tp::amax_slot(mine, tp.L, par, p, r), [want](uint64_t w) { return (uint32_t)(w >> 32) == want; },
+        wait_ns, status, (uint64_t)__float_as_uint(mx), &ok);
+    src_max[p] = __uint_as_float((uint32_t)v);
+  }
+  __syncthreads();
+  float am = src_max[0];
+  for (int i = 1; i < tp.world; i++) am = fmaxf(am, src_max[i]);
+  quant_row64<NT>(row, k, bs, am, q + (uint64_t)r * k, scale + r);
+  __syncthreads();
+  if (threadIdx.x == 0) uwc_tp::call_end(mine, E, gridDim.x);
+}
+
 // det_rmsnorm (core.py:151-159, exact_rowsum core.py:85-108) then quant_act.
 template <int NT>
 __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ x, const float* __restrict__ w,
                                                                int k, int bs, float inv_d, float eps, int L,
                                                                int8_t* __restrict__ q, float* __restrict__ scale) {
   extern __shared__ float row[];
+  pdl_wait();      // launched early behind the previous kernel: its writes are visible from here
   pdl_trigger();   // a weight-streaming GEMM behind this kernel may start fetching its weights
   __shared__ float red[NT / 32];
   __shared__ long long redl[NT / 32];
@@ -236,81 +277,6 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ 
   quant_row64<NT>(row, k, bs, am, q + (uint64_t)r * k, scale + r);
 }
 
-// Few rows (decode): one thread-block cluster of C CTAs per row, CTA c holding elements
-// [c k / C, (c + 1) k / C) (whole Hadamard blocks) in shared memory. The row's maxima and its int64
-// fixed-point sum of squares are combined in rank order through distributed shared memory, so every
-// value is the one-CTA kernel's: RMS = false is quant_act (k_quant_act MODE 0), RMS = true
-// rmsnorm_quant. The kernel waits for its stream predecessor before touching global memory and lets
-// its successor launch at once (a weight-streaming GEMM starts fetching weights meanwhile).
-constexpr int kClThreads = 128;
-constexpr int kClMax = 8;
-
-template <bool RMS>
-__global__ void __launch_bounds__(kClThreads) k_row_cluster(const float* __restrict__ x, const float* __restrict__ w,
-                                                            int k, int bs, float inv_d, float eps, int L,
-                                                            int8_t* __restrict__ q, float* __restrict__ scale) {
-  extern __shared__ float sl[];
-  __shared__ float red[kClThreads / 32];
-  __shared__ long long redl[kClThreads / 32];
-  __shared__ float pub_f[2];        // this CTA's partial maxima, read by the cluster
-  __shared__ long long pub_l;       // its partial sum of squares
-  __shared__ float dummy_scale;
-  pdl_trigger();
-  pdl_wait();
-  cg::cluster_group cl = cg::this_cluster();
-  const int C = (int)cl.num_blocks(), c = (int)cl.block_rank(), r = blockIdx.y;
-  const int len = k / C, off = c * len;
-  const float4* src = reinterpret_cast<const float4*>(x + (uint64_t)r * k + off);
-  for (int i = threadIdx.x; i < len / 4; i += kClThreads) reinterpret_cast<float4*>(sl)[i] = src[i];
-  __syncthreads();
-  if (RMS) {
-    float mx = 0.f;
-    for (int i = 4 * threadIdx.x; i < len; i += 4 * kClThreads) {
-      const float4 v = *reinterpret_cast<const float4*>(sl + i);
-      mx = fmaxf(fmaxf(mx, fmaxf(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y))),
-                 fmaxf(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
-    }
-    mx = block_maxf<kClThreads>(mx, red);
-    if (threadIdx.x == 0) pub_f[0] = mx;
-    cl.sync();
-    for (int j = 0; j < C; j++) mx = fmaxf(mx, *cl.map_shared_rank(&pub_f[0], j));
-    int e;
-    frexpf(mx, &e);
-    const int sh = min(max((62 - L) - e, -1000), 1000);
-    const double up = pow2d(sh);
-    long long acc = 0;
-    for (int i = 4 * threadIdx.x; i < len; i += 4 * kClThreads) {
-      const float4 v = *reinterpret_cast<const float4*>(sl + i);
-      acc += __double2ll_rn((double)__fmul_rn(v.x, v.x) * up) + __double2ll_rn((double)__fmul_rn(v.y, v.y) * up) +
-             __double2ll_rn((double)__fmul_rn(v.z, v.z) * up) + __double2ll_rn((double)__fmul_rn(v.w, v.w) * up);
-    }
-    acc = block_sumll<kClThreads>(acc, redl);
-    if (threadIdx.x == 0) pub_l = acc;
-    cl.sync();
-    long long tot = 0;
-    for (int j = 0; j < C; j++) tot += *cl.map_shared_rank(&pub_l, j);
-    const float ss = __double2float_rn(__ll2double_rn(tot) * pow2d(-sh));
-    const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_d), eps)));
-    for (int i = 4 * threadIdx.x; i < len; i += 4 * kClThreads) {
-      float4 v = *reinterpret_cast<const float4*>(sl + i);
-      const float4 wv = __ldg(reinterpret_cast<const float4*>(w + off + i));
-      v.x = __fmul_rn(__fmul_rn(v.x, rr), wv.x);
-      v.y = __fmul_rn(__fmul_rn(v.y, rr), wv.y);
-      v.z = __fmul_rn(__fmul_rn(v.z, rr), wv.z);
-      v.w = __fmul_rn(__fmul_rn(v.w, rr), wv.w);
-      *reinterpret_cast<float4*>(sl + i) = v;
-    }
-    __syncthreads();
-  }
-  if (bs > 1) fwht_row<kClThreads>(sl, len, bs);
-  float am = row_absmax<kClThreads>(sl, len, red);
-  if (threadIdx.x == 0) pub_f[1] = am;
-  cl.sync();
-  for (int j = 0; j < C; j++) am = fmaxf(am, *cl.map_shared_rank(&pub_f[1], j));
-  quant_row64<kClThreads>(sl, len, bs, am, q + (uint64_t)r * k + off, c == 0 ? scale + r : &dummy_scale);
-  cl.sync();   // the cluster's partials stay readable until every CTA is done with them
-}
-
 // fmul(det_silu(gate), up) of the dequantized gate/up GEMM output (N x 2I int32)
 __device__ __forceinline__ float swiglu_at(const int32_t* ar, float s, const float* sw, int I, int i) {
   return det_swiglu(deq(ar[i], s, sw[i]), deq(ar[I + i], s, sw[I + i]));
@@ -323,6 +289,7 @@ __global__ void __launch_bounds__(NT) k_swiglu_quant(const int32_t* __restrict__
                                                               int I, int bs, int8_t* __restrict__ q,
                                                               float* __restrict__ scale) {
   extern __shared__ float row[];
+  pdl_wait();      // launched early behind the previous kernel: its writes are visible from here
   pdl_trigger();   // a weight-streaming GEMM behind this kernel may start fetching its weights
   __shared__ float red[NT / 32];
   const int r = blockIdx.x;
@@ -479,38 +446,23 @@ bool few_rows(int m) { return m < uwc_num_sms(); }
 
 bool bs_ok(int k, int bs) { return bs <= 1 || ((bs & (bs - 1)) == 0 && k % bs == 0); }
 
-// Cluster size for the few-row kernels: the largest divisor of k / unit that is at most kClMax
-// (unit = max(bs, 512) elements, so slices hold whole Hadamard blocks), or 0 when that is below 2.
-int cluster_split(int k, int bs) {
-  const int unit = std::max(bs, 512);
-  if (k % unit) return 0;
-  const int units = k / unit;
-  for (int c = kClMax; c >= 2; c--)
-    if (units % c == 0) return c;
-  return 0;
-}
-
 std::atomic<int> g_row_pdl{1};
 
-// Launches k_row_cluster<RMS> (cluster of C CTAs per row, programmatic dependent launch).
-template <bool RMS>
-int launch_row_cluster(const float* x, const float* w, int m, int k, int bs, float inv_d, float eps, int8_t* q,
-                       float* scale, int C, cudaStream_t st) {
+// Launches a few-row kernel with programmatic stream serialization: it is scheduled while the
+// previous kernel of the stream finishes and waits for it (pdl_wait) before touching memory.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), int grid, int threads, size_t smem, void* stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(C, m, 1);
-  cfg.blockDim = dim3(kClThreads, 1, 1);
-  cfg.dynamicSmemBytes = 4 * (k / C);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = g_row_pdl.load();
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_row_pdl.load();
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_row_cluster<RMS>, x, w, k, bs, inv_d, eps, ceil_log2(k), q, scale);
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
   uwc_count_launch();
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -527,17 +479,10 @@ int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, fl
   if (!aligned16(x) || (q && ((uintptr_t)q & 3))) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
-  if (MODE == 0 && !BF16 && few_rows(m) && m <= 65535) {
-    const int C = cluster_split(k, bs);
-    if (C)
-      return launch_row_cluster<false>(static_cast<const float*>(x), nullptr, m, k, bs, 0.f, 0.f, q, scale, C,
-                                       (cudaStream_t)stream);
-  }
   if (few_rows(m)) {
     const int rc = row_smem_ok(k, (const void*)k_quant_act<1024, MODE, BF16>);
     if (rc != UWC_OK) return rc;
-    k_quant_act<1024, MODE, BF16><<<m, 1024, 4 * k, (cudaStream_t)stream>>>(x, k, bs, amax, q, scale);
-    uwc_count_launch();
+    return launch_pdl(k_quant_act<1024, MODE, BF16>, m, 1024, 4 * k, stream, x, k, bs, amax, q, scale);
   } else {
     const int rc = row_smem_ok(k, (const void*)k_quant_act<kRowThreads, MODE, BF16>);
     if (rc != UWC_OK) return rc;
@@ -568,6 +513,24 @@ extern "C" int uwc_quant_act_global(const float* x, int m, int k, int bs, const 
   return launch_quant<2, false>(x, m, k, bs, const_cast<float*>(amax), q, scale, stream);
 }
 
+extern "C" int uwc_quant_act_tp(const float* x, int m, int k, int bs, int8_t* q, float* scale, const UwcTP* tp,
+                                void* stream) {
+  if (!x || !q || !scale || m < 0 || k <= 0 || k % 4 || !bs_ok(k, bs)) return UWC_ERR_ARG;
+  if (!aligned16(x) || ((uintptr_t)q & 3)) return UWC_ERR_ALIGN;
+  TPArgs args;
+  const int rc = uwc_tp_args(tp, m, 0, &args);
+  if (rc != UWC_OK) return rc;
+  UWC_CHECK_DEVICE();
+  if (m == 0) return UWC_OK;
+  // one CTA per row, all resident (the rows wait for the peers' rows)
+  if (m > uwc_num_sms()) return UWC_ERR_SHAPE;
+  const int rs = row_smem_ok(k, (const void*)k_quant_act_tp<1024>);
+  if (rs != UWC_OK) return rs;
+  const uint64_t ns = uwc_wait_ns();
+  return launch_pdl(k_quant_act_tp<1024>, m, 1024, 4 * k, stream, x, k, bs, q, scale, args, uwc_status_ptr(),
+                    ns ? ns : (uint64_t)UWC_WAIT_TIMEOUT_NS);
+}
+
 extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, int bs, double eps, int8_t* q,
                                  float* scale, void* stream) {
   if (!x || !w || !q || !scale || m < 0 || k <= 0 || k % 4 || !bs_ok(k, bs)) return UWC_ERR_ARG;
@@ -576,15 +539,11 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
   if (m == 0) return UWC_OK;
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
   const float inv_d = (float)(1.0 / k), eps32 = (float)eps;
-  if (few_rows(m) && m <= 65535) {
-    const int C = cluster_split(k, bs);
-    if (C) return launch_row_cluster<true>(x, w, m, k, bs, inv_d, eps32, q, scale, C, (cudaStream_t)stream);
-  }
   if (few_rows(m)) {
     const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<1024>);
     if (rc != UWC_OK) return rc;
-    k_rmsnorm_quant<1024><<<m, 1024, 4 * k, (cudaStream_t)stream>>>(x, w, k, bs, inv_d, eps32, ceil_log2(k), q, scale);
-    uwc_count_launch();
+    return launch_pdl(k_rmsnorm_quant<1024>, m, 1024, 4 * k, stream, x, w, k, bs, inv_d, eps32, ceil_log2(k), q,
+                      scale);
   } else {
     const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<kRowThreads>);
     if (rc != UWC_OK) return rc;
@@ -604,8 +563,7 @@ extern "C" int uwc_swiglu_quant(const int32_t* acc, const float* s3, const float
   if (few_rows(m)) {
     const int rc = row_smem_ok(I, (const void*)k_swiglu_quant<1024>);
     if (rc != UWC_OK) return rc;
-    k_swiglu_quant<1024><<<m, 1024, 4 * I, (cudaStream_t)stream>>>(acc, s3, sw, I, bs, q, scale);
-    uwc_count_launch();
+    return launch_pdl(k_swiglu_quant<1024>, m, 1024, 4 * I, stream, acc, s3, sw, I, bs, q, scale);
   } else {
     const int rc = row_smem_ok(I, (const void*)k_swiglu_quant<kRowThreads>);
     if (rc != UWC_OK) return rc;

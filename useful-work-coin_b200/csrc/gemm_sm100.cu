@@ -1074,6 +1074,8 @@ bool split_k(int m, int n) {
 }
 }  // namespace
 
+uint64_t uwc_wait_ns() { return g_wait_ns.load(); }
+
 extern "C" int uwc_test_hook(int hook, long long value) {
   if (hook == UWC_HOOK_WAIT_NS && value >= 0) {
     g_wait_ns.store((uint64_t)value);

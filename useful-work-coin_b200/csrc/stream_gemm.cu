@@ -28,6 +28,7 @@
 #include "det_math.cuh"
 #include "uwc_device.cuh"
 #include "uwc_host.h"
+#include "uwc_tp.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -48,6 +49,9 @@ struct SParams {
   void* out;
   int ldo;                           // output row stride in elements (n, or n / 2 for SWIGLU)
   int half;                          // SWIGLU: I = n / 2, the first up row; 0 otherwise
+  int early_w;                       // W may be read before the previous kernel has finished
+  int tp_on;                         // sum the int32 product over the ranks of `tp` first
+  TPArgs tp;
   uint32_t* status;
   uint64_t wait_ns;
 };
@@ -179,9 +183,10 @@ __global__ void __launch_bounds__(kSThreads, 2)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     const bool leader = elect_one();
-    // the first ring's worth of W before the previous kernel has finished (W does not depend on
-    // it), then X behind the grid dependency
+    // the first ring's worth of W, before the previous kernel has finished when the caller says W
+    // is not written by it (UWC_SEPI_EARLY_W), then X behind the grid dependency
     const int pre = min(nkb, C::NST);
+    if (!p.early_w) pdl_wait();
     if (leader) {
       for (int b = 0; b < pre; b++) {
         mbar_expect_tx(&bars->full[b], C::STAGE);
@@ -249,7 +254,8 @@ __global__ void __launch_bounds__(kSThreads, 2)
   // ---------------------------------------------------------------- cluster reduction + epilogue
   // CTA `ks` finishes rows [r0, r1) of the block (SWIGLU: gate rows r0..r1-1 of the first 64 and
   // their up rows + 64), summing the cluster's partial tiles in rank order.
-  if (!*abort_flag) {
+  {
+    const bool live = !*abort_flag;
     const int32_t* peer[kSMaxSplit];
 #pragma unroll
     for (int c = 0; c < kSMaxSplit; c++) peer[c] = c < p.ksplit ? cluster.map_shared_rank(part, c) : part;
@@ -257,9 +263,9 @@ __global__ void __launch_bounds__(kSThreads, 2)
     const int span = swiglu ? kSRows / 2 : kSRows;
     const int r0 = ks * span / p.ksplit, nr = (ks + 1) * span / p.ksplit - r0;
     const int total = nr * p.m;
-    for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
-      const int t = idx / nr, jj = r0 + (idx - t * nr);
-      int32_t acc = 0, acc_up = 0;
+    auto cluster_sum = [&](int t, int jj, int32_t& acc_up) {
+      int32_t acc = 0;
+      acc_up = 0;
 #pragma unroll
       for (int c = 0; c < kSMaxSplit; c++) {
         if (c < p.ksplit) {
@@ -267,17 +273,60 @@ __global__ void __launch_bounds__(kSThreads, 2)
           if (swiglu) acc_up += peer[c][t * kSRows + jj + kSRows / 2];
         }
       }
-      if (swiglu) {
-        const int f = rb * (kSRows / 2) + jj;
-        if (f < p.half) {
-          const float xs = p.x_scale[t];
-          const float g = deq(acc, xs, __ldg(p.w_scale + f));
-          const float u = deq(acc_up, xs, __ldg(p.w_scale + p.half + f));
-          static_cast<float*>(p.out)[(uint64_t)t * p.ldo + f] = det_swiglu(g, u);
+      return acc;
+    };
+    if (p.tp_on) {
+      // the ranks' partial products of this slice: sent to every rank, summed in rank order there
+      uint8_t* const mine = p.tp.base[p.tp.rank];
+      const uint64_t E = uwc_tp::call_epoch(mine);
+      const int par = (int)(E & 1), slot = rb * p.ksplit + ks;
+      const uint32_t ldn = p.tp.L.max_n;
+      for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
+        const int t = idx / nr, jj = r0 + (idx - t * nr), j = rb * kSRows + jj;
+        int32_t up;
+        const int32_t acc = live ? cluster_sum(t, jj, up) : 0;
+        if (j < p.n)
+          for (int d = 0; d < p.tp.world; d++)
+            uwc_tp::data_of(p.tp.base[d], p.tp.L, par, p.tp.rank)[(uint64_t)t * ldn + j] = acc;
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x < p.tp.world)
+        uwc_tp::st_release_sys(uwc_tp::flag_slot(p.tp.base[threadIdx.x], p.tp.L, par, p.tp.rank, slot), E);
+      if (threadIdx.x < p.tp.world) {
+        bool ok = true;
+        uwc_tp::wait_value(uwc_tp::flag_slot(mine, p.tp.L, par, threadIdx.x, slot), [E](uint64_t v) { return v == E; },
+                           p.wait_ns, p.status, 0, &ok);
+      }
+      __syncthreads();
+      __threadfence_system();
+      for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
+        const int t = idx / nr, jj = r0 + (idx - t * nr), j = rb * kSRows + jj;
+        if (j >= p.n) continue;
+        int32_t acc = 0;
+        for (int src = 0; src < p.tp.world; src++)
+          acc += __ldcg(uwc_tp::data_of(mine, p.tp.L, par, src) + (uint64_t)t * ldn + j);
+        store_one(p, t, j, acc);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) uwc_tp::call_end(mine, E, gridDim.x * gridDim.y);
+    } else if (live) {
+      for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
+        const int t = idx / nr, jj = r0 + (idx - t * nr);
+        int32_t acc_up;
+        const int32_t acc = cluster_sum(t, jj, acc_up);
+        if (swiglu) {
+          const int f = rb * (kSRows / 2) + jj;
+          if (f < p.half) {
+            const float xs = p.x_scale[t];
+            const float g = deq(acc, xs, __ldg(p.w_scale + f));
+            const float u = deq(acc_up, xs, __ldg(p.w_scale + p.half + f));
+            static_cast<float*>(p.out)[(uint64_t)t * p.ldo + f] = det_swiglu(g, u);
+          }
+        } else {
+          const int j = rb * kSRows + jj;
+          if (j < p.n) store_one(p, t, j, acc);
         }
-      } else {
-        const int j = rb * kSRows + jj;
-        if (j < p.n) store_one(p, t, j, acc);
       }
     }
   }
@@ -327,8 +376,9 @@ int launch_stream(const SParams& p, const CUtensorMap& tw, const CUtensorMap& tx
 std::atomic<int> g_stream_pdl{1};
 std::atomic<uint64_t> g_stream_wait_ns{0};
 
-// k-splits per 128-row block: enough CTAs to cover the SMs, at least four k-blocks each, at most
-// a portable cluster.
+// k-splits per 128-row block: enough CTAs to cover the SMs once, at least four k-blocks each, at most
+// a portable cluster. (Measured along the C5 decode chain: covering the SMs twice with clusters of 8
+// is faster for one GEMM alone but slower in the chain, where the quantizers' CTAs hold SM space.)
 int pick_split(int nrb, int kblocks) {
   const int want = (uwc_num_sms() + nrb - 1) / nrb;
   return std::max(1, std::min({want, kSMaxSplit, std::max(1, kblocks / 4)}));
@@ -341,26 +391,38 @@ void uwc_stream_set_wait_ns(uint64_t ns) { g_stream_wait_ns.store(ns); }
 
 bool uwc_stream_gemm_fits(int m, int n, int k) { return m >= 1 && m <= 64 && n >= 1 && k >= 16 && k % 16 == 0; }
 
-extern "C" int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
-                               const float* w_scale, const float* resid, void* out, int epi, void* stream) {
+namespace {
+int stream_call(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale, const float* w_scale,
+                const float* resid, void* out, int epi, const UwcTP* tp, void* stream) {
+  const int early_w = (epi & UWC_SEPI_EARLY_W) ? 1 : 0;
+  epi &= ~UWC_SEPI_EARLY_W;
   if (!X || !W || !out || epi < UWC_SEPI_I32 || epi > UWC_SEPI_SWIGLU) return UWC_ERR_ARG;
   if (epi != UWC_SEPI_I32 && (!x_scale || !w_scale)) return UWC_ERR_ARG;
   if (resid && epi != UWC_SEPI_RESID) return UWC_ERR_ARG;
+  if (tp && epi == UWC_SEPI_SWIGLU) return UWC_ERR_ARG;
   if (!uwc_stream_gemm_fits(m, n, k)) return UWC_ERR_SHAPE;
   if (epi == UWC_SEPI_SWIGLU && n % kSRows) return UWC_ERR_SHAPE;   // I % 64 == 0
   if ((((uintptr_t)X) | ((uintptr_t)W)) & 15) return UWC_ERR_ALIGN;
-  UWC_CHECK_DEVICE();
   SParams p{};
+  if (tp) {
+    const int rc = uwc_tp_args(tp, m, n, &p.tp);
+    if (rc != UWC_OK) return rc;
+    p.tp_on = 1;
+  }
+  UWC_CHECK_DEVICE();
   p.m = m; p.n = n; p.k = k; p.epi = epi;
   p.x_scale = x_scale; p.w_scale = w_scale; p.resid = resid; p.out = out;
   p.ldo = epi == UWC_SEPI_SWIGLU ? n / 2 : n;
   p.half = epi == UWC_SEPI_SWIGLU ? n / 2 : 0;
+  p.early_w = early_w;
   p.status = uwc_status_ptr();
   const uint64_t ns = g_stream_wait_ns.load();
   p.wait_ns = ns ? ns : UWC_WAIT_TIMEOUT_NS;
   p.kblocks = (k + kSKB - 1) / kSKB;
   const int nrb = (n + kSRows - 1) / kSRows;
   p.ksplit = pick_split(nrb, p.kblocks);
+  // the exchange waits for the peers' CTAs of the same call: every CTA must be resident (two per SM)
+  if (tp && (long long)nrb * p.ksplit > 2LL * uwc_num_sms()) return UWC_ERR_SHAPE;
   const int MP = m <= 16 ? 16 : (m <= 32 ? 32 : 64);
   CUtensorMap tw, tx;
   int rc = uwc_make_tmap_2d(&tw, W, (uint64_t)n, (uint64_t)k, (uint64_t)k, p.half ? kSRows / 2 : kSRows, kSKB);
@@ -371,4 +433,17 @@ extern "C" int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, i
   if (MP == 16) return launch_stream<16>(p, tw, tx, nrb, st, pdl);
   if (MP == 32) return launch_stream<32>(p, tw, tx, nrb, st, pdl);
   return launch_stream<64>(p, tw, tx, nrb, st, pdl);
+}
+}  // namespace
+
+extern "C" int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
+                               const float* w_scale, const float* resid, void* out, int epi, void* stream) {
+  return stream_call(X, W, m, n, k, x_scale, w_scale, resid, out, epi, nullptr, stream);
+}
+
+extern "C" int uwc_gemm_stream_tp(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
+                                  const float* w_scale, const float* resid, void* out, int epi, const UwcTP* tp,
+                                  void* stream) {
+  if (!tp) return UWC_ERR_ARG;
+  return stream_call(X, W, m, n, k, x_scale, w_scale, resid, out, epi, tp, stream);
 }

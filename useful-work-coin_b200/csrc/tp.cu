@@ -1,0 +1,75 @@
+// Exchange buffers of the tensor-parallel decode kernels: allocation and CUDA IPC mapping.
+#include <cstring>
+
+#include "uwc_host.h"
+#include "uwc_tp.cuh"
+
+extern "C" uint64_t uwc_tp_buffer_bytes(int max_m, int max_n) {
+  if (max_m <= 0 || max_n <= 0) return 0;
+  return uwc_tp::layout((uint32_t)max_m, (uint32_t)max_n).total;
+}
+
+extern "C" int uwc_tp_alloc(int max_m, int max_n, void** buf) {
+  if (!buf || max_m <= 0 || max_n <= 0 || max_m > 65535 || max_n > (1 << 20)) return UWC_ERR_ARG;
+  UWC_CHECK_DEVICE();
+  const uint64_t bytes = uwc_tp_buffer_bytes(max_m, max_n);
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return UWC_ERR_CUDA;
+  }
+  *buf = p;
+  return UWC_OK;
+}
+
+extern "C" int uwc_tp_free(void* buf) {
+  if (!buf) return UWC_ERR_ARG;
+  return cudaFree(buf) == cudaSuccess ? UWC_OK : (cudaGetLastError(), UWC_ERR_CUDA);
+}
+
+extern "C" int uwc_ipc_handle(const void* buf, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == UWC_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!buf || !handle) return UWC_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(buf)) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  return UWC_OK;
+}
+
+extern "C" int uwc_ipc_open(const void* handle, void** peer_buf) {
+  if (!handle || !peer_buf) return UWC_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return UWC_ERR_CUDA;
+  }
+  return UWC_OK;
+}
+
+extern "C" int uwc_ipc_close(void* peer_buf) {
+  if (!peer_buf) return UWC_ERR_ARG;
+  return cudaIpcCloseMemHandle(peer_buf) == cudaSuccess ? UWC_OK : (cudaGetLastError(), UWC_ERR_CUDA);
+}
+
+// The kernel form of a UwcTP, checked against the call's shape.
+int uwc_tp_args(const UwcTP* tp, int m, int n, TPArgs* out) {
+  if (!tp || tp->world < 1 || tp->world > UWC_TP_MAX_WORLD || tp->rank < 0 || tp->rank >= tp->world) return UWC_ERR_ARG;
+  if (m > tp->max_m || n > tp->max_n) return UWC_ERR_SHAPE;
+  out->rank = tp->rank;
+  out->world = tp->world;
+  out->L = uwc_tp::layout((uint32_t)tp->max_m, (uint32_t)tp->max_n);
+  for (int r = 0; r < uwc_tp::kMaxWorld; r++) {
+    out->base[r] = r < tp->world ? static_cast<uint8_t*>(tp->base[r]) : nullptr;
+    if (r < tp->world && (!tp->base[r] || ((uintptr_t)tp->base[r] & 255))) return UWC_ERR_ARG;
+  }
+  return UWC_OK;
+}

@@ -46,3 +46,10 @@ void uwc_stream_set_pdl(int on);
 // Programmatic dependent launch of the few-row quantizers (detq.cu) on / off.
 void uwc_row_set_pdl(int on);
 void uwc_stream_set_wait_ns(uint64_t ns);
+
+// The kernel form of a UwcTP (tp.cu), checked against a call of m rows and n columns.
+struct TPArgs;
+int uwc_tp_args(const UwcTP* tp, int m, int n, TPArgs* out);
+
+// The bound of device-side waits set by UWC_HOOK_WAIT_NS (0: the default).
+uint64_t uwc_wait_ns();

@@ -38,6 +38,14 @@ SIGNATURES = {
     "uwc_gemm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32,
                         _P, _U64, _P]),
     "uwc_gemm_stream": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P]),
+    "uwc_tp_buffer_bytes": (_U64, [_I32, _I32]),
+    "uwc_tp_alloc": (_I32, [_I32, _I32, _P]),
+    "uwc_tp_free": (_I32, [_P]),
+    "uwc_ipc_handle": (_I32, [_P, _P]),
+    "uwc_ipc_open": (_I32, [_P, _P]),
+    "uwc_ipc_close": (_I32, [_P]),
+    "uwc_quant_act_tp": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "uwc_gemm_stream_tp": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
     "uwc_mined_block_layout": (_I32, [_I32, _I32, _I32, _P]),
     "uwc_mined_workspace_layout": (_I32, [_I32, _I32, _I32, _I32, _I32, _I32, _I32, _P]),
     "uwc_mined_setup_block": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _U64, _P, _U64, _P]),

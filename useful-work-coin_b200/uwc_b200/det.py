@@ -12,21 +12,29 @@ import torch
 from . import ops
 
 
-def int_gemm(q: torch.Tensor, Wq: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Exact q @ Wq^T for int8 q (m x k) and Wq (n x k), int32 result (DetLinear.int_gemm)."""
+def int_gemm(q: torch.Tensor, Wq: torch.Tensor, out: torch.Tensor | None = None,
+             static_weights: bool = False) -> torch.Tensor:
+    """Exact q @ Wq^T for int8 q (m x k) and Wq (n x k), int32 result (DetLinear.int_gemm).
+    static_weights: Wq is a model weight, not produced by the kernel just before this call, so a
+    decode-sized call may start streaming it early (ops.gemm_stream's early_w)."""
     m, n = q.shape[0], Wq.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.int32, device=q.device)
+    if static_weights and m <= ops.STREAM_MAX_M:
+        return ops.gemm_stream(q.contiguous(), Wq.contiguous(), ops.SEPI_I32, out=out, early_w=True)
     ops.gemm(q.contiguous(), Wq.contiguous(), out=out, out_mode=ops.OUT_I32)
     return out
 
 
 def linear_f32(q: torch.Tensor, s_x: torch.Tensor, Wq: torch.Tensor, s_w: torch.Tensor,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, static_weights: bool = False) -> torch.Tensor:
     """fmul(fmul(float32(q @ Wq^T), s_x[:, None]), s_w[None, :]) in one kernel (fp32 out)."""
     m, n = q.shape[0], Wq.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=q.device)
+    if static_weights and m <= ops.STREAM_MAX_M:
+        return ops.gemm_stream(q.contiguous(), Wq.contiguous(), ops.SEPI_F32, x_scale=s_x, w_scale=s_w, out=out,
+                               early_w=True)
     ops.gemm(q.contiguous(), Wq.contiguous(), a_scale=s_x.contiguous().float(), b_scale=s_w.contiguous().float(),
              out=out, out_mode=ops.OUT_F32)
     return out

@@ -132,7 +132,7 @@ def qkv_post(acc, s1, sw, qnw, knw, cos, sin, T: int, H: int, Hkv: int, eps: flo
 
 def linear_q(lin, q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     """fmul(fmul(float(q @ Wq^T), s), sw): the dequantized GEMM of already-quantized rows."""
-    return det.linear_f32(q, s, lin.Wq, lin.sw)
+    return det.linear_f32(q, s, lin.Wq, lin.sw, static_weights=True)
 
 
 def linear(lin, x: torch.Tensor) -> torch.Tensor:
@@ -152,7 +152,7 @@ def linear_resid(lin, q: torch.Tensor, s: torch.Tensor, x: torch.Tensor | None) 
     """fadd(x, deq(q @ Wq^T)): the GEMM and dequant_residual (stages.py:117-125); decode-sized rows
     run it as one weight-streaming GEMM with the residual add in its epilogue."""
     if q.shape[0] <= ops.STREAM_MAX_M:
-        return ops.gemm_stream(q, lin.Wq, ops.SEPI_RESID, x_scale=s, w_scale=lin.sw, resid=x)
+        return ops.gemm_stream(q, lin.Wq, ops.SEPI_RESID, x_scale=s, w_scale=lin.sw, resid=x, early_w=True)
     return dequant_residual(det.int_gemm(q, lin.Wq), s, lin.sw, x)
 
 
@@ -163,7 +163,7 @@ def mlp_residual(gu, down, w_norm: torch.Tensor, r1: torch.Tensor, eps: float) -
     SwiGLU row is swiglu_quant's second half)."""
     q3, s3 = rmsnorm_quant(r1, w_norm, eps, gu.bs)
     if q3.shape[0] <= ops.STREAM_MAX_M and gu.Wq.shape[0] % 128 == 0:
-        h = ops.gemm_stream(q3, gu.Wq, ops.SEPI_SWIGLU, x_scale=s3, w_scale=gu.sw)
+        h = ops.gemm_stream(q3, gu.Wq, ops.SEPI_SWIGLU, x_scale=s3, w_scale=gu.sw, early_w=True)
         q4, s4 = quant_act(h, down.bs)
     else:
         q4, s4 = swiglu_quant(det.int_gemm(q3, gu.Wq), s3, gu.sw, down.bs)

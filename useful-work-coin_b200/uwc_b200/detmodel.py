@@ -104,11 +104,11 @@ class Linear:
         self.sw = torch.cat(sw).contiguous()
 
     def int_gemm(self, q: torch.Tensor) -> torch.Tensor:
-        return det.int_gemm(q, self.Wq)
+        return det.int_gemm(q, self.Wq, static_weights=True)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         q, s = detgpu.quant_act(x, self.bs)
-        return det.linear_f32(q, s, self.Wq, self.sw)
+        return det.linear_f32(q, s, self.Wq, self.sw, static_weights=True)
 
 
 class DetQwen3:

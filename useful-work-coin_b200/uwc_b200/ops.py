@@ -208,14 +208,16 @@ def gemm(A, B, *, r=128, flags=0, corrA=None, corrB=None, maxabs=None, key=None,
 
 
 SEPI_I32, SEPI_F32, SEPI_BF16, SEPI_RESID, SEPI_SWIGLU = range(5)
+SEPI_EARLY_W = 0x100
 STREAM_MAX_M = 64
 
 
-def gemm_stream(X, W, epi=SEPI_I32, *, x_scale=None, w_scale=None, resid=None, out=None):
+def gemm_stream(X, W, epi=SEPI_I32, *, x_scale=None, w_scale=None, resid=None, out=None, early_w=False):
     """out = X W^T on the weight-streaming GEMM (m <= 64), with the epilogue `epi` (uwc_gemm_stream):
     SEPI_I32 int32; SEPI_F32 / SEPI_BF16 the dequant fmul(fmul(float(acc), x_scale), w_scale);
     SEPI_RESID that plus `resid` (fp32 m x n); SEPI_SWIGLU det_silu(gate) * up for W = [gate; up]
-    (n / 2 rows each), m x n/2 fp32."""
+    (n / 2 rows each), m x n/2 fp32. early_w: W is a static weight (not written by the kernel
+    launched just before), so the call may stream it while that kernel finishes."""
     m, k = X.shape
     n = W.shape[0]
     assert X.dtype == torch.int8 and W.dtype == torch.int8 and X.is_contiguous() and W.is_contiguous()
@@ -224,7 +226,8 @@ def gemm_stream(X, W, epi=SEPI_I32, *, x_scale=None, w_scale=None, resid=None, o
         out = torch.empty((m, n // 2 if epi == SEPI_SWIGLU else n), dtype=dt, device=X.device)
     f32 = (lambda t: None if t is None else t.contiguous().float())
     check(lib().uwc_gemm_stream(_p(X), _p(W), m, n, k, _p(f32(x_scale)), _p(f32(w_scale)),
-                                _p(None if resid is None else resid.contiguous()), _p(out), epi, _stream()),
+                                _p(None if resid is None else resid.contiguous()), _p(out),
+                                epi | (SEPI_EARLY_W if early_w else 0), _stream()),
           "gemm_stream")
     return out
 

@@ -20,9 +20,13 @@ bit-identical to one device:
 a CPU stand-in built from the oracle to check the sharding and collectives with gloo ranks. A
 backend with `fused = True` also offers quant_act, linear_resid and swiglu_linear: decode-sized
 calls then run the output step inside the weight-streaming GEMM (the row-parallel layer on one
-rank, and the gate/up SwiGLU on any number), with the same bits as the separate kernels.
+rank, and the gate/up SwiGLU on any number), with the same bits as the separate kernels. Given a
+PeerExchange, a row-parallel layer on several ranks runs its two all-reduces (the row absmax and
+the int32 partial products) inside its quantizer and GEMM over NVLink peer memory instead of NCCL.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -32,6 +36,60 @@ def _all_reduce(t: torch.Tensor, op, group) -> None:
     """all_reduce over `group`; a no-op for a single rank (no process group needed)."""
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(t, op=op, group=group)
+
+
+class _UwcTP(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int), ("world", ctypes.c_int), ("max_m", ctypes.c_int), ("max_n", ctypes.c_int),
+                ("base", ctypes.c_void_p * 8)]
+
+
+class PeerExchange:
+    """The NVLink peer exchange of the fused tensor-parallel decode kernels (uwc_quant_act_tp,
+    uwc_gemm_stream_tp): one zero-filled buffer per rank, every peer's buffer mapped here through CUDA
+    IPC. Collective over `group`: every rank constructs it with the same max_m / max_n and makes the
+    same sequence of fused calls; close() (also collective) releases it."""
+
+    def __init__(self, max_m: int, max_n: int, rank: int, world: int, device, group=None):
+        from ._lib import check, lib
+        L = lib()
+        self.rank, self.world, self.group, self.device = rank, world, group, torch.device(device)
+        self._own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(L.uwc_tp_alloc(max_m, max_n, ctypes.byref(self._own)), "tp_alloc")
+            handle = (ctypes.c_uint8 * 64)()
+            check(L.uwc_ipc_handle(self._own, handle), "ipc_handle")
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+            handles = [torch.empty_like(mine) for _ in range(world)]
+            if world > 1:
+                dist.all_gather(handles, mine, group=group)
+            else:
+                handles = [mine]
+            self.peers = []
+            self.tp = _UwcTP(rank, world, max_m, max_n)
+            for r in range(world):
+                if r == rank:
+                    self.tp.base[r] = self._own.value
+                    continue
+                hb = (ctypes.c_uint8 * 64)(*handles[r].cpu().tolist())
+                ptr = ctypes.c_void_p()
+                check(L.uwc_ipc_open(hb, ctypes.byref(ptr)), "ipc_open")
+                self.peers.append(ptr)
+                self.tp.base[r] = ptr.value
+
+    def close(self) -> None:
+        from ._lib import lib
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)          # no peer writes into this buffer any more
+        L = lib()
+        for ptr in self.peers:
+            L.uwc_ipc_close(ptr)
+        if self.world > 1:
+            dist.barrier(group=self.group)          # every peer has unmapped it
+        L.uwc_tp_free(self._own)
+        self._own, self.peers = None, []
 
 
 def even_bounds(n: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
@@ -56,10 +114,10 @@ class GPUKernels:
         return det, detgpu
 
     def linear_f32(self, q, s, Wq, sw):
-        return self._mods()[0].linear_f32(q, s, Wq, sw)
+        return self._mods()[0].linear_f32(q, s, Wq, sw, static_weights=True)
 
     def int_gemm(self, q, Wq):
-        return self._mods()[0].int_gemm(q, Wq)
+        return self._mods()[0].int_gemm(q, Wq, static_weights=True)
 
     def fwht_absmax(self, x, bs):
         return self._mods()[1].fwht_absmax(x, bs)
@@ -89,14 +147,39 @@ class GPUKernels:
         ops = self._stream(q)
         if ops is None:
             return self.dequant_residual(self.int_gemm(q, Wq), s, sw, x)
-        return ops.gemm_stream(q, Wq, ops.SEPI_RESID, x_scale=s, w_scale=sw, resid=x)
+        return ops.gemm_stream(q, Wq, ops.SEPI_RESID, x_scale=s, w_scale=sw, resid=x, early_w=True)
+
+    def quant_act_tp(self, x, bs, exchange):
+        """quant_act of a row-parallel shard with the whole row's absmax, exchanged in the kernel."""
+        from . import ops
+        from ._lib import check, lib
+        x = x.contiguous().float()
+        m, k = x.shape
+        q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+        sc = torch.empty(m, dtype=torch.float32, device=x.device)
+        check(lib().uwc_quant_act_tp(ops._p(x), m, k, bs, ops._p(q), ops._p(sc), ctypes.byref(exchange.tp),
+                                     ops._stream()), "quant_act_tp")
+        return q, sc
+
+    def linear_resid_tp(self, q, s, Wq, sw, x, exchange):
+        """fadd(x, deq(sum over the ranks of q Wq^T)), the sum exchanged in the GEMM's epilogue."""
+        from . import ops
+        from ._lib import check, lib
+        m, n = q.shape[0], Wq.shape[0]
+        out = torch.empty((m, n), dtype=torch.float32, device=q.device)
+        f32 = s.contiguous().float(), sw.contiguous().float()
+        check(lib().uwc_gemm_stream_tp(ops._p(q.contiguous()), ops._p(Wq), m, n, q.shape[1], ops._p(f32[0]),
+                                       ops._p(f32[1]), ops._p(None if x is None else x.contiguous()), ops._p(out),
+                                       ops.SEPI_RESID | ops.SEPI_EARLY_W, ctypes.byref(exchange.tp), ops._stream()),
+              "gemm_stream_tp")
+        return out
 
     def swiglu_linear(self, q, s, Wq, sw):
         """det_silu(deq(gate)) * deq(up) of q [gate; up]^T."""
         ops = self._stream(q)
         if ops is None or Wq.shape[0] % 128:
             return self.swiglu(self.int_gemm(q, Wq), s, sw)
-        return ops.gemm_stream(q, Wq, ops.SEPI_SWIGLU, x_scale=s, w_scale=sw)
+        return ops.gemm_stream(q, Wq, ops.SEPI_SWIGLU, x_scale=s, w_scale=sw, early_w=True)
 
 
 def _default(kernels):
@@ -133,9 +216,9 @@ class RowParallelLinear:
     """W (n x k) split by input columns on Hadamard-block boundaries; forward(x_shard) -> full output."""
 
     def __init__(self, Wq: torch.Tensor, sw: torch.Tensor, bs: int, rank: int, world: int, device, kernels=None,
-                 group=None, bounds: tuple[int, int] | None = None):
+                 group=None, bounds: tuple[int, int] | None = None, exchange: PeerExchange | None = None):
         n, k = Wq.shape
-        self.n, self.k, self.bs, self.group = n, k, bs, group
+        self.n, self.k, self.bs, self.group, self.exchange = n, k, bs, group, exchange
         align = max(bs, 16)
         self.lo, self.hi = bounds if bounds is not None else even_bounds(k, world, rank, align)
         assert self.lo % align == 0 and self.hi % align == 0, "shards must hold whole Hadamard blocks"
@@ -152,6 +235,12 @@ class RowParallelLinear:
             # one rank: the shard is the whole row, so its own absmax is the row's
             q, s = K.quant_act(x_shard, self.bs)
             return K.linear_resid(q, s, self.Wq, self.sw, residual)
+        ex = self.exchange
+        if ex is not None and getattr(K, "fused", False) and x_shard.shape[0] <= min(64, ex.tp.max_m) \
+                and self.n <= ex.tp.max_n:
+            # decode over NVLink: both all-reduces inside the kernels
+            q, s = K.quant_act_tp(x_shard, self.bs, ex)
+            return K.linear_resid_tp(q, s, self.Wq, self.sw, residual, ex)
         amax = K.fwht_absmax(x_shard, self.bs)
         _all_reduce(amax, dist.ReduceOp.MAX, self.group)
         q, s = K.quant_act_global(x_shard, self.bs, amax)
@@ -164,14 +253,15 @@ class TPMLP:
     """gate/up (2I x D, gate rows then up rows) and down (D x I) split over the ranks of `group`."""
 
     def __init__(self, gu_Wq, gu_sw, gu_bs: int, down_Wq, down_sw, down_bs: int, rank: int, world: int, device,
-                 kernels=None, group=None):
+                 kernels=None, group=None, exchange: PeerExchange | None = None):
         I = down_Wq.shape[1]
         assert gu_Wq.shape[0] == 2 * I
         lo, hi = even_bounds(I, world, rank, max(down_bs, 16))
         self.gu_bs = gu_bs
         self.gu_Wq = torch.cat([gu_Wq[lo:hi], gu_Wq[I + lo:I + hi]]).contiguous().to(device)
         self.gu_sw = torch.cat([gu_sw[lo:hi], gu_sw[I + lo:I + hi]]).contiguous().to(device)
-        self.down = RowParallelLinear(down_Wq, down_sw, down_bs, rank, world, device, kernels, group, (lo, hi))
+        self.down = RowParallelLinear(down_Wq, down_sw, down_bs, rank, world, device, kernels, group, (lo, hi),
+                                      exchange)
         self.K = _default(kernels)
 
     def forward(self, r1: torch.Tensor, w_norm: torch.Tensor, eps: float) -> torch.Tensor:
