@@ -195,7 +195,8 @@ int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const
  * the caller's own transport) and maps theirs (uwc_ipc_open). A UwcTP names this rank and every
  * rank's buffer as mapped here (base[rank] = its own). Every rank must make the same sequence of
  * uwc_*_tp calls on its buffer, each on its own GPU; a call waits (bounded, UWC_DEV_TIMEOUT) for
- * the peers' contributions to the same call.
+ * the peers' contributions to the same call. Values cross NVLink as 8-byte words tagged with the
+ * call's epoch (a device-side call counter), which the receiver polls: no flags or fences.
  *   uwc_quant_act_tp    uwc_quant_act of a row-parallel input shard with the absmax of the whole
  *                       row: each rank's shard absmax goes to every peer, each takes the maximum
  *                       (the fwht_absmax + MAX all-reduce + quant_act_global sequence, in one kernel);

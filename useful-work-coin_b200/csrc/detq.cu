@@ -191,8 +191,8 @@ __global__ void __launch_bounds__(NT) k_quant_act(const void* __restrict__ x, in
 }
 
 // quant_act of a row-parallel shard with the whole row's absmax, exchanged in the kernel: each CTA
-// (one row) publishes its shard's absmax to every rank's exchange buffer as (epoch << 32) | bits,
-// waits for every rank's value of the row, and quantizes with the maximum (the fwht_absmax, MAX
+// (one row) stores its shard's absmax, tagged with the call's epoch, into every rank's exchange
+// buffer, polls for every rank's value of the row, and quantizes with the maximum (the fwht_absmax, MAX
 // all-reduce and quant_act_global sequence: the same maximum, so the same bits).
 template <int NT>
 __global__ void __launch_bounds__(NT) k_quant_act_tp(const float* __restrict__ x, int k, int bs,
@@ -211,15 +211,12 @@ __global__ void __launch_bounds__(NT) k_quant_act_tp(const float* __restrict__ x
   if (bs > 1) fwht_row<NT>(row, k, bs);
   const float mx = row_absmax<NT>(row, k, red);
   const int p = threadIdx.x;
-  if (p < tp.world)
-    uwc_tp::st_release_sys(uwc_tp::amax_slot(tp.base[p], tp.L, par, tp.rank, r), (E << 32) | __float_as_uint(mx));
   if (p < tp.world) {
+    uwc_tp::st_sys(uwc_tp::amax_slot(tp.base[p], tp.L, par, tp.rank, r), uwc_tp::tagged(E, __float_as_uint(mx)));
     bool ok = true;
-    const uint32_t want = (uint32_t)E;
-    const uint64_t v = uwc_tp::wait_value(
-        uwc_tp::amax_slot(mine, tp.L, par, p, r), [want](uint64_t w) { return (uint32_t)(w >> 32) == want; },
-        wait_ns, status, (uint64_t)__float_as_uint(mx), &ok);
-    src_max[p] = __uint_as_float((uint32_t)v);
+    const uint32_t v = uwc_tp::wait_tagged(uwc_tp::amax_slot(mine, tp.L, par, p, r), E, uwc_tp::now_ns() + wait_ns,
+                                           status, &ok);
+    src_max[p] = ok ? __uint_as_float(v) : mx;
   }
   __syncthreads();
   float am = src_max[0];

@@ -276,10 +276,11 @@ __global__ void __launch_bounds__(kSThreads, 2)
       return acc;
     };
     if (p.tp_on) {
-      // the ranks' partial products of this slice: sent to every rank, summed in rank order there
+      // the ranks' partial products of this slice, each tagged with the call's epoch: sent to every
+      // rank, polled and summed in rank order there
       uint8_t* const mine = p.tp.base[p.tp.rank];
       const uint64_t E = uwc_tp::call_epoch(mine);
-      const int par = (int)(E & 1), slot = rb * p.ksplit + ks;
+      const int par = (int)(E & 1);
       const uint32_t ldn = p.tp.L.max_n;
       for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
         const int t = idx / nr, jj = r0 + (idx - t * nr), j = rb * kSRows + jj;
@@ -287,26 +288,47 @@ __global__ void __launch_bounds__(kSThreads, 2)
         const int32_t acc = live ? cluster_sum(t, jj, up) : 0;
         if (j < p.n)
           for (int d = 0; d < p.tp.world; d++)
-            uwc_tp::data_of(p.tp.base[d], p.tp.L, par, p.tp.rank)[(uint64_t)t * ldn + j] = acc;
+            uwc_tp::st_sys(uwc_tp::data_of(p.tp.base[d], p.tp.L, par, p.tp.rank) + (uint64_t)t * ldn + j,
+                           uwc_tp::tagged(E, (uint32_t)acc));
       }
-      __threadfence_system();
-      __syncthreads();
-      if (threadIdx.x < p.tp.world)
-        uwc_tp::st_release_sys(uwc_tp::flag_slot(p.tp.base[threadIdx.x], p.tp.L, par, p.tp.rank, slot), E);
-      if (threadIdx.x < p.tp.world) {
-        bool ok = true;
-        uwc_tp::wait_value(uwc_tp::flag_slot(mine, p.tp.L, par, threadIdx.x, slot), [E](uint64_t v) { return v == E; },
-                           p.wait_ns, p.status, 0, &ok);
-      }
-      __syncthreads();
-      __threadfence_system();
-      for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
-        const int t = idx / nr, jj = r0 + (idx - t * nr), j = rb * kSRows + jj;
-        if (j >= p.n) continue;
-        int32_t acc = 0;
-        for (int src = 0; src < p.tp.world; src++)
-          acc += __ldcg(uwc_tp::data_of(mine, p.tp.L, par, src) + (uint64_t)t * ldn + j);
-        store_one(p, t, j, acc);
+      // receive: kPoll items per thread at a time, each source's words loaded together (independent
+      // loads in flight), then only stale words polled again
+      constexpr int kPoll = 4;
+      bool ok = true;
+      const uint64_t deadline = uwc_tp::now_ns() + p.wait_ns;
+      for (int i0 = threadIdx.x; i0 < total; i0 += kSThreads * kPoll) {
+        uint64_t off[kPoll];
+        bool use[kPoll];
+        int32_t acc[kPoll];
+#pragma unroll
+        for (int c = 0; c < kPoll; c++) {
+          const int idx = i0 + c * kSThreads;
+          const int t = idx / nr, j = rb * kSRows + r0 + (idx - t * nr);
+          use[c] = idx < total && j < p.n;
+          off[c] = use[c] ? (uint64_t)t * ldn + j : 0;
+          acc[c] = 0;
+        }
+        for (int src = 0; src < p.tp.world; src++) {
+          const uint64_t* d = uwc_tp::data_of(mine, p.tp.L, par, src);
+          uint64_t w[kPoll];
+#pragma unroll
+          for (int c = 0; c < kPoll; c++) w[c] = use[c] ? uwc_tp::ld_sys(d + off[c]) : 0;
+#pragma unroll
+          for (int c = 0; c < kPoll; c++) {
+            if (!use[c]) continue;
+            const uint32_t v = (uint32_t)(w[c] >> 32) == (uint32_t)E
+                                   ? (uint32_t)w[c]
+                                   : uwc_tp::wait_tagged(d + off[c], E, deadline, p.status, &ok);
+            acc[c] += (int32_t)v;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < kPoll; c++) {
+          if (!use[c]) continue;
+          const int idx = i0 + c * kSThreads;
+          const int t = idx / nr;
+          store_one(p, t, rb * kSRows + r0 + (idx - t * nr), acc[c]);
+        }
       }
       __syncthreads();
       if (threadIdx.x == 0) uwc_tp::call_end(mine, E, gridDim.x * gridDim.y);

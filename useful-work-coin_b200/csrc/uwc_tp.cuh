@@ -4,9 +4,11 @@
 // buffer (CUDA IPC over NVLink) and the kernels write into peers' buffers with plain stores:
 //
 //   header   epoch (u64) = calls completed on this buffer, done counter (u32) of the running call
-//   flags    [2 parities][8 sources][max_slots] u64: the epoch at which a source's slice landed
-//   amax     [2][8][max_m] u64: (epoch << 32) | float bits of a source's row absmax
-//   data     [2][8][max_m][max_n] int32: a source's partial products
+//   amax     [2 parities][8 sources][max_m] u64: (epoch << 32) | float bits of a source's row absmax
+//   data     [2][8][max_m][max_n] u64: (epoch << 32) | a source's int32 partial product
+//
+// Every value carries the epoch of the call that wrote it in the same 8-byte store, so a reader
+// polls the value itself: no flags, no fences, one NVLink write latency per exchange.
 //
 // A call reads E = epoch + 1 and uses parity E & 1; its last CTA sets epoch = E. All ranks run the
 // same sequence of calls, so E agrees across ranks, and a rank can be at most one call ahead of a
@@ -22,21 +24,18 @@ constexpr uint64_t kHeader = 256;
 constexpr int kMaxWorld = UWC_TP_MAX_WORLD;
 
 struct Layout {
-  uint64_t flags, amax, data, total;
-  uint32_t max_m, max_n, max_slots;
+  uint64_t amax, data, total;
+  uint32_t max_m, max_n;
 };
 
-// max_slots: CTAs of one weight-streaming GEMM (128-row blocks x k-splits <= 8).
 __host__ __device__ inline Layout layout(uint32_t max_m, uint32_t max_n) {
   Layout L;
   L.max_m = max_m;
   L.max_n = max_n;
-  L.max_slots = ((max_n + 127) / 128) * 8;
-  L.flags = kHeader;
-  L.amax = L.flags + 2ull * kMaxWorld * L.max_slots * 8;
+  L.amax = kHeader;
   L.data = L.amax + 2ull * kMaxWorld * max_m * 8;
   L.data = (L.data + 255) & ~255ull;
-  L.total = L.data + 2ull * kMaxWorld * max_m * max_n * 4;
+  L.total = L.data + 2ull * kMaxWorld * max_m * max_n * 8;
   return L;
 }
 
@@ -44,15 +43,17 @@ __host__ __device__ inline Layout layout(uint32_t max_m, uint32_t max_n) {
 
 namespace uwc_tp {
 
-// System-scope release store / acquire load (the flag protocol between GPUs).
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// System-scope relaxed 8-byte store / load: single-copy atomic, seen by (and seeing) other GPUs.
+__device__ __forceinline__ void st_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+__device__ __forceinline__ uint64_t ld_sys(const uint64_t* p) {
   uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// The tagged word of epoch E carrying v.
+__device__ __forceinline__ uint64_t tagged(uint64_t E, uint32_t v) { return (E << 32) | v; }
 
 __device__ __forceinline__ uint64_t* header_epoch(uint8_t* base) { return reinterpret_cast<uint64_t*>(base); }
 __device__ __forceinline__ unsigned* header_done(uint8_t* base) { return reinterpret_cast<unsigned*>(base + 8); }
@@ -72,37 +73,36 @@ __device__ __forceinline__ void call_end(uint8_t* base, uint64_t E, unsigned nbl
   }
 }
 
-__device__ __forceinline__ uint64_t* flag_slot(uint8_t* base, const Layout& L, int parity, int src, int slot) {
-  return reinterpret_cast<uint64_t*>(base + L.flags) + ((uint64_t)parity * kMaxWorld + src) * L.max_slots + slot;
-}
 __device__ __forceinline__ uint64_t* amax_slot(uint8_t* base, const Layout& L, int parity, int src, int row) {
   return reinterpret_cast<uint64_t*>(base + L.amax) + ((uint64_t)parity * kMaxWorld + src) * L.max_m + row;
 }
-__device__ __forceinline__ int32_t* data_of(uint8_t* base, const Layout& L, int parity, int src) {
-  return reinterpret_cast<int32_t*>(base + L.data) + ((uint64_t)parity * kMaxWorld + src) * L.max_m * L.max_n;
+__device__ __forceinline__ uint64_t* data_of(uint8_t* base, const Layout& L, int parity, int src) {
+  return reinterpret_cast<uint64_t*>(base + L.data) + ((uint64_t)parity * kMaxWorld + src) * L.max_m * L.max_n;
 }
 
-// Spins (bounded by timeout_ns of globaltimer) until pred(ld_acquire(p)) holds; returns the value,
-// or raises `status` and returns `fallback` on expiry.
-template <typename Pred>
-__device__ __forceinline__ uint64_t wait_value(const uint64_t* p, Pred pred, uint64_t timeout_ns, uint32_t* status,
-                                               uint64_t fallback, bool* ok) {
-  uint64_t v = ld_acquire_sys(p);
-  if (pred(v)) return v;
-  uint64_t t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  for (;;) {
-    __nanosleep(64);
-    v = ld_acquire_sys(p);
-    if (pred(v)) return v;
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > timeout_ns) {
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// The low 32 bits of the tagged word at p once its tag is epoch E. Spins until then or until the
+// globaltimer passes `deadline` (then raises UWC_DEV_TIMEOUT in `status`, clears *ok and returns 0;
+// later waits of the same thread give up at once).
+__device__ __forceinline__ uint32_t wait_tagged(const uint64_t* p, uint64_t E, uint64_t deadline, uint32_t* status,
+                                                bool* ok) {
+  const uint32_t want = (uint32_t)E;
+  uint64_t v = ld_sys(p);
+  while ((uint32_t)(v >> 32) != want) {
+    if (!*ok) return 0;
+    if (now_ns() > deadline) {
       if (status) atomicOr(status, UWC_DEV_TIMEOUT);
       *ok = false;
-      return fallback;
+      return 0;
     }
+    v = ld_sys(p);
   }
+  return (uint32_t)v;
 }
 
 }  // namespace uwc_tp
