@@ -344,6 +344,8 @@ def run_c5(a, world, rank, local):
         r1 = o.forward(oc, residual=xin)
         return mlp.forward(r1, wn, 1e-5)
 
+    torch.cuda.synchronize()
+    barrier(world)                                   # ranks enter the exchange together
     # parity at this N: the TP step's qkv shard and layer output == the one-GPU layer, bit for bit
     oc_full = torch.randn(m, o.k, device=dev, generator=torch.Generator(device=dev).manual_seed(78))
     q1, s1 = detgpu.rmsnorm_quant(x, wn, 1e-5, bs)
@@ -375,6 +377,8 @@ def run_c5(a, world, rank, local):
     evs = []
     for i in range(a.steps):
         evict()
+        if ex is not None:
+            ex.barrier()                             # ranks start the step together
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         graph.replay()
@@ -395,6 +399,8 @@ def run_c5(a, world, rank, local):
     barrier(world)
     for i in range(a.steps):
         evict()
+        if ex is not None:
+            ex.barrier()                             # ranks start the step together
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         xs.copy_(x_host, non_blocking=True)

@@ -196,7 +196,8 @@ int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const
  * rank's buffer as mapped here (base[rank] = its own). Every rank must make the same sequence of
  * uwc_*_tp calls on its buffer, each on its own GPU; a call waits (bounded, UWC_DEV_TIMEOUT) for
  * the peers' contributions to the same call. Values cross NVLink as 8-byte words tagged with the
- * call's epoch (a device-side call counter), which the receiver polls: no flags or fences.
+ * call's epoch (a device-side call counter), which the receiver polls: no flags or fences. The wait
+ * bound is 10 s (ranks may reach a call seconds apart at start-up); UWC_HOOK_WAIT_NS overrides it.
  *   uwc_quant_act_tp    uwc_quant_act of a row-parallel input shard with the absmax of the whole
  *                       row: each rank's shard absmax goes to every peer, each takes the maximum
  *                       (the fwht_absmax + MAX all-reduce + quant_act_global sequence, in one kernel);
@@ -219,6 +220,9 @@ int uwc_ipc_handle(const void* buf, void* handle);
 int uwc_ipc_open(const void* handle, void** peer_buf);
 int uwc_ipc_close(void* peer_buf);
 int uwc_quant_act_tp(const float* x, int m, int k, int bs, int8_t* q, float* scale, const UwcTP* tp, void* stream);
+/* A device-side barrier of the ranks over the same exchange (one more call in the sequence): the
+ * ranks' streams leave it within about one NVLink write latency of each other. */
+int uwc_tp_barrier(const UwcTP* tp, void* stream);
 int uwc_gemm_stream_tp(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
                        const float* w_scale, const float* resid, void* out, int epi, const UwcTP* tp, void* stream);
 

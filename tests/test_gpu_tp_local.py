@@ -2,7 +2,8 @@
 
   - a one-rank exchange (every value sent to itself through the tagged-word protocol) gives the
     local kernels' bits: uwc_quant_act_tp == uwc_quant_act, uwc_gemm_stream_tp == uwc_gemm_stream,
-    eagerly and over many CUDA-graph replays (the device-side call counter advances per call);
+    eagerly and over many CUDA-graph replays with device-side barriers between them (the call
+    counter on the device advances per call);
   - the bounded wait: a two-rank exchange whose second rank never writes (its buffer is a second
     local allocation nothing writes into) ends with UWC_DEV_TIMEOUT after the shortened wait bound,
     and the context stays usable. No GPU fault, no hang: the wait simply runs out."""
@@ -58,6 +59,7 @@ def test_one_rank_exchange_matches_local_kernels(mods):
         with torch.cuda.graph(graph):
             y = step()
         for _ in range(7):
+            ex.barrier()                   # a call of its own in the same sequence
             graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(y, want)

@@ -525,7 +525,7 @@ extern "C" int uwc_quant_act_tp(const float* x, int m, int k, int bs, int8_t* q,
   if (rs != UWC_OK) return rs;
   const uint64_t ns = uwc_wait_ns();
   return launch_pdl(k_quant_act_tp<1024>, m, 1024, 4 * k, stream, x, k, bs, q, scale, args, uwc_status_ptr(),
-                    ns ? ns : (uint64_t)UWC_WAIT_TIMEOUT_NS);
+                    ns ? ns : uwc_tp::kWaitNs);
 }
 
 extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, int bs, double eps, int8_t* q,

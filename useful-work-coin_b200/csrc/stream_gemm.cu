@@ -439,7 +439,7 @@ int stream_call(const int8_t* X, const int8_t* W, int m, int n, int k, const flo
   p.early_w = early_w;
   p.status = uwc_status_ptr();
   const uint64_t ns = g_stream_wait_ns.load();
-  p.wait_ns = ns ? ns : UWC_WAIT_TIMEOUT_NS;
+  p.wait_ns = ns ? ns : (tp ? uwc_tp::kWaitNs : UWC_WAIT_TIMEOUT_NS);
   p.kblocks = (k + kSKB - 1) / kSKB;
   const int nrb = (n + kSRows - 1) / kSRows;
   p.ksplit = pick_split(nrb, p.kblocks);

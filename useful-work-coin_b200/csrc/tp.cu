@@ -1,6 +1,7 @@
 // Exchange buffers of the tensor-parallel decode kernels: allocation and CUDA IPC mapping.
 #include <cstring>
 
+#include "uwc_device.cuh"
 #include "uwc_host.h"
 #include "uwc_tp.cuh"
 
@@ -72,4 +73,33 @@ int uwc_tp_args(const UwcTP* tp, int m, int n, TPArgs* out) {
     if (r < tp->world && (!tp->base[r] || ((uintptr_t)tp->base[r] & 255))) return UWC_ERR_ARG;
   }
   return UWC_OK;
+}
+
+namespace {
+// Every rank stores a tagged word into every rank's buffer and polls its own until all ranks'
+// words of this call have landed: the ranks leave within about one NVLink write latency.
+__global__ void k_tp_barrier(TPArgs tp, uint32_t* status, uint64_t wait_ns) {
+  pdl_wait();
+  uint8_t* const mine = tp.base[tp.rank];
+  const uint64_t E = uwc_tp::call_epoch(mine);
+  const int par = (int)(E & 1), p = threadIdx.x;
+  if (p < tp.world) {
+    uwc_tp::st_sys(uwc_tp::amax_slot(tp.base[p], tp.L, par, tp.rank, 0), uwc_tp::tagged(E, 1u));
+    bool ok = true;
+    uwc_tp::wait_tagged(uwc_tp::amax_slot(mine, tp.L, par, p, 0), E, uwc_tp::now_ns() + wait_ns, status, &ok);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) uwc_tp::call_end(mine, E, gridDim.x);
+}
+}  // namespace
+
+extern "C" int uwc_tp_barrier(const UwcTP* tp, void* stream) {
+  TPArgs args;
+  const int rc = uwc_tp_args(tp, 1, 0, &args);
+  if (rc != UWC_OK) return rc;
+  UWC_CHECK_DEVICE();
+  const uint64_t ns = uwc_wait_ns();
+  k_tp_barrier<<<1, 32, 0, (cudaStream_t)stream>>>(args, uwc_status_ptr(), ns ? ns : uwc_tp::kWaitNs);
+  uwc_count_launch();
+  return uwc_launch_status();
 }

@@ -21,6 +21,9 @@
 namespace uwc_tp {
 
 constexpr uint64_t kHeader = 256;
+// Default bound of a cross-GPU wait: ranks may reach a call seconds apart (process start, lazy
+// module loading, rank-local setup between collectives), so it is longer than the in-GPU waits'.
+constexpr uint64_t kWaitNs = 10ull * 1000000000ull;
 constexpr int kMaxWorld = UWC_TP_MAX_WORLD;
 
 struct Layout {

@@ -44,6 +44,7 @@ SIGNATURES = {
     "uwc_ipc_handle": (_I32, [_P, _P]),
     "uwc_ipc_open": (_I32, [_P, _P]),
     "uwc_ipc_close": (_I32, [_P]),
+    "uwc_tp_barrier": (_I32, [_P, _P]),
     "uwc_quant_act_tp": (_I32, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
     "uwc_gemm_stream_tp": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P, _P]),
     "uwc_mined_block_layout": (_I32, [_I32, _I32, _I32, _P]),

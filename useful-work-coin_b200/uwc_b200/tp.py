@@ -76,6 +76,13 @@ class PeerExchange:
                 self.peers.append(ptr)
                 self.tp.base[r] = ptr.value
 
+    def barrier(self) -> None:
+        """Device-side barrier of the ranks on the current stream (uwc_tp_barrier): the streams
+        leave it within about one NVLink write latency of each other."""
+        from ._lib import check, lib
+        from .ops import _stream
+        check(lib().uwc_tp_barrier(ctypes.byref(self.tp), _stream()), "tp_barrier")
+
     def close(self) -> None:
         from ._lib import lib
         if self._own is None:
