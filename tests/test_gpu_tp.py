@@ -50,6 +50,14 @@ def _worker(rank, world, port, outdir, Dm, I, ms):
             for m in ms:
                 r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
                 res[f"x{m}"] = mlpx.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
+            # the GEMM's exchange in the other form (reduce-scatter + all-gather from 2 ranks on, or
+            # one-shot at any size), same bits
+            from uwc_b200 import _lib
+            _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 2 if world < 4 else 9)
+            m = ms[0]
+            r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
+            res[f"p{m}"] = mlpx.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
+            _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 4)
             m = ms[0]
             r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
             wnd = wn.to(dev)
@@ -100,5 +108,5 @@ def test_tp_mlp_nccl_matches_one_gpu(tmp_path):
         for r in range(world):
             got = np.load(os.path.join(tmp_path, f"rank{r}.npz"))
             assert int(got["status"][0]) == 0, r
-            for key in (f"y{m}", f"x{m}") + ((f"g{m}",) if m == ms[0] else ()):
+            for key in (f"y{m}", f"x{m}") + ((f"g{m}", f"p{m}") if m == ms[0] else ()):
                 assert np.array_equal(got[key].view(np.uint32), ref.view(np.uint32)), (key, r)

@@ -22,8 +22,11 @@ def mods(dev):
     return _lib, detgpu, ops, tp
 
 
-def test_one_rank_exchange_matches_local_kernels(mods):
+@pytest.mark.parametrize("two_phase_min", [4, 1])
+def test_one_rank_exchange_matches_local_kernels(mods, two_phase_min):
+    """two_phase_min 1: the GEMM's exchange in its reduce-scatter + all-gather form."""
     _lib, detgpu, ops, tp = mods
+    assert _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, two_phase_min) == 0
     ex = tp.PeerExchange(64, 4096, 0, 1, torch.device("cuda", 0))
     try:
         g = torch.Generator(device="cuda").manual_seed(4)
@@ -67,6 +70,7 @@ def test_one_rank_exchange_matches_local_kernels(mods):
         assert _lib.device_status(clear=True) == 0
     finally:
         ex.close()
+        _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 4)
 
 
 def test_exchange_wait_runs_out_and_reports(mods):

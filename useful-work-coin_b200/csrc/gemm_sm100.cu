@@ -1082,6 +1082,10 @@ extern "C" int uwc_test_hook(int hook, long long value) {
     uwc_stream_set_wait_ns((uint64_t)value);
     return UWC_OK;
   }
+  if (hook == UWC_HOOK_TP_TWO_PHASE && value >= 1 && value <= 9) {
+    uwc_tp_set_two_phase_min((int)value);
+    return UWC_OK;
+  }
   if (hook == UWC_HOOK_STREAM_PDL && (value == 0 || value == 1)) {
     uwc_stream_set_pdl((int)value);
     uwc_row_set_pdl((int)value);

@@ -276,26 +276,50 @@ __global__ void __launch_bounds__(kSThreads, 2)
       return acc;
     };
     if (p.tp_on) {
-      // the ranks' partial products of this slice, each tagged with the call's epoch: sent to every
-      // rank, polled and summed in rank order there
+      // The ranks' partial products of this slice, as 8-byte words tagged with the call's epoch.
+      // One-shot: every rank sends its partials to every rank, each sums them in rank order.
+      // Two-phase (many ranks): the slot's owner rank receives the partials, sums them in rank
+      // order and sends the total to every rank: 2 (N - 1) / N of the product per rank instead of
+      // N - 1.
       uint8_t* const mine = p.tp.base[p.tp.rank];
       const uint64_t E = uwc_tp::call_epoch(mine);
-      const int par = (int)(E & 1);
+      const int par = (int)(E & 1), world = p.tp.world;
+      const int owner = (rb * p.ksplit + ks) % world;
+      const bool two = p.tp.two_phase != 0;
       const uint32_t ldn = p.tp.L.max_n;
       for (int idx = threadIdx.x; idx < total; idx += kSThreads) {
         const int t = idx / nr, jj = r0 + (idx - t * nr), j = rb * kSRows + jj;
         int32_t up;
         const int32_t acc = live ? cluster_sum(t, jj, up) : 0;
-        if (j < p.n)
-          for (int d = 0; d < p.tp.world; d++)
-            uwc_tp::st_sys(uwc_tp::data_of(p.tp.base[d], p.tp.L, par, p.tp.rank) + (uint64_t)t * ldn + j,
-                           uwc_tp::tagged(E, (uint32_t)acc));
+        if (j >= p.n) continue;
+        const uint64_t w = uwc_tp::tagged(E, (uint32_t)acc), off = (uint64_t)t * ldn + j;
+        if (two) {
+          uwc_tp::st_sys(uwc_tp::data_of(p.tp.base[owner], p.tp.L, par, p.tp.rank) + off, w);
+        } else {
+          for (int d = 0; d < world; d++) uwc_tp::st_sys(uwc_tp::data_of(p.tp.base[d], p.tp.L, par, p.tp.rank) + off, w);
+        }
       }
       // receive: kPoll items per thread at a time, each source's words loaded together (independent
       // loads in flight), then only stale words polled again
       constexpr int kPoll = 4;
       bool ok = true;
       const uint64_t deadline = uwc_tp::now_ns() + p.wait_ns;
+      auto sum_sources = [&](const uint64_t* off, const bool* use, int32_t* acc) {
+        for (int src = 0; src < world; src++) {
+          const uint64_t* d = uwc_tp::data_of(mine, p.tp.L, par, src);
+          uint64_t w[kPoll];
+#pragma unroll
+          for (int c = 0; c < kPoll; c++) w[c] = use[c] ? uwc_tp::ld_sys(d + off[c]) : 0;
+#pragma unroll
+          for (int c = 0; c < kPoll; c++) {
+            if (!use[c]) continue;
+            const uint32_t v = (uint32_t)(w[c] >> 32) == (uint32_t)E
+                                   ? (uint32_t)w[c]
+                                   : uwc_tp::wait_tagged(d + off[c], E, deadline, p.status, &ok);
+            acc[c] += (int32_t)v;
+          }
+        }
+      };
       for (int i0 = threadIdx.x; i0 < total; i0 += kSThreads * kPoll) {
         uint64_t off[kPoll];
         bool use[kPoll];
@@ -308,18 +332,28 @@ __global__ void __launch_bounds__(kSThreads, 2)
           off[c] = use[c] ? (uint64_t)t * ldn + j : 0;
           acc[c] = 0;
         }
-        for (int src = 0; src < p.tp.world; src++) {
-          const uint64_t* d = uwc_tp::data_of(mine, p.tp.L, par, src);
-          uint64_t w[kPoll];
+        if (!two) {
+          sum_sources(off, use, acc);
+        } else {
+          if (owner == p.tp.rank) {
+            sum_sources(off, use, acc);
 #pragma unroll
-          for (int c = 0; c < kPoll; c++) w[c] = use[c] ? uwc_tp::ld_sys(d + off[c]) : 0;
+            for (int c = 0; c < kPoll; c++)
+              if (use[c])
+                for (int d = 0; d < world; d++)
+                  if (d != p.tp.rank)
+                    uwc_tp::st_sys(uwc_tp::sum_of(p.tp.base[d], p.tp.L, par) + off[c], uwc_tp::tagged(E, (uint32_t)acc[c]));
+          } else {
+            const uint64_t* d = uwc_tp::sum_of(mine, p.tp.L, par);
+            uint64_t w[kPoll];
 #pragma unroll
-          for (int c = 0; c < kPoll; c++) {
-            if (!use[c]) continue;
-            const uint32_t v = (uint32_t)(w[c] >> 32) == (uint32_t)E
-                                   ? (uint32_t)w[c]
-                                   : uwc_tp::wait_tagged(d + off[c], E, deadline, p.status, &ok);
-            acc[c] += (int32_t)v;
+            for (int c = 0; c < kPoll; c++) w[c] = use[c] ? uwc_tp::ld_sys(d + off[c]) : 0;
+#pragma unroll
+            for (int c = 0; c < kPoll; c++)
+              if (use[c])
+                acc[c] = (int32_t)((uint32_t)(w[c] >> 32) == (uint32_t)E
+                                       ? (uint32_t)w[c]
+                                       : uwc_tp::wait_tagged(d + off[c], E, deadline, p.status, &ok));
           }
         }
 #pragma unroll

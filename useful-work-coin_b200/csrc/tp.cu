@@ -1,4 +1,5 @@
 // Exchange buffers of the tensor-parallel decode kernels: allocation and CUDA IPC mapping.
+#include <atomic>
 #include <cstring>
 
 #include "uwc_device.cuh"
@@ -61,12 +62,19 @@ extern "C" int uwc_ipc_close(void* peer_buf) {
   return cudaIpcCloseMemHandle(peer_buf) == cudaSuccess ? UWC_OK : (cudaGetLastError(), UWC_ERR_CUDA);
 }
 
+namespace {
+std::atomic<int> g_two_phase_min{4};
+}
+void uwc_tp_set_two_phase_min(int world) { g_two_phase_min.store(world); }
+int uwc_tp_two_phase_min() { return g_two_phase_min.load(); }
+
 // The kernel form of a UwcTP, checked against the call's shape.
 int uwc_tp_args(const UwcTP* tp, int m, int n, TPArgs* out) {
   if (!tp || tp->world < 1 || tp->world > UWC_TP_MAX_WORLD || tp->rank < 0 || tp->rank >= tp->world) return UWC_ERR_ARG;
   if (m > tp->max_m || n > tp->max_n) return UWC_ERR_SHAPE;
   out->rank = tp->rank;
   out->world = tp->world;
+  out->two_phase = tp->world >= uwc_tp_two_phase_min() ? 1 : 0;
   out->L = uwc_tp::layout((uint32_t)tp->max_m, (uint32_t)tp->max_n);
   for (int r = 0; r < uwc_tp::kMaxWorld; r++) {
     out->base[r] = r < tp->world ? static_cast<uint8_t*>(tp->base[r]) : nullptr;

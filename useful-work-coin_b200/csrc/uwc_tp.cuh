@@ -6,6 +6,8 @@
 //   header   epoch (u64) = calls completed on this buffer, done counter (u32) of the running call
 //   amax     [2 parities][8 sources][max_m] u64: (epoch << 32) | float bits of a source's row absmax
 //   data     [2][8][max_m][max_n] u64: (epoch << 32) | a source's int32 partial product
+//   sum      [2][max_m][max_n] u64: (epoch << 32) | the summed product, from its owner rank
+//             (the reduce-scatter + all-gather form of the GEMM's exchange)
 //
 // Every value carries the epoch of the call that wrote it in the same 8-byte store, so a reader
 // polls the value itself: no flags, no fences, one NVLink write latency per exchange.
@@ -27,7 +29,7 @@ constexpr uint64_t kWaitNs = 10ull * 1000000000ull;
 constexpr int kMaxWorld = UWC_TP_MAX_WORLD;
 
 struct Layout {
-  uint64_t amax, data, total;
+  uint64_t amax, data, sum, total;
   uint32_t max_m, max_n;
 };
 
@@ -38,7 +40,8 @@ __host__ __device__ inline Layout layout(uint32_t max_m, uint32_t max_n) {
   L.amax = kHeader;
   L.data = L.amax + 2ull * kMaxWorld * max_m * 8;
   L.data = (L.data + 255) & ~255ull;
-  L.total = L.data + 2ull * kMaxWorld * max_m * max_n * 8;
+  L.sum = L.data + 2ull * kMaxWorld * max_m * max_n * 8;
+  L.total = L.sum + 2ull * max_m * max_n * 8;
   return L;
 }
 
@@ -83,6 +86,10 @@ __device__ __forceinline__ uint64_t* data_of(uint8_t* base, const Layout& L, int
   return reinterpret_cast<uint64_t*>(base + L.data) + ((uint64_t)parity * kMaxWorld + src) * L.max_m * L.max_n;
 }
 
+__device__ __forceinline__ uint64_t* sum_of(uint8_t* base, const Layout& L, int parity) {
+  return reinterpret_cast<uint64_t*>(base + L.sum) + (uint64_t)parity * L.max_m * L.max_n;
+}
+
 __device__ __forceinline__ uint64_t now_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -113,6 +120,7 @@ __device__ __forceinline__ uint32_t wait_tagged(const uint64_t* p, uint64_t E, u
 // Kernel argument form of UwcTP.
 struct TPArgs {
   int rank, world;
+  int two_phase;   // the GEMM's exchange as reduce-scatter + all-gather (else one-shot)
   uwc_tp::Layout L;
   uint8_t* base[uwc_tp::kMaxWorld];
 };

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libuwcb200.so")
 
 OK, ERR_ARG, ERR_SHAPE, ERR_ALIGN, ERR_CUDA, ERR_DEVICE, ERR_SCRATCH = range(7)
 DEV_TIMEOUT = 1
-HOOK_WAIT_NS, HOOK_WITHHOLD, HOOK_STREAM_PDL = 1, 2, 3
+HOOK_WAIT_NS, HOOK_WITHHOLD, HOOK_STREAM_PDL, HOOK_TP_TWO_PHASE = 1, 2, 3, 4
 
 # (name, restype, argtypes) for every function declared in include/uwc_b200.h
 _P, _U32, _U64, _I32, _F64 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_double
