@@ -52,7 +52,7 @@ extern "C" {
  * UWC_HOOK_STREAM_PDL = 0 launches the weight-streaming GEMM and the few-row quantizers without
  * programmatic dependent launch (1, the default, lets them start while the previous kernel of the
  * stream finishes); UWC_HOOK_TP_TWO_PHASE = w (1..9) runs uwc_gemm_stream_tp's exchange as
- * reduce-scatter + all-gather from w ranks on (default 4; 9: never).
+ * reduce-scatter + all-gather from w ranks on (default 8; 9: never).
  * Process-wide; for tests only. Returns UWC_OK or UWC_ERR_ARG. */
 #define UWC_HOOK_WAIT_NS 1
 #define UWC_HOOK_WITHHOLD 2
@@ -206,8 +206,8 @@ int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const
  *                       m <= max_m.
  *   uwc_gemm_stream_tp  uwc_gemm_stream whose int32 product is summed over the ranks before the
  *                       epilogue (the row-parallel GEMM + SUM all-reduce + dequant/residual, in
- *                       one kernel): with fewer than 4 ranks each rank's partial slices go to every
- *                       peer and each rank adds them in rank order; from 4 ranks on each slice's
+ *                       one kernel): with fewer than 8 ranks each rank's partial slices go to every
+ *                       peer and each rank adds them in rank order; from 8 ranks on each slice's
  *                       owner rank adds them and sends the sum to every rank. m <= max_m, n <= max_n,
  *                       epi UWC_SEPI_I32 / F32 / BF16 / RESID (| UWC_SEPI_EARLY_W). */
 #define UWC_TP_MAX_WORLD 8

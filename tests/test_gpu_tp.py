@@ -50,14 +50,14 @@ def _worker(rank, world, port, outdir, Dm, I, ms):
             for m in ms:
                 r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
                 res[f"x{m}"] = mlpx.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
-            # the GEMM's exchange in the other form (reduce-scatter + all-gather from 2 ranks on, or
-            # one-shot at any size), same bits
+            # the GEMM's exchange in its other form (reduce-scatter + all-gather below 8 ranks,
+            # one-shot at 8), same bits
             from uwc_b200 import _lib
-            _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 2 if world < 4 else 9)
+            _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, world if world < 8 else 9)
             m = ms[0]
             r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
             res[f"p{m}"] = mlpx.forward(r1, wn.to(dev), 1e-5).cpu().numpy()
-            _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 4)
+            _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 8)
             m = ms[0]
             r1 = (torch.randn(m, Dm, generator=torch.Generator().manual_seed(m)) * 2).to(dev)
             wnd = wn.to(dev)

@@ -22,7 +22,7 @@ def mods(dev):
     return _lib, detgpu, ops, tp
 
 
-@pytest.mark.parametrize("two_phase_min", [4, 1])
+@pytest.mark.parametrize("two_phase_min", [8, 1])
 def test_one_rank_exchange_matches_local_kernels(mods, two_phase_min):
     """two_phase_min 1: the GEMM's exchange in its reduce-scatter + all-gather form."""
     _lib, detgpu, ops, tp = mods
@@ -70,7 +70,7 @@ def test_one_rank_exchange_matches_local_kernels(mods, two_phase_min):
         assert _lib.device_status(clear=True) == 0
     finally:
         ex.close()
-        _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 4)
+        _lib.lib().uwc_test_hook(_lib.HOOK_TP_TWO_PHASE, 8)
 
 
 def test_exchange_wait_runs_out_and_reports(mods):

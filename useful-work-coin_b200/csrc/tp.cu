@@ -63,7 +63,7 @@ extern "C" int uwc_ipc_close(void* peer_buf) {
 }
 
 namespace {
-std::atomic<int> g_two_phase_min{4};
+std::atomic<int> g_two_phase_min{8};
 }
 void uwc_tp_set_two_phase_min(int world) { g_two_phase_min.store(world); }
 int uwc_tp_two_phase_min() { return g_two_phase_min.load(); }

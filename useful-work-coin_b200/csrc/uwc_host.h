@@ -54,6 +54,6 @@ int uwc_tp_args(const UwcTP* tp, int m, int n, TPArgs* out);
 // The bound of device-side waits set by UWC_HOOK_WAIT_NS (0: the default).
 uint64_t uwc_wait_ns();
 
-// The smallest world size whose GEMM exchange runs as reduce-scatter + all-gather (tp.cu; default 4).
+// The smallest world size whose GEMM exchange runs as reduce-scatter + all-gather (tp.cu; default 8).
 void uwc_tp_set_two_phase_min(int world);
 int uwc_tp_two_phase_min();
