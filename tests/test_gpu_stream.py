@@ -155,8 +155,9 @@ def test_stream_rejects_bad_calls(lib):
 @pytest.mark.parametrize("k,bs", [(4096, 512), (14336, 512), (6144, 512), (1024, 128), (2048, 32), (4096, 1024),
                                   (2048, 1), (512, 512)])
 def test_few_row_quantizers_match_one_cta_rows(lib, k, bs):
-    """Decode-sized calls (fewer rows than SMs) quantize each row with a cluster of CTAs; calls with
-    at least one row per SM use one CTA per row. Both give the same bits for the same row."""
+    """Decode-sized calls (fewer rows than SMs) quantize each row in one CTA of 1024 threads, with
+    512-element blocks held in registers warp by warp; calls with at least one row per SM stage each
+    row in shared memory (256 threads). Both give the same bits for the same row."""
     ops, detgpu, _ = lib
     g = torch.Generator(device="cuda").manual_seed(k + bs)
     big = 160

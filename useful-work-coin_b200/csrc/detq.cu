@@ -274,6 +274,115 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ 
   quant_row64<NT>(row, k, bs, am, q + (uint64_t)r * k, scale + r);
 }
 
+// Few rows with 512-element Hadamard blocks (decode): warp w holds block w of the row in registers,
+// 16 consecutive elements per lane, from the global load to the int8 store; only the block maxima
+// and fixed-point sums pass through shared memory. The transform is fwht_block_lane's stages on the
+// registers, and every other operation is the staged kernels' in the same order: the same bits.
+// RMS = false is quant_act (k_quant_act MODE 0), RMS = true rmsnorm_quant. blockDim = 32 (k / 512).
+__device__ __forceinline__ float cta_maxf(float v, float* red) {
+  v = warp_maxf(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, red[i]);
+  return m;
+}
+__device__ __forceinline__ long long cta_sumll(long long v, long long* red) {
+  v = warp_sumll(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  long long t = 0;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += red[i];
+  return t;
+}
+
+template <bool RMS>
+__global__ void __launch_bounds__(1024) k_row_quant512(const float* __restrict__ x, const float* __restrict__ w, int k,
+                                                       float inv_d, float eps, int L, int8_t* __restrict__ q,
+                                                       float* __restrict__ scale) {
+  __shared__ float redf[32];
+  __shared__ long long redl[32];
+  pdl_wait();      // launched early behind the previous kernel: its writes are visible from here
+  pdl_trigger();   // a weight-streaming GEMM behind this kernel may start fetching its weights
+  const int r = blockIdx.x, lane = threadIdx.x & 31;
+  const size_t off = (size_t)(threadIdx.x >> 5) * 512 + lane * 16;
+  float v[16];
+  {
+    const float4* src = reinterpret_cast<const float4*>(x + (size_t)r * k + off);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float4 a = src[i];
+      v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+    }
+  }
+  if (RMS) {
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) mx = fmaxf(mx, __fmul_rn(v[i], v[i]));
+    mx = cta_maxf(mx, redf);
+    int e;
+    frexpf(mx, &e);
+    const int sh = min(max((62 - L) - e, -1000), 1000);
+    const double up = pow2d(sh);
+    long long acc = 0;
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc += __double2ll_rn((double)__fmul_rn(v[i], v[i]) * up);
+    acc = cta_sumll(acc, redl);
+    const float ss = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
+    const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, inv_d), eps)));
+    const float4* wp = reinterpret_cast<const float4*>(w + off);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float4 wv = __ldg(wp + i);
+      v[4 * i] = __fmul_rn(__fmul_rn(v[4 * i], rr), wv.x);
+      v[4 * i + 1] = __fmul_rn(__fmul_rn(v[4 * i + 1], rr), wv.y);
+      v[4 * i + 2] = __fmul_rn(__fmul_rn(v[4 * i + 2], rr), wv.z);
+      v[4 * i + 3] = __fmul_rn(__fmul_rn(v[4 * i + 3], rr), wv.w);
+    }
+  }
+  // fwht_block_lane<16> on registers: stages inside the lane, then across lanes
+#pragma unroll
+  for (int h = 1; h < 16; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      if (i & h) continue;
+      const float a = v[i], b = v[i + h];
+      v[i] = __fadd_rn(a, b);
+      v[i + h] = __fsub_rn(a, b);
+    }
+  }
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const bool upper = lane & d;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+      v[i] = upper ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
+    }
+  }
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; i++) am = fmaxf(am, fabsf(v[i]));
+  am = cta_maxf(am, redf);
+  // quant_row64: q = clamp(rint(v / s), -64, 64), s = max(amax, tiny) / 64
+  const float s = __fdiv_rn(fmaxf(am, kTiny), 64.0f);
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float t = fminf(fmaxf(rint_small(__fdiv_rn(v[4 * i + j], s)), -64.f), 64.f);
+      word |= ((uint32_t)(uint8_t)(int8_t)int_of_small(t)) << (8 * j);
+    }
+    o[i] = word;
+  }
+  *reinterpret_cast<uint4*>(q + (size_t)r * k + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (threadIdx.x == 0) scale[r] = __fmul_rn(s, __fdiv_rn(1.0f, __fsqrt_rn(512.0f)));
+}
+
 // fmul(det_silu(gate), up) of the dequantized gate/up GEMM output (N x 2I int32)
 __device__ __forceinline__ float swiglu_at(const int32_t* ar, float s, const float* sw, int I, int i) {
   return det_swiglu(deq(ar[i], s, sw[i]), deq(ar[I + i], s, sw[I + i]));
@@ -441,6 +550,9 @@ int row_smem_ok(int k, const void* kernel) {
 // Fewer rows than SMs (decode): 1024 threads per row shorten each row's latency.
 bool few_rows(int m) { return m < uwc_num_sms(); }
 
+// The register-resident few-row kernels: 512-element Hadamard blocks, one warp each, at most 32.
+bool reg_row(int k, int bs) { return bs == 512 && k % 512 == 0 && k <= 32 * 512; }
+
 bool bs_ok(int k, int bs) { return bs <= 1 || ((bs & (bs - 1)) == 0 && k % bs == 0); }
 
 std::atomic<int> g_row_pdl{1};
@@ -476,6 +588,9 @@ int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, fl
   if (!aligned16(x) || (q && ((uintptr_t)q & 3))) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
+  if (MODE == 0 && !BF16 && few_rows(m) && reg_row(k, bs) && aligned16(q))
+    return launch_pdl(k_row_quant512<false>, m, 32 * (k / 512), 0, stream, static_cast<const float*>(x),
+                      static_cast<const float*>(nullptr), k, 0.f, 0.f, 0, q, scale);
   if (few_rows(m)) {
     const int rc = row_smem_ok(k, (const void*)k_quant_act<1024, MODE, BF16>);
     if (rc != UWC_OK) return rc;
@@ -536,6 +651,9 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
   if (m == 0) return UWC_OK;
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
   const float inv_d = (float)(1.0 / k), eps32 = (float)eps;
+  if (few_rows(m) && reg_row(k, bs) && aligned16(q))
+    return launch_pdl(k_row_quant512<true>, m, 32 * (k / 512), 0, stream, x, w, k, inv_d, eps32, ceil_log2(k), q,
+                      scale);
   if (few_rows(m)) {
     const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<1024>);
     if (rc != UWC_OK) return rc;
