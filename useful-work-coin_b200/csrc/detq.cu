@@ -279,6 +279,8 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ 
 // and fixed-point sums pass through shared memory. The transform is fwht_block_lane's stages on the
 // registers, and every other operation is the staged kernels' in the same order: the same bits.
 // RMS = false is quant_act (k_quant_act MODE 0), RMS = true rmsnorm_quant. blockDim = 32 (k / 512).
+// TP: the row-parallel form (k_quant_act_tp): the shard's absmax is exchanged with every rank and
+// the row is quantized with the maximum.
 __device__ __forceinline__ float cta_maxf(float v, float* red) {
   v = warp_maxf(v);
   __syncthreads();
@@ -298,12 +300,14 @@ __device__ __forceinline__ long long cta_sumll(long long v, long long* red) {
   return t;
 }
 
-template <bool RMS>
+template <bool RMS, bool TP>
 __global__ void __launch_bounds__(1024) k_row_quant512(const float* __restrict__ x, const float* __restrict__ w, int k,
                                                        float inv_d, float eps, int L, int8_t* __restrict__ q,
-                                                       float* __restrict__ scale) {
+                                                       float* __restrict__ scale, TPArgs tp, uint32_t* status,
+                                                       uint64_t wait_ns) {
   __shared__ float redf[32];
   __shared__ long long redl[32];
+  __shared__ float src_max[uwc_tp::kMaxWorld];
   pdl_wait();      // launched early behind the previous kernel: its writes are visible from here
   pdl_trigger();   // a weight-streaming GEMM behind this kernel may start fetching its weights
   const int r = blockIdx.x, lane = threadIdx.x & 31;
@@ -366,6 +370,21 @@ __global__ void __launch_bounds__(1024) k_row_quant512(const float* __restrict__
 #pragma unroll
   for (int i = 0; i < 16; i++) am = fmaxf(am, fabsf(v[i]));
   am = cta_maxf(am, redf);
+  uint64_t E = 0;
+  if (TP) {
+    uint8_t* const mine = tp.base[tp.rank];
+    E = uwc_tp::call_epoch(mine);
+    const int par = (int)(E & 1), p = threadIdx.x;
+    if (p < tp.world) {
+      uwc_tp::st_sys(uwc_tp::amax_slot(tp.base[p], tp.L, par, tp.rank, r), uwc_tp::tagged(E, __float_as_uint(am)));
+      bool ok = true;
+      const uint32_t got = uwc_tp::wait_tagged(uwc_tp::amax_slot(mine, tp.L, par, p, r), E,
+                                               uwc_tp::now_ns() + wait_ns, status, &ok);
+      src_max[p] = ok ? __uint_as_float(got) : am;
+    }
+    __syncthreads();
+    for (int i = 0; i < tp.world; i++) am = fmaxf(am, src_max[i]);
+  }
   // quant_row64: q = clamp(rint(v / s), -64, 64), s = max(amax, tiny) / 64
   const float s = __fdiv_rn(fmaxf(am, kTiny), 64.0f);
   uint32_t o[4];
@@ -381,6 +400,10 @@ __global__ void __launch_bounds__(1024) k_row_quant512(const float* __restrict__
   }
   *reinterpret_cast<uint4*>(q + (size_t)r * k + off) = make_uint4(o[0], o[1], o[2], o[3]);
   if (threadIdx.x == 0) scale[r] = __fmul_rn(s, __fdiv_rn(1.0f, __fsqrt_rn(512.0f)));
+  if (TP) {
+    __syncthreads();
+    if (threadIdx.x == 0) uwc_tp::call_end(tp.base[tp.rank], E, gridDim.x);
+  }
 }
 
 // fmul(det_silu(gate), up) of the dequantized gate/up GEMM output (N x 2I int32)
@@ -589,8 +612,9 @@ int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, fl
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
   if (MODE == 0 && !BF16 && few_rows(m) && reg_row(k, bs) && aligned16(q))
-    return launch_pdl(k_row_quant512<false>, m, 32 * (k / 512), 0, stream, static_cast<const float*>(x),
-                      static_cast<const float*>(nullptr), k, 0.f, 0.f, 0, q, scale);
+    return launch_pdl(k_row_quant512<false, false>, m, 32 * (k / 512), 0, stream, static_cast<const float*>(x),
+                      static_cast<const float*>(nullptr), k, 0.f, 0.f, 0, q, scale, TPArgs{},
+                      static_cast<uint32_t*>(nullptr), (uint64_t)0);
   if (few_rows(m)) {
     const int rc = row_smem_ok(k, (const void*)k_quant_act<1024, MODE, BF16>);
     if (rc != UWC_OK) return rc;
@@ -636,6 +660,10 @@ extern "C" int uwc_quant_act_tp(const float* x, int m, int k, int bs, int8_t* q,
   if (m == 0) return UWC_OK;
   // one CTA per row, all resident (the rows wait for the peers' rows)
   if (m > uwc_num_sms()) return UWC_ERR_SHAPE;
+  const uint64_t wns = uwc_wait_ns() ? uwc_wait_ns() : uwc_tp::kWaitNs;
+  if (reg_row(k, bs) && aligned16(q))
+    return launch_pdl(k_row_quant512<false, true>, m, 32 * (k / 512), 0, stream, x, static_cast<const float*>(nullptr),
+                      k, 0.f, 0.f, 0, q, scale, args, uwc_status_ptr(), wns);
   const int rs = row_smem_ok(k, (const void*)k_quant_act_tp<1024>);
   if (rs != UWC_OK) return rs;
   const uint64_t ns = uwc_wait_ns();
@@ -652,8 +680,8 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
   const float inv_d = (float)(1.0 / k), eps32 = (float)eps;
   if (few_rows(m) && reg_row(k, bs) && aligned16(q))
-    return launch_pdl(k_row_quant512<true>, m, 32 * (k / 512), 0, stream, x, w, k, inv_d, eps32, ceil_log2(k), q,
-                      scale);
+    return launch_pdl(k_row_quant512<true, false>, m, 32 * (k / 512), 0, stream, x, w, k, inv_d, eps32, ceil_log2(k),
+                      q, scale, TPArgs{}, static_cast<uint32_t*>(nullptr), (uint64_t)0);
   if (few_rows(m)) {
     const int rc = row_smem_ok(k, (const void*)k_rmsnorm_quant<1024>);
     if (rc != UWC_OK) return rc;
