@@ -189,6 +189,14 @@ int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int f
 #define UWC_SEPI_EARLY_W 0x100
 int uwc_gemm_stream(const int8_t* X, const int8_t* W, int m, int n, int k, const float* x_scale,
                     const float* w_scale, const float* resid, void* out, int epi, void* stream);
+/* The same epilogues at any m (replaces the int32 product + dequant_residual / swiglu passes of
+ * runtime/detgpu/stages.py:117-153 with one kernel): m <= 64 runs uwc_gemm_stream, larger m the
+ * tcgen05 GEMM with the output step in its epilogue (SWIGLU: each 256-row B tile is 128 gate rows
+ * over their 128 up rows; n % 8 == 0). workspace: uwc_gemm_epi_workspace_bytes(m, n, epi) bytes
+ * (a skinny split-K call's int32 sum; 0 otherwise), 16-byte aligned. */
+uint64_t uwc_gemm_epi_workspace_bytes(int m, int n, int epi);
+int uwc_gemm_epi(const int8_t* A, const int8_t* W, int m, int n, int k, const float* a_scale, const float* w_scale,
+                 const float* resid, void* out, int epi, void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* ---- tensor-parallel decode over NVLink peer memory ---------------------------------------
  * New (the reference splits models only into pipeline stages, runtime/detrt/qwen3.py:151-158).

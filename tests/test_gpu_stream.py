@@ -155,9 +155,10 @@ def test_stream_rejects_bad_calls(lib):
 @pytest.mark.parametrize("k,bs", [(4096, 512), (14336, 512), (6144, 512), (1024, 128), (2048, 32), (4096, 1024),
                                   (2048, 1), (512, 512)])
 def test_few_row_quantizers_match_one_cta_rows(lib, k, bs):
-    """Decode-sized calls (fewer rows than SMs) quantize each row in one CTA of 1024 threads, with
-    512-element blocks held in registers warp by warp; calls with at least one row per SM stage each
-    row in shared memory (256 threads). Both give the same bits for the same row."""
+    """A row's quantization does not depend on how many rows the call has: with 512-element blocks
+    every call keeps each row in registers (one warp per block); with other block sizes decode-sized
+    calls (fewer rows than SMs) stage each row in shared memory with 1024 threads and larger calls
+    with 256. Both give the same bits for the same row (the oracle tests pin each path)."""
     ops, detgpu, _ = lib
     g = torch.Generator(device="cuda").manual_seed(k + bs)
     big = 160
@@ -170,3 +171,24 @@ def test_few_row_quantizers_match_one_cta_rows(lib, k, bs):
         assert torch.equal(q1, qa[:m]) and torch.equal(s1, sa[:m])
         q2, s2 = detgpu.rmsnorm_quant(x[:m].contiguous(), w, 1e-6, bs)
         assert torch.equal(q2, qr[:m]) and torch.equal(s2, sr[:m])
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 2048, 1024), (128, 512, 4096), (1000, 400, 2048), (2048, 4096, 1024),
+                                   (48, 1024, 2048)])
+def test_gemm_epi_any_m(lib, m, n, k):
+    """uwc_gemm_epi: the same epilogues at prefill-sized m, in the tcgen05 GEMM's epilogue (SwiGLU
+    from 128 gate rows over their up rows per tile; the residual add in the fp32 store, also after
+    a skinny shape's split-K sum), == the separate output kernels on the exact product."""
+    ops, detgpu, _ = lib
+    X, W, sx, sw = _operands(m, n, k, 31 + m)
+    Xd, Wd = torch.from_numpy(X).cuda(), torch.from_numpy(W).cuda()
+    sxd, swd = torch.from_numpy(sx).cuda(), torch.from_numpy(sw).cuda()
+    acc = torch.from_numpy(O.gemm_i32_blas(X, W)).cuda()
+    x = torch.randn(m, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(m))
+    assert torch.equal(ops.gemm_epi(Xd, Wd, ops.SEPI_I32), acc)
+    assert torch.equal(ops.gemm_epi(Xd, Wd, ops.SEPI_F32, x_scale=sxd, w_scale=swd), detgpu.dequant(acc, sxd, swd))
+    assert torch.equal(ops.gemm_epi(Xd, Wd, ops.SEPI_RESID, x_scale=sxd, w_scale=swd, resid=x),
+                       detgpu.dequant_residual(acc, sxd, swd, x))
+    h = ops.gemm_epi(Xd, Wd, ops.SEPI_SWIGLU, x_scale=sxd, w_scale=swd)
+    assert h.shape == (m, n // 2)
+    assert torch.equal(h, detgpu.swiglu(acc, sxd, swd))

@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* __restrict__ 
   quant_row64<NT>(row, k, bs, am, q + (uint64_t)r * k, scale + r);
 }
 
-// Few rows with 512-element Hadamard blocks (decode): warp w holds block w of the row in registers,
+// Rows with 512-element Hadamard blocks (any number of rows): warp w holds block w of the row in registers,
 // 16 consecutive elements per lane, from the global load to the int8 store; only the block maxima
 // and fixed-point sums pass through shared memory. The transform is fwht_block_lane's stages on the
 // registers, and every other operation is the staged kernels' in the same order: the same bits.
@@ -611,7 +611,7 @@ int launch_quant(const void* x, int m, int k, int bs, float* amax, int8_t* q, fl
   if (!aligned16(x) || (q && ((uintptr_t)q & 3))) return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
-  if (MODE == 0 && !BF16 && few_rows(m) && reg_row(k, bs) && aligned16(q))
+  if (MODE == 0 && !BF16 && reg_row(k, bs) && aligned16(q))
     return launch_pdl(k_row_quant512<false, false>, m, 32 * (k / 512), 0, stream, static_cast<const float*>(x),
                       static_cast<const float*>(nullptr), k, 0.f, 0.f, 0, q, scale, TPArgs{},
                       static_cast<uint32_t*>(nullptr), (uint64_t)0);
@@ -679,7 +679,7 @@ extern "C" int uwc_rmsnorm_quant(const float* x, const float* w, int m, int k, i
   if (m == 0) return UWC_OK;
   // detrt rounds 1/d and eps from float64 to float32 (core.c32)
   const float inv_d = (float)(1.0 / k), eps32 = (float)eps;
-  if (few_rows(m) && reg_row(k, bs) && aligned16(q))
+  if (reg_row(k, bs) && aligned16(q))
     return launch_pdl(k_row_quant512<true, false>, m, 32 * (k / 512), 0, stream, x, w, k, inv_d, eps32, ceil_log2(k),
                       q, scale, TPArgs{}, static_cast<uint32_t*>(nullptr), (uint64_t)0);
   if (few_rows(m)) {

@@ -55,6 +55,7 @@
 #include <algorithm>
 #include <atomic>
 
+#include "det_math.cuh"
 #include "uwc_device.cuh"
 #include "uwc_host.h"
 
@@ -107,6 +108,11 @@ struct Params {
   // each): the k range stops after the last key row (m0 % qrows) + 127 sees.
   int nbatch, b_bdiv, causal, cshift, qrows, units_per_batch;
   long long a_brows, b_brows;
+  // PLAIN fused output steps (uwc_gemm_epi): F32 out + resid (m x n fp32) when resid is set; with
+  // swiglu, B is [gate; up] (2n rows), a unit's 256 B rows are 128 gate rows over the matching up
+  // rows, and out (m x n fp32) = det_silu(deq(gate)) * deq(up) (b_scale in B's row order)
+  const float* resid;
+  int swiglu;
 };
 
 // R: hash chunk width in k (64, 128, 256), or 0 for no hashing.
@@ -284,7 +290,12 @@ __device__ __forceinline__ void store4(const Params& p, int row, int c, int32_t 
   const float f2 = __fmul_rn(__fmul_rn(__int2float_rn(v2), sx), __ldg(p.b_scale + c + 2));
   const float f3 = __fmul_rn(__fmul_rn(__int2float_rn(v3), sx), __ldg(p.b_scale + c + 3));
   if (p.out_mode == UWC_OUT_F32) {
-    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + (uint64_t)row * p.n + c) = make_float4(f0, f1, f2, f3);
+    float4 o = make_float4(f0, f1, f2, f3);
+    if (p.resid) {
+      const float4 x = *reinterpret_cast<const float4*>(p.resid + (uint64_t)row * p.n + c);
+      o = make_float4(__fadd_rn(x.x, f0), __fadd_rn(x.y, f1), __fadd_rn(x.z, f2), __fadd_rn(x.w, f3));
+    }
+    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + (uint64_t)row * p.n + c) = o;
   } else {
     *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + (uint64_t)row * p.n + c) =
         make_uint2(bf16_rne(f0) | (bf16_rne(f1) << 16), bf16_rne(f2) | (bf16_rne(f3) << 16));
@@ -497,7 +508,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             const int kb = kb0 + b - ncorr;
             tma_load_2d(sA, &tmA, &bars->full[s], kb * kKB, (int)(bt * p.a_brows) + m0);
-            tma_load_2d(sB, &tmB, &bars->full[s], kb * kKB, (int)((bt / p.b_bdiv) * p.b_brows) + n0);
+            if (p.swiglu) {
+              // 128 gate rows, then their 128 up rows (tmCB: B with 128-row boxes)
+              tma_load_2d(sB, &tmCB, &bars->full[s], kb * kKB, n0 / 2);
+              tma_load_2d(sB + 128 * kKB, &tmCB, &bars->full[s], kb * kKB, p.n + n0 / 2);
+            } else {
+              tma_load_2d(sB, &tmB, &bars->full[s], kb * kKB, (int)((bt / p.b_bdiv) * p.b_brows) + n0);
+            }
           }
         }
       }
@@ -679,6 +696,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = warp_wait(&bars->acc_full[b], (local >> 1) & 1, abort_flag, p.status, p.wait_ns);
         if (!ok) break;
         tc_fence_after();
+        if (p.swiglu) {
+          // gate columns 32 cb .. 32 cb + 31 and their up columns + 128: 32 outputs per row, built
+          // in two halves, then stored 4 rows x 32 columns per instruction through the warp's tile
+          uint32_t* const tile = tiles + warp * C::TILE_WORDS;
+          const int row = m0 + 32 * q + lane, f0 = n0 / 2 + 32 * cb;
+          const float sx = row < p.m ? p.a_scale[row] : 0.f;
+#pragma unroll 1
+          for (int hh = 0; hh < 2; hh++) {
+            uint32_t g[16], u[16];
+            tmem_ld_32x32b_x16(lane_base + tmem + b * 256 + 32 * cb + 16 * hh, g);
+            tmem_ld_32x32b_x16(lane_base + tmem + b * 256 + 128 + 32 * cb + 16 * hh, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int f = f0 + 16 * hh + i;
+              float hv = 0.f;
+              if (f < p.n)
+                hv = det_swiglu(__fmul_rn(__fmul_rn(__int2float_rn((int)g[i]), sx), __ldg(p.b_scale + f)),
+                                __fmul_rn(__fmul_rn(__int2float_rn((int)u[i]), sx), __ldg(p.b_scale + p.n + f)));
+              tile[lane * 33 + 16 * hh + i] = __float_as_uint(hv);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ACC_ARRIVE(&bars->acc_empty[b]);
+          const int cl = 4 * (lane & 7), c = f0 + cl;
+#pragma unroll
+          for (int pass = 0; pass < 8; pass++) {
+            const int rl = pass * 4 + (lane >> 3), rr = m0 + 32 * q + rl;
+            const uint32_t* t = tile + rl * 33 + cl;
+            if (rr < p.m && c < p.n)
+              *reinterpret_cast<uint4*>(static_cast<float*>(p.out) + (uint64_t)rr * p.n + c) =
+                  make_uint4(t[0], t[1], t[2], t[3]);
+          }
+          __syncwarp();
+          continue;
+        }
         const uint32_t col = tmem + b * 256 + cb * 64;
 #pragma unroll 1
         for (int h = 0; h < 2; h++) {
@@ -1107,11 +1161,13 @@ extern "C" uint64_t uwc_gemm_workspace_bytes(int m, int n, int flags, int out_mo
   return bytes;
 }
 
-extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
-                        const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key,
-                        const uint32_t* target, uint32_t* wins, int max_wins, const float* a_scale,
-                        const float* b_scale, void* out, int out_mode, void* workspace, uint64_t workspace_bytes,
-                        void* stream) {
+namespace {
+// uwc_gemm, plus the fused output steps of uwc_gemm_epi for plain calls: resid (F32 out + x) and
+// swiglu (B = [gate; up] with 2n rows, F32 out m x n).
+int gemm_impl(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
+              const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key, const uint32_t* target,
+              uint32_t* wins, int max_wins, const float* a_scale, const float* b_scale, void* out, int out_mode,
+              void* workspace, uint64_t workspace_bytes, void* stream, const float* resid, int swiglu) {
   const bool hash = flags & UWC_FLAG_HASH, denoise = flags & UWC_FLAG_DENOISE;
   if (!A || !B || (flags & ~3) || out_mode < 0 || out_mode > 3) return UWC_ERR_ARG;
   if (out_mode != UWC_OUT_NONE && !out) return UWC_ERR_ARG;
@@ -1129,10 +1185,10 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
        ((uintptr_t)workspace)) & 15)
     return UWC_ERR_ALIGN;
   UWC_CHECK_DEVICE();
-  const uint64_t need = uwc_gemm_workspace_bytes(m, n, flags, out_mode);
+  const uint64_t need = swiglu ? 0 : uwc_gemm_workspace_bytes(m, n, flags, out_mode);
   if (need && (!workspace || workspace_bytes < need)) return UWC_ERR_SCRATCH;
   // decode-sized m: W streamed once, k split over a cluster, the output step in its epilogue
-  if (!hash && !denoise && out_mode != UWC_OUT_NONE && uwc_stream_gemm_fits(m, n, k)) {
+  if (!hash && !denoise && !resid && !swiglu && out_mode != UWC_OUT_NONE && uwc_stream_gemm_fits(m, n, k)) {
     const int epi = out_mode == UWC_OUT_I32 ? UWC_SEPI_I32 : (out_mode == UWC_OUT_F32 ? UWC_SEPI_F32 : UWC_SEPI_BF16);
     return uwc_gemm_stream(A, B, m, n, k, a_scale, b_scale, nullptr, out, epi, stream);
   }
@@ -1142,6 +1198,7 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   p.hash = hash; p.denoise = denoise; p.lmax = lmax; p.out_mode = out_mode; p.max_wins = max_wins;
   p.maxabs = maxabs; p.key = key; p.target = target; p.wins = wins;
   p.a_scale = a_scale; p.b_scale = b_scale; p.out = out;
+  p.resid = resid; p.swiglu = swiglu;
   p.status = uwc_status_ptr();
   p.one = 1u;
   p.b_bdiv = 1;
@@ -1170,6 +1227,14 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
     p.nm = (m + 127) / 128;
     p.nunits = p.nm * p.nn;
     if (denoise) return launch<MODE_FWD, 0>(p, ta, tb, tca, tcb, st);
+    if (swiglu) {
+      // units of 128 outputs: 128 gate rows of B over their 128 up rows (two 128-row boxes)
+      rc = uwc_make_tmap_2d(&tcb, B, (uint64_t)2 * n, (uint64_t)k, (uint64_t)k, 128, kKB);
+      if (rc != UWC_OK) return rc;
+      p.nn = (n + 127) / 128;
+      p.nunits = p.nm * p.nn;
+      return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
+    }
     if (out_mode == UWC_OUT_NONE || !split_k(m, n) || kblocks < 2)
       return launch<MODE_PLAIN, 0>(p, ta, tb, tca, tcb, st);
     // split-K: each unit owns a k-block range of one output block and adds its int32 partial into
@@ -1207,6 +1272,52 @@ extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, i
   }
   p.stage = stage_bytes(flags, out_mode) ? static_cast<int32_t*>(workspace) : nullptr;
   return launch_r<MODE_MINE_FWD>(p, ta, tb, tca, tcb, st);
+}
+}  // namespace
+
+extern "C" int uwc_gemm(const int8_t* A, const int8_t* B, int m, int n, int k, int r, int flags, const int8_t* corrA,
+                        const int8_t* corrB, const int32_t* maxabs, int lmax, const uint32_t* key,
+                        const uint32_t* target, uint32_t* wins, int max_wins, const float* a_scale,
+                        const float* b_scale, void* out, int out_mode, void* workspace, uint64_t workspace_bytes,
+                        void* stream) {
+  return gemm_impl(A, B, m, n, k, r, flags, corrA, corrB, maxabs, lmax, key, target, wins, max_wins, a_scale,
+                   b_scale, out, out_mode, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+namespace {
+int epi_out_mode(int epi) {
+  switch (epi) {
+    case UWC_SEPI_I32: return UWC_OUT_I32;
+    case UWC_SEPI_BF16: return UWC_OUT_BF16;
+    default: return UWC_OUT_F32;
+  }
+}
+}  // namespace
+
+extern "C" uint64_t uwc_gemm_epi_workspace_bytes(int m, int n, int epi) {
+  epi &= ~UWC_SEPI_EARLY_W;
+  if (m <= 0 || n <= 0 || epi < UWC_SEPI_I32 || epi > UWC_SEPI_SWIGLU) return 0;
+  if (m <= 64 || epi == UWC_SEPI_SWIGLU) return 0;
+  return uwc_gemm_workspace_bytes(m, n, 0, epi_out_mode(epi));
+}
+
+extern "C" int uwc_gemm_epi(const int8_t* A, const int8_t* W, int m, int n, int k, const float* a_scale,
+                            const float* w_scale, const float* resid, void* out, int epi, void* workspace,
+                            uint64_t workspace_bytes, void* stream) {
+  const int kind = epi & ~UWC_SEPI_EARLY_W;
+  if (kind < UWC_SEPI_I32 || kind > UWC_SEPI_SWIGLU) return UWC_ERR_ARG;
+  if (resid && kind != UWC_SEPI_RESID) return UWC_ERR_ARG;
+  // decode-sized m: the weight-streaming GEMM (its own argument checks)
+  if (uwc_stream_gemm_fits(m, n, k) && (kind != UWC_SEPI_SWIGLU || n % 128 == 0))
+    return uwc_gemm_stream(A, W, m, n, k, a_scale, w_scale, resid, out, epi, stream);
+  if (kind == UWC_SEPI_SWIGLU) {
+    if (n % 8) return UWC_ERR_SHAPE;   // n / 2 outputs per row, 16-byte rows
+    return gemm_impl(A, W, m, n / 2, k, 0, 0, nullptr, nullptr, nullptr, 0, nullptr, nullptr, nullptr, 0, a_scale,
+                     w_scale, out, UWC_OUT_F32, workspace, workspace_bytes, stream, nullptr, 1);
+  }
+  return gemm_impl(A, W, m, n, k, 0, 0, nullptr, nullptr, nullptr, 0, nullptr, nullptr, nullptr, 0, a_scale, w_scale,
+                   out, epi_out_mode(kind), workspace, workspace_bytes, stream, kind == UWC_SEPI_RESID ? resid : nullptr,
+                   0);
 }
 
 // Batched exact int8 GEMM, int32 out: out[bt] (m x n) = A[bt] B[bt / b_bdiv]^T for bt < nbatch, A[bt]

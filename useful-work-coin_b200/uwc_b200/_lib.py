@@ -38,6 +38,8 @@ SIGNATURES = {
     "uwc_gemm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32,
                         _P, _U64, _P]),
     "uwc_gemm_stream": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P]),
+    "uwc_gemm_epi_workspace_bytes": (_U64, [_I32, _I32, _I32]),
+    "uwc_gemm_epi": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _I32, _P, _U64, _P]),
     "uwc_tp_buffer_bytes": (_U64, [_I32, _I32]),
     "uwc_tp_alloc": (_I32, [_I32, _I32, _P]),
     "uwc_tp_free": (_I32, [_P]),

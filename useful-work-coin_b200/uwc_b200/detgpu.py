@@ -149,21 +149,19 @@ def norm_linear(lin, w_norm: torch.Tensor, x: torch.Tensor, eps: float) -> torch
 
 
 def linear_resid(lin, q: torch.Tensor, s: torch.Tensor, x: torch.Tensor | None) -> torch.Tensor:
-    """fadd(x, deq(q @ Wq^T)): the GEMM and dequant_residual (stages.py:117-125); decode-sized rows
-    run it as one weight-streaming GEMM with the residual add in its epilogue."""
-    if q.shape[0] <= ops.STREAM_MAX_M:
-        return ops.gemm_stream(q, lin.Wq, ops.SEPI_RESID, x_scale=s, w_scale=lin.sw, resid=x, early_w=True)
-    return dequant_residual(det.int_gemm(q, lin.Wq), s, lin.sw, x)
+    """fadd(x, deq(q @ Wq^T)): the GEMM and dequant_residual (stages.py:117-125) as one kernel, the
+    residual add in the GEMM's epilogue (decode-sized rows: the weight-streaming GEMM)."""
+    return ops.gemm_epi(q, lin.Wq, ops.SEPI_RESID, x_scale=s, w_scale=lin.sw, resid=x, early_w=True)
 
 
 def mlp_residual(gu, down, w_norm: torch.Tensor, r1: torch.Tensor, eps: float) -> torch.Tensor:
     """The MLP half of runtime/detgpu/stages.py layer_fused (:148-153): rmsnorm_quant, gate/up GEMM,
-    swiglu_quant, down GEMM, dequant_residual -- bit-identical to detrt.fast (:182-189). Decode-sized
-    rows take the SwiGLU and the residual add inside the weight-streaming GEMMs (quant_act of the
-    SwiGLU row is swiglu_quant's second half)."""
+    swiglu_quant, down GEMM, dequant_residual -- bit-identical to detrt.fast (:182-189). The SwiGLU and
+    the residual add run inside the GEMMs' epilogues (quant_act of the SwiGLU row is swiglu_quant's
+    second half), so no int32 product goes through HBM."""
     q3, s3 = rmsnorm_quant(r1, w_norm, eps, gu.bs)
-    if q3.shape[0] <= ops.STREAM_MAX_M and gu.Wq.shape[0] % 128 == 0:
-        h = ops.gemm_stream(q3, gu.Wq, ops.SEPI_SWIGLU, x_scale=s3, w_scale=gu.sw, early_w=True)
+    if gu.Wq.shape[0] % 8 == 0:
+        h = ops.gemm_epi(q3, gu.Wq, ops.SEPI_SWIGLU, x_scale=s3, w_scale=gu.sw, early_w=True)
         q4, s4 = quant_act(h, down.bs)
     else:
         q4, s4 = swiglu_quant(det.int_gemm(q3, gu.Wq), s3, gu.sw, down.bs)

@@ -232,6 +232,31 @@ def gemm_stream(X, W, epi=SEPI_I32, *, x_scale=None, w_scale=None, resid=None, o
     return out
 
 
+def gemm_epi(X, W, epi=SEPI_I32, *, x_scale=None, w_scale=None, resid=None, out=None, early_w=False):
+    """gemm_stream's epilogues at any m (uwc_gemm_epi): m <= 64 streams W; larger m runs the tcgen05
+    GEMM with the output step (dequant, + resid, SwiGLU of W = [gate; up]) in its epilogue, so no
+    int32 product goes through HBM."""
+    m, k = X.shape
+    n = W.shape[0]
+    assert X.dtype == torch.int8 and W.dtype == torch.int8 and X.is_contiguous() and W.is_contiguous()
+    if out is None:
+        dt = {SEPI_I32: torch.int32, SEPI_BF16: torch.bfloat16}.get(epi, torch.float32)
+        out = torch.empty((m, n // 2 if epi == SEPI_SWIGLU else n), dtype=dt, device=X.device)
+    f32 = (lambda t: None if t is None else t.contiguous().float())
+    flags = epi | (SEPI_EARLY_W if early_w else 0)
+    nbytes = int(lib().uwc_gemm_epi_workspace_bytes(m, n, epi))
+    ws = None
+    if nbytes:
+        key = str(torch.device(X.device))
+        ws = _GEMM_WS.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = _GEMM_WS[key] = torch.empty(nbytes, dtype=torch.uint8, device=X.device)
+    check(lib().uwc_gemm_epi(_p(X), _p(W), m, n, k, _p(f32(x_scale)), _p(f32(w_scale)),
+                             _p(None if resid is None else resid.contiguous()), _p(out), flags, _p(ws),
+                             0 if ws is None else ws.numel(), _stream()), "gemm_epi")
+    return out
+
+
 # ------------------------------------------------------------------ one mined linear layer
 MB_CONSTS, MB_EBRT, MB_PB, MB_SBT, MB_BPEBT, MB_BYTES = range(6)
 MW_A_SEED, MW_MAXABS, MW_EAL, MW_PA, MW_APEA, MW_B3, MW_GEMM, MW_SAT, MW_CORRA, MW_CORRB, MW_PROJA, MW_PROJB, \

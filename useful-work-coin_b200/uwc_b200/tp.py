@@ -18,9 +18,10 @@ bit-identical to one device:
 
 `kernels` is the device backend: by default this library's CUDA kernels (GPUKernels); tests pass
 a CPU stand-in built from the oracle to check the sharding and collectives with gloo ranks. A
-backend with `fused = True` also offers quant_act, linear_resid and swiglu_linear: decode-sized
-calls then run the output step inside the weight-streaming GEMM (the row-parallel layer on one
-rank, and the gate/up SwiGLU on any number), with the same bits as the separate kernels. Given a
+backend with `fused = True` also offers quant_act, linear_resid and swiglu_linear: the output step
+then runs inside the GEMM's epilogue (the row-parallel layer on one rank, and the gate/up SwiGLU on
+any number; the weight-streaming GEMM for decode-sized calls), with the same bits as the separate
+kernels. Given a
 PeerExchange, a row-parallel layer on several ranks runs its two all-reduces (the row absmax and
 the int32 partial products) inside its quantizer and GEMM over NVLink peer memory instead of NCCL.
 """
@@ -144,17 +145,10 @@ class GPUKernels:
     def quant_act(self, x, bs):
         return self._mods()[1].quant_act(x, bs)
 
-    @staticmethod
-    def _stream(q):
-        from . import ops
-        return ops if q.shape[0] <= ops.STREAM_MAX_M else None
-
     def linear_resid(self, q, s, Wq, sw, x):
-        """fadd(x, deq(q Wq^T)) (x None: deq alone)."""
-        ops = self._stream(q)
-        if ops is None:
-            return self.dequant_residual(self.int_gemm(q, Wq), s, sw, x)
-        return ops.gemm_stream(q, Wq, ops.SEPI_RESID, x_scale=s, w_scale=sw, resid=x, early_w=True)
+        """fadd(x, deq(q Wq^T)) (x None: deq alone), the output step in the GEMM's epilogue."""
+        from . import ops
+        return ops.gemm_epi(q, Wq, ops.SEPI_RESID, x_scale=s, w_scale=sw, resid=x, early_w=True)
 
     def quant_act_tp(self, x, bs, exchange):
         """quant_act of a row-parallel shard with the whole row's absmax, exchanged in the kernel."""
@@ -182,11 +176,11 @@ class GPUKernels:
         return out
 
     def swiglu_linear(self, q, s, Wq, sw):
-        """det_silu(deq(gate)) * deq(up) of q [gate; up]^T."""
-        ops = self._stream(q)
-        if ops is None or Wq.shape[0] % 128:
+        """det_silu(deq(gate)) * deq(up) of q [gate; up]^T, computed in the GEMM's epilogue."""
+        from . import ops
+        if Wq.shape[0] % 8:
             return self.swiglu(self.int_gemm(q, Wq), s, sw)
-        return ops.gemm_stream(q, Wq, ops.SEPI_SWIGLU, x_scale=s, w_scale=sw, early_w=True)
+        return ops.gemm_epi(q, Wq, ops.SEPI_SWIGLU, x_scale=s, w_scale=sw, early_w=True)
 
 
 def _default(kernels):
