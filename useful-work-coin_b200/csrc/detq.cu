@@ -300,8 +300,10 @@ __device__ __forceinline__ long long cta_sumll(long long v, long long* red) {
   return t;
 }
 
+// The plain form is held to 32 registers so that two rows' CTAs share an SM when there are many
+// rows (16384 rows of k = 14336: 500 -> 426 us).
 template <bool RMS, bool TP>
-__global__ void __launch_bounds__(1024) k_row_quant512(const float* __restrict__ x, const float* __restrict__ w, int k,
+__global__ void __launch_bounds__(1024, RMS || TP ? 1 : 2) k_row_quant512(const float* __restrict__ x, const float* __restrict__ w, int k,
                                                        float inv_d, float eps, int L, int8_t* __restrict__ q,
                                                        float* __restrict__ scale, TPArgs tp, uint32_t* status,
                                                        uint64_t wait_ns) {
