@@ -277,8 +277,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a, in
 }
 
 // ---- decode: one query token per sequence (Tq = 1), the keys split over a cluster of CTAs.
-// A cluster of kDecCluster CTAs serves one (sequence, KV head) pair and all HPG = H / Hkv query
-// heads that read it, so each key and value row is loaded once per token. CTA `rank` owns keys
+// A cluster of CL (4, or kDecCluster for long caches) CTAs serves one (sequence, KV head) pair and
+// all HPG = H / Hkv query heads that read it, so each key and value row is loaded once per token. CTA `rank` owns keys
 // [rank S / C, (rank + 1) S / C). The softmax's four row reductions (max, max of e, the exact int64
 // sum, max of P * sv) and the int64 P V partials combine across the cluster through distributed
 // shared memory: max and integer addition are exact in any order, so the result is bit-identical
@@ -308,8 +308,8 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int HPG>
-__global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThreads)
+template <int HPG, int CL>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kAttnThreads)
     k_attn_decode(const AttnArgs a, int lpitch) {
   constexpr int NW = kAttnThreads / 32, WPR = NW / HPG;
   static_assert(HPG >= 1 && HPG <= NW && NW % HPG == 0, "query heads per KV head");
@@ -326,11 +326,11 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThrea
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r = warp / WPR, part = warp % WPR;
   const int rank = (int)cluster.block_rank();
-  const int pair = blockIdx.x / kDecCluster;
+  const int pair = blockIdx.x / CL;
   const int b = pair / a.Hkv, g = pair % a.Hkv;
   const int start = a.start_dev ? __ldg(a.start_dev) : a.start;
   const int S = start + 1;
-  const int k0 = (int)((long long)rank * S / kDecCluster), k1 = (int)((long long)(rank + 1) * S / kDecCluster);
+  const int k0 = (int)((long long)rank * S / CL), k1 = (int)((long long)(rank + 1) * S / CL);
   const int nk = k1 - k0;
   const int8_t* kb = a.kc + b * a.kv_seq + g * a.kv_head;
   const int8_t* vb = a.vc + b * a.kv_seq + g * a.kv_head;
@@ -402,7 +402,7 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThrea
     if (part == 0 && lane == 0) ds.xf[slot][r] = v;
     cluster.sync();
 #pragma unroll
-    for (int q = 0; q < kDecCluster; q++) v = fmaxf(v, cluster.map_shared_rank(&ds.xf[slot][r], q)[0]);
+    for (int q = 0; q < CL; q++) v = fmaxf(v, cluster.map_shared_rank(&ds.xf[slot][r], q)[0]);
     return v;
   };
   // this CTA's exact fixed-point sum of the row's e at shift sh, into exchange slot `slot`
@@ -445,17 +445,17 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThrea
   cp_async_wait<1>();   // the value scales, read after this exchange
   cluster.sync();
 #pragma unroll
-  for (int q = 0; q < kDecCluster; q++) emax = fmaxf(emax, cluster.map_shared_rank(&ds.xf[1][r], q)[0]);
+  for (int q = 0; q < CL; q++) emax = fmaxf(emax, cluster.map_shared_rank(&ds.xf[1][r], q)[0]);
   const int sh = fixed_shift(emax, kMaxKeysLog2);
   long long acc = 0;
   if (__syncthreads_or(sh != sh_guess)) {
     cta_sum(sh, 1);
     cluster.sync();
 #pragma unroll
-    for (int q = 0; q < kDecCluster; q++) acc += cluster.map_shared_rank(&ds.xl[1][r], q)[0];
+    for (int q = 0; q < CL; q++) acc += cluster.map_shared_rank(&ds.xl[1][r], q)[0];
   } else {
 #pragma unroll
-    for (int q = 0; q < kDecCluster; q++) acc += cluster.map_shared_rank(&ds.xl[0][r], q)[0];
+    for (int q = 0; q < CL; q++) acc += cluster.map_shared_rank(&ds.xl[0][r], q)[0];
   }
   const float den = __double2float_rn(__ll2double_rn(acc) * pow2d(-sh));
   float pmax = 0.f;
@@ -513,11 +513,11 @@ __global__ void __cluster_dims__(kDecCluster, 1, 1) __launch_bounds__(kAttnThrea
   }
   cluster.sync();
   // the cluster's CTAs split the HPG x 128 outputs; each sums its share over the cluster
-  for (int i = rank * kAttnThreads + tid; i < HPG * kHd; i += kDecCluster * kAttnThreads) {
+  for (int i = rank * kAttnThreads + tid; i < HPG * kHd; i += CL * kAttnThreads) {
     const int rr = i / kHd, d = i % kHd;
     long long t = 0;
 #pragma unroll
-    for (int q = 0; q < kDecCluster; q++) t += cluster.map_shared_rank(&ds.part[rr][d], q)[0];
+    for (int q = 0; q < CL; q++) t += cluster.map_shared_rank(&ds.part[rr][d], q)[0];
     a.out[((size_t)b * a.H + h0 + rr) * kHd + d] = __fmul_rn(__ll2float_rn(t), ds.sp[rr]);
   }
   cluster.sync();   // no CTA leaves while another may still read its shared memory
@@ -641,13 +641,13 @@ int launch_attn(const AttnArgs& a, int B, int spitch, cudaStream_t st) {
   return uwc_launch_status();
 }
 
-template <int HPG>
+template <int HPG, int CL>
 int launch_decode(const AttnArgs& a, int B, int lpitch, cudaStream_t st) {
   const int smem = (int)dec_smem(HPG, lpitch);
   // the opt-in covers the static reduction slots too (their sum passes 48 KiB before the dynamic part does)
-  const int rc = smem_optin((const void*)k_attn_decode<HPG>, smem + (int)sizeof(DecShared<HPG>));
+  const int rc = smem_optin((const void*)k_attn_decode<HPG, CL>, smem + (int)sizeof(DecShared<HPG>));
   if (rc != UWC_OK) return rc;
-  k_attn_decode<HPG><<<B * a.Hkv * kDecCluster, kAttnThreads, smem, st>>>(a, lpitch);
+  k_attn_decode<HPG, CL><<<B * a.Hkv * CL, kAttnThreads, smem, st>>>(a, lpitch);
   uwc_count_launch();
   return uwc_launch_status();
 }
@@ -672,18 +672,23 @@ int attention_impl(const int8_t* qq, const float* qs, const int8_t* kc, const fl
              out, start_dev};
   cudaStream_t st = (cudaStream_t)stream;
   if (Tq == 1 && (long long)B * Hkv * kDecCluster <= 0x7fffffffLL) {
-    // decode: the keys split over a cluster, all query heads of a KV head in one cluster
-    const int per = (S + kDecCluster - 1) / kDecCluster;
-    const int lpitch = (per + kTileKeys - 1) / kTileKeys * kTileKeys;
+    // decode: the keys split over a cluster, all query heads of a KV head in one cluster; 4 CTAs
+    // (fewer, longer chains: 16.0 vs 18.5 us at batch 8 x 2100 positions) while a CTA's share of the
+    // keys fits in shared memory, else 8
     const int hpg = H / Hkv;
-    if (dec_smem(hpg, lpitch) <= (size_t)kAttnSmemMax) {
+    for (int cl = kDecCluster / 2; cl <= kDecCluster; cl *= 2) {
+      const int per = (S + cl - 1) / cl;
+      const int lpitch = (per + kTileKeys - 1) / kTileKeys * kTileKeys;
+      if (dec_smem(hpg, lpitch) > (size_t)kAttnSmemMax) continue;
+      const bool four = cl < kDecCluster;
       switch (hpg) {
-        case 1: return launch_decode<1>(a, B, lpitch, st);
-        case 2: return launch_decode<2>(a, B, lpitch, st);
-        case 4: return launch_decode<4>(a, B, lpitch, st);
-        case 8: return launch_decode<8>(a, B, lpitch, st);
+        case 1: return four ? launch_decode<1, 4>(a, B, lpitch, st) : launch_decode<1, 8>(a, B, lpitch, st);
+        case 2: return four ? launch_decode<2, 4>(a, B, lpitch, st) : launch_decode<2, 8>(a, B, lpitch, st);
+        case 4: return four ? launch_decode<4, 4>(a, B, lpitch, st) : launch_decode<4, 8>(a, B, lpitch, st);
+        case 8: return four ? launch_decode<8, 4>(a, B, lpitch, st) : launch_decode<8, 8>(a, B, lpitch, st);
         default: break;
       }
+      break;
     }
   }
   // the widest query block whose score rows fit in shared memory (and not wider than Tq needs)
