@@ -830,7 +830,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             red_xor_shared(msg + sl * kMaxTiles + slot[a], __funnelshift_l(x, x, rot));
           }
         };
-        // the last chunk of a forward (which also writes the output) is peeled off the loop
+        // the last chunk of a forward (which also writes the output) is peeled off the loop; two
+        // chunks per iteration let the scheduler interleave one chunk's fold with the next's loads
+        // (C3 r = 64: 0.6195 -> 0.6072 ms)
+#pragma unroll 2
         for (int c = 0; c < (FWDH ? nch - 1 : nch) && ok; c++) chunk(c, false);
         if (FWDH && ok) chunk(nch - 1, true);
         if (!ok) break;
