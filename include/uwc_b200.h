@@ -351,6 +351,14 @@ int uwc_qkv_post_at(const int32_t* acc, const float* s1, const float* sw, const 
                     const float* cos_table, const float* sin_table, const int* pos, int N, int T, int H, int Hkv,
                     double eps, int qknorm, int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs,
                     void* stream);
+/* uwc_qkv_post_at with the keys and values written straight into a KV cache (the qkv_post +
+ * kv_append pair of a decode step as one kernel): token r % T of sequence r / T lands at cache
+ * position *pos + r % T of kc / vc ((B, Hkv, maxlen, 128) int8) and skc / svc ((B, Hkv, maxlen)
+ * scales); positions >= maxlen are not written. Same values as uwc_qkv_post_at + uwc_kv_append. */
+int uwc_qkv_post_kv(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
+                    const float* cos_table, const float* sin_table, const int* pos, int N, int T, int H, int Hkv,
+                    double eps, int qknorm, int8_t* qq, float* qs, int8_t* kc, float* skc, int8_t* vc, float* svc,
+                    int maxlen, void* stream);
 
 /* Deterministic attention from quantized q, k, v (runtime/detrt/qwen3.py:254-283 _attention;
  * GPU form runtime/detgpu/kernels.py:731-771 attention): exact int32 Q K^T, scores

@@ -214,3 +214,37 @@ def test_many_rows_path_matches_oracle(dg):
     wq, ws = D.swiglu_quant(acc, s3, sw, 256)
     same(q, wq)
     same(s, ws)
+
+
+@pytest.mark.parametrize("B,T,start,maxlen", [(8, 1, 2099, 2176), (2, 3, 10, 64), (3, 4, 62, 64)])
+def test_qkv_post_kv_equals_post_at_then_append(dg, B, T, start, maxlen):
+    """The decode step's fused qkv_post + KV-cache store == qkv_post_at followed by kv_append,
+    including tokens whose cache position falls past maxlen (left unwritten by both)."""
+    H, Hkv = 16, 8
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + T)
+    N, width = B * T, (H + 2 * Hkv) * 128
+    acc = torch.randint(-2 ** 20, 2 ** 20, (N, width), dtype=torch.int32, device="cuda", generator=g)
+    s1 = torch.rand(N, device="cuda", generator=g) * 1e-3 + 1e-5
+    sw = torch.rand(width, device="cuda", generator=g) * 1e-3 + 1e-5
+    qnw = 1 + 0.1 * torch.randn(128, device="cuda", generator=g)
+    knw = 1 + 0.1 * torch.randn(128, device="cuda", generator=g)
+    ang = torch.arange(maxlen + 8, device="cuda")[:, None] * (1e-4 ** (torch.arange(64, device="cuda") / 64))[None]
+    cos = torch.cat([torch.cos(ang), torch.cos(ang)], 1).float().contiguous()
+    sin = torch.cat([torch.sin(ang), torch.sin(ang)], 1).float().contiguous()
+    pos = torch.tensor([start], dtype=torch.int32, device="cuda")
+
+    def cache():
+        z = lambda *s, dt=torch.int8: torch.full(s, 7, dtype=dt, device="cuda")
+        return dict(k=z(B, Hkv, maxlen, 128), sk=z(B, Hkv, maxlen, 1, dt=torch.float32),
+                    v=z(B, Hkv, maxlen, 128), sv=z(B, Hkv, maxlen, 1, dt=torch.float32))
+
+    want_c = cache()
+    qq, qs, kq, ks, vq, vs = dg.qkv_post_at(acc, s1, sw, qnw, knw, cos, sin, pos, T, H, Hkv, 1e-6)
+    dg.kv_append(kq, ks, vq, vs, want_c, B, T, pos)
+    got_c = cache()
+    qq2, qs2 = dg.qkv_post_kv(acc, s1, sw, qnw, knw, cos, sin, pos, T, H, Hkv, 1e-6, got_c)
+    assert torch.equal(qq2, qq) and torch.equal(qs2.view(-1).view(torch.int32), qs.view(-1).view(torch.int32))
+    for key in ("k", "v"):
+        assert torch.equal(got_c[key], want_c[key]), key
+    for key in ("sk", "sv"):
+        assert torch.equal(got_c[key].view(torch.int32), want_c[key].view(torch.int32)), key

@@ -489,13 +489,26 @@ __device__ __forceinline__ void head_quant127(const float* v, int lane, int8_t* 
 // The qkv GEMM's int32 row -> quantized q, k, v heads (detrt/fast.py:108-120). One CTA per row
 // (token), one warp per head; element i of a head is v[j] of lane i % 32 with j = i / 32, so the
 // rope partner i +- 64 is v[j +- 2] of the same lane.
+// The KV cache a decode step's keys and values go straight into (uwc_qkv_post_kv): (B, Hkv, maxlen,
+// 128) int8 rows and (B, Hkv, maxlen) scales; k == nullptr: write the kq / vq rows instead.
+struct KVDest {
+  int8_t* k;
+  float* sk;
+  int8_t* v;
+  float* sv;
+  int maxlen;
+};
+
 __global__ void __launch_bounds__(kRowThreads) k_qkv_post(
     const int32_t* __restrict__ acc, const float* __restrict__ s1, const float* __restrict__ sw,
     const float* __restrict__ qnw, const float* __restrict__ knw, const float* __restrict__ cosT,
     const float* __restrict__ sinT, int T, int H, int Hkv, float inv_hd, float eps, int qknorm,
     int8_t* __restrict__ qq, float* __restrict__ qs, int8_t* __restrict__ kq, float* __restrict__ ks,
-    int8_t* __restrict__ vq, float* __restrict__ vs, const int* __restrict__ pos0) {
+    int8_t* __restrict__ vq, float* __restrict__ vs, const int* __restrict__ pos0, const KVDest kv) {
   const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // with a cache destination: token row % T of sequence row / T lands at position pos0 + row % T
+  const int cpos = kv.k ? __ldg(pos0) + row % T : 0;
+  const long long cbase = kv.k ? (long long)(row / T) * Hkv * kv.maxlen + cpos : 0;   // (b, head 0, cpos)
   // rope table row: position r % T, offset by a device-side start position when given
   const int nh = H + 2 * Hkv, width = nh * 128, t = row % T + (pos0 ? __ldg(pos0) : 0);
   const float s = s1[row];
@@ -508,7 +521,12 @@ __global__ void __launch_bounds__(kRowThreads) k_qkv_post(
     }
     if (hh >= H + Hkv) {
       const int hv = hh - H - Hkv;
-      head_quant127(v, lane, vq + ((uint64_t)row * Hkv + hv) * 128, vs + (uint64_t)row * Hkv + hv);
+      if (!kv.k) {
+        head_quant127(v, lane, vq + ((uint64_t)row * Hkv + hv) * 128, vs + (uint64_t)row * Hkv + hv);
+      } else if (cpos < kv.maxlen) {
+        const long long d = cbase + (long long)hv * kv.maxlen;
+        head_quant127(v, lane, kv.v + d * 128, kv.sv + d);
+      }
       continue;
     }
     if (qknorm) {
@@ -537,10 +555,14 @@ __global__ void __launch_bounds__(kRowThreads) k_qkv_post(
       const float rot = j < 2 ? -v[j + 2] : v[j - 2];
       o[j] = __fadd_rn(__fmul_rn(v[j], cosT[t * 128 + i]), __fmul_rn(rot, sinT[t * 128 + i]));
     }
-    if (hh < H)
+    if (hh < H) {
       head_quant127(o, lane, qq + ((uint64_t)row * H + hh) * 128, qs + (uint64_t)row * H + hh);
-    else
+    } else if (!kv.k) {
       head_quant127(o, lane, kq + ((uint64_t)row * Hkv + hh - H) * 128, ks + (uint64_t)row * Hkv + hh - H);
+    } else if (cpos < kv.maxlen) {
+      const long long d = cbase + (long long)(hh - H) * kv.maxlen;
+      head_quant127(o, lane, kv.k + d * 128, kv.sk + d);
+    }
   }
 }
 
@@ -745,15 +767,16 @@ namespace {
 int qkv_post_launch(const int32_t* acc, const float* s1, const float* sw, const float* qnw, const float* knw,
                     const float* cos_t, const float* sin_t, int N, int T, int H, int Hkv, double eps, int qknorm,
                     int8_t* qq, float* qs, int8_t* kq, float* ks, int8_t* vq, float* vs, const int* pos0,
-                    void* stream) {
-  if (!acc || !s1 || !sw || !cos_t || !sin_t || !qq || !qs || !kq || !ks || !vq || !vs) return UWC_ERR_ARG;
+                    void* stream, KVDest kv = KVDest{}) {
+  if (!acc || !s1 || !sw || !cos_t || !sin_t || !qq || !qs) return UWC_ERR_ARG;
+  if (kv.k ? (!kv.sk || !kv.v || !kv.sv || kv.maxlen <= 0 || !pos0) : (!kq || !ks || !vq || !vs)) return UWC_ERR_ARG;
   if (qknorm && (!qnw || !knw)) return UWC_ERR_ARG;
   if (N < 0 || T <= 0 || H <= 0 || Hkv <= 0) return UWC_ERR_SHAPE;
   UWC_CHECK_DEVICE();
   if (N == 0) return UWC_OK;
   k_qkv_post<<<N, kRowThreads, 0, (cudaStream_t)stream>>>(acc, s1, sw, qnw, knw, cos_t, sin_t, T, H, Hkv,
                                                           (float)(1.0 / 128), (float)eps, qknorm, qq, qs, kq, ks, vq,
-                                                          vs, pos0);
+                                                          vs, pos0, kv);
   uwc_count_launch();
   return uwc_launch_status();
 }
@@ -765,6 +788,15 @@ extern "C" int uwc_qkv_post(const int32_t* acc, const float* s1, const float* sw
                             void* stream) {
   return qkv_post_launch(acc, s1, sw, qnw, knw, cos_t, sin_t, N, T, H, Hkv, eps, qknorm, qq, qs, kq, ks, vq, vs,
                          nullptr, stream);
+}
+
+extern "C" int uwc_qkv_post_kv(const int32_t* acc, const float* s1, const float* sw, const float* qnw,
+                               const float* knw, const float* cos_table, const float* sin_table, const int* pos,
+                               int N, int T, int H, int Hkv, double eps, int qknorm, int8_t* qq, float* qs,
+                               int8_t* kc, float* skc, int8_t* vc, float* svc, int maxlen, void* stream) {
+  if (!pos || !kc) return UWC_ERR_ARG;
+  return qkv_post_launch(acc, s1, sw, qnw, knw, cos_table, sin_table, N, T, H, Hkv, eps, qknorm, qq, qs, nullptr,
+                         nullptr, nullptr, nullptr, pos, stream, KVDest{kc, skc, vc, svc, maxlen});
 }
 
 extern "C" int uwc_qkv_post_at(const int32_t* acc, const float* s1, const float* sw, const float* qnw,

@@ -77,6 +77,8 @@ SIGNATURES = {
     "uwc_kv_append": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
     "uwc_qkv_post_at": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F64, _I32, _P, _P, _P, _P,
                                _P, _P, _P]),
+    "uwc_qkv_post_kv": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _F64, _I32, _P, _P, _P, _P,
+                               _P, _P, _I32, _P]),
     "uwc_rmsnorm": (_I32, [_P, _P, _I32, _I32, _F64, _P, _P]),
     "uwc_logprobs": (_I32, [_P, _I32, _I32, _P, _P, _P]),
     "uwc_stage_scratch_words": (_U64, [_I64, _I32]),

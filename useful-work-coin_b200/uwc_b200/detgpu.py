@@ -275,6 +275,25 @@ def qkv_post_at(acc, s1, sw, qnw, knw, cos_table, sin_table, pos: torch.Tensor, 
     return qq, qs, kq, ks, vq, vs
 
 
+def qkv_post_kv(acc, s1, sw, qnw, knw, cos_table, sin_table, pos: torch.Tensor, T: int, H: int, Hkv: int, eps: float,
+                cache: dict, qknorm: bool = True):
+    """qkv_post_at with the keys / values stored straight into `cache` at pos (+ r % T): the
+    qkv_post_at + kv_append pair of a decode step in one kernel. Returns (qq, qs)."""
+    acc = acc.contiguous()
+    assert acc.dtype == torch.int32 and pos.dtype == torch.int32
+    N = acc.shape[0]
+    qq = torch.empty((N, H, 128), dtype=torch.int8, device=acc.device)
+    qs = torch.empty((N, H, 1), dtype=torch.float32, device=acc.device)
+    k, v, sk, sv = cache["k"], cache["v"], cache["sk"], cache["sv"]
+    assert k.shape[1] == Hkv and k.is_contiguous() and v.is_contiguous() and sk.is_contiguous() and sv.is_contiguous()
+    qn = _f32(qnw) if qknorm else None
+    kn = _f32(knw) if qknorm else None
+    check(lib().uwc_qkv_post_kv(_p(acc), _p(_f32(s1)), _p(_f32(sw)), _p(qn), _p(kn), _p(_f32(cos_table)),
+                                _p(_f32(sin_table)), _p(pos), N, T, H, Hkv, float(eps), int(bool(qknorm)), _p(qq),
+                                _p(qs), _p(k), _p(sk), _p(v), _p(sv), k.shape[2], _stream()), "qkv_post_kv")
+    return qq, qs
+
+
 def kv_append(kq, ks, vq, vs, cache: dict, B: int, T: int, pos: torch.Tensor) -> None:
     """Write the new tokens' keys / values into the cache at the device-side position pos."""
     k, v, sk, sv = cache["k"], cache["v"], cache["sk"], cache["sv"]

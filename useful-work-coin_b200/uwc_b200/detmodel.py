@@ -244,10 +244,8 @@ class DetQwen3:
         x = self.embed[tok]
         for L, c in zip(self.layers, cache):
             q1, s1 = detgpu.rmsnorm_quant(x, L["in_norm"], self.eps, L["qkv"].bs)
-            qq, qs, kq, ks, vq, vs = detgpu.qkv_post_at(L["qkv"].int_gemm(q1), s1, L["qkv"].sw, L["q_norm"],
-                                                        L["k_norm"], self.cos, self.sin, pos, 1, H, Hkv, self.eps,
-                                                        self.qk_norm)
-            detgpu.kv_append(kq, ks, vq, vs, c, B, 1, pos)
+            qq, qs = detgpu.qkv_post_kv(L["qkv"].int_gemm(q1), s1, L["qkv"].sw, L["q_norm"], L["k_norm"], self.cos,
+                                        self.sin, pos, 1, H, Hkv, self.eps, c, self.qk_norm)
             o = detgpu.attention_cache_at(qq, qs, c, B, 1, pos, max_start, H, Hkv, self.inv_sqrt_hd)
             q2, s2 = detgpu.quant_act(o, L["o"].bs)
             r1 = detgpu.linear_resid(L["o"], q2, s2, x)
