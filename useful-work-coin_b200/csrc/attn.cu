@@ -606,6 +606,80 @@ __global__ void __launch_bounds__(NT) k_logprobs(const float* __restrict__ lg, i
   }
 }
 
+// Few rows (a decode step's greedy tokens): k_logprobs with each row split over a cluster of
+// kLpCluster CTAs, CTA c owning elements [c V / C, (c + 1) V / C). The row max, the max of det_exp,
+// the exact fixed-point sum and the first maximal index are combined through distributed shared
+// memory; each is exact and order-free, so the outputs are k_logprobs' bits.
+constexpr int kLpCluster = 8, kLpThreads = 256;   // 8: the portable cluster size
+__global__ void __cluster_dims__(kLpCluster, 1, 1) __launch_bounds__(kLpThreads)
+    k_logprobs_cl(const float* __restrict__ lg, int V, float* __restrict__ lp, long long* __restrict__ tok) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  __shared__ float red[kLpThreads / 32];
+  __shared__ long long redl[kLpThreads / 32];
+  __shared__ float rv[kLpThreads / 32];
+  __shared__ int ri[kLpThreads / 32];
+  __shared__ float pub_f[2];
+  __shared__ long long pub_l;
+  __shared__ float pub_v;
+  __shared__ int pub_i;
+  const int c = (int)cl.block_rank(), row = blockIdx.x / kLpCluster;
+  const int i0 = (int)((long long)c * V / kLpCluster), i1 = (int)((long long)(c + 1) * V / kLpCluster);
+  const float* x = lg + (size_t)row * V;
+  float mx = __int_as_float(0xff800000);
+  for (int i = i0 + threadIdx.x; i < i1; i += kLpThreads) mx = fmaxf(mx, x[i]);
+  mx = block_maxf<kLpThreads>(mx, red);
+  if (threadIdx.x == 0) pub_f[0] = mx;
+  cl.sync();
+  for (int q = 0; q < kLpCluster; q++) mx = fmaxf(mx, *cl.map_shared_rank(&pub_f[0], q));
+  float emax = 0.f;
+  for (int i = i0 + threadIdx.x; i < i1; i += kLpThreads) emax = fmaxf(emax, det_exp(__fsub_rn(x[i], mx)));
+  emax = block_maxf<kLpThreads>(emax, red);
+  if (threadIdx.x == 0) pub_f[1] = emax;
+  cl.sync();
+  for (int q = 0; q < kLpCluster; q++) emax = fmaxf(emax, *cl.map_shared_rank(&pub_f[1], q));
+  const int sh = fixed_shift(emax, 18);
+  const double up = pow2d(sh);
+  long long acc = 0;
+  for (int i = i0 + threadIdx.x; i < i1; i += kLpThreads) acc += fixed_term(det_exp(__fsub_rn(x[i], mx)), up);
+  acc = block_sumll<kLpThreads>(acc, redl);
+  if (threadIdx.x == 0) pub_l = acc;
+  cl.sync();
+  long long tot = 0;
+  for (int q = 0; q < kLpCluster; q++) tot += *cl.map_shared_rank(&pub_l, q);
+  const float lden = det_log(__double2float_rn(__ll2double_rn(tot) * pow2d(-sh)));
+  float bv = __int_as_float(0xff800000);
+  int bi = 0x7fffffff;
+  float* o = lp ? lp + (size_t)row * V : nullptr;
+  for (int i = i0 + threadIdx.x; i < i1; i += kLpThreads) {
+    const float v = __fsub_rn(__fsub_rn(x[i], mx), lden);
+    if (o) o[i] = v;
+    better(bv, bi, v, i);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, off);
+    better(bv, bi, v2, i2);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    rv[threadIdx.x >> 5] = bv;
+    ri[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kLpThreads / 32; w++) better(bv, bi, rv[w], ri[w]);
+    pub_v = bv;
+    pub_i = bi;
+  }
+  cl.sync();
+  if (tok && c == 0 && threadIdx.x == 0) {
+    for (int q = 1; q < kLpCluster; q++) better(bv, bi, *cl.map_shared_rank(&pub_v, q), *cl.map_shared_rank(&pub_i, q));
+    tok[row] = bi;
+  }
+  cl.sync();   // peers keep their shared memory until rank 0 has read it
+}
+
 constexpr int kAttnSmemMax = 200 * 1024;
 
 // scores (QT x spitch floats), query rows, the transposed V tile, and for rows split over several
@@ -1072,7 +1146,10 @@ extern "C" int uwc_logprobs(const float* logits, int m, int V, float* lp, long l
   if (!logits || m < 0 || V <= 0 || (!lp && !tok)) return UWC_ERR_ARG;
   UWC_CHECK_DEVICE();
   if (m == 0) return UWC_OK;
-  k_logprobs<1024><<<m, 1024, 0, (cudaStream_t)stream>>>(logits, V, lp, tok);
+  if (m < uwc_num_sms() && V >= 64 * kLpCluster)
+    k_logprobs_cl<<<m * kLpCluster, kLpThreads, 0, (cudaStream_t)stream>>>(logits, V, lp, tok);
+  else
+    k_logprobs<1024><<<m, 1024, 0, (cudaStream_t)stream>>>(logits, V, lp, tok);
   uwc_count_launch();
   return uwc_launch_status();
 }
